@@ -1,0 +1,145 @@
+/*
+ * opencuda_cuda.h -- C ABI of libopencuda_cuda.so, the B200 (sm_100a)
+ * backend for the open-cuda workspace's matmul / attention hot path.
+ *
+ * Each entry point names the reference interface it replaces (paths are
+ * relative to the open-cuda workspace):
+ *   core  = crates/opencuda-core/src/device.rs  (the GpuDevice trait)
+ *   blas  = crates/opencuda-blas/src/lib.rs
+ *   llm   = crates/open-cuda-llm/src/lib.rs
+ *
+ * Conventions
+ *  - Every function returns an int status: 0 on success, otherwise one of
+ *    the OC_ERR_* codes.  The codes of GpuError::to_cuda_code
+ *    (crates/opencuda-core/src/error.rs:39-48) are kept: 1 invalid
+ *    value/pointer, 2 out of memory, 8 launch failure/unsupported kernel,
+ *    100 no device.  oc_get_last_error() returns this thread's message.
+ *  - No function calls exit/abort or traps on the device.
+ *  - Device-pointer entry points (oc_sgemm, oc_qgemm_*, ...) take raw CUDA
+ *    device addresses and a cudaStream_t passed as void*; they are
+ *    asynchronous on that stream.  Host-slice entry points (oc_blas_*)
+ *    mirror the reference's blas signatures on host memory: they copy the
+ *    inputs to the device, launch, copy the result back and synchronize.
+ *  - Matrices are row-major and densely packed unless a leading dimension
+ *    is given.
+ */
+#ifndef OPENCUDA_CUDA_H
+#define OPENCUDA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OC_OK 0
+#define OC_ERR_INVALID_VALUE 1   /* GpuError::InvalidPtr / bad shapes */
+#define OC_ERR_OUT_OF_MEMORY 2   /* GpuError::OutOfMemory */
+#define OC_ERR_LAUNCH_FAILED 8   /* GpuError::LaunchFailed / UnsupportedKernel */
+#define OC_ERR_NO_DEVICE 100     /* GpuError::NoDevice */
+#define OC_ERR_NOT_SUPPORTED 801 /* shape or device not handled by this build */
+#define OC_ERR_TIMEOUT 702       /* a bounded wait inside a kernel expired */
+
+/* ---- device object: implements GpuDevice (core:88-132) ----------------- */
+
+typedef struct oc_device oc_device;
+
+typedef struct {
+  int ordinal;              /* DeviceInfo::id (core:35-42) */
+  int cc_major, cc_minor;   /* GpuVendor::Nvidia{compute_capability} */
+  uint64_t total_memory;    /* DeviceInfo::total_memory */
+  uint32_t compute_units;   /* DeviceInfo::compute_units (SM count) */
+  char name[256];           /* DeviceInfo::name */
+} oc_device_info;
+
+/* Number of CUDA devices (registry enumerate, crates/opencuda-core/src/registry.rs). */
+int oc_get_device_count(int *count);
+/* Opens device `ordinal` (a GpuDevice instance). */
+int oc_device_open(int ordinal, oc_device **dev);
+/* Frees every allocation still held and the device object. */
+int oc_device_close(oc_device *dev);
+/* GpuDevice::info (core:89) */
+int oc_device_get_info(const oc_device *dev, oc_device_info *info);
+/* GpuDevice::alloc (core:92): bytes == 0 is an error, as on the CPU backend
+ * (crates/opencuda-cpu/src/lib.rs:85-87).  *addr receives the raw CUDA
+ * address, which is DevicePtr.addr. */
+int oc_device_alloc(oc_device *dev, size_t bytes, uint64_t *addr);
+/* GpuDevice::free (core:93): unknown address -> OC_ERR_INVALID_VALUE. */
+int oc_device_free(oc_device *dev, uint64_t addr);
+/* GpuDevice::memcpy_h2d/d2h/d2d (core:94-96): copies larger than the
+ * allocation are rejected (crates/opencuda-cpu/src/lib.rs:120-151). */
+int oc_device_memcpy_h2d(oc_device *dev, uint64_t dst, const void *src, size_t bytes);
+int oc_device_memcpy_d2h(oc_device *dev, void *dst, uint64_t src, size_t bytes);
+int oc_device_memcpy_d2d(oc_device *dev, uint64_t dst, uint64_t src, size_t bytes);
+/* GpuDevice::synchronize (core:106); also reports kernel status words. */
+int oc_device_synchronize(oc_device *dev);
+/* The stream this device object launches on (a cudaStream_t). */
+void *oc_device_stream(oc_device *dev);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *oc_get_last_error(void);
+/* Reads and clears the current device's kernel status word: 0 if every
+ * kernel since the last call finished normally, else the code of the
+ * first bounded wait that expired.  Synchronizes the device. */
+int oc_get_device_status(int *status);
+
+/* ---- quantization (blas:777-945) ---------------------------------------
+ * Groups are contiguous runs of `group` elements of the flat input
+ * (group_scales, blas:797-809); scale = max|x| / qmax (0 for an all-zero
+ * group); q = clamp(round_half_away(x / scale), -qmax, qmax). */
+
+/* quantize_int8 (blas:935-940): data[len] int8, scales[ceil(len/group)]. */
+int oc_quantize_int8(const float *x, size_t len, size_t group, int8_t *data, float *scales, void *stream);
+/* quantize_int4 (blas:901-919): data[(len+1)/2] bytes, nibble = q + 8,
+ * even index in the low nibble, odd in the high nibble. */
+int oc_quantize_int4(const float *x, size_t len, size_t group, uint8_t *data, float *scales, void *stream);
+/* dequantize_int8 / dequantize_int4 (blas:922-945). */
+int oc_dequantize_int8(const int8_t *data, const float *scales, size_t len, size_t group, float *out,
+                       void *stream);
+int oc_dequantize_int4(const uint8_t *data, const float *scales, size_t len, size_t group, float *out,
+                       void *stream);
+
+/* ---- quantized matmul (new API: the reference only quantizes) ----------
+ * Y[m][n] = A[m][k] . W^T + bias with W^T stored as the reference quantizes
+ * it: a [n][k] matrix flattened and passed to quantize_int8 (group = k, one
+ * scale per output channel) or quantize_int4 (group = `group`, packed two
+ * per byte).  The activation rows are quantized on the device with
+ * quantize_int8(A, group = k).  Integer products accumulate exactly in
+ * int32 on the tcgen05 kind::i8 tensor cores (INT4 weights are widened to
+ * int8 in shared memory), then
+ *   W8A8:  y = ((float)acc * sa[m]) * sw[n] + bias[n]
+ *   W4A8:  s = 0; for each group j: s = fma((float)P_j, sw[n][j], s);
+ *          y = s * sa[m] + bias[n]
+ * with P_j the exact int32 partial sum of group j.  `workspace` is device
+ * scratch of at least oc_qgemm_workspace_size() bytes (quantized
+ * activations and their scales); bias may be NULL.  acc_out (optional,
+ * NULL to skip): the int32 accumulators, [m][n] for W8A8 and
+ * [m][n][k/group] for W4A8. */
+int oc_qgemm_workspace_size(int m, int k, size_t *bytes);
+int oc_qgemm_w8a8(int m, int n, int k, const float *A, const int8_t *Wq, const float *w_scales,
+                  const float *bias, float *Y, void *workspace, size_t workspace_bytes, int32_t *acc_out,
+                  void *stream);
+int oc_qgemm_w4a8(int m, int n, int k, int group, const float *A, const uint8_t *Wq, const float *w_scales,
+                  const float *bias, float *Y, void *workspace, size_t workspace_bytes, int32_t *acc_out,
+                  void *stream);
+
+/* ---- host-slice entry points (blas signatures on host memory) ---------- */
+
+/* quantize_int8 / quantize_int4 (blas:901, 935); empty input or group 0
+ * is OC_ERR_INVALID_VALUE (blas:867-872). */
+int oc_blas_quantize_int8(oc_device *dev, const float *input, size_t len, size_t group, int8_t *data,
+                          float *scales);
+int oc_blas_quantize_int4(oc_device *dev, const float *input, size_t len, size_t group, uint8_t *data,
+                          float *scales);
+/* The quantized matmuls on host memory: A [m][k] f32, W^T quantized as
+ * above, bias [n] (may be NULL), Y [m][n]. */
+int oc_blas_qgemm_w8a8(oc_device *dev, size_t m, size_t n, size_t k, const float *a, const int8_t *wq,
+                       const float *w_scales, const float *bias, float *y);
+int oc_blas_qgemm_w4a8(oc_device *dev, size_t m, size_t n, size_t k, size_t group, const float *a,
+                       const uint8_t *wq, const float *w_scales, const float *bias, float *y);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OPENCUDA_CUDA_H */

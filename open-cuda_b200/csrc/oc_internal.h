@@ -1,0 +1,59 @@
+// oc_internal.h -- shared host-side plumbing of libopencuda_cuda.so:
+// status codes, the thread-local error message, argument checks, tensor
+// map encoding and the per-device properties cache.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "../../include/opencuda_cuda.h"
+
+namespace oc {
+
+// Records `msg` as this thread's last error and returns `code`.
+int fail(int code, const std::string& msg);
+// Maps a CUDA runtime error to a status code (GpuError::to_cuda_code,
+// crates/opencuda-core/src/error.rs:39-48) and records its message.
+int from_cuda(cudaError_t e, const char* what);
+
+#define OC_CHECK_CUDA(expr)                                   \
+  do {                                                        \
+    cudaError_t _e = (expr);                                  \
+    if (_e != cudaSuccess) return ::oc::from_cuda(_e, #expr); \
+  } while (0)
+
+#define OC_REQUIRE(cond, msg)                                           \
+  do {                                                                  \
+    if (!(cond)) return ::oc::fail(OC_ERR_INVALID_VALUE, (msg));        \
+  } while (0)
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+// True when the current device is a compute capability 10.x part, i.e. has
+// tcgen05 tensor cores and TMEM.
+bool is_sm100();
+
+// Encodes a 2-D tiled tensor map for a row-major [rows][cols] matrix of
+// `elem_bytes`-sized elements with row stride `row_stride_bytes`, box
+// {box_cols, box_rows} and the given swizzle.  Returns a status code.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t cols,
+                 uint64_t rows, uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle);
+
+// Device-side status word per device: kernels write a nonzero code there
+// instead of trapping (bounded waits that expired, bad indices).
+int* device_status_word();
+// Reads and clears the device status word after `stream` drained; returns
+// OC_ERR_TIMEOUT (and records which wait expired) if a kernel reported one.
+int check_device_status(cudaStream_t stream);
+
+// Raises the dynamic shared-memory limit of kernel `fn` to `bytes` once per
+// device; returns false if the runtime refused.
+bool smem_attr_once(const void* fn, size_t bytes);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace oc

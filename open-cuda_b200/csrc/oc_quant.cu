@@ -1,0 +1,210 @@
+// oc_quant.cu -- symmetric group quantization on the device, bit-exact with
+// the reference (crates/opencuda-blas/src/lib.rs:797-945):
+//   scale = max|x| / qmax per contiguous group (0 for an all-zero group),
+//   q     = scale == 0 ? 0 : clamp(round_half_away(x / scale), -qmax, qmax)
+//   INT4 packs nibble = q + 8, even index low, odd index high.
+// All divisions are IEEE round-to-nearest (__fdiv_rn) and roundf rounds
+// half away from zero, exactly like the reference's f32 `/` and `round`.
+// These kernels are HBM-bound: each element is read once and written once.
+#include "oc_internal.h"
+#include "oc_quant.cuh"
+
+namespace oc {
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ int quant_one(float x, float s, float qmax) {
+  if (s == 0.0f) return 0;
+  float q = roundf(__fdiv_rn(x, s));
+  if (q != q) return 0;  // Rust: NaN.clamp(..) as i8 == 0
+  return (int)fminf(fmaxf(q, -qmax), qmax);
+}
+
+// One warp per group: scale of group g (blas:797-809).
+__global__ void group_scales_kernel(const float* __restrict__ x, size_t len, size_t group, float qmax,
+                                    float* __restrict__ scales, size_t ngroups) {
+  const int lane = threadIdx.x & 31;
+  const size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  const size_t nwarps = (gridDim.x * (size_t)blockDim.x) >> 5;
+  for (size_t g = warp; g < ngroups; g += nwarps) {
+    size_t b = g * group, e = b + group < len ? b + group : len;
+    float m = 0.0f;
+    for (size_t i = b + lane; i < e; i += 32) m = fmaxf(m, fabsf(x[i]));
+    m = warp_max(m);
+    if (lane == 0) scales[g] = (m == 0.0f) ? 0.0f : __fdiv_rn(m, qmax);
+  }
+}
+
+// Elementwise quantization to one int8 per element (blas:834-852).
+__global__ void quantize_i8_kernel(const float* __restrict__ x, size_t len, const float* __restrict__ scales,
+                                   size_t group, float qmax, int8_t* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < len; i += gridDim.x * (size_t)blockDim.x)
+    out[i] = (int8_t)quant_one(x[i], scales[i / group], qmax);
+}
+
+// One output byte per thread: elements 2b (low nibble) and 2b+1 (high).
+__global__ void quantize_i4_kernel(const float* __restrict__ x, size_t len, const float* __restrict__ scales,
+                                   size_t group, uint8_t* __restrict__ out) {
+  const size_t nbytes = (len + 1) / 2;
+  for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < nbytes; b += gridDim.x * (size_t)blockDim.x) {
+    size_t i0 = 2 * b, i1 = i0 + 1;
+    uint32_t lo = (uint32_t)(quant_one(x[i0], scales[i0 / group], 7.0f) + 8) & 0xFu;
+    uint32_t hi = i1 < len ? ((uint32_t)(quant_one(x[i1], scales[i1 / group], 7.0f) + 8) & 0xFu) : 0u;
+    out[b] = (uint8_t)(lo | (hi << 4));
+  }
+}
+
+__global__ void dequantize_i8_kernel(const int8_t* __restrict__ q, const float* __restrict__ scales, size_t len,
+                                     size_t group, float* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < len; i += gridDim.x * (size_t)blockDim.x)
+    out[i] = __fmul_rn((float)q[i], scales[i / group]);
+}
+
+__global__ void dequantize_i4_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scales, size_t len,
+                                     size_t group, float* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < len; i += gridDim.x * (size_t)blockDim.x) {
+    uint8_t byte = q[i / 2];
+    int v = (int)((i & 1) ? (byte >> 4) : (byte & 0xF)) - 8;
+    out[i] = __fmul_rn((float)v, scales[i / group]);
+  }
+}
+
+// Row quantization of activations, quantize_int8(A, group = k): one CTA of
+// 128 threads per row, the row held in registers (VPT float4 per thread),
+// a block max-reduction, then int8 stores.  Requires k % 4 == 0 and a
+// 16-byte aligned A; k <= 128 * 4 * VPT.
+template <int VPT>
+__global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __restrict__ A, int m, int k,
+                                                               int8_t* __restrict__ qa, float* __restrict__ sa) {
+  __shared__ float red[4];
+  const int row = blockIdx.x;
+  if (row >= m) return;
+  const float4* a4 = reinterpret_cast<const float4*>(A + (size_t)row * k);
+  const int n4 = k >> 2;
+  float4 v[VPT];
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPT; j++) {
+    int idx = threadIdx.x + j * 128;
+    if (idx < n4) {
+      v[j] = __ldg(a4 + idx);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+    }
+  }
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const float s = (mx == 0.0f) ? 0.0f : __fdiv_rn(mx, 127.0f);
+  if (threadIdx.x == 0) sa[row] = s;
+  char4* q4 = reinterpret_cast<char4*>(qa + (size_t)row * k);
+#pragma unroll
+  for (int j = 0; j < VPT; j++) {
+    int idx = threadIdx.x + j * 128;
+    if (idx < n4) {
+      char4 o;
+      o.x = (signed char)quant_one(v[j].x, s, 127.0f);
+      o.y = (signed char)quant_one(v[j].y, s, 127.0f);
+      o.z = (signed char)quant_one(v[j].z, s, 127.0f);
+      o.w = (signed char)quant_one(v[j].w, s, 127.0f);
+      q4[idx] = o;
+    }
+  }
+}
+
+static int grid_for(size_t n, int threads) {
+  size_t b = (n + threads - 1) / threads;
+  size_t cap = (size_t)sm_count() * 16;
+  if (cap == 0) cap = 2048;
+  return (int)(b < cap ? (b ? b : 1) : cap);
+}
+
+int launch_group_scales(const float* x, size_t len, size_t group, float qmax, float* scales, cudaStream_t s) {
+  size_t ng = (len + group - 1) / group;
+  group_scales_kernel<<<grid_for(ng * 32, 256), 256, 0, s>>>(x, len, group, qmax, scales, ng);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "group_scales_kernel");
+}
+
+int launch_quantize_i8(const float* x, size_t len, const float* scales, size_t group, float qmax, int8_t* out,
+                       cudaStream_t s) {
+  quantize_i8_kernel<<<grid_for(len, 256), 256, 0, s>>>(x, len, scales, group, qmax, out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_i8_kernel");
+}
+
+int launch_quantize_rows_i8(const float* A, int m, int k, int8_t* qa, float* sa, cudaStream_t s) {
+  if (m <= 0) return OC_OK;
+  const bool vec_ok = (k % 4 == 0) && aligned16(A) && (reinterpret_cast<uintptr_t>(qa) % 4 == 0);
+  const int n4 = k / 4;
+  if (vec_ok && n4 <= 128 * 8) {
+    if (n4 <= 128 * 2)
+      quantize_rows_i8_kernel<2><<<m, 128, 0, s>>>(A, m, k, qa, sa);
+    else if (n4 <= 128 * 4)
+      quantize_rows_i8_kernel<4><<<m, 128, 0, s>>>(A, m, k, qa, sa);
+    else
+      quantize_rows_i8_kernel<8><<<m, 128, 0, s>>>(A, m, k, qa, sa);
+  } else {
+    size_t len = (size_t)m * k;
+    group_scales_kernel<<<grid_for((size_t)m * 32, 256), 256, 0, s>>>(A, len, (size_t)k, 127.0f, sa, (size_t)m);
+    quantize_i8_kernel<<<grid_for(len, 256), 256, 0, s>>>(A, len, sa, (size_t)k, 127.0f, qa);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_rows_i8_kernel");
+}
+
+}  // namespace oc
+
+using namespace oc;
+
+extern "C" {
+
+int oc_quantize_int8(const float* x, size_t len, size_t group, int8_t* data, float* scales, void* stream) {
+  OC_REQUIRE(len > 0, "quantize: input must not be empty");
+  OC_REQUIRE(group > 0, "quantize: group_size must be > 0");
+  OC_REQUIRE(x && data && scales, "quantize: NULL pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = launch_group_scales(x, len, group, 127.0f, scales, s);
+  if (rc) return rc;
+  return launch_quantize_i8(x, len, scales, group, 127.0f, data, s);
+}
+
+int oc_quantize_int4(const float* x, size_t len, size_t group, uint8_t* data, float* scales, void* stream) {
+  OC_REQUIRE(len > 0, "quantize: input must not be empty");
+  OC_REQUIRE(group > 0, "quantize: group_size must be > 0");
+  OC_REQUIRE(x && data && scales, "quantize: NULL pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = launch_group_scales(x, len, group, 7.0f, scales, s);
+  if (rc) return rc;
+  quantize_i4_kernel<<<grid_for((len + 1) / 2, 256), 256, 0, s>>>(x, len, scales, group, data);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_i4_kernel");
+}
+
+int oc_dequantize_int8(const int8_t* data, const float* scales, size_t len, size_t group, float* out,
+                       void* stream) {
+  OC_REQUIRE(group > 0, "dequantize: group_size must be > 0");
+  if (len == 0) return OC_OK;
+  OC_REQUIRE(data && scales && out, "dequantize: NULL pointer");
+  dequantize_i8_kernel<<<grid_for(len, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(data, scales, len,
+                                                                                          group, out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "dequantize_i8_kernel");
+}
+
+int oc_dequantize_int4(const uint8_t* data, const float* scales, size_t len, size_t group, float* out,
+                       void* stream) {
+  OC_REQUIRE(group > 0, "dequantize: group_size must be > 0");
+  if (len == 0) return OC_OK;
+  OC_REQUIRE(data && scales && out, "dequantize: NULL pointer");
+  dequantize_i4_kernel<<<grid_for(len, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(data, scales, len,
+                                                                                          group, out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "dequantize_i4_kernel");
+}
+
+}  // extern "C"
