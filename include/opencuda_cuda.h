@@ -124,6 +124,16 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float *A, const uint8_t 
                   const float *bias, float *Y, void *workspace, size_t workspace_bytes, int32_t *acc_out,
                   void *stream);
 
+/* The same products on activations that are already quantized, as
+ * quantize_int8(A, group = k) returns them: qa [m][k] int8 and sa [m] f32
+ * (for example tokens that arrive quantized).  No workspace needed. */
+int oc_igemm_w8a8(int m, int n, int k, const int8_t *qa, const float *sa, const int8_t *Wq, const float *w_scales,
+                  const float *bias, float *Y, int32_t *acc_out, void *stream);
+int oc_igemm_w4a8(int m, int n, int k, int group, const int8_t *qa, const float *sa, const uint8_t *Wq,
+                  const float *w_scales, const float *bias, float *Y, int32_t *acc_out, void *stream);
+/* quantize_int8(A, group = k) for a row-major A [m][k]: qa [m][k], sa [m]. */
+int oc_quantize_rows_int8(const float *A, int m, int k, int8_t *qa, float *sa, void *stream);
+
 /* ---- host-slice entry points (blas signatures on host memory) ---------- */
 
 /* quantize_int8 / quantize_int4 (blas:901, 935); empty input or group 0

@@ -335,6 +335,22 @@ int oc_qgemm_workspace_size(int m, int k, size_t* bytes) {
   return OC_OK;
 }
 
+int oc_igemm_w8a8(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* Wq, const float* w_scales,
+                  const float* bias, float* Y, int32_t* acc_out, void* stream) {
+  OC_REQUIRE(m > 0 && n > 0 && k > 0, "igemm_w8a8: m, n, k must be > 0");
+  OC_REQUIRE(qa && sa && Wq && w_scales && Y, "igemm_w8a8: NULL pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool tc_ok = is_sm100() && (k % 16 == 0) && aligned16(Wq) && aligned16(qa) && m > kSkinnyM;
+  if (tc_ok) return run_w8a8_tc(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
+  return run_w8a8_skinny(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
+}
+
+int oc_quantize_rows_int8(const float* A, int m, int k, int8_t* qa, float* sa, void* stream) {
+  OC_REQUIRE(m > 0 && k > 0, "quantize_rows_int8: m and k must be > 0");
+  OC_REQUIRE(A && qa && sa, "quantize_rows_int8: NULL pointer");
+  return launch_quantize_rows_i8(A, m, k, qa, sa, static_cast<cudaStream_t>(stream));
+}
+
 int oc_qgemm_w8a8(int m, int n, int k, const float* A, const int8_t* Wq, const float* w_scales, const float* bias,
                   float* Y, void* workspace, size_t workspace_bytes, int32_t* acc_out, void* stream) {
   OC_REQUIRE(m > 0 && n > 0 && k > 0, "qgemm_w8a8: m, n, k must be > 0");
@@ -343,14 +359,31 @@ int oc_qgemm_w8a8(int m, int n, int k, const float* A, const int8_t* Wq, const f
   oc_qgemm_workspace_size(m, k, &need);
   OC_REQUIRE(workspace_bytes >= need, "qgemm_w8a8: workspace too small");
   OC_REQUIRE(aligned16(workspace), "qgemm_w8a8: workspace must be 16-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   int8_t* qa = static_cast<int8_t*>(workspace);
   float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k));
-  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, s);
+  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, static_cast<cudaStream_t>(stream));
   if (rc) return rc;
-  const bool tc_ok = is_sm100() && (k % 16 == 0) && aligned16(Wq) && m > kSkinnyM;
-  if (tc_ok) return run_w8a8_tc(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
-  return run_w8a8_skinny(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
+  return oc_igemm_w8a8(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, stream);
+}
+
+int oc_igemm_w4a8(int m, int n, int k, int group, const int8_t* qa, const float* sa, const uint8_t* Wq,
+                  const float* w_scales, const float* bias, float* Y, int32_t* acc_out, void* stream) {
+  OC_REQUIRE(m > 0 && n > 0 && k > 0, "igemm_w4a8: m, n, k must be > 0");
+  OC_REQUIRE(group > 0 && group % 32 == 0 && k % group == 0,
+             "igemm_w4a8: group must be a multiple of 32 that divides k");
+  OC_REQUIRE(qa && sa && Wq && w_scales && Y, "igemm_w4a8: NULL pointer");
+  OC_REQUIRE(aligned16(Wq), "igemm_w4a8: packed weights must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (m > kSkinnyM && is_sm100() && group == 32 && k % 128 == 0 && aligned16(w_scales) && aligned16(qa))
+    return run_w4a8_tc(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
+  // The skinny kernel handles up to kSkinnyM rows per launch.
+  for (int r0 = 0; r0 < m; r0 += kSkinnyM) {
+    const int mr = std::min(kSkinnyM, m - r0);
+    int rc = run_w4a8_skinny(mr, n, k, group, qa + (size_t)r0 * k, sa + r0, Wq, w_scales, bias, Y + (size_t)r0 * n,
+                             acc_out ? acc_out + (size_t)r0 * n * (k / group) : nullptr, s);
+    if (rc) return rc;
+  }
+  return OC_OK;
 }
 
 int oc_qgemm_w4a8(int m, int n, int k, int group, const float* A, const uint8_t* Wq, const float* w_scales,
@@ -360,26 +393,15 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float* A, const uint8_t*
   OC_REQUIRE(group > 0 && group % 32 == 0 && k % group == 0,
              "qgemm_w4a8: group must be a multiple of 32 that divides k");
   OC_REQUIRE(A && Wq && w_scales && Y && workspace, "qgemm_w4a8: NULL pointer");
-  OC_REQUIRE(aligned16(Wq), "qgemm_w4a8: packed weights must be 16-byte aligned");
   size_t need = 0;
   oc_qgemm_workspace_size(m, k, &need);
   OC_REQUIRE(workspace_bytes >= need, "qgemm_w4a8: workspace too small");
   OC_REQUIRE(aligned16(workspace), "qgemm_w4a8: workspace must be 16-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   int8_t* qa = static_cast<int8_t*>(workspace);
   float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k));
-  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, s);
+  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, static_cast<cudaStream_t>(stream));
   if (rc) return rc;
-  if (m > kSkinnyM && is_sm100() && group == 32 && k % 128 == 0 && aligned16(w_scales))
-    return run_w4a8_tc(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
-  // Larger m on the skinny kernel: process row blocks of kSkinnyM.
-  for (int r0 = 0; r0 < m; r0 += kSkinnyM) {
-    const int mr = std::min(kSkinnyM, m - r0);
-    rc = run_w4a8_skinny(mr, n, k, group, qa + (size_t)r0 * k, sa + r0, Wq, w_scales, bias, Y + (size_t)r0 * n,
-                         acc_out ? acc_out + (size_t)r0 * n * (k / group) : nullptr, s);
-    if (rc) return rc;
-  }
-  return OC_OK;
+  return oc_igemm_w4a8(m, n, k, group, qa, sa, Wq, w_scales, bias, Y, acc_out, stream);
 }
 
 }  // extern "C"

@@ -88,6 +88,9 @@ _SIGS = {
     "oc_qgemm_workspace_size": (ci, [ci, ci, C.POINTER(sz)]),
     "oc_qgemm_w8a8": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp, sz, vp, vp]),
     "oc_qgemm_w4a8": (ci, [ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, sz, vp, vp]),
+    "oc_igemm_w8a8": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "oc_igemm_w4a8": (ci, [ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "oc_quantize_rows_int8": (ci, [vp, ci, ci, vp, vp, vp]),
     "oc_blas_quantize_int8": (ci, [vp, vp, sz, sz, vp, vp]),
     "oc_blas_quantize_int4": (ci, [vp, vp, sz, sz, vp, vp]),
     "oc_blas_qgemm_w8a8": (ci, [vp, sz, sz, sz, vp, vp, vp, vp, vp]),
@@ -235,6 +238,40 @@ def qgemm_w4a8(A, Wq, w_scales, group: int, bias=None, out=None, want_acc=False)
     check(lib().oc_qgemm_w4a8(m, n, k, group, _ptr(A), _ptr(Wq), _ptr(w_scales), _ptr(bias), _ptr(Y), _ptr(ws),
                               ws.numel(), _ptr(acc), _stream()))
     return (Y, acc) if want_acc else Y
+
+
+def quantize_rows_int8(A):
+    """quantize_int8(A, group = k) of a [m, k] f32 matrix: (qa [m, k] int8, sa [m] f32)."""
+    torch = _torch()
+    _need_cuda(A)
+    A = A.contiguous()
+    m, k = A.shape
+    qa = torch.empty(m, k, dtype=torch.int8, device=A.device)
+    sa = torch.empty(m, dtype=torch.float32, device=A.device)
+    check(lib().oc_quantize_rows_int8(_ptr(A), m, k, _ptr(qa), _ptr(sa), _stream()))
+    return qa, sa
+
+
+def igemm_w8a8(qa, sa, Wq, w_scales, bias=None, out=None):
+    """W8A8 product on pre-quantized activations (qa [m, k] int8, sa [m])."""
+    torch = _torch()
+    m, k = qa.shape
+    n = Wq.numel() // k
+    Y = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=qa.device)
+    check(lib().oc_igemm_w8a8(m, n, k, _ptr(qa), _ptr(sa), _ptr(Wq), _ptr(w_scales), _ptr(bias), _ptr(Y), None,
+                              _stream()))
+    return Y
+
+
+def igemm_w4a8(qa, sa, Wq, w_scales, group: int, bias=None, out=None):
+    """W4A8 product on pre-quantized activations."""
+    torch = _torch()
+    m, k = qa.shape
+    n = Wq.numel() * 2 // k
+    Y = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=qa.device)
+    check(lib().oc_igemm_w4a8(m, n, k, group, _ptr(qa), _ptr(sa), _ptr(Wq), _ptr(w_scales), _ptr(bias), _ptr(Y),
+                              None, _stream()))
+    return Y
 
 
 # ---- host slices: the GpuDevice object ---------------------------------------
