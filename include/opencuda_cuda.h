@@ -134,6 +134,22 @@ int oc_igemm_w4a8(int m, int n, int k, int group, const int8_t *qa, const float 
 /* quantize_int8(A, group = k) for a row-major A [m][k]: qa [m][k], sa [m]. */
 int oc_quantize_rows_int8(const float *A, int m, int k, int8_t *qa, float *sa, void *stream);
 
+/* oc_qgemm_w8a8 for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Same arguments and result as
+ * oc_qgemm_w8a8, minus the workspace: the quantized activations live in a
+ * 16 MiB device array inside the library, so the call allocates nothing.
+ * For hosts that may not call cudaMalloc (stream callbacks, embedders whose
+ * device memory belongs to another allocator, bindings that only receive
+ * input and output buffers).  Requires align256(m*k) + align256(4*m) <=
+ * 16 MiB, else OC_ERR_INVALID_VALUE.  Every GPU that loads the library
+ * keeps the array until exit; concurrent calls on one device that overlap
+ * on the GPU race on it, so order them on one stream.  The first call on a
+ * device looks up the array's address; make it before any stream capture. */
+int oc_qgemm_w8a8_noalloc(int m, int n, int k, const float *A, const int8_t *Wq, const float *w_scales,
+                          const float *bias, float *Y, void *stream);
+/* The size of that array in bytes (16 MiB). */
+int oc_qgemm_w8a8_noalloc_max_bytes(size_t *bytes);
+
 /* ---- host-slice entry points (blas signatures on host memory) ---------- */
 
 /* quantize_int8 / quantize_int4 (blas:901, 935); empty input or group 0

@@ -91,6 +91,8 @@ _SIGS = {
     "oc_igemm_w8a8": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
     "oc_igemm_w4a8": (ci, [ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
     "oc_quantize_rows_int8": (ci, [vp, ci, ci, vp, vp, vp]),
+    "oc_qgemm_w8a8_noalloc": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp]),
+    "oc_qgemm_w8a8_noalloc_max_bytes": (ci, [C.POINTER(sz)]),
     "oc_blas_quantize_int8": (ci, [vp, vp, sz, sz, vp, vp]),
     "oc_blas_quantize_int4": (ci, [vp, vp, sz, sz, vp, vp]),
     "oc_blas_qgemm_w8a8": (ci, [vp, sz, sz, sz, vp, vp, vp, vp, vp]),
