@@ -53,6 +53,26 @@ typedef struct {
   char name[256];           /* DeviceInfo::name */
 } oc_device_info;
 
+/* A launch configuration as the reference describes it (LaunchConfig,
+ * core:45-85).  The CUDA backend picks its own launch shape for each named
+ * kernel, so grid/block are accepted for contract compatibility only. */
+typedef struct {
+  uint32_t grid[3], block[3], shared_mem;
+} oc_launch_config;
+
+/* KernelArg (crates/opencuda-core/src/kernel.rs:88-100). */
+enum { OC_ARG_PTR = 0, OC_ARG_U32 = 1, OC_ARG_I32 = 2, OC_ARG_F32 = 3, OC_ARG_USIZE = 4 };
+typedef struct {
+  int kind;
+  union {
+    uint64_t ptr; /* a DevicePtr.addr returned by oc_device_alloc */
+    uint32_t u32;
+    int32_t i32;
+    float f32;
+    uint64_t usize;
+  } v;
+} oc_kernel_arg;
+
 /* Number of CUDA devices (registry enumerate, crates/opencuda-core/src/registry.rs). */
 int oc_get_device_count(int *count);
 /* Opens device `ordinal` (a GpuDevice instance). */
@@ -74,6 +94,23 @@ int oc_device_memcpy_d2h(oc_device *dev, void *dst, uint64_t src, size_t bytes);
 int oc_device_memcpy_d2d(oc_device *dev, uint64_t dst, uint64_t src, size_t bytes);
 /* GpuDevice::synchronize (core:106); also reports kernel status words. */
 int oc_device_synchronize(oc_device *dev);
+/* GpuDevice::launch_kernel (core:99-104), routed by kernel name the way the
+ * Vulkan backend routes SPIR-V entry points
+ * (crates/opencuda-vulkan/src/real.rs:868-887).  Names and argument
+ * contracts (the reference's KernelArg lists):
+ *   "sgemm_naive"        [A,B,C ptr; m,k,n usize; alpha,beta f32] plus an
+ *                        optional trailing u32 transpose_b (blas:183-232)
+ *   "matmul"             [A,B,C ptr; m,k,n usize], C = A.B (blas:335-348)
+ *   "quantize_symmetric" [in,scales,out ptr; len,group usize; qmin,qmax f32]
+ *                        (blas:834-868), one int8 per element
+ *   "softmax"            [data ptr; rows,cols usize], in place (blas:383-385)
+ *   "flash_attention"    [q,k,v,o ptr; seq,head_dim,block usize; scale f32]
+ *                        (blas:745-760)
+ * Pointer arguments must be allocations of this device large enough for
+ * the shapes.  Other names: OC_ERR_LAUNCH_FAILED ("kernel source not
+ * supported by this backend").  Asynchronous until oc_device_synchronize. */
+int oc_device_launch(oc_device *dev, const char *kernel_name, const oc_launch_config *cfg,
+                     const oc_kernel_arg *args, size_t nargs);
 /* The stream this device object launches on (a cudaStream_t). */
 void *oc_device_stream(oc_device *dev);
 
@@ -83,6 +120,65 @@ const char *oc_get_last_error(void);
  * kernel since the last call finished normally, else the code of the
  * first bounded wait that expired.  Synchronizes the device. */
 int oc_get_device_status(int *status);
+
+/* ---- GEMM (blas:148-295) ------------------------------------------------ */
+
+/* C = alpha * A.op(B) + beta * C (+ bias[n] per column if bias != NULL).
+ * A [m][lda], op(B) = B [k][ldb] (trans_b = 0, the reference's b[kk*n+col])
+ * or B^T with B [n][ldb] (trans_b = 1, the transpose_b form of
+ * launch_naive_gemm, blas:206-210); C [m][ldc].  f32 in and out; products on
+ * the tcgen05 tf32 tensor cores with the 3xTF32 split (f32-level accuracy),
+ * small m on a CUDA-core split-K GEMV.  beta == 0 does not read C.  Replaces
+ * the GemmPath::CuBlas arm of sgemm (blas:293). */
+int oc_sgemm(int m, int n, int k, float alpha, const float *A, int lda, const float *B, int ldb, int trans_b,
+             float beta, float *C, int ldc, const float *bias, void *stream);
+/* For a B that is reused across calls (weights): oc_sgemm splits B into
+ * tf32 hi/lo halves laid out [n][k] on every call; these entry points do it
+ * once.  prepared holds oc_sgemm_prepared_b_size() bytes; then
+ * oc_sgemm_prepared computes the same product as oc_sgemm on the tensor
+ * cores (A must be 16-byte aligned with lda % 4 == 0). */
+int oc_sgemm_prepared_b_size(int k, int n, size_t *bytes);
+int oc_sgemm_prepare_b(int k, int n, const float *B, int ldb, int trans_b, float *prepared, void *stream);
+int oc_sgemm_prepared(int m, int n, int k, float alpha, const float *A, int lda, const float *prepared, float beta,
+                      float *C, int ldc, const float *bias, void *stream);
+
+/* ---- attention (blas:373-766) ------------------------------------------ */
+
+/* In-place row softmax of data [rows][cols]: e = exp(x - max), divided by
+ * the sum only if the sum is > 0 (cpu_row_softmax, blas:545-562;
+ * softmax_vulkan_generic's contract, blas:373-391). */
+int oc_softmax_rows(float *data, int rows, int cols, void *stream);
+/* The fused slot flash_attention_with_spirv (blas:707-766): q, k, v, o are
+ * [seq_len][head_dim]; every query row attends to all seq_len keys with
+ * scale 1/sqrt(head_dim) and an online softmax (flash_attention,
+ * blas:589-678).  block_size must be > 0; head_dim and block_size <= 256
+ * (the limits the reference's shader enforces,
+ * crates/opencuda-vulkan/src/real.rs:524-533).  The kernel tiles keys by 64
+ * regardless of block_size; results match the reference up to rounding. */
+int oc_flash_attention(const float *q, const float *k, const float *v, float *o, int seq_len, int head_dim,
+                       int block_size, void *stream);
+/* General form: q/o [batch_heads][q_len][head_dim], k/v
+ * [batch_heads][kv_len][head_dim], any scale; causal = 1 lets query i see
+ * keys j <= i + (kv_len - q_len).  Covers multi-head SDPA (BERT,
+ * crates/open-cuda-bert/src/lib.rs:141-167) and q_len != kv_len cross
+ * attention (crates/open-cuda-whisper/src/lib.rs:288-300). */
+int oc_flash_attention_fwd(const float *q, const float *k, const float *v, float *o, int batch_heads, int q_len,
+                           int kv_len, int head_dim, float scale, int causal, void *stream);
+/* Unfused scaled_dot_product_attention (blas:411-540): scores = Q.K^T /
+ * sqrt(d) (oc_sgemm, transpose_b), row softmax, O = P.V.  workspace holds
+ * the seq_len x seq_len scores. */
+int oc_sdpa_workspace_size(int seq_len, size_t *bytes);
+int oc_sdpa(const float *q, const float *k, const float *v, float *o, int seq_len, int head_dim, void *workspace,
+            size_t workspace_bytes, void *stream);
+
+/* ---- MLA low-rank KV projections (blas:1045-1078) ----------------------- */
+
+/* mla_compress_kv: latent [seq][d_c] = kv [seq][d_h] . down [d_h][d_c]. */
+int oc_mla_compress_kv(int seq_len, int d_h, int d_c, const float *kv, const float *down_proj, float *latent,
+                       void *stream);
+/* mla_decompress_kv: out [seq][d_h] = latent [seq][d_c] . up [d_c][d_h]. */
+int oc_mla_decompress_kv(int seq_len, int d_c, int d_h, const float *latent, const float *up_proj, float *out,
+                         void *stream);
 
 /* ---- quantization (blas:777-945) ---------------------------------------
  * Groups are contiguous runs of `group` elements of the flat input
@@ -152,6 +248,22 @@ int oc_qgemm_w8a8_noalloc_max_bytes(size_t *bytes);
 
 /* ---- host-slice entry points (blas signatures on host memory) ---------- */
 
+/* sgemm (blas:260-271): a [m][k], b [k][n], c [m][n] in/out. */
+int oc_blas_sgemm(oc_device *dev, size_t m, size_t k, size_t n, float alpha, const float *a, const float *b,
+                  float beta, float *c);
+/* softmax_vulkan_generic (blas:373-391): out = row softmax of data. */
+int oc_blas_softmax_rows(oc_device *dev, size_t rows, size_t cols, const float *data, float *out);
+/* flash_attention_with_spirv (blas:707-766) without the SPIR-V bytes. */
+int oc_blas_flash_attention(oc_device *dev, const float *q, const float *k, const float *v, size_t seq_len,
+                            size_t head_dim, size_t block_size, float *out);
+/* scaled_dot_product_attention (blas:411-423). */
+int oc_blas_sdpa(oc_device *dev, const float *q, const float *k, const float *v, size_t seq_len, size_t head_dim,
+                 float *out);
+/* mla_compress_kv / mla_decompress_kv (blas:1045-1067). */
+int oc_blas_mla_compress_kv(oc_device *dev, size_t seq_len, size_t d_h, size_t d_c, const float *kv,
+                            const float *down_proj, float *latent);
+int oc_blas_mla_decompress_kv(oc_device *dev, size_t seq_len, size_t d_c, size_t d_h, const float *latent,
+                              const float *up_proj, float *out);
 /* quantize_int8 / quantize_int4 (blas:901, 935); empty input or group 0
  * is OC_ERR_INVALID_VALUE (blas:867-872). */
 int oc_blas_quantize_int8(oc_device *dev, const float *input, size_t len, size_t group, int8_t *data,

@@ -12,20 +12,11 @@
 #include "oc_internal.h"
 
 namespace oc {
-int device_ordinal(const oc_device* d);
-cudaStream_t device_stream(const oc_device* d);
 
-// Grow-only device scratch, one per device object (calls on one device
-// object are serialized by `mu`).
-struct Arena {
-  std::mutex mu;
-  void* ptr = nullptr;
-  size_t bytes = 0;
-};
 static std::mutex g_arena_mu;
 static std::map<const oc_device*, Arena*> g_arenas;
 
-static Arena& arena_of(const oc_device* d) {
+Arena& arena_of(const oc_device* d) {
   std::lock_guard<std::mutex> lk(g_arena_mu);
   Arena*& a = g_arenas[d];
   if (!a) a = new Arena();
@@ -35,7 +26,7 @@ static Arena& arena_of(const oc_device* d) {
 static size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Returns a device pointer with at least `bytes` bytes (caller holds mu).
-static int arena_get(Arena& a, size_t bytes, cudaStream_t s, uint8_t** out) {
+int arena_get(Arena& a, size_t bytes, cudaStream_t s, uint8_t** out) {
   if (a.bytes < bytes) {
     if (a.ptr) {
       cudaStreamSynchronize(s);
@@ -53,19 +44,6 @@ static int arena_get(Arena& a, size_t bytes, cudaStream_t s, uint8_t** out) {
   *out = static_cast<uint8_t*>(a.ptr);
   return OC_OK;
 }
-
-struct Scope {
-  int prev = -1;
-  explicit Scope(int dev) {
-    cudaGetDevice(&prev);
-    if (prev != dev) cudaSetDevice(dev);
-  }
-  ~Scope() {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (prev >= 0 && prev != cur) cudaSetDevice(prev);
-  }
-};
 
 }  // namespace oc
 

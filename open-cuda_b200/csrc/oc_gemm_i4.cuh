@@ -29,11 +29,13 @@ struct I4Gemm {
   static constexpr int A_BYTES = BM * BK;       // int8 activations
   static constexpr int BU_BYTES = BN * BK;      // widened weights
   static constexpr int BP_BYTES = BN * BK / 2;  // packed weights
-  static constexpr int SC_BYTES = BN * GPK * 4; // f32 scales [n][4]
+  static constexpr int SC_BYTES = BN * GPK * 4; // f32 scales [n][4] (TMA)
+  static constexpr int SCT_BYTES = SC_BYTES;    // the same, [4][n]
   static constexpr int TX_BYTES = A_BYTES + BP_BYTES + SC_BYTES;
   static constexpr int TMEM_COLS = 4 * BN;
   static constexpr int THREADS = 448;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * (A_BYTES + BU_BYTES + BP_BYTES + SC_BYTES) + 512;
+  static constexpr size_t SMEM =
+      1024 + (size_t)STAGES * (A_BYTES + BU_BYTES + BP_BYTES + SC_BYTES + SCT_BYTES) + 512;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
 };
 
@@ -67,7 +69,8 @@ __global__ void __launch_bounds__(448, 1)
   uint8_t* sBU = sA + C::STAGES * C::A_BYTES;
   uint8_t* sBP = sBU + C::STAGES * C::BU_BYTES;
   uint8_t* sSC = sBP + C::STAGES * C::BP_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSC + C::STAGES * C::SC_BYTES);
+  uint8_t* sSCT = sSC + C::STAGES * C::SC_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSCT + C::STAGES * C::SCT_BYTES);
   uint64_t* conv = full + C::STAGES;
   uint64_t* empty = conv + C::STAGES;
   uint64_t* gfull = empty + C::STAGES;
@@ -193,6 +196,14 @@ __global__ void __launch_bounds__(448, 1)
           *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c) ^ sw) << 4)) = o0;
           *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c + 1) ^ sw) << 4)) = o1;
         }
+        {  // scales [col][group] -> [group][col] for 128-bit epilogue loads
+          const float4 v = reinterpret_cast<const float4*>(sSC + stage * C::SC_BYTES)[t];
+          float* sct = reinterpret_cast<float*>(sSCT + stage * C::SCT_BYTES);
+          sct[0 * C::BN + t] = v.x;
+          sct[1 * C::BN + t] = v.y;
+          sct[2 * C::BN + t] = v.z;
+          sct[3 * C::BN + t] = v.w;
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[stage]);
@@ -215,7 +226,11 @@ __global__ void __launch_bounds__(448, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) s[i] = 0.0f;
       for (int kb = 0; kb < nkb; ++kb) {
-        const float* sc = reinterpret_cast<const float*>(sSC + stage * C::SC_BYTES);
+        if (!mbar_wait(&conv[stage], phase, abort_flag)) {  // transposed scales ready
+          kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
+          goto done;
+        }
+        const float* sct = reinterpret_cast<const float*>(sSCT + stage * C::SCT_BYTES);
 #pragma unroll 1
         for (int j = 0; j < C::GPK; ++j) {
           if (!mbar_wait(&gfull[gb], gphase, abort_flag)) {
@@ -235,11 +250,15 @@ __global__ void __launch_bounds__(448, 1)
               __syncwarp();
               if (lane == 0) mbar_arrive(&gempty[gb]);
             }
+            const float4* sc4 = reinterpret_cast<const float4*>(sct + j * C::BN + h * 64 + half * 32);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int ci = half * 32 + i;
-              const float scl = sc[(h * 64 + ci) * C::GPK + j];
-              s[ci] = __fmaf_rn(exact_i2f(r[i]), scl, s[ci]);
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const float4 sv = sc4[i4];  // same address in every lane: broadcast
+              const int ci = half * 32 + i4 * 4;
+              s[ci + 0] = __fmaf_rn(exact_i2f(r[i4 * 4 + 0]), sv.x, s[ci + 0]);
+              s[ci + 1] = __fmaf_rn(exact_i2f(r[i4 * 4 + 1]), sv.y, s[ci + 1]);
+              s[ci + 2] = __fmaf_rn(exact_i2f(r[i4 * 4 + 2]), sv.z, s[ci + 2]);
+              s[ci + 3] = __fmaf_rn(exact_i2f(r[i4 * 4 + 3]), sv.w, s[ci + 3]);
             }
             if (acc_out && row < M) {
               const int col0 = tn * C::BN + h * 64 + half * 32;

@@ -148,23 +148,32 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t aphase = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int tm = tile % tiles_m, tn = tile / tiles_m;
+      const int row = tm * C::BM + q * 32 + lane;
+      // Prefetch this tile's row scale and the column scales / bias (lane l
+      // holds column c*32 + l of chunk c) while the MMAs are still running.
+      const float sar = row < M ? __ldg(sa + row) : 0.0f;
+      float swv[BN / 32], bv[BN / 32];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        const int cl = tn * BN + c * 32 + lane;
+        swv[c] = cl < N ? __ldg(sw + cl) : 0.0f;
+        bv[c] = (bias && cl < N) ? __ldg(bias + cl) : 0.0f;
+      }
       if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
         kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
         break;
       }
       tc_fence_after();
-      const int row = tm * C::BM + q * 32 + lane;
-      const float sar = row < M ? sa[row] : 0.0f;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        const int c0 = c * 32;
         const int col0 = tn * BN + c0;
         if (col0 >= N) break;  // uniform across the warp
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c0), r);
         tmem_ld_wait();
-        const int cl = col0 + lane;
-        const float swl = cl < N ? __ldg(sw + cl) : 0.0f;
-        const float bl = (bias && cl < N) ? __ldg(bias + cl) : 0.0f;
+        const float swl = swv[c];
+        const float bl = bv[c];
         float y[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {

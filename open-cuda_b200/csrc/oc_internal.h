@@ -7,6 +7,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 #include "../../include/opencuda_cuda.h"
@@ -55,5 +56,34 @@ int check_device_status(cudaStream_t stream);
 bool smem_attr_once(const void* fn, size_t bytes);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- host-slice support (oc_blas_*) ----------------------------------------
+int device_ordinal(const oc_device* d);
+cudaStream_t device_stream(const oc_device* d);
+bool device_owns(oc_device* d, uint64_t addr, size_t bytes);
+
+// Grow-only device scratch, one per device object; callers hold `mu` for
+// the whole host-slice call (so calls on one device object serialize).
+struct Arena {
+  std::mutex mu;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+Arena& arena_of(const oc_device* d);
+int arena_get(Arena& a, size_t bytes, cudaStream_t s, uint8_t** out);
+
+// Makes `dev` current for the scope, restoring the previous device after.
+struct Scope {
+  int prev = -1;
+  explicit Scope(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~Scope() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && prev != cur) cudaSetDevice(prev);
+  }
+};
 
 }  // namespace oc

@@ -81,6 +81,24 @@ _SIGS = {
     "oc_device_synchronize": (ci, [vp]),
     "oc_device_stream": (vp, [vp]),
     "oc_get_device_status": (ci, [C.POINTER(ci)]),
+    "oc_sgemm": (ci, [ci, ci, ci, cf, vp, ci, vp, ci, ci, cf, vp, ci, vp, vp]),
+    "oc_sgemm_prepared_b_size": (ci, [ci, ci, C.POINTER(sz)]),
+    "oc_sgemm_prepare_b": (ci, [ci, ci, vp, ci, ci, vp, vp]),
+    "oc_sgemm_prepared": (ci, [ci, ci, ci, cf, vp, ci, vp, cf, vp, ci, vp, vp]),
+    "oc_softmax_rows": (ci, [vp, ci, ci, vp]),
+    "oc_flash_attention": (ci, [vp, vp, vp, vp, ci, ci, ci, vp]),
+    "oc_flash_attention_fwd": (ci, [vp, vp, vp, vp, ci, ci, ci, ci, cf, ci, vp]),
+    "oc_sdpa_workspace_size": (ci, [ci, C.POINTER(sz)]),
+    "oc_sdpa": (ci, [vp, vp, vp, vp, ci, ci, vp, sz, vp]),
+    "oc_mla_compress_kv": (ci, [ci, ci, ci, vp, vp, vp, vp]),
+    "oc_mla_decompress_kv": (ci, [ci, ci, ci, vp, vp, vp, vp]),
+    "oc_device_launch": (ci, [vp, C.c_char_p, vp, vp, sz]),
+    "oc_blas_sgemm": (ci, [vp, sz, sz, sz, cf, vp, vp, cf, vp]),
+    "oc_blas_softmax_rows": (ci, [vp, sz, sz, vp, vp]),
+    "oc_blas_flash_attention": (ci, [vp, vp, vp, vp, sz, sz, sz, vp]),
+    "oc_blas_sdpa": (ci, [vp, vp, vp, vp, sz, sz, vp]),
+    "oc_blas_mla_compress_kv": (ci, [vp, sz, sz, sz, vp, vp, vp]),
+    "oc_blas_mla_decompress_kv": (ci, [vp, sz, sz, sz, vp, vp, vp]),
     "oc_quantize_int8": (ci, [vp, sz, sz, vp, vp, vp]),
     "oc_quantize_int4": (ci, [vp, sz, sz, vp, vp, vp]),
     "oc_dequantize_int8": (ci, [vp, vp, sz, sz, vp, vp]),
@@ -153,6 +171,90 @@ def _need_cuda(*ts):
     for t in ts:
         if t is not None and not t.is_cuda:
             raise ValueError("expected CUDA tensors")
+
+
+def sgemm(A, B, alpha: float = 1.0, beta: float = 0.0, C=None, transpose_b: bool = False, bias=None):
+    """sgemm (blas:260-295): C = alpha*A.B + beta*C on the device.
+
+    A [m, k]; B [k, n] (or [n, k] with transpose_b, the launch_naive_gemm
+    form); returns C [m, n] (allocated when C is None)."""
+    torch = _torch()
+    _need_cuda(A, B, C, bias)
+    m, k = A.shape
+    n = B.shape[0] if transpose_b else B.shape[1]
+    if (B.shape[1] if transpose_b else B.shape[0]) != k:
+        raise ValueError(f"sgemm: B shape {tuple(B.shape)} does not match k={k}")
+    if C is None:
+        C = torch.zeros(m, n, dtype=torch.float32, device=A.device)
+    check(lib().oc_sgemm(m, n, k, alpha, _ptr(A), A.stride(0), _ptr(B), B.stride(0), int(transpose_b), beta,
+                         _ptr(C), C.stride(0), _ptr(bias), _stream()))
+    return C
+
+
+def softmax_rows(x):
+    """In-place row softmax of a [rows, cols] CUDA tensor (cpu_row_softmax semantics)."""
+    _need_cuda(x)
+    rows, cols = x.shape
+    check(lib().oc_softmax_rows(_ptr(x), rows, cols, _stream()))
+    return x
+
+
+def flash_attention(q, k, v, block_size: int):
+    """flash_attention_with_spirv (blas:707-766): q, k, v [seq, d] -> [seq, d]."""
+    torch = _torch()
+    _need_cuda(q, k, v)
+    seq, d = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"flash_attention_with_spirv: q/k/v shapes differ: {q.shape} {k.shape} {v.shape}")
+    o = torch.empty_like(q)
+    check(lib().oc_flash_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(o), seq, d, block_size, _stream()))
+    return o
+
+
+def flash_attention_fwd(q, k, v, scale=None, causal=False):
+    """Multi-head attention: q [bh, sq, d], k/v [bh, skv, d] -> [bh, sq, d]."""
+    torch = _torch()
+    _need_cuda(q, k, v)
+    bh, sq, d = q.shape
+    skv = k.shape[1]
+    o = torch.empty_like(q)
+    s = (1.0 / d ** 0.5) if scale is None else scale
+    check(lib().oc_flash_attention_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), bh, sq, skv, d, s, int(causal),
+                                       _stream()))
+    return o
+
+
+def scaled_dot_product_attention(q, k, v):
+    """scaled_dot_product_attention (blas:411-540), unfused, on the device."""
+    torch = _torch()
+    _need_cuda(q, k, v)
+    seq, d = q.shape
+    need = sz(0)
+    check(lib().oc_sdpa_workspace_size(seq, C.byref(need)))
+    ws = torch.empty(max(need.value, 4), dtype=torch.uint8, device=q.device)
+    o = torch.empty_like(q)
+    check(lib().oc_sdpa(_ptr(q), _ptr(k), _ptr(v), _ptr(o), seq, d, _ptr(ws), ws.numel(), _stream()))
+    return o
+
+
+def mla_compress_kv(kv, down_proj):
+    """mla_compress_kv (blas:1045-1052): kv [seq, d_h] . down [d_h, d_c]."""
+    torch = _torch()
+    seq, dh = kv.shape
+    dc = down_proj.shape[1]
+    out = torch.empty(seq, dc, dtype=torch.float32, device=kv.device)
+    check(lib().oc_mla_compress_kv(seq, dh, dc, _ptr(kv), _ptr(down_proj), _ptr(out), _stream()))
+    return out
+
+
+def mla_decompress_kv(latent, up_proj):
+    """mla_decompress_kv (blas:1060-1067): latent [seq, d_c] . up [d_c, d_h]."""
+    torch = _torch()
+    seq, dc = latent.shape
+    dh = up_proj.shape[1]
+    out = torch.empty(seq, dh, dtype=torch.float32, device=latent.device)
+    check(lib().oc_mla_decompress_kv(seq, dc, dh, _ptr(latent), _ptr(up_proj), _ptr(out), _stream()))
+    return out
 
 
 def quantize_int8(x, group_size: int):
@@ -380,3 +482,126 @@ class Device:
                                        _np_ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
                                        _np_ptr(y)))
         return y
+
+
+class LaunchConfig(C.Structure):
+    """LaunchConfig (crates/opencuda-core/src/device.rs:45-85)."""
+
+    _fields_ = [("grid", C.c_uint32 * 3), ("block", C.c_uint32 * 3), ("shared_mem", C.c_uint32)]
+
+
+class _ArgV(C.Union):
+    _fields_ = [("ptr", C.c_uint64), ("u32", C.c_uint32), ("i32", C.c_int32), ("f32", C.c_float),
+                ("usize", C.c_uint64)]
+
+
+class KernelArg(C.Structure):
+    """KernelArg (crates/opencuda-core/src/kernel.rs:88-100)."""
+
+    _fields_ = [("kind", ci), ("v", _ArgV)]
+
+    @staticmethod
+    def ptr(addr):
+        a = KernelArg(0)
+        a.v.ptr = addr
+        return a
+
+    @staticmethod
+    def usize(x):
+        a = KernelArg(4)
+        a.v.usize = x
+        return a
+
+    @staticmethod
+    def u32(x):
+        a = KernelArg(1)
+        a.v.u32 = x
+        return a
+
+    @staticmethod
+    def f32(x):
+        a = KernelArg(3)
+        a.v.f32 = x
+        return a
+
+
+def _f32c(x):
+    return np.ascontiguousarray(x, np.float32).ravel()
+
+
+def _device_blas_methods():
+    """Host-slice blas methods of Device (the reference's signatures)."""
+
+    def launch_kernel(self, name: str, args, grid=(1, 1, 1), block=(1, 1, 1)):
+        cfg = LaunchConfig((C.c_uint32 * 3)(*grid), (C.c_uint32 * 3)(*block), 0)
+        arr = (KernelArg * len(args))(*args)
+        check(lib().oc_device_launch(self._h, name.encode(), C.byref(cfg), arr, len(args)))
+
+    def sgemm(self, m, k, n, alpha, a, b, beta, c):
+        a, b = _f32c(a), _f32c(b)
+        c = np.ascontiguousarray(c, np.float32).ravel().copy()
+        if a.size != m * k:
+            raise ValueError(f"sgemm: a.len()={a.size} != m*k={m * k}")
+        if b.size != k * n:
+            raise ValueError(f"sgemm: b.len()={b.size} != k*n={k * n}")
+        if c.size != m * n:
+            raise ValueError(f"sgemm: c.len()={c.size} != m*n={m * n}")
+        check(lib().oc_blas_sgemm(self._h, m, k, n, alpha, _np_ptr(a), _np_ptr(b), beta, _np_ptr(c)))
+        return c
+
+    def softmax_rows(self, rows, cols, data):
+        d = _f32c(data)
+        if d.size != rows * cols:
+            raise ValueError(f"softmax_vulkan_generic: data.len()={d.size} != rows*cols={rows * cols}")
+        out = np.zeros(rows * cols, np.float32)
+        check(lib().oc_blas_softmax_rows(self._h, rows, cols, _np_ptr(d), _np_ptr(out)))
+        return out
+
+    def _qkv(self, name, q, k, v, seq, d):
+        q, k, v = _f32c(q), _f32c(k), _f32c(v)
+        for nm, x in (("q", q), ("k", k), ("v", v)):
+            if x.size != seq * d:
+                raise ValueError(f"{name}: {nm}.len()={x.size} != seq_len*head_dim={seq * d}")
+        return q, k, v
+
+    def flash_attention(self, q, k, v, seq_len, head_dim, block_size):
+        q, k, v = self._qkv("flash_attention_with_spirv", q, k, v, seq_len, head_dim)
+        if block_size == 0:
+            raise ValueError("flash_attention_with_spirv: block_size must be > 0")
+        out = np.zeros(seq_len * head_dim, np.float32)
+        check(lib().oc_blas_flash_attention(self._h, _np_ptr(q), _np_ptr(k), _np_ptr(v), seq_len, head_dim,
+                                            block_size, _np_ptr(out)))
+        return out
+
+    def scaled_dot_product_attention(self, q, k, v, seq_len, head_dim):
+        q, k, v = self._qkv("attention", q, k, v, seq_len, head_dim)
+        out = np.zeros(seq_len * head_dim, np.float32)
+        check(lib().oc_blas_sdpa(self._h, _np_ptr(q), _np_ptr(k), _np_ptr(v), seq_len, head_dim, _np_ptr(out)))
+        return out
+
+    def mla_compress_kv(self, seq_len, d_h, d_c, kv, down_proj):
+        kv, dp = _f32c(kv), _f32c(down_proj)
+        if kv.size != seq_len * d_h:
+            raise ValueError(f"mla_compress_kv: kv.len()={kv.size} != seq_len*d_h={seq_len * d_h}")
+        if dp.size != d_h * d_c:
+            raise ValueError(f"mla_compress_kv: down_proj.len()={dp.size} != d_h*d_c={d_h * d_c}")
+        out = np.zeros(seq_len * d_c, np.float32)
+        check(lib().oc_blas_mla_compress_kv(self._h, seq_len, d_h, d_c, _np_ptr(kv), _np_ptr(dp), _np_ptr(out)))
+        return out
+
+    def mla_decompress_kv(self, seq_len, d_c, d_h, latent, up_proj):
+        lt, up = _f32c(latent), _f32c(up_proj)
+        if lt.size != seq_len * d_c:
+            raise ValueError(f"mla_decompress_kv: latent.len()={lt.size} != seq_len*d_c={seq_len * d_c}")
+        if up.size != d_c * d_h:
+            raise ValueError(f"mla_decompress_kv: up_proj.len()={up.size} != d_c*d_h={d_c * d_h}")
+        out = np.zeros(seq_len * d_h, np.float32)
+        check(lib().oc_blas_mla_decompress_kv(self._h, seq_len, d_c, d_h, _np_ptr(lt), _np_ptr(up), _np_ptr(out)))
+        return out
+
+    for f in (launch_kernel, sgemm, softmax_rows, _qkv, flash_attention, scaled_dot_product_attention,
+              mla_compress_kv, mla_decompress_kv):
+        setattr(Device, f.__name__, f)
+
+
+_device_blas_methods()
