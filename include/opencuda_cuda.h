@@ -180,6 +180,45 @@ int oc_mla_compress_kv(int seq_len, int d_h, int d_c, const float *kv, const flo
 int oc_mla_decompress_kv(int seq_len, int d_c, int d_h, const float *latent, const float *up_proj, float *out,
                          void *stream);
 
+/* ---- GPT decoder (crates/open-cuda-llm/src/lib.rs:45-942) --------------- */
+
+/* GptConfig (llm:45-69). */
+typedef struct {
+  size_t vocab_size, hidden_size, num_layers, num_heads, intermediate_size, max_seq_len;
+  float layer_norm_eps;
+} oc_gpt_config;
+
+typedef struct oc_gpt oc_gpt;
+/* A device-resident GptModel on CUDA device `device` for up to max_batch
+ * sequences with prompts of up to max_prompt_len tokens.  head_dim
+ * (hidden_size / num_heads) must be <= 128 and hidden / intermediate sizes
+ * multiples of 4.  Weights, KV cache and activations live in HBM; nothing is
+ * copied per token. */
+int oc_gpt_create(int device, const oc_gpt_config *cfg, int max_batch, int max_prompt_len, oc_gpt **model);
+int oc_gpt_destroy(oc_gpt *model);
+/* GptModel::load_random (llm:635-646): weights generated on the device from
+ * SplitMix64(seed) in the reference's draw order, bit-identical to the
+ * reference's values. */
+int oc_gpt_load_random(oc_gpt *model, uint64_t seed);
+/* Uploads one weight tensor from host memory (for real checkpoints,
+ * llm:661-731).  which: 0 wte [V][H], 1 wpe [ctx][H], per layer 2 qkv_w
+ * [H][3H], 3 qkv_b, 4 attn_out_w [H][H], 5 attn_out_b, 6 fc_w [H][I], 7 fc_b,
+ * 8 proj_w [I][H], 9 proj_b, 10 ln1_w, 11 ln1_b, 12 ln2_w, 13 ln2_b; 14
+ * lnf_w, 15 lnf_b, 16 lm_head_w [H][V], 17 lm_head_b.  Linear weights are
+ * weight_t = [in][out] as the reference stores them. */
+int oc_gpt_set_weight(oc_gpt *model, int which, int layer, const float *host, size_t len);
+/* Copies one weight tensor back to host memory (same ids and shapes). */
+int oc_gpt_get_weight(oc_gpt *model, int which, int layer, float *host, size_t len);
+/* GptModel::generate (llm:910-929), greedy, for `batch` independent
+ * sequences with prompts [batch][prompt_len] (host).  out [batch][max_new]
+ * (host); logits_out (optional, host) [batch][max_new][vocab], the logits
+ * each token was taken from; *produced = tokens per sequence (fewer than
+ * max_new only when max_seq_len is reached, as in the reference). */
+int oc_gpt_generate(oc_gpt *model, int batch, const uint32_t *prompts, int prompt_len, int max_new,
+                    uint32_t *out, float *logits_out, int *produced);
+/* The stream the model runs on (a cudaStream_t). */
+int oc_gpt_stream(oc_gpt *model, void **stream);
+
 /* ---- quantization (blas:777-945) ---------------------------------------
  * Groups are contiguous runs of `group` elements of the flat input
  * (group_scales, blas:797-809); scale = max|x| / qmax (0 for an all-zero

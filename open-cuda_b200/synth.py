@@ -57,6 +57,15 @@ def normal(seed: int, n: int, mu: float = 0.0, sigma: float = 1.0) -> np.ndarray
     return (mu + sigma * z[:n]).astype(np.float32)
 
 
+def gpt_prompts(batch: int, length: int = 32, vocab: int = 50257, seed: int = 3) -> np.ndarray:
+    """Prompt ids of the GPT-2 decode workload: sequence b takes `length`
+    outputs of SplitMix64(seed + 1000*(b+1)) modulo the vocabulary."""
+    out = np.zeros((batch, length), np.uint32)
+    for b in range(batch):
+        out[b] = (splitmix64(seed + 1000 * (b + 1), length) % np.uint64(vocab)).astype(np.uint32)
+    return out
+
+
 def qgemm_case(m: int, k: int, n: int, seed_a: int = 1, seed_w: int = 2, seed_b: int = 3):
     """A [m][k] ~ U(-1,1), W [k][n] ~ N(0, 0.02), bias [n] ~ N(0, 0.02).
 
