@@ -235,6 +235,17 @@ int oc_dequantize_int8(const int8_t *data, const float *scales, size_t len, size
 int oc_dequantize_int4(const uint8_t *data, const float *scales, size_t len, size_t group, float *out,
                        void *stream);
 
+/* quantize_int4_awq / dequantize_int4_awq (blas:958-1012) for a row-major
+ * weight [rows][cols]: oc_awq_scales computes the per-column scales on the
+ * host exactly as the reference does (s <= 0 ? 1 : powf(s, alpha)); the
+ * device routines quantize weight * awq_scale[col] with quantize_int4 and
+ * undo the column scale on dequantization.  awq_scale is device memory. */
+int oc_awq_scales(const float *act_scale, size_t cols, float alpha, float *awq_scale);
+int oc_quantize_int4_awq(const float *weight, size_t rows, size_t cols, const float *awq_scale, size_t group,
+                         uint8_t *data, float *scales, void *stream);
+int oc_dequantize_int4_awq(const uint8_t *data, const float *scales, size_t rows, size_t cols, size_t group,
+                           const float *awq_scale, float *out, void *stream);
+
 /* ---- quantized matmul (new API: the reference only quantizes) ----------
  * Y[m][n] = A[m][k] . W^T + bias with W^T stored as the reference quantizes
  * it: a [n][k] matrix flattened and passed to quantize_int8 (group = k, one
@@ -284,6 +295,15 @@ int oc_qgemm_w8a8_noalloc(int m, int n, int k, const float *A, const int8_t *Wq,
                           const float *bias, float *Y, void *stream);
 /* The size of that array in bytes (16 MiB). */
 int oc_qgemm_w8a8_noalloc_max_bytes(size_t *bytes);
+
+/* ---- multi-GPU column sharding (no counterpart in the reference, whose
+ * only multi-device code is a layer partition stub,
+ * crates/opencuda-multidev/src/lib.rs:28-83) ------------------------------
+ * Each of g ranks computes Y_r = A . W_r^T for its block of N/g output
+ * columns (rows of the quantized W^T); after an all-gather the shards sit
+ * as [g][m][shard_cols].  oc_gather_columns writes them as out [m][g *
+ * shard_cols], shard r at columns r*shard_cols .. */
+int oc_gather_columns(const float *shards, float *out, int num_shards, int m, int shard_cols, void *stream);
 
 /* ---- host-slice entry points (blas signatures on host memory) ---------- */
 

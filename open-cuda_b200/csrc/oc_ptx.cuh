@@ -1,7 +1,7 @@
 // oc_ptx.cuh -- thin inline-PTX wrappers for sm_100a: mbarrier, TMA tile
 // loads, and the tcgen05 (5th-gen tensor core / TMEM) instructions used by
-// the GEMM kernels.  No cluster multicast anywhere: every TMA load targets
-// this CTA's own shared memory from this GPU's own global memory.
+// the GEMM kernels.  Every TMA load is a plain (single-CTA) copy into this
+// CTA's own shared memory from this GPU's own global memory.
 #pragma once
 #include <cstdint>
 #include <cuda.h>

@@ -99,6 +99,10 @@ _SIGS = {
     "oc_blas_sdpa": (ci, [vp, vp, vp, vp, sz, sz, vp]),
     "oc_blas_mla_compress_kv": (ci, [vp, sz, sz, sz, vp, vp, vp]),
     "oc_blas_mla_decompress_kv": (ci, [vp, sz, sz, sz, vp, vp, vp]),
+    "oc_gather_columns": (ci, [vp, vp, ci, ci, ci, vp]),
+    "oc_awq_scales": (ci, [vp, sz, cf, vp]),
+    "oc_quantize_int4_awq": (ci, [vp, sz, sz, vp, sz, vp, vp, vp]),
+    "oc_dequantize_int4_awq": (ci, [vp, vp, sz, sz, sz, vp, vp, vp]),
     "oc_quantize_int8": (ci, [vp, sz, sz, vp, vp, vp]),
     "oc_quantize_int4": (ci, [vp, sz, sz, vp, vp, vp]),
     "oc_dequantize_int8": (ci, [vp, vp, sz, sz, vp, vp]),
@@ -279,6 +283,36 @@ def quantize_int4(x, group_size: int):
     s = torch.empty(max(1, -(-n // max(group_size, 1))), dtype=torch.float32, device=x.device)
     check(lib().oc_quantize_int4(_ptr(x), n, group_size, _ptr(q), _ptr(s), _stream()))
     return q, s
+
+
+def quantize_int4_awq(weight, activation_scale, group_size: int, alpha: float):
+    """quantize_int4_awq (blas:958-989): weight [rows, cols] CUDA tensor,
+    activation_scale [cols] host values.  Returns (packed, scales, awq_scale)."""
+    torch = _torch()
+    _need_cuda(weight)
+    rows, cols = weight.shape
+    act = np.ascontiguousarray(activation_scale, np.float32).ravel()
+    if rows == 0 or cols == 0:
+        raise ValueError("quantize_int4_awq: rows and cols must be > 0")
+    if act.size != cols:
+        raise ValueError("quantize_int4_awq: activation_scale.len() must equal cols")
+    awq = np.zeros(cols, np.float32)
+    check(lib().oc_awq_scales(act.ctypes.data_as(vp), cols, alpha, awq.ctypes.data_as(vp)))
+    awq_d = torch.from_numpy(awq).to(weight.device)
+    n = rows * cols
+    q = torch.empty((n + 1) // 2, dtype=torch.uint8, device=weight.device)
+    s = torch.empty(-(-n // max(group_size, 1)), dtype=torch.float32, device=weight.device)
+    check(lib().oc_quantize_int4_awq(_ptr(weight.contiguous()), rows, cols, _ptr(awq_d), group_size, _ptr(q),
+                                     _ptr(s), _stream()))
+    return q, s, awq_d
+
+
+def dequantize_int4_awq(q, scales, rows: int, cols: int, group_size: int, awq_scale):
+    torch = _torch()
+    out = torch.empty(rows * cols, dtype=torch.float32, device=q.device)
+    check(lib().oc_dequantize_int4_awq(_ptr(q), _ptr(scales), rows, cols, group_size, _ptr(awq_scale), _ptr(out),
+                                       _stream()))
+    return out
 
 
 def dequantize_int8(q, scales, length: int, group_size: int):

@@ -154,6 +154,27 @@ def test_qgemm_matches_weight_only_reference_loosely(oc, oracle):
     assert rel < 2e-2
 
 
+@pytest.mark.parametrize("rows,cols,group,alpha", [(1, 4, 4, 1.0), (96, 768, 32, 0.5), (7, 33, 5, 0.8)])
+def test_awq_bit_exact(oc, oracle, rows, cols, group, alpha):
+    if rows == 1:  # blas:1274-1305 known answer: the salient channel survives
+        w = np.array([10.0, 10.0, 10.0, 0.1], np.float32)
+        act = np.array([1.0, 1.0, 1.0, 100.0], np.float32)
+    else:
+        w = synth.normal(rows + cols, rows * cols, 0.0, 0.02)
+        act = np.abs(synth.normal(cols, cols, 0.0, 2.0))
+        act[::7] = 0.0  # non-positive scales map to 1
+    ref = oracle.quantize_int4_awq(w, rows, cols, act, group, alpha)
+    q, s, awq = oc.quantize_int4_awq(torch.from_numpy(w).cuda().view(rows, cols), act, group, alpha)
+    torch.cuda.synchronize()
+    bits_equal(awq.cpu().numpy(), ref.awq_scale)
+    bits_equal(s.cpu().numpy(), ref.inner.scales)
+    bits_equal(q.cpu().numpy(), ref.inner.data)
+    d = oc.dequantize_int4_awq(q, s, rows, cols, group, awq)
+    bits_equal(d.cpu().numpy(), oracle.dequantize_int4_awq(ref))
+    if rows == 1:
+        assert abs(w[3] - d.cpu().numpy()[3]) < abs(w[3] - 0.0)
+
+
 def test_device_alloc_copy_contract(oc):
     dev = oc.Device(0)
     with pytest.raises(MemoryError):

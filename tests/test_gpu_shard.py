@@ -1,0 +1,79 @@
+"""Column-sharded W4A8 GEMM on 2+ GPUs (one process per GPU, NCCL
+all-gather): the gathered [M][N] result must equal the single-GPU result
+bit for bit (each output column is computed by the same kernel either way).
+Skipped when fewer than two GPUs are visible."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, shape, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        import opencuda_cuda as oc
+        import shard
+        import synth
+
+        m, k, n, g = shape
+        A, WT, bias = synth.qgemm_case(m, k, n, 4, 5, 6)
+        Wd = torch.from_numpy(WT).to(dev)
+        q4, s4 = oc.quantize_int4(Wd, g)
+        Ad = torch.from_numpy(A).to(dev)
+        bd = torch.from_numpy(bias).to(dev)
+        plan = shard.ColumnShard(n, world)
+        y = shard.sharded_qgemm_w4a8(Ad, q4, s4, g, bd, plan, rank)
+        full = oc.qgemm_w4a8(Ad, q4, s4, g, bd)
+        torch.cuda.synchronize()
+        ok = torch.equal(y.view(torch.int32), full.view(torch.int32))
+        q.put((rank, "ok" if ok else "mismatch"))
+    except Exception as e:
+        q.put((rank, f"error:{e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("shape", [(64, 3584, 3584, 32), (512, 3584, 18944, 32), (1, 3584, 152064, 32)])
+def test_sharded_w4a8_matches_single_gpu(shape):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+    res = {}
+    while not q.empty():
+        r, v = q.get()
+        res[r] = v
+    assert res == {0: "ok", 1: "ok"}, res
