@@ -9,14 +9,14 @@
 // One MMA instruction (M=128, N=128, K=32) is exactly one group, so each
 // group's partial is produced into its own TMEM buffer (4 buffers x 128
 // columns) and promoted to f32 by the epilogue while the tensor core works
-// on the next groups.  Roles (448 threads):
+// on the next groups.  Roles (640 threads):
 //   warp 0      TMA producer: int8 A tile (128B swizzle), packed B tile
 //               (64 bytes x 128 rows) and the 128 x 4 scale tile per k-block
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one MMA per group)
-//   warps 2..5  converters: widen the packed nibbles to signed int8 in the
+//   warps 2..3  converters: widen the packed nibbles to signed int8 in the
 //               128-byte-swizzled K-major layout the MMA reads
-//   warps 6..13 epilogue: 2 warps per TMEM lane quadrant, 64 columns each,
-//               64 running f32 sums per thread; (float)P is formed exactly
+//   warps 4..19 epilogue: 4 warps per TMEM lane quadrant, 32 columns each,
+//               32 running f32 sums per thread; (float)P is formed exactly
 //               with the 1.5*2^23 magic-number add (|P| < 2^22).
 #pragma once
 #include "oc_gemm_i8.cuh"
@@ -33,7 +33,7 @@ struct I4Gemm {
   static constexpr int SCT_BYTES = SC_BYTES;    // the same, [4][n]
   static constexpr int TX_BYTES = A_BYTES + BP_BYTES + SC_BYTES;
   static constexpr int TMEM_COLS = 4 * BN;
-  static constexpr int THREADS = 448;
+  static constexpr int THREADS = 640;
   static constexpr size_t SMEM =
       1024 + (size_t)STAGES * (A_BYTES + BU_BYTES + BP_BYTES + SC_BYTES + SCT_BYTES) + 512;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
@@ -57,7 +57,7 @@ __device__ __forceinline__ float exact_i2f(uint32_t p) {
   return __fadd_rn(__int_as_float((int)(p + 0x4B400000u)), -12582912.0f);
 }
 
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(640, 1)
     gemm_w4a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBp,
                         const __grid_constant__ CUtensorMap tmS, int M, int N, int K,
                         const float* __restrict__ sa, const float* __restrict__ bias, float* __restrict__ Y,
@@ -82,12 +82,12 @@ __global__ void __launch_bounds__(448, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);
-      mbar_init(&empty[s], 1 + 8);  // MMA commit + 8 epilogue warps (scales)
+      mbar_init(&conv[s], 2);
+      mbar_init(&empty[s], 1 + 16);  // MMA commit + 16 epilogue warps (scales)
     }
     for (int b = 0; b < 4; ++b) {
       mbar_init(&gfull[b], 1);
-      mbar_init(&gempty[b], 8);
+      mbar_init(&gempty[b], 16);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -168,8 +168,8 @@ __global__ void __launch_bounds__(448, 1)
         }
       }
     }
-  } else if (warp < 6) {
-    // Converters: thread t widens row (t/4 + 32*i), 16-byte input chunk t%4
+  } else if (warp < 4) {
+    // Converters: thread t widens row (t/4 + 16*i), 16-byte input chunk t%4
     // (32 elements) into output chunks 2c and 2c+1 of the swizzled row.
     const int t = threadIdx.x - 64;
     const int c = t & 3;
@@ -184,8 +184,8 @@ __global__ void __launch_bounds__(448, 1)
         const uint8_t* src = sBP + stage * C::BP_BYTES;
         uint8_t* dst = sBU + stage * C::BU_BYTES;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = (t >> 2) + 32 * i;
+        for (int i = 0; i < 8; ++i) {
+          const int r = (t >> 2) + 16 * i;
           const uint4 w = *reinterpret_cast<const uint4*>(src + r * 64 + c * 16);
           uint4 o0, o1;
           widen8(w.x, o0.x, o0.y);
@@ -196,13 +196,15 @@ __global__ void __launch_bounds__(448, 1)
           *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c) ^ sw) << 4)) = o0;
           *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c + 1) ^ sw) << 4)) = o1;
         }
-        {  // scales [col][group] -> [group][col] for 128-bit epilogue loads
-          const float4 v = reinterpret_cast<const float4*>(sSC + stage * C::SC_BYTES)[t];
-          float* sct = reinterpret_cast<float*>(sSCT + stage * C::SCT_BYTES);
-          sct[0 * C::BN + t] = v.x;
-          sct[1 * C::BN + t] = v.y;
-          sct[2 * C::BN + t] = v.z;
-          sct[3 * C::BN + t] = v.w;
+        float* sct = reinterpret_cast<float*>(sSCT + stage * C::SCT_BYTES);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // scales [col][group] -> [group][col]
+          const int col = t + 64 * h;
+          const float4 v = reinterpret_cast<const float4*>(sSC + stage * C::SC_BYTES)[col];
+          sct[0 * C::BN + col] = v.x;
+          sct[1 * C::BN + col] = v.y;
+          sct[2 * C::BN + col] = v.z;
+          sct[3 * C::BN + col] = v.w;
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -214,17 +216,19 @@ __global__ void __launch_bounds__(448, 1)
       }
     }
   } else {
-    // Epilogue: quadrant q = warp % 4 (TMEM lanes 32q..32q+31 = tile rows),
-    // column half h: columns 64h .. 64h+63 of the tile.
-    const int q = warp & 3, h = (warp - 6) >> 2;
+    // Epilogue: 16 warps; quadrant q = warp % 4 (TMEM lanes 32q..32q+31 =
+    // tile rows), column quarter cq: columns 32cq .. 32cq+31 of the tile.
+    const int q = warp & 3, cq = (warp - 4) >> 2;
     int stage = 0, gb = 0;
     uint32_t phase = 0, gphase = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int tm = tile % tiles_m, tn = tile / tiles_m;
       const int row = tm * C::BM + q * 32 + lane;
-      float s[64];
+      const int col0 = tn * C::BN + cq * 32;
+      const float bl = (bias && col0 + lane < N) ? __ldg(bias + col0 + lane) : 0.0f;
+      float s[32];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) s[i] = 0.0f;
+      for (int i = 0; i < 32; ++i) s[i] = 0.0f;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&conv[stage], phase, abort_flag)) {  // transposed scales ready
           kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
@@ -238,34 +242,26 @@ __global__ void __launch_bounds__(448, 1)
             goto done;
           }
           tc_fence_after();
-          const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(gb * C::BN + h * 64);
-          const int gidx = kb * C::GPK + j;
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(gb * C::BN + cq * 32), r);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&gempty[gb]);
+          const float4* sc4 = reinterpret_cast<const float4*>(sct + j * C::BN + cq * 32);
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t r[32];
-            tmem_ld32(taddr + half * 32, r);
-            tmem_ld_wait();
-            if (half == 1) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&gempty[gb]);
-            }
-            const float4* sc4 = reinterpret_cast<const float4*>(sct + j * C::BN + h * 64 + half * 32);
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 sv = sc4[i4];  // same address in every lane: broadcast
+            s[i4 * 4 + 0] = __fmaf_rn(exact_i2f(r[i4 * 4 + 0]), sv.x, s[i4 * 4 + 0]);
+            s[i4 * 4 + 1] = __fmaf_rn(exact_i2f(r[i4 * 4 + 1]), sv.y, s[i4 * 4 + 1]);
+            s[i4 * 4 + 2] = __fmaf_rn(exact_i2f(r[i4 * 4 + 2]), sv.z, s[i4 * 4 + 2]);
+            s[i4 * 4 + 3] = __fmaf_rn(exact_i2f(r[i4 * 4 + 3]), sv.w, s[i4 * 4 + 3]);
+          }
+          if (acc_out && row < M) {
+            const int gidx = kb * C::GPK + j;
 #pragma unroll
-            for (int i4 = 0; i4 < 8; ++i4) {
-              const float4 sv = sc4[i4];  // same address in every lane: broadcast
-              const int ci = half * 32 + i4 * 4;
-              s[ci + 0] = __fmaf_rn(exact_i2f(r[i4 * 4 + 0]), sv.x, s[ci + 0]);
-              s[ci + 1] = __fmaf_rn(exact_i2f(r[i4 * 4 + 1]), sv.y, s[ci + 1]);
-              s[ci + 2] = __fmaf_rn(exact_i2f(r[i4 * 4 + 2]), sv.z, s[ci + 2]);
-              s[ci + 3] = __fmaf_rn(exact_i2f(r[i4 * 4 + 3]), sv.w, s[ci + 3]);
-            }
-            if (acc_out && row < M) {
-              const int col0 = tn * C::BN + h * 64 + half * 32;
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < N) acc_out[((size_t)row * N + col0 + i) * ng + gidx] = (int32_t)r[i];
-            }
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < N) acc_out[((size_t)row * N + col0 + i) * ng + gidx] = (int32_t)r[i];
           }
           if (++gb == 4) {
             gb = 0;
@@ -279,24 +275,26 @@ __global__ void __launch_bounds__(448, 1)
           phase ^= 1u;
         }
       }
-      if (row < M) {
-        const float sar = sa[row];
-        const int col0 = tn * C::BN + h * 64;
-        float* yrow = Y + (size_t)row * N + col0;
-        if ((N & 3) == 0 && col0 + 64 <= N && (reinterpret_cast<uintptr_t>(Y) & 15u) == 0) {
+      const float sar = row < M ? sa[row] : 0.0f;
 #pragma unroll
-          for (int i = 0; i < 64; i += 4) {
+      for (int i = 0; i < 32; ++i)  // y = s * sa + bias (bias of column col0+i from lane i)
+        s[i] = __fadd_rn(__fmul_rn(s[i], sar), __shfl_sync(0xffffffffu, bl, i));
+      if (row < M && col0 < N) {
+        float* yrow = Y + (size_t)row * N + col0;
+        if ((N & 3) == 0 && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(Y) & 15u) == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
             float4 v;
-            v.x = __fadd_rn(__fmul_rn(s[i + 0], sar), bias ? __ldg(bias + col0 + i + 0) : 0.0f);
-            v.y = __fadd_rn(__fmul_rn(s[i + 1], sar), bias ? __ldg(bias + col0 + i + 1) : 0.0f);
-            v.z = __fadd_rn(__fmul_rn(s[i + 2], sar), bias ? __ldg(bias + col0 + i + 2) : 0.0f);
-            v.w = __fadd_rn(__fmul_rn(s[i + 3], sar), bias ? __ldg(bias + col0 + i + 3) : 0.0f);
+            v.x = s[i + 0];
+            v.y = s[i + 1];
+            v.z = s[i + 2];
+            v.w = s[i + 3];
             *reinterpret_cast<float4*>(yrow + i) = v;
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (col0 + i < N) yrow[i] = __fadd_rn(__fmul_rn(s[i], sar), bias ? __ldg(bias + col0 + i) : 0.0f);
+          for (int i = 0; i < 32; ++i)
+            if (col0 + i < N) yrow[i] = s[i];
         }
       }
     }

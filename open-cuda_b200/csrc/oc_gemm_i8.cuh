@@ -26,7 +26,8 @@ struct I8Gemm {
   static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // power of two, <= 512
   static constexpr int THREADS = 192;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static constexpr int YSTAGE_BYTES = 4 * 2 * 4096;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + YSTAGE_BYTES + 256;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
 };
 
@@ -37,16 +38,17 @@ __device__ __forceinline__ void kernel_fail(int* status, volatile int* abort_fla
 
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
-    gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                        int N, int K, const float* __restrict__ sa, const float* __restrict__ sw,
-                        const float* __restrict__ bias, float* __restrict__ Y, int32_t* __restrict__ acc_out,
-                        int* status) {
+    gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmY, int y_tma, int M, int N, int K,
+                        const float* __restrict__ sa, const float* __restrict__ sw, const float* __restrict__ bias,
+                        float* __restrict__ Y, int32_t* __restrict__ acc_out, int* status) {
   using C = I8Gemm<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint8_t* ystage = sB + C::STAGES * C::B_BYTES;  // 4 warps x 2 x 4 KB output staging
+  uint64_t* full = reinterpret_cast<uint64_t*>(ystage + C::YSTAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -144,6 +146,7 @@ __global__ void __launch_bounds__(192, 1)
     // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = tile rows.
     const int q = warp & 3;
     const bool vec = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15u) == 0);
+    uint32_t ybuf = 0;
     int acc = 0;
     uint32_t aphase = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
@@ -181,7 +184,25 @@ __global__ void __launch_bounds__(192, 1)
           const float bj = __shfl_sync(0xffffffffu, bl, j);
           y[j] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sar), swj), bj);
         }
-        if (row < M) {
+        if (y_tma) {
+          // Stage the warp's 32x32 block in shared memory (128-byte swizzle:
+          // 16-byte chunk cc of row t at (cc ^ t%8)) and write it with one
+          // TMA store; rows/columns past M/N are clipped by the TMA unit.
+          uint8_t* buf = ystage + (size_t)((q * 2 + (ybuf & 1)) * 4096);
+          if (lane == 0) bulk_wait_read<1>();  // the store that last used buf has read it
+          __syncwarp();
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc)
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((cc ^ (lane & 7)) << 4)) =
+                make_float4(y[4 * cc], y[4 * cc + 1], y[4 * cc + 2], y[4 * cc + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmY, buf, col0, tm * C::BM + q * 32);
+            bulk_commit();
+          }
+          ++ybuf;
+        } else if (row < M) {
           float* yrow = Y + (size_t)row * N + col0;
           if (vec && col0 + 32 <= N) {
 #pragma unroll
@@ -192,12 +213,12 @@ __global__ void __launch_bounds__(192, 1)
             for (int j = 0; j < 32; ++j)
               if (col0 + j < N) yrow[j] = y[j];
           }
-          if (acc_out) {
-            int32_t* arow = acc_out + (size_t)row * N + col0;
+        }
+        if (acc_out && row < M) {
+          int32_t* arow = acc_out + (size_t)row * N + col0;
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) arow[j] = (int32_t)r[j];
-          }
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < N) arow[j] = (int32_t)r[j];
         }
       }
       tc_fence_before();
@@ -208,6 +229,8 @@ __global__ void __launch_bounds__(192, 1)
         aphase ^= 1u;
       }
     }
+    if (y_tma && lane == 0) bulk_wait<0>();  // all output stores complete
+    __syncwarp();
   }
 done:
   tc_fence_before();

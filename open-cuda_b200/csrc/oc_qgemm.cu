@@ -113,7 +113,7 @@ __global__ void w8a8_generic_kernel(int m, int n, int k, const int8_t* __restric
   }
 }
 
-// ---- skinny W4A8: one thread per output column ----------------------------
+// ---- skinny W4A8 -----------------------------------------------------------
 // Packed row col: k/2 bytes; byte b holds elements 2b (low nibble) and 2b+1
 // (high nibble) as q + 8.  A 16-byte load covers 32 consecutive elements.
 // Activations are staged in shared memory de-interleaved per 8 elements so
@@ -127,17 +127,28 @@ __device__ __forceinline__ int dp4a_su(int a, uint32_t b, int c) {
   return d;
 }
 
+// One warp per output column: lane j owns group j (and j+32, ...), loads
+// its 16-byte chunks (a group of 32 INT4 values per chunk, coalesced across
+// lanes), and forms the exact partials P[r][j] for all rows r with
+// dp4a.s32.u32; the partials and the column's group scales go through shared
+// memory, and lane r then runs row r's f32 promotion in ascending group
+// order (s = fma((float)P, sw, s)), the order the oracle defines.
+constexpr int kW4Warps = 8;
 template <int MR>
-__global__ void __launch_bounds__(128) w4a8_skinny_kernel(int m, int n, int k, int group,
-                                                          const int8_t* __restrict__ qa,
-                                                          const float* __restrict__ sa,
-                                                          const uint8_t* __restrict__ wq,
-                                                          const float* __restrict__ sw,
-                                                          const float* __restrict__ bias, float* __restrict__ Y,
-                                                          int32_t* __restrict__ acc_out) {
-  extern __shared__ int s_act[];  // [m][k/32][8] words, then [m][k/32] sums
+__global__ void __launch_bounds__(kW4Warps * 32) w4a8_skinny_kernel(int m, int n, int k, int group,
+                                                                    const int8_t* __restrict__ qa,
+                                                                    const float* __restrict__ sa,
+                                                                    const uint8_t* __restrict__ wq,
+                                                                    const float* __restrict__ sw,
+                                                                    const float* __restrict__ bias,
+                                                                    float* __restrict__ Y,
+                                                                    int32_t* __restrict__ acc_out) {
+  extern __shared__ int s_dyn[];
   const int nch = k >> 5;         // 32-element chunks per row
-  int* s_sum = s_act + m * nch * 8;
+  const int ng = k / group, cpg = group >> 5;
+  int* s_act = s_dyn;             // [m][nch][8] de-interleaved activation words
+  int* s_sum = s_act + m * nch * 8;  // [m][nch] chunk sums of the activations
+  int* s_warp = s_sum + m * nch;  // per warp: P [MR][ng] then scales [ng]
   for (int i = threadIdx.x; i < m * nch; i += blockDim.x) {
     const int r = i / nch, ch = i % nch;
     const int8_t* a = qa + (size_t)r * k + ch * 32;
@@ -156,13 +167,13 @@ __global__ void __launch_bounds__(128) w4a8_skinny_kernel(int m, int n, int k, i
     s_sum[i] = sum;
   }
   __syncthreads();
-  const int ng = k / group, cpg = group >> 5;  // chunks per group
-  for (int col = blockIdx.x * blockDim.x + threadIdx.x; col < n; col += gridDim.x * blockDim.x) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* sP = s_warp + warp * (MR * ng + ng);
+  float* sS = reinterpret_cast<float*>(sP + MR * ng);
+  const int warps = gridDim.x * kW4Warps;
+  for (int col = blockIdx.x * kW4Warps + warp; col < n; col += warps) {
     const uint4* wrow = reinterpret_cast<const uint4*>(wq + (size_t)col * (k >> 1));
-    float s[MR];
-#pragma unroll
-    for (int r = 0; r < MR; ++r) s[r] = 0.0f;
-    for (int j = 0; j < ng; ++j) {
+    for (int j = lane; j < ng; j += 32) {
       int part[MR];
 #pragma unroll
       for (int r = 0; r < MR; ++r) part[r] = 0;
@@ -190,19 +201,23 @@ __global__ void __launch_bounds__(128) w4a8_skinny_kernel(int m, int n, int k, i
           }
         }
       }
-      const float scj = __ldg(sw + (size_t)col * ng + j);
 #pragma unroll
-      for (int r = 0; r < MR; ++r) {
-        if (r < m) {
-          s[r] = __fmaf_rn(__int2float_rn(part[r]), scj, s[r]);
-          if (acc_out) acc_out[((size_t)r * n + col) * ng + j] = part[r];
-        }
-      }
+      for (int r = 0; r < MR; ++r)
+        if (r < m) sP[r * ng + j] = part[r];
+      sS[j] = __ldg(sw + (size_t)col * ng + j);
     }
-    const float bc = bias ? __ldg(bias + col) : 0.0f;
-#pragma unroll
-    for (int r = 0; r < MR; ++r)
-      if (r < m) Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(s[r], sa[r]), bc);
+    __syncwarp();
+    if (lane < m) {
+      const int r = lane;
+      float acc = 0.0f;
+      for (int j = 0; j < ng; ++j) {
+        const int p = sP[r * ng + j];
+        acc = __fmaf_rn(__int2float_rn(p), sS[j], acc);
+        if (acc_out) acc_out[((size_t)r * n + col) * ng + j] = p;
+      }
+      Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(acc, sa[r]), bias ? __ldg(bias + col) : 0.0f);
+    }
+    __syncwarp();
   }
 }
 
@@ -244,18 +259,21 @@ int run_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, cons
 
 int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const float* sa, const uint8_t* wq,
                     const float* sw, const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
-  const size_t smem = (size_t)m * (k / 32) * 9 * sizeof(int);
+  const int ng = k / group, nch = k / 32;
+  auto smem_for = [&](int mr) { return ((size_t)m * nch * 9 + (size_t)kW4Warps * (mr * ng + ng)) * sizeof(int); };
+  const int mr = m <= 1 ? 1 : m <= 4 ? 4 : m <= 8 ? 8 : 16;
+  const size_t smem = smem_for(mr);
   if (smem > 200 * 1024) return fail(OC_ERR_NOT_SUPPORTED, "w4a8 skinny: m*k too large for shared memory");
-  const int grid = grid_cols(n, 128);
+  const int grid = std::max(1, std::min((n + kW4Warps - 1) / kW4Warps, std::max(1, sm_count()) * 8));
   auto launch = [&](auto kern) {
     smem_attr_once(reinterpret_cast<const void*>(kern), 200 * 1024);
-    kern<<<grid, 128, smem, s>>>(m, n, k, group, qa, sa, wq, sw, bias, Y, acc_out);
+    kern<<<grid, kW4Warps * 32, smem, s>>>(m, n, k, group, qa, sa, wq, sw, bias, Y, acc_out);
   };
-  if (m <= 1)
+  if (mr == 1)
     launch(w4a8_skinny_kernel<1>);
-  else if (m <= 4)
+  else if (mr == 4)
     launch(w4a8_skinny_kernel<4>);
-  else if (m <= 8)
+  else if (mr == 8)
     launch(w4a8_skinny_kernel<8>);
   else
     launch(w4a8_skinny_kernel<16>);
@@ -284,11 +302,20 @@ static int launch_w8a8_tc(int m, int n, int k, const int8_t* qa, const float* sa
   rc = make_tmap_2d(&tb, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k, (uint64_t)n, (uint64_t)k, C::BK, BN,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  // Output through TMA stores when Y's rows are 16-byte aligned.
+  CUtensorMap ty = tb;
+  int y_tma = 0;
+  if (n % 4 == 0 && aligned16(Y)) {
+    rc = make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)n, (uint64_t)m, (uint64_t)n * 4, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    y_tma = 1;
+  }
   if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<BN>), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w8a8_tc_kernel) failed");
   const int tiles = ((m + C::BM - 1) / C::BM) * ((n + BN - 1) / BN);
   const int grid = std::min(tiles, std::max(1, sm_count()));
-  gemm_w8a8_tc_kernel<BN><<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, m, n, k, sa, sw, bias, Y, acc_out,
+  gemm_w8a8_tc_kernel<BN><<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, ty, y_tma, m, n, k, sa, sw, bias, Y, acc_out,
                                                             device_status_word());
   return launch_err("gemm_w8a8_tc_kernel");
 }
