@@ -52,11 +52,14 @@ __device__ __forceinline__ void widen8(uint32_t w, uint32_t& o0, uint32_t& o1) {
   o1 = __byte_perm(lo, hi, 0x7362);  // e4 e5 e6 e7
 }
 
+constexpr uint32_t kMagic = 0x4B400000u;  // bits of 1.5 * 2^23
+
 __device__ __forceinline__ float exact_i2f(uint32_t p) {
   // p + 0x4B400000 is the float 1.5*2^23 + p for |p| < 2^22.
   return __fadd_rn(__int_as_float((int)(p + 0x4B400000u)), -12582912.0f);
 }
 
+template <bool ACC_OUT>
 __global__ void __launch_bounds__(640, 1)
     gemm_w4a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBp,
                         const __grid_constant__ CUtensorMap tmS, int M, int N, int K,
@@ -226,9 +229,10 @@ __global__ void __launch_bounds__(640, 1)
       const int row = tm * C::BM + q * 32 + lane;
       const int col0 = tn * C::BN + cq * 32;
       const float bl = (bias && col0 + lane < N) ? __ldg(bias + col0 + lane) : 0.0f;
-      float s[32];
+      uint64_t s2[16];  // running f32 sums, packed pairs of columns
 #pragma unroll
-      for (int i = 0; i < 32; ++i) s[i] = 0.0f;
+      for (int i = 0; i < 16; ++i) s2[i] = 0;
+      const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&conv[stage], phase, abort_flag)) {  // transposed scales ready
           kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
@@ -242,22 +246,24 @@ __global__ void __launch_bounds__(640, 1)
             goto done;
           }
           tc_fence_after();
+          const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(gb * C::BN + cq * 32);
           uint32_t r[32];
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(gb * C::BN + cq * 32), r);
+          tmem_ld32(taddr, r);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&gempty[gb]);
+          if (lane == 0) mbar_arrive(&gempty[gb]);  // buffer free: the MMA overwrites it
           const float4* sc4 = reinterpret_cast<const float4*>(sct + j * C::BN + cq * 32);
 #pragma unroll
           for (int i4 = 0; i4 < 8; ++i4) {
             const float4 sv = sc4[i4];  // same address in every lane: broadcast
-            s[i4 * 4 + 0] = __fmaf_rn(exact_i2f(r[i4 * 4 + 0]), sv.x, s[i4 * 4 + 0]);
-            s[i4 * 4 + 1] = __fmaf_rn(exact_i2f(r[i4 * 4 + 1]), sv.y, s[i4 * 4 + 1]);
-            s[i4 * 4 + 2] = __fmaf_rn(exact_i2f(r[i4 * 4 + 2]), sv.z, s[i4 * 4 + 2]);
-            s[i4 * 4 + 3] = __fmaf_rn(exact_i2f(r[i4 * 4 + 3]), sv.w, s[i4 * 4 + 3]);
+            // bits of 1.5*2^23 + P, then one packed subtraction: exact (float)P
+            const uint64_t p0 = f2_add(u2_pack(r[i4 * 4 + 0] + kMagic, r[i4 * 4 + 1] + kMagic), neg_magic);
+            const uint64_t p1 = f2_add(u2_pack(r[i4 * 4 + 2] + kMagic, r[i4 * 4 + 3] + kMagic), neg_magic);
+            s2[i4 * 2 + 0] = f2_fma(p0, f2_pack(sv.x, sv.y), s2[i4 * 2 + 0]);
+            s2[i4 * 2 + 1] = f2_fma(p1, f2_pack(sv.z, sv.w), s2[i4 * 2 + 1]);
           }
-          if (acc_out && row < M) {
+          if (ACC_OUT && row < M) {
             const int gidx = kb * C::GPK + j;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
@@ -275,6 +281,9 @@ __global__ void __launch_bounds__(640, 1)
           phase ^= 1u;
         }
       }
+      float s[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) f2_unpack(s2[i], s[2 * i], s[2 * i + 1]);
       const float sar = row < M ? sa[row] : 0.0f;
 #pragma unroll
       for (int i = 0; i < 32; ++i)  // y = s * sa + bias (bias of column col0+i from lane i)
@@ -283,14 +292,7 @@ __global__ void __launch_bounds__(640, 1)
         float* yrow = Y + (size_t)row * N + col0;
         if ((N & 3) == 0 && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(Y) & 15u) == 0) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            float4 v;
-            v.x = s[i + 0];
-            v.y = s[i + 1];
-            v.z = s[i + 2];
-            v.w = s[i + 3];
-            *reinterpret_cast<float4*>(yrow + i) = v;
-          }
+          for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(yrow + i) = make_float4(s[i], s[i + 1], s[i + 2], s[i + 3]);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i)

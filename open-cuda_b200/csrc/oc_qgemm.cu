@@ -340,12 +340,16 @@ int run_w4a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const ui
   rc = make_tmap_2d(&tsc, sw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ng, (uint64_t)n, ng * 4, C::GPK, C::BN,
                     CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_tc_kernel), C::SMEM))
-    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_tc_kernel) failed");
-  const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
-  const int grid = std::min(tiles, std::max(1, sm_count()));
-  gemm_w4a8_tc_kernel<<<grid, C::THREADS, C::SMEM, s>>>(ta, tbp, tsc, m, n, k, sa, bias, Y, acc_out,
-                                                        device_status_word());
+  auto go = [&](auto kern) {
+    if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
+      return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_tc_kernel) failed");
+    const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
+    const int grid = std::min(tiles, std::max(1, sm_count()));
+    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tbp, tsc, m, n, k, sa, bias, Y, acc_out, device_status_word());
+    return OC_OK;
+  };
+  rc = acc_out ? go(gemm_w4a8_tc_kernel<true>) : go(gemm_w4a8_tc_kernel<false>);
+  if (rc) return rc;
   return launch_err("gemm_w4a8_tc_kernel");
 }
 
