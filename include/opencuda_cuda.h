@@ -296,6 +296,36 @@ int oc_qgemm_w8a8_noalloc(int m, int n, int k, const float *A, const int8_t *Wq,
 /* The size of that array in bytes (16 MiB). */
 int oc_qgemm_w8a8_noalloc_max_bytes(size_t *bytes);
 
+/* ---- mixture of experts (no counterpart in the reference, which has no
+ * MoE; the semantics are defined here) -----------------------------------
+ * Experts are MLPs fc [F][D] -> gelu_new -> proj [D][F] with INT8
+ * per-output-channel weights (W8A8 products as oc_qgemm_w8a8, no biases).
+ * oc_moe_route: top-k of each token's logits [T][E] (ties -> lower expert
+ *   index, NaN never chosen); topk_w = softmax of the k chosen logits:
+ *   (float)exp((double)(l - l_max)) summed in f32 in selection order, then
+ *   divided; 1/k each when every chosen logit is -inf or NaN.
+ * oc_moe_dispatch: counts [E], offs [E+1] (row offsets of each expert's
+ *   rows), pos [T*k] (row of each (token, choice)), src [T*k] (token of each
+ *   row) and the gathered int8 rows xg [T*k][D] with scales sg; cursor is
+ *   [E] ints of scratch.  Rows of one expert are contiguous; their order
+ *   inside the expert is unspecified (results do not depend on it).  Ids
+ *   outside [0, E) are dropped: their pos is -1 and the combine skips them.
+ * oc_grouped_igemm_w8a8: Y[r] = xg[r] . W_g^T for the group g owning row r
+ *   (offs in device memory, G <= 1024, non-decreasing from >= 0 to <= R),
+ *   W stacked [G*N][K] with scales [G*N] and optional biases [G*N]; tiles
+ *   are scheduled on the device.  Rows outside the groups are not written.
+ * oc_gelu_quantize_rows: q, s = quantize_int8(gelu_new(H[r]), group = F).
+ * oc_moe_combine: y[t] = shared[t] (or 0) + sum_{i<k} w[t][i] *
+ *   expert_out[pos[t][i]], i ascending, multiply then add. */
+int oc_moe_route(const float *logits, int T, int E, int k, int *topk_idx, float *topk_w, void *stream);
+int oc_moe_dispatch(const int *topk_idx, int T, int k, int E, const int8_t *qx, const float *sx, int D, int *counts,
+                    int *offs, int *pos, int *src, int8_t *xg, float *sg, int *cursor, void *stream);
+int oc_grouped_igemm_w8a8(int R, int N, int K, const int8_t *xg, const float *sg, const int8_t *W, const float *sw,
+                          const float *bias, const int *offs, int G, float *Y, void *stream);
+int oc_gelu_quantize_rows(const float *H, int R, int F, int8_t *q, float *s, void *stream);
+int oc_moe_combine(const float *shared_out, const float *expert_out, const int *pos, const float *topk_w, int T,
+                   int k, int D, float *y, void *stream);
+
 /* ---- multi-GPU column sharding (no counterpart in the reference, whose
  * only multi-device code is a layer partition stub,
  * crates/opencuda-multidev/src/lib.rs:28-83) ------------------------------

@@ -320,6 +320,38 @@ static int launch_w8a8_tc(int m, int n, int k, const int8_t* qa, const float* sa
   return launch_err("gemm_w8a8_tc_kernel");
 }
 
+// Grouped GEMM: tiles are scheduled on the device from offs (G+1 row
+// offsets); the grid covers every SM and CTAs without tiles exit at once.
+int run_grouped_w8a8_tc(int R, int N, int K, const int8_t* xg, const float* sg, const int8_t* W, const float* sw,
+                        const float* bias, const int* offs, int G, float* Y, cudaStream_t s) {
+  constexpr int BN = 128;
+  using C = I8Gemm<BN, true>;
+  CUtensorMap ta, tb, ty;
+  int rc = make_tmap_2d(&ta, xg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)R, (uint64_t)K, C::BK,
+                        C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)G * N, (uint64_t)K, C::BK, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  ty = tb;
+  int y_tma = 0;
+  if (N % 4 == 0 && aligned16(Y)) {
+    rc = make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N, (uint64_t)R, (uint64_t)N * 4, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    y_tma = 1;
+  }
+  auto kern = gemm_w8a8_tc_kernel<BN, true>;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(grouped gemm) failed");
+  // upper bound on tiles: every group adds at most one partial 128-row tile
+  const long max_tiles = ((long)(R + 127) / 128 + G) * ((N + BN - 1) / BN);
+  const int grid = (int)std::min<long>(max_tiles, std::max(1, sm_count()));
+  kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, ty, y_tma, R, N, K, sg, sw, bias, Y, nullptr, device_status_word(),
+                                         offs, G);
+  return launch_err("grouped gemm_w8a8_tc_kernel");
+}
+
 int run_w8a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq, const float* sw,
                 const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
   return pick_bn(m, n) == 256 ? launch_w8a8_tc<256>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s)

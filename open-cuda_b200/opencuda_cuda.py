@@ -100,6 +100,11 @@ _SIGS = {
     "oc_blas_mla_compress_kv": (ci, [vp, sz, sz, sz, vp, vp, vp]),
     "oc_blas_mla_decompress_kv": (ci, [vp, sz, sz, sz, vp, vp, vp]),
     "oc_gather_columns": (ci, [vp, vp, ci, ci, ci, vp]),
+    "oc_moe_route": (ci, [vp, ci, ci, ci, vp, vp, vp]),
+    "oc_moe_dispatch": (ci, [vp, ci, ci, ci, vp, vp, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "oc_grouped_igemm_w8a8": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp, ci, vp, vp]),
+    "oc_gelu_quantize_rows": (ci, [vp, ci, ci, vp, vp, vp]),
+    "oc_moe_combine": (ci, [vp, vp, vp, vp, ci, ci, ci, vp, vp]),
     "oc_awq_scales": (ci, [vp, sz, cf, vp]),
     "oc_quantize_int4_awq": (ci, [vp, sz, sz, vp, sz, vp, vp, vp]),
     "oc_dequantize_int4_awq": (ci, [vp, vp, sz, sz, sz, vp, vp, vp]),

@@ -75,3 +75,17 @@ def qgemm_case(m: int, k: int, n: int, seed_a: int = 1, seed_w: int = 2, seed_b:
     W = normal(seed_w, k * n, 0.0, 0.02).reshape(k, n)
     bias = normal(seed_b, n, 0.0, 0.02)
     return A, np.ascontiguousarray(W.T), bias
+
+
+def moe_case(T: int, D: int, F: int, E: int, seed: int = 7):
+    """MoE block inputs: tokens x [T][D] ~ U(-1,1), router logits [T][E] ~
+    N(0,1), expert weights fc W1 [E][F][D] and proj W2 [E][D][F] ~ N(0,0.02)
+    (stored out x in, as the reference quantizes per output channel), and
+    the shared expert SW1 [F][D], SW2 [D][F]."""
+    x = uniform(seed, T * D).reshape(T, D)
+    logits = normal(seed + 1, T * E).reshape(T, E)
+    W1 = normal(seed + 2, E * F * D, 0.0, 0.02).reshape(E, F, D)
+    W2 = normal(seed + 3, E * D * F, 0.0, 0.02).reshape(E, D, F)
+    SW1 = normal(seed + 4, F * D, 0.0, 0.02).reshape(F, D)
+    SW2 = normal(seed + 5, D * F, 0.0, 0.02).reshape(D, F)
+    return x, logits, W1, W2, SW1, SW2

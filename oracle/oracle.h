@@ -112,6 +112,14 @@ int ocr_qgemm_weight_only(int bits, size_t m, size_t k, size_t n,
                           const float *wscale, const float *bias, float *y,
                           int faithful);
 
+/* ---- mixture of experts (oracle_moe.c; no reference counterpart) -------- */
+int ocr_moe_route(const float *logits, size_t T, size_t E, size_t k, int32_t *idx, float *w);
+/* x [T][D], logits [T][E]; expert e: w1 [E][F][D] (scales s1 [E][F]),
+ * w2 [E][D][F] (s2 [E][D]); shared expert sw1 [F][D], sw2 [D][F]. */
+int ocr_moe_forward(size_t T, size_t D, size_t F, size_t E, size_t k, const float *x, const float *logits,
+                    const int8_t *w1, const float *s1, const int8_t *w2, const float *s2, const int8_t *sw1,
+                    const float *ss1, const int8_t *sw2, const float *ss2, float *y);
+
 /* ---- GPT decoder (llm:45-942) -------------------------------------------- */
 typedef struct ocr_gpt ocr_gpt;
 typedef struct {

@@ -87,6 +87,9 @@ def lib():
         "ocr_qgemm_w4a8": (C.c_int, [sz, sz, sz, sz, f32p, u8p, f32p, f32p, f32p, i32p]),
         "ocr_qgemm_weight_only": (C.c_int, [C.c_int, sz, sz, sz, sz, f32p, C.c_void_p, f32p, f32p, f32p, C.c_int]),
         "ocr_splitmix64_fill": (None, [C.c_uint64, C.c_float, sz, f32p]),
+        "ocr_moe_route": (C.c_int, [f32p, sz, sz, sz, i32p, f32p]),
+        "ocr_moe_forward": (C.c_int, [sz, sz, sz, sz, sz, f32p, f32p, i8p, f32p, i8p, f32p, i8p, f32p, i8p, f32p,
+                                      f32p]),
         "ocr_gpt_load_random": (C.c_void_p, [C.POINTER(GptConfig), C.c_uint64]),
         "ocr_gpt_free": (None, [C.c_void_p]),
         "ocr_gpt_set_attention": (None, [C.c_void_p, C.c_int, sz, C.c_int]),
@@ -337,6 +340,32 @@ def qgemm_weight_only(bits, m, k, n, group, a, wq, wscale, bias, faithful=False)
                                      None if b is None else _p(b), _p(y), int(faithful))
     if rc:
         raise ValueError(f"qgemm_weight_only rc={rc}")
+    return y
+
+
+# ---- mixture of experts -------------------------------------------------------
+
+def moe_route(logits, T, E, k):
+    lg = _f32(logits).ravel()
+    idx = np.zeros(T * k, np.int32)
+    w = np.zeros(T * k, np.float32)
+    if lib().ocr_moe_route(_p(lg), T, E, k, _p(idx, i32p), _p(w)):
+        raise ValueError("moe_route: bad arguments")
+    return idx.reshape(T, k), w.reshape(T, k)
+
+
+def moe_forward(x, logits, w1, s1, w2, s2, sw1, ss1, sw2, ss2, k):
+    """x [T][D]; w1 [E][F][D] int8 + s1 [E][F]; w2 [E][D][F] + s2 [E][D]; shared sw1 [F][D], sw2 [D][F]."""
+    x = _f32(x)
+    T, D = x.shape
+    E, F, _ = w1.shape
+    y = np.zeros((T, D), np.float32)
+    args = [np.ascontiguousarray(a) for a in (w1, s1, w2, s2, sw1, ss1, sw2, ss2)]
+    rc = lib().ocr_moe_forward(T, D, F, E, k, _p(x), _p(_f32(logits)), _p(args[0], i8p), _p(_f32(args[1])),
+                               _p(args[2], i8p), _p(_f32(args[3])), _p(args[4], i8p), _p(_f32(args[5])),
+                               _p(args[6], i8p), _p(_f32(args[7])), _p(y))
+    if rc:
+        raise RuntimeError(f"ocr_moe_forward rc={rc}")
     return y
 
 
