@@ -218,6 +218,10 @@ int oc_gpt_generate(oc_gpt *model, int batch, const uint32_t *prompts, int promp
                     uint32_t *out, float *logits_out, int *produced);
 /* The stream the model runs on (a cudaStream_t). */
 int oc_gpt_stream(oc_gpt *model, void **stream);
+/* Kernels launched by oc_gpt_generate on this model since it was created
+ * (graph replays count every kernel node).  No counterpart in the
+ * reference; for benchmarks and launch accounting. */
+int oc_gpt_kernel_launches(oc_gpt *model, uint64_t *total);
 
 /* ---- quantization (blas:777-945) ---------------------------------------
  * Groups are contiguous runs of `group` elements of the flat input

@@ -77,10 +77,11 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // LayerNorm (llm:252-262): mean, var = mean((x-mean)^2), inv_std =
 // 1/sqrt(var+eps), y = (x-mean)*inv_std*w + b.  One CTA per row.
-__global__ void layernorm_kernel(const float* __restrict__ x, float* __restrict__ y, int H,
+// Row r of y = LayerNorm(row r of x); x rows are x_stride floats apart.
+__global__ void layernorm_kernel(const float* __restrict__ x, size_t x_stride, float* __restrict__ y, int H,
                                  const float* __restrict__ w, const float* __restrict__ b, float eps) {
   __shared__ float red[32];
-  const float* xr = x + (size_t)blockIdx.x * H;
+  const float* xr = x + (size_t)blockIdx.x * x_stride;
   float* yr = y + (size_t)blockIdx.x * H;
   float s = 0.0f;
   for (int c = threadIdx.x; c < H; c += blockDim.x) s += xr[c];
@@ -356,6 +357,8 @@ struct oc_gpt {
   size_t keep_logits_floats = 0;
   // decode-step graph
   cudaGraphExec_t graph = nullptr;
+  int graph_launches = 0;  // kernels in one replay of the decode graph
+  uint64_t launches = 0;   // kernels launched by generate since creation
   int graph_batch = 0;
   uint32_t* graph_out = nullptr;
   float* graph_keep = nullptr;
@@ -393,10 +396,14 @@ int linear_alloc(oc_gpt* g, GptLinear& L, int in, int out) {
   return OC_OK;
 }
 
-// out[rows][L.out] = x[rows][L.in] . W + b
-int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* out) {
+// out[rows][L.out] = x[rows][L.in] . W + b; *n += kernels launched
+int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* out, int* n) {
   cudaStream_t s = g->stream;
-  if (rows > 32) return oc_sgemm_prepared(rows, L.out, L.in, 1.0f, x, L.in, L.prep, 0.0f, out, L.out, L.b, s);
+  if (rows > 32) {
+    *n += 1;  // one tensor-core GEMM launch
+    return oc_sgemm_prepared(rows, L.out, L.in, 1.0f, x, L.in, L.prep, 0.0f, out, L.out, L.b, s);
+  }
+  *n += 2;  // partial products + reduction
   const int ks = gemv_kslice(L.in, L.out);
   const int slices = (L.in + ks - 1) / ks;
   dim3 grid((L.out + 511) / 512, slices);
@@ -417,8 +424,10 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
 
 // One pass of all layers over `rows` = batch * L rows at positions
 // *pos .. *pos + L - 1 (L = 1: decode step), then final LN + lm_head on the
-// last row of each sequence and the argmax.
-int forward(oc_gpt* g, int batch, int L, const uint32_t* tokens, uint32_t* out, int out_stride, float* keep) {
+// last row of each sequence and the argmax.  *n = kernels launched.
+int forward(oc_gpt* g, int batch, int L, const uint32_t* tokens, uint32_t* out, int out_stride, float* keep,
+            int* n) {
+  *n = 0;
   const oc_gpt_config& c = g->cfg;
   const int H = (int)c.hidden_size, nh = (int)c.num_heads, I = (int)c.intermediate_size, V = (int)c.vocab_size;
   const int ms = (int)c.max_seq_len, rows = batch * L;
@@ -431,27 +440,27 @@ int forward(oc_gpt* g, int batch, int L, const uint32_t* tokens, uint32_t* out, 
     GptLayer& Ly = g->layers[li];
     float* kc = g->kc + li * (size_t)g->max_batch * ms * H;
     float* vc = g->vc + li * (size_t)g->max_batch * ms * H;
-    layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, g->normed, H, Ly.ln1w, Ly.ln1b, c.layer_norm_eps);
-    if ((rc = linear_fwd(g, Ly.qkv, g->normed, rows, g->qkv))) return rc;
+    layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, H, g->normed, H, Ly.ln1w, Ly.ln1b, c.layer_norm_eps);
+    if ((rc = linear_fwd(g, Ly.qkv, g->normed, rows, g->qkv, n))) return rc;
     kv_store_kernel<<<rows, 256, 0, s>>>(g->qkv, L, g->pos, H, kc, vc, ms, rows);
     decode_attention_kernel<<<(rows * nh + kAttnWarps - 1) / kAttnWarps, kAttnWarps * 32, attn_smem, s>>>(
         g->qkv, L, g->pos, H, nh, H / nh, kc, vc, ms, g->ctx, rows, scale);
-    if ((rc = linear_fwd(g, Ly.ao, g->ctx, rows, g->tmp))) return rc;
+    if ((rc = linear_fwd(g, Ly.ao, g->ctx, rows, g->tmp, n))) return rc;
     add_kernel<<<ew_blocks((size_t)rows * H), 256, 0, s>>>(g->hidden, g->tmp, (size_t)rows * H);
-    layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, g->normed, H, Ly.ln2w, Ly.ln2b, c.layer_norm_eps);
-    if ((rc = linear_fwd(g, Ly.fc, g->normed, rows, g->inter))) return rc;
+    layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, H, g->normed, H, Ly.ln2w, Ly.ln2b, c.layer_norm_eps);
+    if ((rc = linear_fwd(g, Ly.fc, g->normed, rows, g->inter, n))) return rc;
     gelu_kernel<<<ew_blocks((size_t)rows * I), 256, 0, s>>>(g->inter, (size_t)rows * I);
-    if ((rc = linear_fwd(g, Ly.pj, g->inter, rows, g->tmp))) return rc;
+    if ((rc = linear_fwd(g, Ly.pj, g->inter, rows, g->tmp, n))) return rc;
     add_kernel<<<ew_blocks((size_t)rows * H), 256, 0, s>>>(g->hidden, g->tmp, (size_t)rows * H);
+    *n += 7;  // two layer norms, kv store, attention, gelu, two residual adds (+ linears above)
   }
-  // last row of each sequence: rows b*L + L-1 -> normed[b]
-  for (int b = 0; b < batch; ++b) {
-    layernorm_kernel<<<1, 256, 0, s>>>(g->hidden + ((size_t)b * L + L - 1) * H, g->normed + (size_t)b * H, H,
-                                       g->lnfw, g->lnfb, c.layer_norm_eps);
-  }
-  if ((rc = linear_fwd(g, g->lm, g->normed, batch, g->logits))) return rc;
+  // last row of each sequence (rows b*L + L-1) -> normed[b], one launch
+  layernorm_kernel<<<batch, 256, 0, s>>>(g->hidden + (size_t)(L - 1) * H, (size_t)L * H, g->normed, H, g->lnfw,
+                                         g->lnfb, c.layer_norm_eps);
+  if ((rc = linear_fwd(g, g->lm, g->normed, batch, g->logits, n))) return rc;
   argmax_kernel<<<batch, 1024, 0, s>>>(g->logits, V, g->next, out, out_stride, g->step, g->pos, L, keep);
   advance_kernel<<<1, 1, 0, s>>>(g->step, g->pos, L);
+  *n += 1 + 1 + 2;  // embed, final layer norm, argmax, advance
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? OC_OK : from_cuda(e, "gpt forward");
 }
@@ -697,8 +706,10 @@ int oc_gpt_generate(oc_gpt* g, int batch, const uint32_t* prompts, int prompt_le
   OC_CHECK_CUDA(cudaMemsetAsync(g->step, 0, sizeof(int), s));
   const int out_stride = std::max(steps, 1);
   // prefill: writes token 0 (step 0) into out_tokens and advances pos by L
-  int rc = forward(g, batch, prompt_len, g->tok_in, steps > 0 ? g->out_tokens : nullptr, out_stride, keep);
+  int nl = 0;
+  int rc = forward(g, batch, prompt_len, g->tok_in, steps > 0 ? g->out_tokens : nullptr, out_stride, keep, &nl);
   if (rc) return rc;
+  g->launches += (uint64_t)nl;
   // decode steps 1 .. steps-1 consume next[] and produce token i; the final
   // forward of the reference (whose logits are unused) runs as well unless
   // the sequence hit max_seq_len.
@@ -711,7 +722,7 @@ int oc_gpt_generate(oc_gpt* g, int batch, const uint32_t* prompts, int prompt_le
       g->graph = nullptr;
       cudaGraph_t graph;
       OC_CHECK_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-      rc = forward(g, batch, 1, g->next, g->out_tokens, out_stride, keep);
+      rc = forward(g, batch, 1, g->next, g->out_tokens, out_stride, keep, &g->graph_launches);
       cudaError_t e = cudaStreamEndCapture(s, &graph);
       if (rc) return rc;
       if (e != cudaSuccess) return from_cuda(e, "cudaStreamEndCapture");
@@ -726,6 +737,7 @@ int oc_gpt_generate(oc_gpt* g, int batch, const uint32_t* prompts, int prompt_le
       // the out_tokens slot for the step past the last kept token is never
       // read: the argmax writes it only while *step < out_stride
       OC_CHECK_CUDA(cudaGraphLaunch(g->graph, s));
+      g->launches += (uint64_t)g->graph_launches;
     }
   }
   OC_CHECK_CUDA(cudaStreamSynchronize(s));
@@ -742,8 +754,12 @@ int oc_gpt_generate(oc_gpt* g, int batch, const uint32_t* prompts, int prompt_le
   return check_device_status(s);
 }
 
-// Device pointer of the last generate's output tokens ([batch][stride]) and
-// the stride, for callers that keep the tokens on the device.
+int oc_gpt_kernel_launches(oc_gpt* g, uint64_t* total) {
+  OC_REQUIRE(g && total, "NULL argument");
+  *total = g->launches;
+  return OC_OK;
+}
+
 int oc_gpt_stream(oc_gpt* g, void** stream) {
   OC_REQUIRE(g && stream, "NULL argument");
   *stream = g->stream;

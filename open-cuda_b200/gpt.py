@@ -41,6 +41,7 @@ _SIGS = {
     "oc_gpt_generate": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                   C.POINTER(C.c_int)]),
     "oc_gpt_stream": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "oc_gpt_kernel_launches": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),
 }
 
 WEIGHT_IDS = {
@@ -105,6 +106,17 @@ class GptModel:
         oc.check(_lib().oc_gpt_get_weight(self._h, WEIGHT_IDS[name], layer, out.ctypes.data_as(C.c_void_p),
                                           out.size))
         return out
+
+    def kernel_launches(self) -> int:
+        """Kernels launched by generate on this model so far."""
+        n = C.c_uint64(0)
+        oc.check(_lib().oc_gpt_kernel_launches(self._h, C.byref(n)))
+        return n.value
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        oc.check(_lib().oc_gpt_stream(self._h, C.byref(s)))
+        return s.value or 0
 
     def generate(self, prompt_ids, max_new_tokens: int, want_logits: bool = False):
         """generate (llm:910-929).  prompt_ids: [len] or [batch, len]."""
