@@ -131,14 +131,15 @@ __global__ void kv_store_kernel(const float* __restrict__ qkv, int L, const int*
 // Attention of one query row per (row, head) warp over the cached keys
 // 0 .. pos0 + i (causal, the cache holds no future positions, llm:322-410):
 // scores q.k * (1/sqrt(d)), exact softmax (max, exp, sum, divide), P.V.
-// head_dim d <= 128 (lane owns dims lane + 32t); scores staged in shared
-// memory.
+// Scores: lane l takes keys l, l+32, ... (a whole dot product each, q from
+// shared memory, 16-byte key loads); P.V: lane owns dims lane + 32t
+// (head_dim d <= 128).  Scores and q are staged in shared memory.
 constexpr int kAttnWarps = 4, kAttnDpl = 4;
 __global__ void __launch_bounds__(kAttnWarps * 32)
     decode_attention_kernel(const float* __restrict__ qkv, int L, const int* __restrict__ pos0, int H, int heads,
                             int d, const float* __restrict__ kc, const float* __restrict__ vc, int max_seq,
                             float* __restrict__ ctx, int rows, float scale) {
-  extern __shared__ float sc[];  // [kAttnWarps][max_seq]
+  extern __shared__ float sc[];  // [kAttnWarps][max_seq] scores, then [kAttnWarps][128] q
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kAttnWarps + warp;
   if (gw >= rows * heads) return;
@@ -146,25 +147,36 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
   const int b = r / L, i = r % L;
   const int n = *pos0 + i + 1;
   const float* q = qkv + (size_t)r * 3 * H + h * d;
-  float qv[kAttnDpl];
+  float* qs = sc + (size_t)kAttnWarps * max_seq + warp * 32 * kAttnDpl;
 #pragma unroll
-  for (int t = 0; t < kAttnDpl; ++t) qv[t] = (lane + 32 * t < d) ? q[lane + 32 * t] : 0.0f;
+  for (int t = 0; t < kAttnDpl; ++t)
+    if (lane + 32 * t < d) qs[lane + 32 * t] = q[lane + 32 * t];
+  __syncwarp();
   const float* kb = kc + (size_t)b * max_seq * H + h * d;
   const float* vb = vc + (size_t)b * max_seq * H + h * d;
   float* s = sc + warp * max_seq;
   float mx = -INFINITY;
-  for (int j = 0; j < n; ++j) {
+  const bool vec = (d & 3) == 0 && (H & 3) == 0;
+  for (int j = lane; j < n; j += 32) {
     const float* kr = kb + (size_t)j * H;
     float p = 0.0f;
-#pragma unroll
-    for (int t = 0; t < kAttnDpl; ++t)
-      if (lane + 32 * t < d) p = __fmaf_rn(qv[t], kr[lane + 32 * t], p);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+    if (vec) {
+      for (int c = 0; c < d; c += 4) {
+        const float4 kv = *reinterpret_cast<const float4*>(kr + c);
+        p = __fmaf_rn(qs[c], kv.x, p);
+        p = __fmaf_rn(qs[c + 1], kv.y, p);
+        p = __fmaf_rn(qs[c + 2], kv.z, p);
+        p = __fmaf_rn(qs[c + 3], kv.w, p);
+      }
+    } else {
+      for (int c = 0; c < d; ++c) p = __fmaf_rn(qs[c], kr[c], p);
+    }
     p = __fmul_rn(p, scale);
-    if (lane == 0) s[j] = p;
+    s[j] = p;
     mx = fmaxf(mx, p);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   __syncwarp();
   float sum = 0.0f;
   for (int j = lane; j < n; j += 32) {
@@ -249,79 +261,198 @@ __global__ void advance_kernel(int* __restrict__ step, int* __restrict__ pos, in
   *pos += pos_advance;
 }
 
-// Decode GEMV for up to MR rows: out[r][col] = x[r] . W[:, col] + bias, W
-// [K][N] row-major (the reference's weight_t), split over k-slices of ks <=
-// kGKs rows (chosen so the grid covers the GPU); each weight element is
-// read once and used for all rows; part[slice][r][col] then a fixed-order
-// reduction.
-constexpr int kGKs = 64;
-template <int MR>
-__global__ void __launch_bounds__(256) gemv_partial_kernel(int m, int n, int k, int ks, const float* __restrict__ x,
-                                                           const float* __restrict__ W,
-                                                           float* __restrict__ part) {
-  __shared__ float sx[MR][kGKs];
-  const int k0 = blockIdx.y * ks, kn = min(ks, k - k0);
-  for (int i = threadIdx.x; i < MR * kGKs; i += 256) {
-    const int r = i / kGKs, kk = i % kGKs;
-    sx[r][kk] = (r < m && kk < kn) ? x[(size_t)r * k + k0 + kk] : 0.0f;
-  }
-  __syncthreads();
-  const int col = (blockIdx.x * 256 + threadIdx.x) * 2;
-  if (col >= n) return;
-  const bool two = col + 1 < n;
-  float acc0[MR], acc1[MR];
-#pragma unroll
-  for (int r = 0; r < MR; ++r) acc0[r] = acc1[r] = 0.0f;
-  const float* wp = W + (size_t)k0 * n + col;
-  const bool vec = two && ((n & 1) == 0);
-#pragma unroll 4
-  for (int kk = 0; kk < kn; ++kk) {
-    float w0, w1;
-    if (vec) {
-      const float2 w2 = __ldg(reinterpret_cast<const float2*>(wp + (size_t)kk * n));
-      w0 = w2.x;
-      w1 = w2.y;
-    } else {
-      w0 = __ldg(wp + (size_t)kk * n);
-      w1 = two ? __ldg(wp + (size_t)kk * n + 1) : 0.0f;
+// gelu_new in f64, cast to f32 (llm:268-275), for the GEMV epilogue.
+__device__ __forceinline__ float gelu_new_dev(float v) {
+  const double xf = (double)v;
+  const double inner = 0.7978845608028654 * (xf + 0.044715 * (xf * xf * xf));
+  return (float)(0.5 * xf * (1.0 + tanh(inner)));
+}
+
+// Epilogues fused into the decode GEMV (y = x.W + bias, the reference's
+// sgemm then host bias add, llm:227-238):
+//   kEpiPlain     out = y
+//   kEpiGelu      out = gelu_new(y)                       (fc, llm:400-402)
+//   kEpiResidual  out = out + y                           (residual adds, llm:396, 404)
+//   kEpiQkv       out = y, and the k / v thirds of the row also go to the
+//                 KV cache at the row's position           (llm:568-590)
+enum GemvEpi { kEpiPlain = 0, kEpiGelu = 1, kEpiResidual = 2, kEpiQkv = 3 };
+
+struct GemvArgs {
+  int m, n, k, ks, slices, epi;
+  const float* x;      // [m][k]
+  const float* W;      // [k][n] row-major (weight_t)
+  const float* bias;   // [n]
+  float* part;         // [slices][m][n] per-slice partial sums
+  unsigned* counters;  // [column tiles], zero between launches
+  float* out;          // [m][n]
+  float *kc, *vc;      // kEpiQkv: caches [batch][max_seq][H]
+  const int* pos;      // kEpiQkv: position of row i of each sequence = *pos + i
+  int L, H, max_seq;
+};
+
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int r, int col, float s) {
+  const float y = __fadd_rn(s, a.bias[col]);
+  float* o = a.out + (size_t)r * a.n + col;
+  switch (a.epi) {
+    case kEpiGelu:
+      *o = gelu_new_dev(y);
+      break;
+    case kEpiResidual:
+      *o = __fadd_rn(*o, y);
+      break;
+    case kEpiQkv: {
+      *o = y;
+      if (col >= a.H) {
+        const int b = r / a.L, i = r % a.L;
+        const size_t slot = ((size_t)b * a.max_seq + *a.pos + i) * a.H;
+        if (col < 2 * a.H) a.kc[slot + col - a.H] = y;
+        else a.vc[slot + col - 2 * a.H] = y;
+      }
+      break;
     }
-#pragma unroll
-    for (int r = 0; r < MR; ++r) {
-      acc0[r] = __fmaf_rn(sx[r][kk], w0, acc0[r]);
-      acc1[r] = __fmaf_rn(sx[r][kk], w1, acc1[r]);
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < MR; ++r) {
-    if (r < m) {
-      part[((size_t)blockIdx.y * m + r) * n + col] = acc0[r];
-      if (two) part[((size_t)blockIdx.y * m + r) * n + col + 1] = acc1[r];
-    }
+    default:
+      *o = y;
   }
 }
 
-__global__ void gemv_reduce_kernel(int m, int n, int slices, const float* __restrict__ part,
-                                   const float* __restrict__ bias, float* __restrict__ out) {
-  const size_t total = (size_t)m * n;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int r = (int)(i / n), col = (int)(i % n);
-    float s = 0.0f;
-    for (int sl = 0; sl < slices; ++sl) s = __fadd_rn(s, part[((size_t)sl * m + r) * n + col]);
-    out[i] = __fadd_rn(s, bias[col]);
+// Decode GEMV for up to MR rows, split over k: CTA (tile, slice) computes
+// columns tile*TN .. +TN (TN = 32*VEC, VEC consecutive columns per lane, so
+// a warp reads 32*VEC*4 contiguous bytes of a weight row) over k rows
+// slice*ks .. +ks, its 8 warps taking every 8th row; the warps' sums meet in
+// shared memory, each slice's partial goes to `part`, and the last CTA of a
+// column tile to finish (an atomic count) adds the slices in slice order --
+// the result does not depend on scheduling -- and applies the epilogue.
+// Every weight element is read once and used for all MR rows.
+template <int MR, int VEC>
+__global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
+  constexpr int TN = 32 * VEC;
+  extern __shared__ float gsm[];
+  float* xs = gsm;              // [MR][ks]
+  float* red = gsm + MR * a.ks;  // [8][MR][TN]
+  __shared__ int is_last;
+  const int tile = blockIdx.x, slice = blockIdx.y;
+  const int k0 = slice * a.ks, kn = min(a.ks, a.k - k0);
+  for (int i = threadIdx.x; i < MR * a.ks; i += 256) {
+    const int r = i / a.ks, kk = i - r * a.ks;
+    xs[i] = (r < a.m && kk < kn) ? a.x[(size_t)r * a.k + k0 + kk] : 0.0f;
   }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = tile * TN + lane * VEC;
+  float acc[MR][VEC];
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) acc[r][v] = 0.0f;
+  if (c0 + VEC <= a.n && (a.n % VEC) == 0) {
+    const float* wp = a.W + (size_t)k0 * a.n + c0;
+#pragma unroll 8
+    for (int kk = warp; kk < kn; kk += 8) {
+      float w[VEC];
+      if constexpr (VEC == 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(wp + (size_t)kk * a.n));
+        w[0] = t.x;
+        w[1] = t.y;
+        w[2] = t.z;
+        w[3] = t.w;
+      } else {
+        const float2 t = __ldg(reinterpret_cast<const float2*>(wp + (size_t)kk * a.n));
+        w[0] = t.x;
+        w[1] = t.y;
+      }
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const float xv = xs[r * a.ks + kk];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc[r][v] = __fmaf_rn(xv, w[v], acc[r][v]);
+      }
+    }
+  } else if (c0 < a.n) {
+    const float* wp = a.W + (size_t)k0 * a.n + c0;
+    for (int kk = warp; kk < kn; kk += 8) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        const float w = (c0 + v < a.n) ? __ldg(wp + (size_t)kk * a.n + v) : 0.0f;
+#pragma unroll
+        for (int r = 0; r < MR; ++r) acc[r][v] = __fmaf_rn(xs[r * a.ks + kk], w, acc[r][v]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) red[(warp * MR + r) * TN + lane * VEC + v] = acc[r][v];
+  __syncthreads();
+  // warp sums in warp order; entry e = r*TN + column-in-tile (the warp-0 slot)
+  for (int e = threadIdx.x; e < MR * TN; e += 256) {
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t = __fadd_rn(t, red[w * MR * TN + e]);
+    red[e] = t;
+  }
+  __syncthreads();
+  const int col_base = tile * TN;
+  if (a.slices == 1) {
+    for (int e = threadIdx.x; e < MR * TN; e += 256) {
+      const int r = e / TN, col = col_base + e % TN;
+      if (r < a.m && col < a.n) gemv_epilogue(a, r, col, red[e]);
+    }
+    return;
+  }
+  for (int e = threadIdx.x; e < MR * TN; e += 256) {
+    const int r = e / TN, col = col_base + e % TN;
+    if (r < a.m && col < a.n) a.part[((size_t)slice * a.m + r) * a.n + col] = red[e];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.slices - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < MR * TN; e += 256) {
+    const int r = e / TN, col = col_base + e % TN;
+    if (r >= a.m || col >= a.n) continue;
+    const float* pp = a.part + (size_t)r * a.n + col;
+    const size_t stride = (size_t)a.m * a.n;
+    float t = 0.0f;
+    int sl = 0;
+    for (; sl + 8 <= a.slices; sl += 8) {  // eight loads in flight, added in slice order
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __ldcg(pp + (size_t)(sl + j) * stride);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t = __fadd_rn(t, v[j]);
+    }
+    for (; sl < a.slices; ++sl) t = __fadd_rn(t, __ldcg(pp + (size_t)sl * stride));
+    gemv_epilogue(a, r, col, t);
+  }
+  if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
+}
+
+struct GemvPlan {
+  int vec, tn, tiles, ks, slices;
+  size_t smem;
+};
+
+// Launch shape of the decode GEMV: VEC = 4 columns per lane up to 8 rows, 2
+// beyond (register budget); k split so that about 1.5 CTAs per SM run.
+static GemvPlan gemv_plan(int in, int out, int rows) {
+  GemvPlan p;
+  const int mr = rows <= 1 ? 1 : rows <= 4 ? 4 : rows <= 8 ? 8 : rows <= 16 ? 16 : 32;
+  p.vec = mr <= 8 ? 4 : 2;
+  p.tn = 32 * p.vec;
+  p.tiles = (out + p.tn - 1) / p.tn;
+  const int want = std::max(1, sm_count()) * 3 / 2;
+  const int s = std::max(1, (want + p.tiles - 1) / p.tiles);
+  int ks = (in + s - 1) / s;
+  ks = std::max(16, (ks + 7) / 8 * 8);
+  p.ks = std::min(ks, (in + 7) / 8 * 8);
+  p.slices = (in + p.ks - 1) / p.ks;
+  p.smem = ((size_t)mr * p.ks + (size_t)8 * mr * p.tn) * sizeof(float);
+  return p;
 }
 
 static int ew_blocks(size_t n) { return (int)std::min<size_t>((n + 255) / 256, (size_t)std::max(1, sm_count()) * 8); }
-
-// k-slice of the decode GEMV: the largest multiple of 8 (<= kGKs) that still
-// gives about four CTAs per SM.
-static int gemv_kslice(int in, int out) {
-  const int bx = (out + 511) / 512;
-  const int want = 4 * std::max(1, sm_count());
-  int ks = kGKs;
-  while (ks > 8 && (long)bx * ((in + ks - 1) / ks) < want) ks -= 8;
-  return ks;
-}
 
 }  // namespace oc
 
@@ -350,6 +481,8 @@ struct oc_gpt {
   // activations
   float *hidden, *normed, *qkv, *ctx, *tmp, *inter, *logits, *part;
   size_t part_floats = 0;
+  unsigned* counters = nullptr;  // decode GEMV column-tile counters
+  size_t counter_count = 0;
   float *kc, *vc;  // [layer][batch][max_seq][H]
   uint32_t *tok_in, *next, *out_tokens;
   int *pos, *step;
@@ -396,30 +529,43 @@ int linear_alloc(oc_gpt* g, GptLinear& L, int in, int out) {
   return OC_OK;
 }
 
-// out[rows][L.out] = x[rows][L.in] . W + b; *n += kernels launched
-int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* out, int* n) {
+template <int MR, int VEC>
+static void launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
+  auto kern = gemv_splitk_kernel<MR, VEC>;
+  smem_attr_once(reinterpret_cast<const void*>(kern), std::max<size_t>(p.smem, 48 * 1024));
+  kern<<<dim3(p.tiles, p.slices), 256, p.smem, s>>>(a);
+}
+
+// out[rows][L.out] = epilogue(x[rows][L.in] . W + b) (GemvEpi); *n += kernels
+// launched.  Up to 32 rows: one split-K GEMV with the epilogue fused; more
+// rows: the tensor-core GEMM, then the epilogue as its own kernel.
+int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* out, int epi, int* n,
+               float* kc = nullptr, float* vc = nullptr, int seq_rows = 1) {
   cudaStream_t s = g->stream;
+  const int H = (int)g->cfg.hidden_size, ms = (int)g->cfg.max_seq_len;
   if (rows > 32) {
+    float* dst = epi == kEpiResidual ? g->tmp : out;
+    int rc = oc_sgemm_prepared(rows, L.out, L.in, 1.0f, x, L.in, L.prep, 0.0f, dst, L.out, L.b, s);
+    if (rc) return rc;
     *n += 1;  // one tensor-core GEMM launch
-    return oc_sgemm_prepared(rows, L.out, L.in, 1.0f, x, L.in, L.prep, 0.0f, out, L.out, L.b, s);
+    const size_t total = (size_t)rows * L.out;
+    if (epi == kEpiGelu) gelu_kernel<<<ew_blocks(total), 256, 0, s>>>(out, total);
+    if (epi == kEpiResidual) add_kernel<<<ew_blocks(total), 256, 0, s>>>(out, g->tmp, total);
+    if (epi == kEpiQkv) kv_store_kernel<<<rows, 256, 0, s>>>(out, seq_rows, g->pos, H, kc, vc, ms, rows);
+    if (epi != kEpiPlain) *n += 1;
+  } else {
+    const GemvPlan p = gemv_plan(L.in, L.out, rows);
+    GemvArgs a{rows, L.out, L.in, p.ks, p.slices, epi, x, L.w, L.b, g->part, g->counters, out,
+               kc, vc, g->pos, seq_rows, H, ms};
+    if (rows <= 1) launch_gemv<1, 4>(p, a, s);
+    else if (rows <= 4) launch_gemv<4, 4>(p, a, s);
+    else if (rows <= 8) launch_gemv<8, 4>(p, a, s);
+    else if (rows <= 16) launch_gemv<16, 2>(p, a, s);
+    else launch_gemv<32, 2>(p, a, s);
+    *n += 1;
   }
-  *n += 2;  // partial products + reduction
-  const int ks = gemv_kslice(L.in, L.out);
-  const int slices = (L.in + ks - 1) / ks;
-  dim3 grid((L.out + 511) / 512, slices);
-  if (rows <= 1)
-    gemv_partial_kernel<1><<<grid, 256, 0, s>>>(rows, L.out, L.in, ks, x, L.w, g->part);
-  else if (rows <= 4)
-    gemv_partial_kernel<4><<<grid, 256, 0, s>>>(rows, L.out, L.in, ks, x, L.w, g->part);
-  else if (rows <= 8)
-    gemv_partial_kernel<8><<<grid, 256, 0, s>>>(rows, L.out, L.in, ks, x, L.w, g->part);
-  else if (rows <= 16)
-    gemv_partial_kernel<16><<<grid, 256, 0, s>>>(rows, L.out, L.in, ks, x, L.w, g->part);
-  else
-    gemv_partial_kernel<32><<<grid, 256, 0, s>>>(rows, L.out, L.in, ks, x, L.w, g->part);
-  gemv_reduce_kernel<<<ew_blocks((size_t)rows * L.out), 256, 0, s>>>(rows, L.out, slices, g->part, L.b, out);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? OC_OK : from_cuda(e, "gpt gemv");
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "gpt linear");
 }
 
 // One pass of all layers over `rows` = batch * L rows at positions
@@ -435,29 +581,25 @@ int forward(oc_gpt* g, int batch, int L, const uint32_t* tokens, uint32_t* out, 
   int rc;
   embed_kernel<<<rows, 256, 0, s>>>(tokens, L, g->pos, g->wte, g->wpe, H, g->hidden, rows);
   const float scale = 1.0f / sqrtf((float)(H / nh));
-  const size_t attn_smem = (size_t)kAttnWarps * ms * sizeof(float);
+  const size_t attn_smem = (size_t)kAttnWarps * (ms + 32 * kAttnDpl) * sizeof(float);
   for (size_t li = 0; li < c.num_layers; ++li) {
     GptLayer& Ly = g->layers[li];
     float* kc = g->kc + li * (size_t)g->max_batch * ms * H;
     float* vc = g->vc + li * (size_t)g->max_batch * ms * H;
     layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, H, g->normed, H, Ly.ln1w, Ly.ln1b, c.layer_norm_eps);
-    if ((rc = linear_fwd(g, Ly.qkv, g->normed, rows, g->qkv, n))) return rc;
-    kv_store_kernel<<<rows, 256, 0, s>>>(g->qkv, L, g->pos, H, kc, vc, ms, rows);
+    if ((rc = linear_fwd(g, Ly.qkv, g->normed, rows, g->qkv, kEpiQkv, n, kc, vc, L))) return rc;
     decode_attention_kernel<<<(rows * nh + kAttnWarps - 1) / kAttnWarps, kAttnWarps * 32, attn_smem, s>>>(
         g->qkv, L, g->pos, H, nh, H / nh, kc, vc, ms, g->ctx, rows, scale);
-    if ((rc = linear_fwd(g, Ly.ao, g->ctx, rows, g->tmp, n))) return rc;
-    add_kernel<<<ew_blocks((size_t)rows * H), 256, 0, s>>>(g->hidden, g->tmp, (size_t)rows * H);
+    if ((rc = linear_fwd(g, Ly.ao, g->ctx, rows, g->hidden, kEpiResidual, n))) return rc;
     layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, H, g->normed, H, Ly.ln2w, Ly.ln2b, c.layer_norm_eps);
-    if ((rc = linear_fwd(g, Ly.fc, g->normed, rows, g->inter, n))) return rc;
-    gelu_kernel<<<ew_blocks((size_t)rows * I), 256, 0, s>>>(g->inter, (size_t)rows * I);
-    if ((rc = linear_fwd(g, Ly.pj, g->inter, rows, g->tmp, n))) return rc;
-    add_kernel<<<ew_blocks((size_t)rows * H), 256, 0, s>>>(g->hidden, g->tmp, (size_t)rows * H);
-    *n += 7;  // two layer norms, kv store, attention, gelu, two residual adds (+ linears above)
+    if ((rc = linear_fwd(g, Ly.fc, g->normed, rows, g->inter, kEpiGelu, n))) return rc;
+    if ((rc = linear_fwd(g, Ly.pj, g->inter, rows, g->hidden, kEpiResidual, n))) return rc;
+    *n += 3;  // two layer norms and the attention (+ the linears and their epilogues above)
   }
   // last row of each sequence (rows b*L + L-1) -> normed[b], one launch
   layernorm_kernel<<<batch, 256, 0, s>>>(g->hidden + (size_t)(L - 1) * H, (size_t)L * H, g->normed, H, g->lnfw,
                                          g->lnfb, c.layer_norm_eps);
-  if ((rc = linear_fwd(g, g->lm, g->normed, batch, g->logits, n))) return rc;
+  if ((rc = linear_fwd(g, g->lm, g->normed, batch, g->logits, kEpiPlain, n))) return rc;
   argmax_kernel<<<batch, 1024, 0, s>>>(g->logits, V, g->next, out, out_stride, g->step, g->pos, L, keep);
   advance_kernel<<<1, 1, 0, s>>>(g->step, g->pos, L);
   *n += 1 + 1 + 2;  // embed, final layer norm, argmax, advance
@@ -508,13 +650,17 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
       return bail(rc);
   }
   if ((rc = linear_alloc(g, g->lm, (int)H, (int)V))) return bail(rc);
-  auto part_of = [](const GptLinear& L) {
-    const int ks = gemv_kslice(L.in, L.out);
-    return (size_t)((L.in + ks - 1) / ks) * 32 * L.out;
-  };
-  g->part_floats = part_of(g->lm);
-  for (auto& Ly : g->layers)
-    for (const GptLinear* L : {&Ly.qkv, &Ly.ao, &Ly.fc, &Ly.pj}) g->part_floats = std::max(g->part_floats, part_of(*L));
+  // decode GEMV scratch: per-slice partials [slices][rows][out] and the
+  // column-tile counters, for every row bucket the GEMV path serves
+  // (rows <= min(R, 32))
+  const int gemv_rows = (int)std::min<size_t>(R, 32);
+  for (const GptLinear* L : {&g->lm, &g->layers[0].qkv, &g->layers[0].ao, &g->layers[0].fc, &g->layers[0].pj}) {
+    for (int bucket : {1, 4, 8, 16, 32}) {
+      const GemvPlan p = gemv_plan(L->in, L->out, bucket);
+      g->part_floats = std::max(g->part_floats, (size_t)p.slices * std::min(bucket, gemv_rows) * L->out);
+      g->counter_count = std::max(g->counter_count, (size_t)p.tiles);
+    }
+  }
   if ((rc = galloc_t(g, R * H, &g->hidden)) || (rc = galloc_t(g, R * H, &g->normed)) ||
       (rc = galloc_t(g, R * 3 * H, &g->qkv)) || (rc = galloc_t(g, R * H, &g->ctx)) ||
       (rc = galloc_t(g, R * H, &g->tmp)) || (rc = galloc_t(g, R * I, &g->inter)) ||
@@ -523,9 +669,11 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
       (rc = galloc_t(g, cfg->num_layers * (size_t)max_batch * ms * H, &g->vc)) ||
       (rc = galloc_t(g, R, &g->tok_in)) || (rc = galloc_t(g, (size_t)max_batch, &g->next)) ||
       (rc = galloc_t(g, (size_t)max_batch * ms, &g->out_tokens)) || (rc = galloc_t(g, 1, &g->pos)) ||
-      (rc = galloc_t(g, 1, &g->step)))
+      (rc = galloc_t(g, 1, &g->step)) || (rc = galloc_t(g, g->counter_count, &g->counters)))
     return bail(rc);
-  const size_t attn_smem = (size_t)kAttnWarps * ms * sizeof(float);
+  if (cudaMemset(g->counters, 0, std::max<size_t>(g->counter_count, 1) * sizeof(unsigned)) != cudaSuccess)
+    return bail(from_cuda(cudaGetLastError(), "gpt_create: counters"));
+  const size_t attn_smem = (size_t)kAttnWarps * (ms + 32 * kAttnDpl) * sizeof(float);
   if (!smem_attr_once(reinterpret_cast<const void*>(decode_attention_kernel), attn_smem))
     return bail(fail(OC_ERR_NOT_SUPPORTED, "gpt_create: max_seq_len too large for the attention kernel"));
   *out = g;
