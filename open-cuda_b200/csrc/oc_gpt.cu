@@ -20,8 +20,20 @@
 #include <vector>
 
 #include "oc_internal.h"
+#include "oc_ptx.cuh"
 
 namespace oc {
+
+// Programmatic dependent launch: the decode kernels are launched with
+// programmatic stream serialization, so a kernel may start while its
+// predecessor drains.  pdl_wait() returns once every predecessor grid has
+// completed and its memory is visible; nothing a predecessor writes is read
+// before it, and nothing a predecessor reads is written before it.
+// pdl_launch() lets the successor be scheduled.  Without the launch
+// attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 
 // ---- SplitMix64 weights (llm:178-206, 635-646) ------------------------------
 // Output i of a generator seeded with s: mix(s + (i+1) * golden); next_f32
@@ -53,6 +65,8 @@ __global__ void fill_kernel(float* __restrict__ out, size_t n, float v) {
 __global__ void embed_kernel(const uint32_t* __restrict__ tok, int L, const int* __restrict__ pos0,
                              const float* __restrict__ wte, const float* __restrict__ wpe, int H,
                              float* __restrict__ hidden, int rows) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (r >= rows) return;
   const int i = r % L;
@@ -80,6 +94,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // Row r of y = LayerNorm(row r of x); x rows are x_stride floats apart.
 __global__ void layernorm_kernel(const float* __restrict__ x, size_t x_stride, float* __restrict__ y, int H,
                                  const float* __restrict__ w, const float* __restrict__ b, float eps) {
+  pdl_wait();
+  pdl_launch();
   __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * x_stride;
   float* yr = y + (size_t)blockIdx.x * H;
@@ -128,99 +144,183 @@ __global__ void kv_store_kernel(const float* __restrict__ qkv, int L, const int*
   }
 }
 
-// Attention of one query row per (row, head) warp over the cached keys
-// 0 .. pos0 + i (causal, the cache holds no future positions, llm:322-410):
+// Attention of one query row per (row, head) CTA over the cached keys
+// 0 .. pos0 + i (causal: the cache holds no future positions, llm:322-410):
 // scores q.k * (1/sqrt(d)), exact softmax (max, exp, sum, divide), P.V.
-// Scores: lane l takes keys l, l+32, ... (a whole dot product each, q from
-// shared memory, 16-byte key loads); P.V: lane owns dims lane + 32t
-// (head_dim d <= 128).  Scores and q are staged in shared memory.
-constexpr int kAttnWarps = 4, kAttnDpl = 4;
-__global__ void __launch_bounds__(kAttnWarps * 32)
+// Key and value rows are staged in shared memory a tile of kAttnTile rows at
+// a time with cp.async (all of a tile's copies in flight, the next tile's
+// copies issued before the current tile is used); one thread per key for
+// the scores (rotated column order: no bank conflicts), threads over
+// (dimension, key parity) for P.V.  head_dim d <= 128.
+constexpr int kAttnThreads = 128, kAttnTile = 128, kAttnMaxD = 128;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// rows j0 .. j0+cnt-1 of a [*, row stride H] cache slice -> dst [cnt][d];
+// one commit group per call (empty when cnt == 0)
+__device__ __forceinline__ void attn_stage(float* dst, const float* src, int j0, int cnt, int d, int H, bool vec) {
+  if (vec) {
+    const int per = d >> 2;
+    for (int e = threadIdx.x; e < cnt * per; e += kAttnThreads) {
+      const int j = e / per, c = (e - j * per) << 2;
+      cp_async16(dst + j * d + c, src + (size_t)(j0 + j) * H + c);
+    }
+  } else {
+    for (int e = threadIdx.x; e < cnt * d; e += kAttnThreads) {
+      const int j = e / d, c = e - j * d;
+      dst[j * d + c] = src[(size_t)(j0 + j) * H + c];
+    }
+  }
+  cp_async_commit();
+}
+
+__device__ __forceinline__ float attn_block_reduce(float v, float* red, bool is_max) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, t) : __fadd_rn(v, t);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int i = 1; i < kAttnThreads / 32; ++i) r = is_max ? fmaxf(r, red[i]) : __fadd_rn(r, red[i]);
+  return r;
+}
+
+static size_t attn_smem_bytes(int max_seq, int d) {
+  return ((size_t)max_seq + kAttnMaxD + 2 * (size_t)kAttnTile * d + kAttnThreads + 32) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(kAttnThreads)
     decode_attention_kernel(const float* __restrict__ qkv, int L, const int* __restrict__ pos0, int H, int heads,
                             int d, const float* __restrict__ kc, const float* __restrict__ vc, int max_seq,
                             float* __restrict__ ctx, int rows, float scale) {
-  extern __shared__ float sc[];  // [kAttnWarps][max_seq] scores, then [kAttnWarps][128] q
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * kAttnWarps + warp;
+  extern __shared__ float asm_[];
+  float* buf = asm_;                      // [2][kAttnTile][d] (16-byte aligned for cp.async)
+  float* part = buf + 2 * kAttnTile * d;  // [kAttnThreads] P.V partials
+  float* red = part + kAttnThreads;       // [32]
+  float* qs = red + 32;                   // [kAttnMaxD]
+  float* s = qs + kAttnMaxD;              // [max_seq] scores, then exp
+  pdl_wait();
+  pdl_launch();
+  const int gw = blockIdx.x;
   if (gw >= rows * heads) return;
   const int r = gw / heads, h = gw % heads;
   const int b = r / L, i = r % L;
   const int n = *pos0 + i + 1;
   const float* q = qkv + (size_t)r * 3 * H + h * d;
-  float* qs = sc + (size_t)kAttnWarps * max_seq + warp * 32 * kAttnDpl;
-#pragma unroll
-  for (int t = 0; t < kAttnDpl; ++t)
-    if (lane + 32 * t < d) qs[lane + 32 * t] = q[lane + 32 * t];
-  __syncwarp();
   const float* kb = kc + (size_t)b * max_seq * H + h * d;
   const float* vb = vc + (size_t)b * max_seq * H + h * d;
-  float* s = sc + warp * max_seq;
-  float mx = -INFINITY;
   const bool vec = (d & 3) == 0 && (H & 3) == 0;
-  for (int j = lane; j < n; j += 32) {
-    const float* kr = kb + (size_t)j * H;
-    float p = 0.0f;
-    if (vec) {
-      for (int c = 0; c < d; c += 4) {
-        const float4 kv = *reinterpret_cast<const float4*>(kr + c);
-        p = __fmaf_rn(qs[c], kv.x, p);
-        p = __fmaf_rn(qs[c + 1], kv.y, p);
-        p = __fmaf_rn(qs[c + 2], kv.z, p);
-        p = __fmaf_rn(qs[c + 3], kv.w, p);
+  const int ntiles = (n + kAttnTile - 1) / kAttnTile;
+  const int tile_f = kAttnTile * d;
+  attn_stage(buf, kb, 0, min(kAttnTile, n), d, H, vec);
+  for (int c = threadIdx.x; c < d; c += kAttnThreads) qs[c] = q[c];
+  // pass 1: scores
+  float mx = -INFINITY;
+  for (int t = 0; t < ntiles; ++t) {
+    const int nj = (t + 1) * kAttnTile;
+    attn_stage(buf + ((t + 1) & 1) * tile_f, kb, nj, t + 1 < ntiles ? min(kAttnTile, n - nj) : 0, d, H, vec);
+    cp_async_wait1();
+    __syncthreads();
+    const float* kt = buf + (t & 1) * tile_f;
+    const int j = threadIdx.x, cnt = min(kAttnTile, n - t * kAttnTile);
+    if (j < cnt) {
+      const float* kr = kt + j * d;
+      const int st = j % d;  // rotated start column: the lanes of a warp hit distinct banks
+      float p = 0.0f;
+      for (int c0 = 0; c0 < d; ++c0) {
+        int c = c0 + st;
+        if (c >= d) c -= d;
+        p = __fmaf_rn(qs[c], kr[c], p);
       }
-    } else {
-      for (int c = 0; c < d; ++c) p = __fmaf_rn(qs[c], kr[c], p);
+      p = __fmul_rn(p, scale);
+      s[t * kAttnTile + j] = p;
+      mx = fmaxf(mx, p);
     }
-    p = __fmul_rn(p, scale);
-    s[j] = p;
-    mx = fmaxf(mx, p);
+    __syncthreads();  // the tile buffer is refilled two iterations later
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  __syncwarp();
+  mx = attn_block_reduce(mx, red, true);
   float sum = 0.0f;
-  for (int j = lane; j < n; j += 32) {
+  for (int j = threadIdx.x; j < n; j += kAttnThreads) {
     const float e = expf(__fsub_rn(s[j], mx));
     s[j] = e;
-    sum += e;
+    sum = __fadd_rn(sum, e);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  __syncwarp();
-  float acc[kAttnDpl];
-#pragma unroll
-  for (int t = 0; t < kAttnDpl; ++t) acc[t] = 0.0f;
-  for (int j = 0; j < n; ++j) {
-    const float p = s[j];
-    const float* vr = vb + (size_t)j * H;
-#pragma unroll
-    for (int t = 0; t < kAttnDpl; ++t)
-      if (lane + 32 * t < d) acc[t] = __fmaf_rn(p, vr[lane + 32 * t], acc[t]);
+  sum = attn_block_reduce(sum, red, false);  // also orders the s[] writes before pass 2
+  // pass 2: P.V; thread = (dimension, key group), G groups take keys j = g mod G
+  const int G = kAttnThreads / d >= 1 ? kAttnThreads / d : 1;
+  const int dim = threadIdx.x % d, g = threadIdx.x / d;
+  float acc = 0.0f;
+  attn_stage(buf, vb, 0, min(kAttnTile, n), d, H, vec);
+  for (int t = 0; t < ntiles; ++t) {
+    const int nj = (t + 1) * kAttnTile;
+    attn_stage(buf + ((t + 1) & 1) * tile_f, vb, nj, t + 1 < ntiles ? min(kAttnTile, n - nj) : 0, d, H, vec);
+    cp_async_wait1();
+    __syncthreads();
+    const float* vt = buf + (t & 1) * tile_f;
+    const int cnt = min(kAttnTile, n - t * kAttnTile);
+    if (g < G && threadIdx.x < G * d)
+      for (int j = g; j < cnt; j += G) acc = __fmaf_rn(s[t * kAttnTile + j], vt[j * d + dim], acc);
+    __syncthreads();
   }
-  float* o = ctx + (size_t)r * H + h * d;
-#pragma unroll
-  for (int t = 0; t < kAttnDpl; ++t)
-    if (lane + 32 * t < d) o[lane + 32 * t] = sum > 0.0f ? __fdiv_rn(acc[t], sum) : 0.0f;
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x < d) {
+    float o = 0.0f;
+    for (int gg = 0; gg < G; ++gg) o = __fadd_rn(o, part[gg * d + threadIdx.x]);
+    ctx[(size_t)r * H + h * d + threadIdx.x] = sum > 0.0f ? __fdiv_rn(o, sum) : 0.0f;
+  }
 }
 
 // argmax of each row, first maximum wins (llm:932-942): strict > keeps the
-// lowest index on ties; NaN never wins.  Writes the token to next[b] and
-// out[b * out_stride + *step]; thread 0 of block 0 advances pos / step.
-__global__ void argmax_kernel(const float* __restrict__ logits, int V, uint32_t* __restrict__ next,
-                              uint32_t* __restrict__ out, int out_stride, int* __restrict__ step,
-                              int* __restrict__ pos, int pos_advance, float* __restrict__ keep_logits) {
-  __shared__ float bv[32];
-  __shared__ int bi[32];
-  const int b = blockIdx.x;
+// lowest index on ties; NaN never wins; all NaN / -inf gives index 0.  Grid
+// (chunks of kArgChunk logits, batch): each CTA reduces its chunk to
+// (value, index); the last CTA of a row (atomic count) combines the chunks in
+// order and writes the token to next[b] and out[b * out_stride + *step]; the
+// last row to finish advances *step by one and *pos by pos_advance.  With
+// keep_logits, every CTA copies its chunk of the row to
+// keep_logits[b][*step][:] (the logits the token was taken from).
+constexpr int kArgChunk = 4096, kArgThreads = 256;
+struct ArgmaxScratch {
+  float* best_v;      // [batch][chunks]
+  int* best_i;        // [batch][chunks]
+  unsigned* row_cnt;  // [batch], zero between launches
+  unsigned* done;     // [1], zero between launches
+};
+
+__global__ void __launch_bounds__(kArgThreads)
+    argmax_kernel(const float* __restrict__ logits, int V, uint32_t* __restrict__ next, uint32_t* __restrict__ out,
+                  int out_stride, int* __restrict__ step, int* __restrict__ pos, int pos_advance,
+                  float* __restrict__ keep_logits, ArgmaxScratch sc) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float bv[kArgThreads / 32];
+  __shared__ int bi[kArgThreads / 32];
+  __shared__ int is_last;
+  const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
   const float* x = logits + (size_t)b * V;
+  const int c0 = ch * kArgChunk, c1 = min(V, c0 + kArgChunk);
+  const int st = *step;
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int c = threadIdx.x; c < V; c += blockDim.x) {
+#pragma unroll 16
+  for (int c = c0 + threadIdx.x; c < c1; c += kArgThreads) {
     const float v = x[c];
     if (v > best) {  // first max within this thread's strided subsequence
       best = v;
       idx = c;
     }
+  }
+  if (keep_logits && out && st < out_stride) {
+    float* dst = keep_logits + ((size_t)b * out_stride + st) * V;
+    for (int c = c0 + threadIdx.x; c < c1; c += kArgThreads) dst[c] = x[c];
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -237,28 +337,40 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int V, uint32_t*
     bi[w] = idx;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float B = -INFINITY;
-    int I = 0x7fffffff;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i)
-      if (bv[i] > B || (bv[i] == B && bi[i] < I)) {
-        B = bv[i];
-        I = bi[i];
-      }
-    if (I == 0x7fffffff) I = 0;  // all NaN / -inf: index 0 like the reference
-    next[b] = (uint32_t)I;
-    if (out && *step < out_stride) out[(size_t)b * out_stride + *step] = (uint32_t)I;
+  if (threadIdx.x != 0) return;
+  float B = -INFINITY;
+  int I = 0x7fffffff;
+  for (int i = 0; i < kArgThreads / 32; ++i)
+    if (bv[i] > B || (bv[i] == B && bi[i] < I)) {
+      B = bv[i];
+      I = bi[i];
+    }
+  sc.best_v[(size_t)b * nch + ch] = B;
+  sc.best_i[(size_t)b * nch + ch] = I;
+  __threadfence();
+  is_last = atomicAdd(&sc.row_cnt[b], 1u) == (unsigned)(nch - 1);
+  if (!is_last) return;
+  __threadfence();
+  B = -INFINITY;
+  I = 0x7fffffff;
+  for (int i = 0; i < nch; ++i) {  // chunks in order: ties keep the lower index
+    const float v = __ldcg(sc.best_v + (size_t)b * nch + i);
+    const int j = __ldcg(sc.best_i + (size_t)b * nch + i);
+    if (v > B || (v == B && j < I)) {
+      B = v;
+      I = j;
+    }
   }
-  if (keep_logits && out && *step < out_stride) {
-    // the logits each generated token was taken from: [B][out_stride][V]
-    float* dst = keep_logits + ((size_t)b * out_stride + *step) * V;
-    for (int c = threadIdx.x; c < V; c += blockDim.x) dst[c] = x[c];
+  if (I == 0x7fffffff) I = 0;  // all NaN / -inf: index 0 like the reference
+  next[b] = (uint32_t)I;
+  if (out && st < out_stride) out[(size_t)b * out_stride + st] = (uint32_t)I;
+  sc.row_cnt[b] = 0u;
+  __threadfence();
+  if (atomicAdd(sc.done, 1u) == gridDim.y - 1) {
+    *step = st + 1;
+    *pos += pos_advance;
+    *sc.done = 0u;
   }
-}
-
-__global__ void advance_kernel(int* __restrict__ step, int* __restrict__ pos, int pos_advance) {
-  *step += 1;
-  *pos += pos_advance;
 }
 
 // gelu_new in f64, cast to f32 (llm:268-275), for the GEMV epilogue.
@@ -288,6 +400,8 @@ struct GemvArgs {
   float *kc, *vc;      // kEpiQkv: caches [batch][max_seq][H]
   const int* pos;      // kEpiQkv: position of row i of each sequence = *pos + i
   int L, H, max_seq;
+  const float *ln_w, *ln_b;  // optional LayerNorm of the x rows (llm:252-262) before the product
+  float ln_eps;
 };
 
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int r, int col, float s) {
@@ -323,43 +437,121 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int r, int col,
 // column tile to finish (an atomic count) adds the slices in slice order --
 // the result does not depend on scheduling -- and applies the epilogue.
 // Every weight element is read once and used for all MR rows.
+template <int VEC>
+struct GemvVec;
+template <>
+struct GemvVec<4> {
+  using T = float4;
+  static __device__ __forceinline__ void get(const T& t, float* w) {
+    w[0] = t.x;
+    w[1] = t.y;
+    w[2] = t.z;
+    w[3] = t.w;
+  }
+};
+template <>
+struct GemvVec<2> {
+  using T = float2;
+  static __device__ __forceinline__ void get(const T& t, float* w) {
+    w[0] = t.x;
+    w[1] = t.y;
+  }
+};
+
 template <int MR, int VEC>
 __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
   constexpr int TN = 32 * VEC;
+  using VT = typename GemvVec<VEC>::T;
   extern __shared__ float gsm[];
   float* xs = gsm;              // [MR][ks]
   float* red = gsm + MR * a.ks;  // [8][MR][TN]
   __shared__ int is_last;
+  __shared__ float ln_mean[MR], ln_inv[MR];
   const int tile = blockIdx.x, slice = blockIdx.y;
   const int k0 = slice * a.ks, kn = min(a.ks, a.k - k0);
-  for (int i = threadIdx.x; i < MR * a.ks; i += 256) {
-    const int r = i / a.ks, kk = i - r * a.ks;
-    xs[i] = (r < a.m && kk < kn) ? a.x[(size_t)r * a.k + k0 + kk] : 0.0f;
-  }
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c0 = tile * TN + lane * VEC;
+  const bool fast = c0 + VEC <= a.n && (a.n % VEC) == 0;
+  const float* wp = a.W + (size_t)k0 * a.n + c0;
+  // the first eight weight rows of this thread are requested before the x
+  // rows are staged: the two latencies overlap
+  VT pre[8];
+  if (fast) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int kk = warp + 8 * u;
+      if (kk < kn) pre[u] = __ldg(reinterpret_cast<const VT*>(wp + (size_t)kk * a.n));
+    }
+  }
+  pdl_wait();  // x, out, the KV cache and the counters belong to the predecessors until here
+  pdl_launch();
+  if (a.ln_w) {
+    // LayerNorm statistics of each x row (warp per row): mean = sum / k,
+    // var = sum (x - mean)^2 / k, inv = 1 / sqrt(var + eps)
+    for (int r = warp; r < a.m; r += 8) {
+      const float* xr = a.x + (size_t)r * a.k;
+      float sm = 0.0f;
+      if ((a.k & 3) == 0) {
+#pragma unroll 4
+        for (int c = lane * 4; c < a.k; c += 128) {
+          const float4 v = *reinterpret_cast<const float4*>(xr + c);
+          sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v.x), v.y), v.z), v.w);
+        }
+      } else {
+        for (int c = lane; c < a.k; c += 32) sm = __fadd_rn(sm, xr[c]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+      const float mean = __fdiv_rn(sm, (float)a.k);
+      float vs = 0.0f;
+      for (int c = lane; c < a.k; c += 32) {
+        const float dv = __fsub_rn(xr[c], mean);
+        vs = __fmaf_rn(dv, dv, vs);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+      if (lane == 0) {
+        ln_mean[r] = mean;
+        ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)a.k), a.ln_eps)));
+      }
+    }
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < MR * a.ks; i += 256) {
+    const int r = i / a.ks, kk = i - r * a.ks;
+    float v = 0.0f;
+    if (r < a.m && kk < kn) {
+      v = a.x[(size_t)r * a.k + k0 + kk];
+      if (a.ln_w)
+        v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, ln_mean[r]), ln_inv[r]), a.ln_w[k0 + kk]), a.ln_b[k0 + kk]);
+    }
+    xs[i] = v;
+  }
+  __syncthreads();
   float acc[MR][VEC];
 #pragma unroll
   for (int r = 0; r < MR; ++r)
 #pragma unroll
     for (int v = 0; v < VEC; ++v) acc[r][v] = 0.0f;
-  if (c0 + VEC <= a.n && (a.n % VEC) == 0) {
-    const float* wp = a.W + (size_t)k0 * a.n + c0;
-#pragma unroll 8
-    for (int kk = warp; kk < kn; kk += 8) {
-      float w[VEC];
-      if constexpr (VEC == 4) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(wp + (size_t)kk * a.n));
-        w[0] = t.x;
-        w[1] = t.y;
-        w[2] = t.z;
-        w[3] = t.w;
-      } else {
-        const float2 t = __ldg(reinterpret_cast<const float2*>(wp + (size_t)kk * a.n));
-        w[0] = t.x;
-        w[1] = t.y;
+  if (fast) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int kk = warp + 8 * u;
+      if (kk < kn) {
+        float w[VEC];
+        GemvVec<VEC>::get(pre[u], w);
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          const float xv = xs[r * a.ks + kk];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) acc[r][v] = __fmaf_rn(xv, w[v], acc[r][v]);
+        }
       }
+    }
+#pragma unroll 8
+    for (int kk = warp + 64; kk < kn; kk += 8) {
+      float w[VEC];
+      GemvVec<VEC>::get(__ldg(reinterpret_cast<const VT*>(wp + (size_t)kk * a.n)), w);
 #pragma unroll
       for (int r = 0; r < MR; ++r) {
         const float xv = xs[r * a.ks + kk];
@@ -368,7 +560,6 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
       }
     }
   } else if (c0 < a.n) {
-    const float* wp = a.W + (size_t)k0 * a.n + c0;
     for (int kk = warp; kk < kn; kk += 8) {
 #pragma unroll
       for (int v = 0; v < VEC; ++v) {
@@ -483,6 +674,7 @@ struct oc_gpt {
   size_t part_floats = 0;
   unsigned* counters = nullptr;  // decode GEMV column-tile counters
   size_t counter_count = 0;
+  ArgmaxScratch arg{};
   float *kc, *vc;  // [layer][batch][max_seq][H]
   uint32_t *tok_in, *next, *out_tokens;
   int *pos, *step;
@@ -529,20 +721,55 @@ int linear_alloc(oc_gpt* g, GptLinear& L, int in, int out) {
   return OC_OK;
 }
 
+// First launch error of launch_pdl on this thread, reported by launch_status().
+static thread_local cudaError_t t_launch_err = cudaSuccess;
+
+static cudaError_t launch_status() {
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = t_launch_err;
+  t_launch_err = cudaSuccess;
+  return e;
+}
+
+// Launch with programmatic stream serialization (see pdl_wait / pdl_launch).
+template <typename... KArgs, typename... Args>
+static void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess && t_launch_err == cudaSuccess) t_launch_err = e;
+}
+
 template <int MR, int VEC>
 static void launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
   auto kern = gemv_splitk_kernel<MR, VEC>;
   smem_attr_once(reinterpret_cast<const void*>(kern), std::max<size_t>(p.smem, 48 * 1024));
-  kern<<<dim3(p.tiles, p.slices), 256, p.smem, s>>>(a);
+  launch_pdl(kern, dim3(p.tiles, p.slices), dim3(256), p.smem, s, a);
 }
 
 // out[rows][L.out] = epilogue(x[rows][L.in] . W + b) (GemvEpi); *n += kernels
 // launched.  Up to 32 rows: one split-K GEMV with the epilogue fused; more
 // rows: the tensor-core GEMM, then the epilogue as its own kernel.
+// With ln_w, x is first normalised: LayerNorm(x; ln_w, ln_b) (fused into the
+// GEMV; a separate kernel into g->normed on the tensor-core path).
 int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* out, int epi, int* n,
-               float* kc = nullptr, float* vc = nullptr, int seq_rows = 1) {
+               float* kc = nullptr, float* vc = nullptr, int seq_rows = 1, const float* ln_w = nullptr,
+               const float* ln_b = nullptr) {
   cudaStream_t s = g->stream;
   const int H = (int)g->cfg.hidden_size, ms = (int)g->cfg.max_seq_len;
+  if (rows > 32 && ln_w) {
+    layernorm_kernel<<<rows, 256, 0, s>>>(x, L.in, g->normed, L.in, ln_w, ln_b, g->cfg.layer_norm_eps);
+    *n += 1;
+    x = g->normed;
+  }
   if (rows > 32) {
     float* dst = epi == kEpiResidual ? g->tmp : out;
     int rc = oc_sgemm_prepared(rows, L.out, L.in, 1.0f, x, L.in, L.prep, 0.0f, dst, L.out, L.b, s);
@@ -556,7 +783,7 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
   } else {
     const GemvPlan p = gemv_plan(L.in, L.out, rows);
     GemvArgs a{rows, L.out, L.in, p.ks, p.slices, epi, x, L.w, L.b, g->part, g->counters, out,
-               kc, vc, g->pos, seq_rows, H, ms};
+               kc, vc, g->pos, seq_rows, H, ms, ln_w, ln_b, g->cfg.layer_norm_eps};
     if (rows <= 1) launch_gemv<1, 4>(p, a, s);
     else if (rows <= 4) launch_gemv<4, 4>(p, a, s);
     else if (rows <= 8) launch_gemv<8, 4>(p, a, s);
@@ -564,7 +791,7 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
     else launch_gemv<32, 2>(p, a, s);
     *n += 1;
   }
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_status();
   return e == cudaSuccess ? OC_OK : from_cuda(e, "gpt linear");
 }
 
@@ -579,31 +806,31 @@ int forward(oc_gpt* g, int batch, int L, const uint32_t* tokens, uint32_t* out, 
   const int ms = (int)c.max_seq_len, rows = batch * L;
   cudaStream_t s = g->stream;
   int rc;
-  embed_kernel<<<rows, 256, 0, s>>>(tokens, L, g->pos, g->wte, g->wpe, H, g->hidden, rows);
+  launch_pdl(embed_kernel, dim3(rows), dim3(256), 0, s, tokens, L, (const int*)g->pos, (const float*)g->wte,
+             (const float*)g->wpe, H, g->hidden, rows);
   const float scale = 1.0f / sqrtf((float)(H / nh));
-  const size_t attn_smem = (size_t)kAttnWarps * (ms + 32 * kAttnDpl) * sizeof(float);
+  const size_t attn_smem = attn_smem_bytes(ms, H / nh);
   for (size_t li = 0; li < c.num_layers; ++li) {
     GptLayer& Ly = g->layers[li];
     float* kc = g->kc + li * (size_t)g->max_batch * ms * H;
     float* vc = g->vc + li * (size_t)g->max_batch * ms * H;
-    layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, H, g->normed, H, Ly.ln1w, Ly.ln1b, c.layer_norm_eps);
-    if ((rc = linear_fwd(g, Ly.qkv, g->normed, rows, g->qkv, kEpiQkv, n, kc, vc, L))) return rc;
-    decode_attention_kernel<<<(rows * nh + kAttnWarps - 1) / kAttnWarps, kAttnWarps * 32, attn_smem, s>>>(
+    if ((rc = linear_fwd(g, Ly.qkv, g->hidden, rows, g->qkv, kEpiQkv, n, kc, vc, L, Ly.ln1w, Ly.ln1b))) return rc;
+    launch_pdl(decode_attention_kernel, dim3(rows * nh), dim3(kAttnThreads), attn_smem, s,
         g->qkv, L, g->pos, H, nh, H / nh, kc, vc, ms, g->ctx, rows, scale);
     if ((rc = linear_fwd(g, Ly.ao, g->ctx, rows, g->hidden, kEpiResidual, n))) return rc;
-    layernorm_kernel<<<rows, 256, 0, s>>>(g->hidden, H, g->normed, H, Ly.ln2w, Ly.ln2b, c.layer_norm_eps);
-    if ((rc = linear_fwd(g, Ly.fc, g->normed, rows, g->inter, kEpiGelu, n))) return rc;
+    if ((rc = linear_fwd(g, Ly.fc, g->hidden, rows, g->inter, kEpiGelu, n, nullptr, nullptr, 1, Ly.ln2w, Ly.ln2b)))
+      return rc;
     if ((rc = linear_fwd(g, Ly.pj, g->inter, rows, g->hidden, kEpiResidual, n))) return rc;
-    *n += 3;  // two layer norms and the attention (+ the linears and their epilogues above)
+    *n += 1;  // the attention (+ the linears, their layer norms and epilogues above)
   }
   // last row of each sequence (rows b*L + L-1) -> normed[b], one launch
-  layernorm_kernel<<<batch, 256, 0, s>>>(g->hidden + (size_t)(L - 1) * H, (size_t)L * H, g->normed, H, g->lnfw,
-                                         g->lnfb, c.layer_norm_eps);
+  launch_pdl(layernorm_kernel, dim3(batch), dim3(256), 0, s, (const float*)(g->hidden + (size_t)(L - 1) * H),
+             (size_t)L * H, g->normed, H, (const float*)g->lnfw, (const float*)g->lnfb, c.layer_norm_eps);
   if ((rc = linear_fwd(g, g->lm, g->normed, batch, g->logits, kEpiPlain, n))) return rc;
-  argmax_kernel<<<batch, 1024, 0, s>>>(g->logits, V, g->next, out, out_stride, g->step, g->pos, L, keep);
-  advance_kernel<<<1, 1, 0, s>>>(g->step, g->pos, L);
-  *n += 1 + 1 + 2;  // embed, final layer norm, argmax, advance
-  cudaError_t e = cudaGetLastError();
+  launch_pdl(argmax_kernel, dim3((V + kArgChunk - 1) / kArgChunk, batch), dim3(kArgThreads), 0, s,
+             (const float*)g->logits, V, g->next, out, out_stride, g->step, g->pos, L, keep, g->arg);
+  *n += 1 + 1 + 1;  // embed, final layer norm, argmax (which also advances step and pos)
+  cudaError_t e = launch_status();
   return e == cudaSuccess ? OC_OK : from_cuda(e, "gpt forward");
 }
 
@@ -615,7 +842,7 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
   OC_REQUIRE(cfg && out, "gpt_create: NULL argument");
   OC_REQUIRE(max_batch >= 1 && max_batch <= 1024 && max_prompt_len >= 1, "gpt_create: bad batch / prompt sizes");
   OC_REQUIRE(cfg->num_heads > 0 && cfg->hidden_size % cfg->num_heads == 0 &&
-                 cfg->hidden_size / cfg->num_heads <= 32 * kAttnDpl && cfg->hidden_size % 4 == 0 &&
+                 cfg->hidden_size / cfg->num_heads <= kAttnMaxD && cfg->hidden_size % 4 == 0 &&
                  cfg->intermediate_size % 4 == 0,
              "gpt_create: needs hidden_size % num_heads == 0, head_dim <= 128, hidden/intermediate % 4 == 0");
   OC_REQUIRE(cfg->vocab_size > 0 && cfg->num_layers > 0 && cfg->intermediate_size > 0 && cfg->max_seq_len > 0,
@@ -669,11 +896,17 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
       (rc = galloc_t(g, cfg->num_layers * (size_t)max_batch * ms * H, &g->vc)) ||
       (rc = galloc_t(g, R, &g->tok_in)) || (rc = galloc_t(g, (size_t)max_batch, &g->next)) ||
       (rc = galloc_t(g, (size_t)max_batch * ms, &g->out_tokens)) || (rc = galloc_t(g, 1, &g->pos)) ||
-      (rc = galloc_t(g, 1, &g->step)) || (rc = galloc_t(g, g->counter_count, &g->counters)))
+      (rc = galloc_t(g, 1, &g->step)) || (rc = galloc_t(g, g->counter_count, &g->counters)) ||
+      (rc = galloc_t(g, (size_t)max_batch * ((V + kArgChunk - 1) / kArgChunk), &g->arg.best_v)) ||
+      (rc = galloc_t(g, (size_t)max_batch * ((V + kArgChunk - 1) / kArgChunk), &g->arg.best_i)) ||
+      (rc = galloc_t(g, (size_t)max_batch, &g->arg.row_cnt)) || (rc = galloc_t(g, 1, &g->arg.done)))
     return bail(rc);
+  if (cudaMemset(g->arg.row_cnt, 0, (size_t)max_batch * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(g->arg.done, 0, sizeof(unsigned)) != cudaSuccess)
+    return bail(from_cuda(cudaGetLastError(), "gpt_create: argmax counters"));
   if (cudaMemset(g->counters, 0, std::max<size_t>(g->counter_count, 1) * sizeof(unsigned)) != cudaSuccess)
     return bail(from_cuda(cudaGetLastError(), "gpt_create: counters"));
-  const size_t attn_smem = (size_t)kAttnWarps * (ms + 32 * kAttnDpl) * sizeof(float);
+  const size_t attn_smem = attn_smem_bytes((int)ms, (int)(H / cfg->num_heads));
   if (!smem_attr_once(reinterpret_cast<const void*>(decode_attention_kernel), attn_smem))
     return bail(fail(OC_ERR_NOT_SUPPORTED, "gpt_create: max_seq_len too large for the attention kernel"));
   *out = g;
