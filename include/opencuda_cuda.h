@@ -255,13 +255,16 @@ int oc_dequantize_int4_awq(const uint8_t *data, const float *scales, size_t rows
  * it: a [n][k] matrix flattened and passed to quantize_int8 (group = k, one
  * scale per output channel) or quantize_int4 (group = `group`, packed two
  * per byte).  The activation rows are quantized on the device with
- * quantize_int8(A, group = k).  Integer products accumulate exactly in
- * int32 on the tcgen05 kind::i8 tensor cores (INT4 weights are widened to
- * int8 in shared memory), then
+ * quantize_int8(A, group = k).  The defined results are
  *   W8A8:  y = ((float)acc * sa[m]) * sw[n] + bias[n]
  *   W4A8:  s = 0; for each group j: s = fma((float)P_j, sw[n][j], s);
  *          y = s * sa[m] + bias[n]
- * with P_j the exact int32 partial sum of group j.  `workspace` is device
+ * with acc / P_j the exact int32 (group) partial sums.  W8A8 is computed
+ * exactly so (tcgen05 kind::i8, exact int32).  W4A8 is computed exactly so
+ * when acc_out is requested, for m <= 16, or when k % 128 != 0; otherwise
+ * by the dequantizing tensor-core GEMM (each weight dequantized in f32 as
+ * dequantize_int4 does, carried as two f16 terms, f32 accumulation), whose
+ * y agrees with the definition to about 1e-6 relative.  `workspace` is device
  * scratch of at least oc_qgemm_workspace_size() bytes (quantized
  * activations and their scales); bias may be NULL.  acc_out (optional,
  * NULL to skip): the int32 accumulators, [m][n] for W8A8 and

@@ -5,10 +5,13 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstddef>
 #include <cstdint>
+#include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/opencuda_cuda.h"
 
@@ -71,6 +74,36 @@ struct Arena {
 };
 Arena& arena_of(const oc_device* d);
 int arena_get(Arena& a, size_t bytes, cudaStream_t s, uint8_t** out);
+
+// Grow-only scratch buffers, one per (device, stream) and reused in stream
+// order: a call's kernels finish before the next call's kernels on that
+// stream start.  Growing a buffer synchronizes the device, so the first call
+// of a given size must not be made while the stream is being captured into a
+// CUDA graph.
+struct StreamScratch {
+  std::mutex mu;
+  std::map<std::pair<int, cudaStream_t>, std::pair<float*, size_t>> bufs;  // per (device, stream)
+  float* get(size_t floats, cudaStream_t s) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    auto& e = bufs[std::make_pair(dev, s)];
+    if (e.second < floats) {
+      if (e.first) {
+        cudaDeviceSynchronize();
+        cudaFree(e.first);
+      }
+      size_t want = std::max(floats, (size_t)1 << 22);
+      if (cudaMalloc(&e.first, want * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        e = {nullptr, 0};
+        return nullptr;
+      }
+      e.second = want;
+    }
+    return e.first;
+  }
+};
 
 // Makes `dev` current for the scope, restoring the previous device after.
 struct Scope {

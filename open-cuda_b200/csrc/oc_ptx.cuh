@@ -3,6 +3,7 @@
 // the GEMM kernels.  Every TMA load is a plain (single-CTA) copy into this
 // CTA's own shared memory from this GPU's own global memory.
 #pragma once
+#include <cuda_fp16.h>
 #include <cstdint>
 #include <cuda.h>
 
@@ -151,6 +152,17 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem], f16 operands (both), f32 accumulate.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem], tf32 operands, f32 accumulate.
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
@@ -249,6 +261,10 @@ __device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t smem_addr, uint3
 // 1 = MN-major), [17,23) N >> 3, [24,29) M >> 4.
 __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+// kind::f16 with f16 A and B (formats 0), f32 accumulator (c_format 1), both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, int b_mn_major) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)b_mn_major << 16) | ((uint32_t)(n >> 3) << 17) |

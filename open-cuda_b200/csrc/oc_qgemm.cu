@@ -11,6 +11,7 @@
 #include <algorithm>
 
 #include "oc_gemm_i4.cuh"
+#include "oc_gemm_i4s.cuh"
 #include "oc_gemm_i8.cuh"
 #include "oc_internal.h"
 #include "oc_quant.cuh"
@@ -385,6 +386,41 @@ int run_w4a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const ui
   return launch_err("gemm_w4a8_tc_kernel");
 }
 
+// per-column range factors and f16 activations of the dequantizing W4A8
+// GEMM, one buffer each per (device, stream)
+static StreamScratch g_w4_colscale, g_w4_a16;
+
+static bool w4_split_ok(int m, int k, int group, const void* sw, const void* wq) {
+  return m > kSkinnyM && is_sm100() && group == 32 && k % I4Split::RBK == 0 && aligned16(sw) && aligned16(wq);
+}
+
+// Y = dequantizing W4A8 GEMM on f16 activations qa16 [m][k] (exact integers).
+int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq, const float* sw,
+                   const float* bias, float* Y, cudaStream_t s) {
+  using C = I4Split;
+  float* cs = g_w4_colscale.get((size_t)n, s);
+  if (!cs) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
+  const int G = k / 32;
+  w4_colscale_kernel<<<(n + 7) / 8, 256, 0, s>>>(sw, n, G, cs);
+  CUtensorMap ta, tbp, tsc;
+  int rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
+                        C::BK, C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tbp, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, (uint64_t)k / 2,
+                    C::RBK / 2, C::BN, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tsc, sw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)G, (uint64_t)n, (uint64_t)G * 4,
+                    C::RGROUPS, C::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_split_kernel), C::SMEM))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_split_kernel) failed");
+  const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
+  const int grid = std::min(tiles, std::max(1, sm_count()));
+  gemm_w4a8_split_kernel<<<grid, C::THREADS, C::SMEM, s>>>(ta, tbp, tsc, m, n, k, sa, cs, bias, Y,
+                                                           device_status_word());
+  return launch_err("gemm_w4a8_split_kernel");
+}
+
 }  // namespace oc
 
 using namespace oc;
@@ -394,7 +430,7 @@ extern "C" {
 int oc_qgemm_workspace_size(int m, int k, size_t* bytes) {
   OC_REQUIRE(bytes, "NULL argument");
   OC_REQUIRE(m > 0 && k > 0, "qgemm: m and k must be > 0");
-  *bytes = align256((size_t)m * k) + align256((size_t)m * sizeof(float));
+  *bytes = align256((size_t)m * k * 2) + align256((size_t)m * sizeof(float));  // f16 or int8 rows + scales
   return OC_OK;
 }
 
@@ -437,6 +473,15 @@ int oc_igemm_w4a8(int m, int n, int k, int group, const int8_t* qa, const float*
   OC_REQUIRE(qa && sa && Wq && w_scales && Y, "igemm_w4a8: NULL pointer");
   OC_REQUIRE(aligned16(Wq), "igemm_w4a8: packed weights must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!acc_out && w4_split_ok(m, k, group, w_scales, Wq) && (reinterpret_cast<uintptr_t>(qa) & 7u) == 0 &&
+      k % 8 == 0) {
+    // no int32 partials requested: the dequantizing GEMM on f16 activations
+    __half* a16 = reinterpret_cast<__half*>(g_w4_a16.get(((size_t)m * k + 1) / 2, s));
+    if (!a16) return fail(OC_ERR_OUT_OF_MEMORY, "igemm_w4a8: scratch allocation failed");
+    int rc = launch_i8_to_f16(qa, (size_t)m * k, a16, s);
+    if (rc) return rc;
+    return run_w4a8_split(m, n, k, a16, sa, Wq, w_scales, bias, Y, s);
+  }
   if (m > kSkinnyM && is_sm100() && group == 32 && k % 128 == 0 && aligned16(w_scales) && aligned16(qa))
     return run_w4a8_tc(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
   // The skinny kernel handles up to kSkinnyM rows per launch.
@@ -460,9 +505,18 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float* A, const uint8_t*
   oc_qgemm_workspace_size(m, k, &need);
   OC_REQUIRE(workspace_bytes >= need, "qgemm_w4a8: workspace too small");
   OC_REQUIRE(aligned16(workspace), "qgemm_w4a8: workspace must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!acc_out && w4_split_ok(m, k, group, w_scales, Wq)) {
+    // activations quantized straight to f16 for the dequantizing tensor-core GEMM
+    __half* qa16 = static_cast<__half*>(workspace);
+    float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k * 2));
+    int rc = launch_quantize_rows_f16(A, m, k, qa16, sa, s);
+    if (rc == OC_OK) return run_w4a8_split(m, n, k, qa16, sa, Wq, w_scales, bias, Y, s);
+    if (rc != OC_ERR_NOT_SUPPORTED) return rc;
+  }
   int8_t* qa = static_cast<int8_t*>(workspace);
-  float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k));
-  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, static_cast<cudaStream_t>(stream));
+  float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k * 2));
+  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, s);
   if (rc) return rc;
   return oc_igemm_w4a8(m, n, k, group, qa, sa, Wq, w_scales, bias, Y, acc_out, stream);
 }

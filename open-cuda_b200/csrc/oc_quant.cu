@@ -77,9 +77,11 @@ __global__ void dequantize_i4_kernel(const uint8_t* __restrict__ q, const float*
 // 128 threads per row, the row held in registers (VPT float4 per thread),
 // a block max-reduction, then int8 stores.  Requires k % 4 == 0 and a
 // 16-byte aligned A; k <= 128 * 4 * VPT.
-template <int VPT>
+// quantize_int8(A row, group = k); F16: the quantized integers are written as
+// f16 (exact, |q| <= 127) for the f16 tensor-core path, else as int8.
+template <int VPT, bool F16 = false>
 __global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __restrict__ A, int m, int k,
-                                                               int8_t* __restrict__ qa, float* __restrict__ sa) {
+                                                               void* __restrict__ qout, float* __restrict__ sa) {
   __shared__ float red[4];
   const int row = blockIdx.x;
   if (row >= m) return;
@@ -101,7 +103,20 @@ __global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __re
   mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const float s = (mx == 0.0f) ? 0.0f : __fdiv_rn(mx, 127.0f);
   if (threadIdx.x == 0) sa[row] = s;
-  char4* q4 = reinterpret_cast<char4*>(qa + (size_t)row * k);
+  if (F16) {
+    uint2* h4 = reinterpret_cast<uint2*>(static_cast<__half*>(qout) + (size_t)row * k);
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      int idx = threadIdx.x + j * 128;
+      if (idx < n4) {
+        const __half2 a = __floats2half2_rn((float)quant_one(v[j].x, s, 127.0f), (float)quant_one(v[j].y, s, 127.0f));
+        const __half2 b = __floats2half2_rn((float)quant_one(v[j].z, s, 127.0f), (float)quant_one(v[j].w, s, 127.0f));
+        h4[idx] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+      }
+    }
+    return;
+  }
+  char4* q4 = reinterpret_cast<char4*>(static_cast<int8_t*>(qout) + (size_t)row * k);
 #pragma unroll
   for (int j = 0; j < VPT; j++) {
     int idx = threadIdx.x + j * 128;
@@ -113,6 +128,23 @@ __global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __re
       o.w = (signed char)quant_one(v[j].w, s, 127.0f);
       q4[idx] = o;
     }
+  }
+}
+
+// int8 -> f16 (exact), 8 elements per thread per step.
+__global__ void i8_to_f16_kernel(const int8_t* __restrict__ q, size_t n8, __half* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const uint2 w = reinterpret_cast<const uint2*>(q)[i];
+    const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+    __half2 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn((float)b[2 * e], (float)b[2 * e + 1]);
+    uint4 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&h[0]);
+    o.y = *reinterpret_cast<const uint32_t*>(&h[1]);
+    o.z = *reinterpret_cast<const uint32_t*>(&h[2]);
+    o.w = *reinterpret_cast<const uint32_t*>(&h[3]);
+    reinterpret_cast<uint4*>(out)[i] = o;
   }
 }
 
@@ -135,6 +167,27 @@ int launch_quantize_i8(const float* x, size_t len, const float* scales, size_t g
   quantize_i8_kernel<<<grid_for(len, 256), 256, 0, s>>>(x, len, scales, group, qmax, out);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_i8_kernel");
+}
+
+int launch_quantize_rows_f16(const float* A, int m, int k, __half* qa16, float* sa, cudaStream_t s) {
+  if (m <= 0) return OC_OK;
+  const int n4 = k / 4;
+  if (k % 8 || !aligned16(A) || !aligned16(qa16) || n4 > 128 * 8) return OC_ERR_NOT_SUPPORTED;
+  if (n4 <= 128 * 2)
+    quantize_rows_i8_kernel<2, true><<<m, 128, 0, s>>>(A, m, k, qa16, sa);
+  else if (n4 <= 128 * 4)
+    quantize_rows_i8_kernel<4, true><<<m, 128, 0, s>>>(A, m, k, qa16, sa);
+  else
+    quantize_rows_i8_kernel<8, true><<<m, 128, 0, s>>>(A, m, k, qa16, sa);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_rows_i8_kernel<f16>");
+}
+
+int launch_i8_to_f16(const int8_t* q, size_t n, __half* out, cudaStream_t s) {
+  if (n % 8 || !aligned16(out) || (reinterpret_cast<uintptr_t>(q) & 7u)) return OC_ERR_NOT_SUPPORTED;
+  i8_to_f16_kernel<<<grid_for(n / 8, 256), 256, 0, s>>>(q, n / 8, out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "i8_to_f16_kernel");
 }
 
 int launch_quantize_rows_i8(const float* A, int m, int k, int8_t* qa, float* sa, cudaStream_t s) {

@@ -396,36 +396,7 @@ __global__ void sgemv_reduce(int m, int n, int slices, const float* __restrict__
   }
 }
 
-// Grow-only scratch buffers (GEMV partials, prepared B), one per (device,
-// stream) and reused in stream order: a call's kernels finish before the
-// next call's kernels on that stream start.  Growing a buffer synchronizes
-// the device, so the first call of a given size must not be made while the
-// stream is being captured into a CUDA graph.
-struct Scratch {
-  std::mutex mu;
-  std::map<std::pair<int, cudaStream_t>, std::pair<float*, size_t>> bufs;  // per (device, stream)
-  float* get(size_t floats, cudaStream_t s) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lk(mu);
-    auto& e = bufs[std::make_pair(dev, s)];
-    if (e.second < floats) {
-      if (e.first) {
-        cudaDeviceSynchronize();
-        cudaFree(e.first);
-      }
-      size_t want = std::max(floats, (size_t)1 << 22);
-      if (cudaMalloc(&e.first, want * sizeof(float)) != cudaSuccess) {
-        cudaGetLastError();
-        e = {nullptr, 0};
-        return nullptr;
-      }
-      e.second = want;
-    }
-    return e.first;
-  }
-};
-static Scratch g_gemv_ws, g_bprep_ws;
+static StreamScratch g_gemv_ws, g_bprep_ws;
 
 static int launch_gemv(int m, int n, int k, float alpha, const float* A, int lda, const float* B, int ldb,
                        int trans_b, float beta, float* Cm, int ldc, const float* bias, cudaStream_t s) {
