@@ -8,20 +8,29 @@
 // lo = f16(x * c_n - hi) (22 significant bits; c_n = 2^e per output column
 // keeps |x * c_n| < 2^15, inside f16's range), and the quantized activations
 // arrive as f16 (exact integers, written so by the row quantization), so
-// each K-step is two kind::f16 MMAs (A.hi, A.lo) with f32 accumulation; the
+// each K-step is two kind::f16 MMAs (hi.A, lo.A) with f32 accumulation; the
 // epilogue divides by c_n (exact).  The result agrees with the exact
 // per-group definition to ~1e-6 relative; the exact int32 group partials,
 // when a caller asks for them, come from oc_gemm_i4.cuh.
 //
-// Rings: raw k-blocks of 128 by TMA (packed B [128][64 bytes] with the
-// 64-byte swizzle, scales [128][4]) and k-blocks of 64 for the MMA (f16 A by
-// TMA, weights hi and lo written by the converters, all in the
-// 128-byte-swizzled K-major layout).  Roles (480 threads):
+// The converted weights never touch shared memory: the converters store hi
+// and lo into tensor memory (tcgen05.st), where the MMA takes them as its A
+// operand (M = 128 weight rows = output columns), and the f16 activation
+// tile (N = 128 output rows) is the shared-memory B operand.  The
+// accumulator is the output tile transposed: TMEM lane = output column,
+// TMEM column = output row, so the epilogue's stores are coalesced across a
+// warp.  Shared memory then carries only the activation tiles (TMA, read by
+// the MMA) and the packed weights (TMA, read once by the converters).
+// Rings: raw k-blocks of 128 (packed B [128][64 bytes] with the 64-byte
+// swizzle, scales [128][4]) and k-blocks of 64 (activation tile in smem,
+// weight terms in TMEM).  Roles (864 threads):
 //   warp 0       TMA producer of the raw ring
 //   warp 1       TMEM allocator + MMA issuer (two 128-column accumulators)
 //   warp 2       TMA producer of the f16 activation tiles
-//   warps 3..10  converters: thread = (row, group of the k-block) of B
-//   warps 11..14 epilogue: TMEM -> registers, / c_n, * sa, + bias, stores
+//   warps 3..18  converters: warp = (TMEM lane quadrant, 16-k quarter of
+//                the k-block), thread = one weight row
+//   warps 19..26 epilogue: warp = (TMEM lane quadrant, half of the output
+//                rows): TMEM -> registers, / c_n, * sa, + bias, stores
 // Every wait is bounded (oc_ptx.cuh).
 #pragma once
 #include "oc_gemm_i8.cuh"
@@ -30,21 +39,22 @@
 namespace oc {
 
 struct I4Split {
-  static constexpr int BM = 128, BN = 128;
-  static constexpr int RBK = 128, RSTAGES = 4, RGROUPS = RBK / 32;
+  static constexpr int BM = 128, BN = 128;  // output rows (activations) x output columns (weights)
+  static constexpr int RBK = 128, RGROUPS = RBK / 32, RSTAGES = 4;
   static constexpr int BP_BYTES = BN * RBK / 2, S_BYTES = BN * RGROUPS * 4;
-  static constexpr int RSTAGE_BYTES = 16384;  // BP + S padded to keep 1024-byte alignment
-  static constexpr int BK = 64, CSTAGES = 3;
-  static constexpr int A16_BYTES = BM * BK * 2, BH_BYTES = BN * BK * 2, BL_BYTES = BN * BK * 2;
-  static constexpr int CSTAGE_BYTES = A16_BYTES + BH_BYTES + BL_BYTES;
-  static constexpr int CONV_WARPS = 8, EPI_WARPS = 4;
+  static constexpr int RSTAGE_BYTES = (BP_BYTES + S_BYTES + 1023) / 1024 * 1024;
+  static constexpr int BK = 64, CSTAGES = 4;
+  static constexpr int A16_BYTES = BM * BK * 2;  // activation tile per k-block (smem)
+  static constexpr int WCOLS = BK;               // TMEM columns per k-block: hi 32 + lo 32
+  static constexpr int CONV_WARPS = 16, EPI_WARPS = 8;
   static constexpr int THREADS = 32 * (3 + CONV_WARPS + EPI_WARPS);
-  static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = 1024 + (size_t)CSTAGES * CSTAGE_BYTES + (size_t)RSTAGES * RSTAGE_BYTES + 512;
-  static constexpr uint32_t IDESC = idesc_f16(BM, BN);
-  static_assert(BP_BYTES + S_BYTES <= RSTAGE_BYTES, "raw stage too small");
-  static_assert(CSTAGE_BYTES % 1024 == 0 && RSTAGE_BYTES % 1024 == 0, "1024-byte stage alignment");
-  static_assert(CONV_WARPS * 32 == 2 * BN, "one converter thread per (row, group of a k-block)");
+  static constexpr int ACC_COLS = 2 * BM;        // two accumulators (transposed tiles: BM columns)
+  static constexpr int TMEM_COLS = 512;
+  static constexpr size_t SMEM = 1024 + (size_t)CSTAGES * A16_BYTES + (size_t)RSTAGES * RSTAGE_BYTES + 512;
+  static constexpr uint32_t IDESC = idesc_f16(BN, BM);  // MMA M = weight rows, N = activation rows
+  static_assert(ACC_COLS + CSTAGES * WCOLS <= TMEM_COLS, "tensor memory budget");
+  static_assert(RSTAGE_BYTES % 1024 == 0 && A16_BYTES % 1024 == 0, "1024-byte stage alignment");
+  static_assert(CONV_WARPS == 16 && EPI_WARPS == 8, "four converter and two epilogue warps per TMEM lane quadrant");
 };
 
 // a - b on two f16 lanes (exact for the integers used here)
@@ -110,8 +120,9 @@ struct KbCursor {
 };
 
 // Per-column range factor c_n = 2^(11 - e) with e the exponent of
-// max_j |sw[n][j]|, so |(nib - 8) * sw * c_n| < 8 * 2^(e+1) * 2^(11-e) = 2^15.
-// One warp per column.
+// max_j |sw[n][j]|, so |(nib - 8) * sw * c_n| < 8 * 2^(e+1) * 2^(11-e) = 2^15;
+// cs[n] = c_n, cs[N + n] = 1 / c_n (both exact powers of two).  One warp per
+// column.
 __global__ void w4_colscale_kernel(const float* __restrict__ sw, int N, int G, float* __restrict__ cs) {
   const int lane = threadIdx.x & 31;
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -124,7 +135,9 @@ __global__ void w4_colscale_kernel(const float* __restrict__ sw, int N, int G, f
     int e = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;  // subnormal or zero: -127
     int ce = 11 - e;
     ce = ce < -126 ? -126 : (ce > 126 ? 126 : ce);
-    cs[col] = (mx > 0.0f && mx <= 3.0e38f) ? __uint_as_float((uint32_t)(ce + 127) << 23) : 1.0f;
+    if (!(mx > 0.0f && mx <= 3.0e38f)) ce = 0;
+    cs[col] = __uint_as_float((uint32_t)(ce + 127) << 23);
+    cs[N + col] = __uint_as_float((uint32_t)(127 - ce) << 23);
   }
 }
 
@@ -137,10 +150,8 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* const cbase = smem;
-  uint8_t* const rbase = smem + (size_t)C::CSTAGES * C::CSTAGE_BYTES;
-  auto sA16 = [&](int c) { return cbase + (size_t)c * C::CSTAGE_BYTES; };
-  auto sBH = [&](int c) { return sA16(c) + C::A16_BYTES; };
-  auto sBL = [&](int c) { return sBH(c) + C::BH_BYTES; };
+  uint8_t* const rbase = smem + (size_t)C::CSTAGES * C::A16_BYTES;
+  auto sA16 = [&](int c) { return cbase + (size_t)c * C::A16_BYTES; };
   auto sBP = [&](int r) { return rbase + (size_t)r * C::RSTAGE_BYTES; };
   auto sS = [&](int r) { return reinterpret_cast<float*>(sBP(r) + C::BP_BYTES); };
   uint64_t* rfull = reinterpret_cast<uint64_t*>(rbase + (size_t)C::RSTAGES * C::RSTAGE_BYTES);
@@ -216,7 +227,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
           goto done;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(acc * C::BN);
+        const uint32_t d = tmem_base + (uint32_t)(acc * C::BM);
         for (int kb = 0; kb < ncb; ++kb, ++ci) {
           const int cs = ci % C::CSTAGES;
           const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
@@ -225,12 +236,12 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
             goto done;
           }
           tc_fence_after();
-          const uint32_t a = smem_u32(sA16(cs)), bh = smem_u32(sBH(cs)), bl = smem_u32(sBL(cs));
+          const uint32_t a = smem_u32(sA16(cs));
+          const uint32_t w = tmem_base + (uint32_t)(C::ACC_COLS + cs * C::WCOLS);
 #pragma unroll
-          for (int kk = 0; kk < C::BK / 16; ++kk) {  // K = 16 f16 per MMA = 32 bytes of the 128-byte row
-            mma_f16(d, desc_kmajor_sw128(a + kk * 32), desc_kmajor_sw128(bh + kk * 32), C::IDESC,
-                    (kb | kk) != 0 ? 1u : 0u);
-            mma_f16(d, desc_kmajor_sw128(a + kk * 32), desc_kmajor_sw128(bl + kk * 32), C::IDESC, 1u);
+          for (int kk = 0; kk < C::BK / 16; ++kk) {  // K = 16 f16 per MMA: 8 TMEM columns, 32 smem bytes
+            mma_f16_ta(d, w + kk * 8, desc_kmajor_sw128(a + kk * 32), C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+            mma_f16_ta(d, w + 32 + kk * 8, desc_kmajor_sw128(a + kk * 32), C::IDESC, 1u);
           }
           tc_commit(&cempty[cs]);
         }
@@ -258,10 +269,11 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       }
     }
   } else if (warp < 3 + C::CONV_WARPS) {
-    // converter thread: weight row cr of the tile, group ch of the 64-k block
-    const int t = threadIdx.x - 96;
-    const int cr = t >> 1, ch = t & 1;
-    const int sw_r = cr & 7;
+    // converter: TMEM lane quadrant q = warp % 4 (the lanes this warp may
+    // write), weight row cr = 32q + lane of the tile, 16-k quarter cq of the
+    // 64-k block (group cq / 2 of the block, half cq % 2 of the group)
+    const int q = warp & 3, cq = (warp - 3) >> 2;
+    const int cr = q * 32 + lane, g = cq >> 1;
     int ci = 0;
     KbCursor cur;
     cur.start(tiles_m);
@@ -278,26 +290,28 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
           kernel_fail(status, abort_flag, kDevTimeoutProducer);
           goto done;
         }
-        // 16 packed bytes = 32 nibbles of group (2h + ch); the raw tile is
-        // TMA-swizzled (64 B: chunk j of row r at j ^ ((r >> 1) & 3))
-        const uint4 w = *reinterpret_cast<const uint4*>(sBP(rs) + cr * (C::RBK / 2) +
-                                                       (((2 * h + ch) ^ ((cr >> 1) & 3)) << 4));
-        const float swc = __fmul_rn(sS(rs)[cr * C::RGROUPS + 2 * h + ch], cval);  // exact: cval = 2^e
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        uint8_t* dh = sBH(cs) + cr * 128;
-        uint8_t* dl = sBL(cs) + cr * 128;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          uint4 hi, lo;
-          split_pair(nib_pair_to_f16<0>(ws[e]), swc, hi.x, lo.x);
-          split_pair(nib_pair_to_f16<1>(ws[e]), swc, hi.y, lo.y);
-          split_pair(nib_pair_to_f16<2>(ws[e]), swc, hi.z, lo.z);
-          split_pair(nib_pair_to_f16<3>(ws[e]), swc, hi.w, lo.w);
-          const int off = ((4 * ch + e) ^ sw_r) << 4;
-          *reinterpret_cast<uint4*>(dh + off) = hi;
-          *reinterpret_cast<uint4*>(dl + off) = lo;
-        }
-        fence_proxy_async_smem();
+        tc_fence_after();
+        // 8 packed bytes = 16 nibbles; the raw tile is TMA-swizzled (64 B:
+        // 16-byte chunk j of row r at j ^ ((r >> 1) & 3))
+        const uint2 w = *reinterpret_cast<const uint2*>(sBP(rs) + cr * (C::RBK / 2) +
+                                                       (((2 * h + g) ^ ((cr >> 1) & 3)) << 4) + 8 * (cq & 1));
+        const float swc = __fmul_rn(sS(rs)[cr * C::RGROUPS + 2 * h + g], cval);  // exact: cval = 2^e
+        uint32_t hi[8], lo[8];
+        split_pair(nib_pair_to_f16<0>(w.x), swc, hi[0], lo[0]);
+        split_pair(nib_pair_to_f16<1>(w.x), swc, hi[1], lo[1]);
+        split_pair(nib_pair_to_f16<2>(w.x), swc, hi[2], lo[2]);
+        split_pair(nib_pair_to_f16<3>(w.x), swc, hi[3], lo[3]);
+        split_pair(nib_pair_to_f16<0>(w.y), swc, hi[4], lo[4]);
+        split_pair(nib_pair_to_f16<1>(w.y), swc, hi[5], lo[5]);
+        split_pair(nib_pair_to_f16<2>(w.y), swc, hi[6], lo[6]);
+        split_pair(nib_pair_to_f16<3>(w.y), swc, hi[7], lo[7]);
+        // k-block columns: hi k = 2c, 2c+1 at column c (c < 32), lo at 32 + c
+        const uint32_t taddr =
+            tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::ACC_COLS + cs * C::WCOLS + cq * 8);
+        tmem_st8(taddr, hi);
+        tmem_st8(taddr + 32, lo);
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&cfull[cs]);
@@ -306,50 +320,43 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       }
     }
   } else {
-    // Epilogue: TMEM lane quadrant q = warp % 4 = tile rows 32q .. 32q+31.
-    const int q = warp & 3;
+    // Epilogue: TMEM lane quadrant q = warp % 4 = output columns 32q .. 32q+31
+    // of the tile (one per thread); TMEM columns = output rows, half eh of them.
+    const int q = warp & 3, eh = (warp - 3 - C::CONV_WARPS) >> 2;
     int acc = 0;
     uint32_t aphase = 0;
     KbCursor cur;
     cur.start(tiles_m);
     for (int tt = 0; tt < my_tiles; ++tt, cur.next(1, tiles_m, step_m, step_n)) {
-      const int row = cur.tm * C::BM + q * 32 + lane;
-      const float sar = row < M ? __ldg(sa + row) : 0.0f;
+      const int col = cur.tn * C::BN + q * 32 + lane;
+      // prefetch while the MMAs run
+      const float icn = col < N ? __ldg(colscale + N + col) : 0.0f;  // 1 / c_n, exact
+      const float bn = (bias && col < N) ? __ldg(bias + col) : 0.0f;
+      float sav[2];  // lane l holds sa of row tm*BM + 32c + l, c = 2eh + i
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int rr = cur.tm * C::BM + (2 * eh + i) * 32 + lane;
+        sav[i] = rr < M ? __ldg(sa + rr) : 0.0f;
+      }
       if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
         kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
         goto done;
       }
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < C::BN / 32; ++c) {
-        const int col0 = cur.tn * C::BN + c * 32;
-        if (col0 >= N) break;  // uniform across the warp
-        const int cl = col0 + lane;
-        const float icl = cl < N ? __fdiv_rn(1.0f, __ldg(colscale + cl)) : 0.0f;  // exact: 2^-e
-        const float bl = (bias && cl < N) ? __ldg(bias + cl) : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int c = 2 * eh + i;
+        const int row0 = cur.tm * C::BM + c * 32;
+        if (row0 >= M) break;  // uniform across the warp
         uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BN + c * 32), r);
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BM + c * 32), r);
         tmem_ld_wait();
-        float* yrow = Y + (size_t)row * N + col0;
-        const bool vec = (N & 3) == 0 && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(Y) & 15u) == 0;
+        float* ycol = Y + (size_t)row0 * N + col;
 #pragma unroll
-        for (int i4 = 0; i4 < 8; ++i4) {
-          float y[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = 4 * i4 + e;
-            const float v = __fmul_rn(__uint_as_float(r[j]), __shfl_sync(0xffffffffu, icl, j));
-            y[e] = __fadd_rn(__fmul_rn(v, sar), __shfl_sync(0xffffffffu, bl, j));
-          }
-          if (row < M) {
-            if (vec) {
-              *reinterpret_cast<float4*>(yrow + 4 * i4) = make_float4(y[0], y[1], y[2], y[3]);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (col0 + 4 * i4 + e < N) yrow[4 * i4 + e] = y[e];
-            }
-          }
+        for (int j = 0; j < 32; ++j) {
+          const float v = __fmul_rn(__uint_as_float(r[j]), icn);
+          const float y = __fadd_rn(__fmul_rn(v, __shfl_sync(0xffffffffu, sav[i], j)), bn);
+          if (col < N && row0 + j < M) ycol[(size_t)j * N] = y;  // a warp writes 32 adjacent columns
         }
       }
       tc_fence_before();

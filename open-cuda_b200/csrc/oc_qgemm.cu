@@ -389,7 +389,6 @@ int run_w4a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const ui
 // per-column range factors and f16 activations of the dequantizing W4A8
 // GEMM, one buffer each per (device, stream)
 static StreamScratch g_w4_colscale, g_w4_a16;
-
 static bool w4_split_ok(int m, int k, int group, const void* sw, const void* wq) {
   return m > kSkinnyM && is_sm100() && group == 32 && k % I4Split::RBK == 0 && aligned16(sw) && aligned16(wq);
 }
@@ -398,7 +397,7 @@ static bool w4_split_ok(int m, int k, int group, const void* sw, const void* wq)
 int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq, const float* sw,
                    const float* bias, float* Y, cudaStream_t s) {
   using C = I4Split;
-  float* cs = g_w4_colscale.get((size_t)n, s);
+  float* cs = g_w4_colscale.get((size_t)2 * n, s);
   if (!cs) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
   const int G = k / 32;
   w4_colscale_kernel<<<(n + 7) / 8, 256, 0, s>>>(sw, n, G, cs);

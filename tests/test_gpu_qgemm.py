@@ -108,6 +108,8 @@ QGEMM_SHAPES = [
     (3, 64, 40), (17, 96, 72), (37, 256, 200), (129, 384, 130), (300, 512, 264),
     # 7B-class K
     (8, 3584, 512), (64, 3584, 384),
+    # enough 128 x 256 tiles to fill the GPU, ragged N
+    (1200, 384, 4100),
 ]
 
 
