@@ -65,6 +65,8 @@ __global__ void __launch_bounds__(640, 1)
                         const __grid_constant__ CUtensorMap tmS, int M, int N, int K,
                         const float* __restrict__ sa, const float* __restrict__ bias, float* __restrict__ Y,
                         int32_t* __restrict__ acc_out, int* status) {
+  pdl_wait();
+  pdl_launch();
   using C = I4Gemm;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -96,26 +96,17 @@ __device__ __forceinline__ void split_pair(uint32_t w2, float swc, uint32_t& hi2
   lo2 = f32x2_to_f16x2(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
 }
 
-// Position in a CTA's k-block sequence: tile (tm, tn) = blockIdx.x +
-// t * gridDim.x (tm fastest), k-block kb of nkb; advanced without divisions
-// (step_m / step_n = gridDim.x split into whole columns of tiles and rest).
-struct KbCursor {
-  int kb, tm, tn;
-  __device__ __forceinline__ void start(int tiles_m) {
-    kb = 0;
-    tm = (int)blockIdx.x % tiles_m;
-    tn = (int)blockIdx.x / tiles_m;
-  }
-  __device__ __forceinline__ void next(int nkb, int tiles_m, int step_m, int step_n) {
-    if (++kb == nkb) {
-      kb = 0;
-      tm += step_m;
-      tn += step_n;
-      if (tm >= tiles_m) {
-        tm -= tiles_m;
-        ++tn;
-      }
-    }
+// Work item w of the dequantizing kernel: tile w / ksplit (tm fastest) and
+// K slice w % ksplit, covering raw k-blocks [rb0, rb1).
+struct WorkItem {
+  int tm, tn, ks, rb0, rb1;
+  __device__ __forceinline__ void set(int w, int ksplit, int tiles_m, int nrb) {
+    const int tile = w / ksplit;
+    ks = w - tile * ksplit;
+    tm = tile % tiles_m;
+    tn = tile / tiles_m;
+    rb0 = ks * nrb / ksplit;
+    rb1 = (ks + 1) * nrb / ksplit;
   }
 };
 
@@ -124,6 +115,8 @@ struct KbCursor {
 // cs[n] = c_n, cs[N + n] = 1 / c_n (both exact powers of two).  One warp per
 // column.
 __global__ void w4_colscale_kernel(const float* __restrict__ sw, int N, int G, float* __restrict__ cs) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (col >= N) return;
@@ -145,7 +138,10 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     gemm_w4a8_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBp,
                            const __grid_constant__ CUtensorMap tmS, int M, int N, int K,
                            const float* __restrict__ sa, const float* __restrict__ colscale,
-                           const float* __restrict__ bias, float* __restrict__ Y, int* status) {
+                           const float* __restrict__ bias, float* __restrict__ Y, int ksplit,
+                           float* __restrict__ part, int* status) {
+  pdl_wait();
+  pdl_launch();
   using C = I4Split;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -196,39 +192,41 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
   const int tiles_n = (N + C::BN - 1) / C::BN;
   const int ntiles = tiles_m * tiles_n;
   const int nrb = K / C::RBK;  // K % 128 == 0 on this path
-  const int ncb = 2 * nrb;     // k-blocks of 64 per tile
-  const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int step_m = (int)gridDim.x % tiles_m, step_n = (int)gridDim.x / tiles_m;
+  const int nitems = ntiles * ksplit;  // ksplit <= nrb: every item has raw blocks
 
   if (warp == 0) {
     if (lane == 0) {  // raw ring: packed weights and scales
-      KbCursor cur;
-      cur.start(tiles_m);
-      const int total_r = my_tiles * nrb;
-      for (int ri = 0; ri < total_r; ++ri, cur.next(nrb, tiles_m, step_m, step_n)) {
-        const int rs = ri % C::RSTAGES;
-        const uint32_t rph = (uint32_t)(ri / C::RSTAGES) & 1u;
-        if (!mbar_wait(&rempty[rs], rph ^ 1u, abort_flag)) {
-          kernel_fail(status, abort_flag, kDevTimeoutProducer);
-          goto done;
+      int ri = 0;
+      for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+        WorkItem it;
+        it.set(w, ksplit, tiles_m, nrb);
+        for (int rb = it.rb0; rb < it.rb1; ++rb, ++ri) {
+          const int rs = ri % C::RSTAGES;
+          const uint32_t rph = (uint32_t)(ri / C::RSTAGES) & 1u;
+          if (!mbar_wait(&rempty[rs], rph ^ 1u, abort_flag)) {
+            kernel_fail(status, abort_flag, kDevTimeoutProducer);
+            goto done;
+          }
+          mbar_arrive_expect_tx(&rfull[rs], C::BP_BYTES + C::S_BYTES);
+          tma_load_2d(sBP(rs), &tmBp, rb * (C::RBK / 2), it.tn * C::BN, &rfull[rs]);
+          tma_load_2d(sS(rs), &tmS, rb * C::RGROUPS, it.tn * C::BN, &rfull[rs]);
         }
-        mbar_arrive_expect_tx(&rfull[rs], C::BP_BYTES + C::S_BYTES);
-        tma_load_2d(sBP(rs), &tmBp, cur.kb * (C::RBK / 2), cur.tn * C::BN, &rfull[rs]);
-        tma_load_2d(sS(rs), &tmS, cur.kb * C::RGROUPS, cur.tn * C::BN, &rfull[rs]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       int ci = 0, acc = 0;
       uint32_t aphase = 0;
-      for (int t = 0; t < my_tiles; ++t) {
+      for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+        WorkItem it;
+        it.set(w, ksplit, tiles_m, nrb);
         if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) {
           kernel_fail(status, abort_flag, kDevTimeoutMma);
           goto done;
         }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * C::BM);
-        for (int kb = 0; kb < ncb; ++kb, ++ci) {
+        for (int kb = 0; kb < 2 * (it.rb1 - it.rb0); ++kb, ++ci) {
           const int cs = ci % C::CSTAGES;
           const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
           if (!mbar_wait(&cfull[cs], cph, abort_flag)) {
@@ -254,18 +252,20 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     }
   } else if (warp == 2) {
     if (lane == 0) {  // f16 activation tiles straight into the MMA layout
-      KbCursor cur;
-      cur.start(tiles_m);
-      const int total_c = my_tiles * ncb;
-      for (int ci = 0; ci < total_c; ++ci, cur.next(ncb, tiles_m, step_m, step_n)) {
-        const int cs = ci % C::CSTAGES;
-        const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
-        if (!mbar_wait(&cempty[cs], cph ^ 1u, abort_flag)) {
-          kernel_fail(status, abort_flag, kDevTimeoutProducer);
-          goto done;
+      int ci = 0;
+      for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+        WorkItem it;
+        it.set(w, ksplit, tiles_m, nrb);
+        for (int cb = 2 * it.rb0; cb < 2 * it.rb1; ++cb, ++ci) {
+          const int cs = ci % C::CSTAGES;
+          const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
+          if (!mbar_wait(&cempty[cs], cph ^ 1u, abort_flag)) {
+            kernel_fail(status, abort_flag, kDevTimeoutProducer);
+            goto done;
+          }
+          mbar_arrive_expect_tx(&cfull[cs], C::A16_BYTES);
+          tma_load_2d(sA16(cs), &tmA, cb * C::BK, it.tm * C::BM, &cfull[cs]);
         }
-        mbar_arrive_expect_tx(&cfull[cs], C::A16_BYTES);
-        tma_load_2d(sA16(cs), &tmA, cur.kb * C::BK, cur.tm * C::BM, &cfull[cs]);
       }
     }
   } else if (warp < 3 + C::CONV_WARPS) {
@@ -275,12 +275,12 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     const int q = warp & 3, cq = (warp - 3) >> 2;
     const int cr = q * 32 + lane, g = cq >> 1;
     int ci = 0;
-    KbCursor cur;
-    cur.start(tiles_m);
-    for (int tt = 0; tt < my_tiles; ++tt, cur.next(1, tiles_m, step_m, step_n)) {
-      const int col = cur.tn * C::BN + cr;
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+      WorkItem it;
+      it.set(w, ksplit, tiles_m, nrb);
+      const int col = it.tn * C::BN + cr;
       const float cval = col < N ? __ldg(colscale + col) : 1.0f;
-      for (int kb = 0; kb < ncb; ++kb, ++ci) {
+      for (int kb = 0; kb < 2 * (it.rb1 - it.rb0); ++kb, ++ci) {
         const int cs = ci % C::CSTAGES;
         const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
         const int ri = ci >> 1, h = ci & 1;
@@ -325,17 +325,17 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     const int q = warp & 3, eh = (warp - 3 - C::CONV_WARPS) >> 2;
     int acc = 0;
     uint32_t aphase = 0;
-    KbCursor cur;
-    cur.start(tiles_m);
-    for (int tt = 0; tt < my_tiles; ++tt, cur.next(1, tiles_m, step_m, step_n)) {
-      const int col = cur.tn * C::BN + q * 32 + lane;
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+      WorkItem it;
+      it.set(w, ksplit, tiles_m, nrb);
+      const int col = it.tn * C::BN + q * 32 + lane;
       // prefetch while the MMAs run
       const float icn = col < N ? __ldg(colscale + N + col) : 0.0f;  // 1 / c_n, exact
       const float bn = (bias && col < N) ? __ldg(bias + col) : 0.0f;
       float sav[2];  // lane l holds sa of row tm*BM + 32c + l, c = 2eh + i
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const int rr = cur.tm * C::BM + (2 * eh + i) * 32 + lane;
+        const int rr = it.tm * C::BM + (2 * eh + i) * 32 + lane;
         sav[i] = rr < M ? __ldg(sa + rr) : 0.0f;
       }
       if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
@@ -343,19 +343,23 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         goto done;
       }
       tc_fence_after();
+      // K-split: the raw sum of this slice goes to part[ks] (summed in slice
+      // order and finished by gemm_w4a8_splitk_reduce); else the finished y
+      float* out = ksplit > 1 ? part + (size_t)it.ks * M * N : Y;
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int c = 2 * eh + i;
-        const int row0 = cur.tm * C::BM + c * 32;
+        const int row0 = it.tm * C::BM + c * 32;
         if (row0 >= M) break;  // uniform across the warp
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BM + c * 32), r);
         tmem_ld_wait();
-        float* ycol = Y + (size_t)row0 * N + col;
+        float* ycol = out + (size_t)row0 * N + col;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float v = __fmul_rn(__uint_as_float(r[j]), icn);
-          const float y = __fadd_rn(__fmul_rn(v, __shfl_sync(0xffffffffu, sav[i], j)), bn);
+          float y = __uint_as_float(r[j]);
+          if (ksplit == 1)
+            y = __fadd_rn(__fmul_rn(__fmul_rn(y, icn), __shfl_sync(0xffffffffu, sav[i], j)), bn);
           if (col < N && row0 + j < M) ycol[(size_t)j * N] = y;  // a warp writes 32 adjacent columns
         }
       }
@@ -374,6 +378,23 @@ done:
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// Finishes a K-split dequantizing GEMM: y = ((sum_s part[s]) / c_n) * sa + bias,
+// the slices added in slice order.
+__global__ void gemm_w4a8_splitk_reduce(const float* __restrict__ part, int ksplit, int M, int N,
+                                        const float* __restrict__ colscale, const float* __restrict__ sa,
+                                        const float* __restrict__ bias, float* __restrict__ Y) {
+  pdl_wait();
+  pdl_launch();
+  const size_t total = (size_t)M * N, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int row = (int)(i / N), col = (int)(i - (size_t)row * N);
+    float v = 0.0f;
+    for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(part + (size_t)s * total + i));
+    const float y = __fmul_rn(__fmul_rn(v, __ldg(colscale + N + col)), __ldg(sa + row));
+    Y[i] = __fadd_rn(y, bias ? __ldg(bias + col) : 0.0f);
   }
 }
 

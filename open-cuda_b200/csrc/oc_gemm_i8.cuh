@@ -139,6 +139,8 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
                         const float* __restrict__ sa, const float* __restrict__ sw, const float* __restrict__ bias,
                         float* __restrict__ Y, int32_t* __restrict__ acc_out, int* status,
                         const int* __restrict__ offs = nullptr, int G = 0) {
+  pdl_wait();
+  pdl_launch();
   using C = I8Gemm<BN, GROUPED>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -24,15 +24,8 @@
 
 namespace oc {
 
-// Programmatic dependent launch: the decode kernels are launched with
-// programmatic stream serialization, so a kernel may start while its
-// predecessor drains.  pdl_wait() returns once every predecessor grid has
-// completed and its memory is visible; nothing a predecessor writes is read
-// before it, and nothing a predecessor reads is written before it.
-// pdl_launch() lets the successor be scheduled.  Without the launch
-// attribute both are no-ops.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// pdl_wait / pdl_launch (oc_ptx.cuh): the decode kernels are launched with
+// programmatic stream serialization.
 
 
 // ---- SplitMix64 weights (llm:178-206, 635-646) ------------------------------

@@ -105,6 +105,24 @@ struct StreamScratch {
   }
 };
 
+// Launches `kern` with programmatic stream serialization (the kernel must
+// begin with pdl_wait(), oc_ptx.cuh); returns the launch status.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                 Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Makes `dev` current for the scope, restoring the previous device after.
 struct Scope {
   int prev = -1;

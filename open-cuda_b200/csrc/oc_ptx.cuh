@@ -9,6 +9,16 @@
 
 namespace oc {
 
+// Programmatic dependent launch: kernels launched with programmatic stream
+// serialization (launch_pdl_ex, oc_internal.h) may be scheduled while their
+// predecessor on the stream drains.  pdl_wait() returns once every
+// predecessor grid has completed and its memory is visible, so a kernel
+// that calls it before touching global memory reads nothing early and
+// overwrites nothing still in use.  pdl_launch() lets the successor be
+// scheduled.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Error words a kernel writes to its status slot instead of trapping.
 enum : int {
   kDevOk = 0,

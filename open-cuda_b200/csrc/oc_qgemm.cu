@@ -33,6 +33,8 @@ __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, c
                                                           const float* __restrict__ sw,
                                                           const float* __restrict__ bias, float* __restrict__ Y,
                                                           int32_t* __restrict__ acc_out) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ int4 s_qa4[];
   const int nchunk = k >> 4;
   for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x)
@@ -99,6 +101,8 @@ __global__ void w8a8_generic_kernel(int m, int n, int k, const int8_t* __restric
                                     const int8_t* __restrict__ wq, const float* __restrict__ sw,
                                     const float* __restrict__ bias, float* __restrict__ Y,
                                     int32_t* __restrict__ acc_out) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const size_t warps = ((size_t)gridDim.x * blockDim.x) >> 5;
   for (size_t o = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < (size_t)m * n; o += warps) {
@@ -144,6 +148,8 @@ __global__ void __launch_bounds__(kW4Warps * 32) w4a8_skinny_kernel(int m, int n
                                                                     const float* __restrict__ bias,
                                                                     float* __restrict__ Y,
                                                                     int32_t* __restrict__ acc_out) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ int s_dyn[];
   const int nch = k >> 5;         // 32-element chunks per row
   const int ng = k / group, cpg = group >> 5;
@@ -227,6 +233,11 @@ static int launch_err(const char* what) {
   return e == cudaSuccess ? OC_OK : from_cuda(e, what);
 }
 
+static int launch_rc(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return from_cuda(e, what);
+  return launch_err(what);
+}
+
 static int grid_cols(int n, int cols_per_block) {
   int want = (n + cols_per_block - 1) / cols_per_block;
   int cap = std::max(1, sm_count()) * 8;
@@ -237,25 +248,22 @@ int run_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, cons
                     const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
   const bool vec = (k % 16 == 0) && aligned16(qa) && aligned16(wq);
   if (!vec || m > kSkinnyM) {
-    w8a8_generic_kernel<<<std::max(1, sm_count()) * 8, 256, 0, s>>>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out);
-    return launch_err("w8a8_generic_kernel");
+    return launch_rc(launch_pdl_ex(w8a8_generic_kernel, dim3(std::max(1, sm_count()) * 8), dim3(256), 0, s, m, n, k,
+                                   qa, sa, wq, sw, bias, Y, acc_out),
+                     "w8a8_generic_kernel");
   }
   const size_t smem = (size_t)m * k;
   if (smem > 200 * 1024) return fail(OC_ERR_NOT_SUPPORTED, "w8a8 skinny: m*k too large for shared memory");
   const int grid = grid_cols(n, 8);
   auto launch = [&](auto kern) {
     smem_attr_once(reinterpret_cast<const void*>(kern), 200 * 1024);
-    kern<<<grid, 256, smem, s>>>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out);
+    return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(256), smem, s, m, n, k, qa, sa, wq, sw, bias, Y, acc_out),
+                     "w8a8_skinny_kernel");
   };
-  if (m <= 1)
-    launch(w8a8_skinny_kernel<1>);
-  else if (m <= 4)
-    launch(w8a8_skinny_kernel<4>);
-  else if (m <= 8)
-    launch(w8a8_skinny_kernel<8>);
-  else
-    launch(w8a8_skinny_kernel<16>);
-  return launch_err("w8a8_skinny_kernel");
+  if (m <= 1) return launch(w8a8_skinny_kernel<1>);
+  if (m <= 4) return launch(w8a8_skinny_kernel<4>);
+  if (m <= 8) return launch(w8a8_skinny_kernel<8>);
+  return launch(w8a8_skinny_kernel<16>);
 }
 
 int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const float* sa, const uint8_t* wq,
@@ -268,17 +276,14 @@ int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const floa
   const int grid = std::max(1, std::min((n + kW4Warps - 1) / kW4Warps, std::max(1, sm_count()) * 8));
   auto launch = [&](auto kern) {
     smem_attr_once(reinterpret_cast<const void*>(kern), 200 * 1024);
-    kern<<<grid, kW4Warps * 32, smem, s>>>(m, n, k, group, qa, sa, wq, sw, bias, Y, acc_out);
+    return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(kW4Warps * 32), smem, s, m, n, k, group, qa, sa, wq, sw,
+                                   bias, Y, acc_out),
+                     "w4a8_skinny_kernel");
   };
-  if (mr == 1)
-    launch(w4a8_skinny_kernel<1>);
-  else if (mr == 4)
-    launch(w4a8_skinny_kernel<4>);
-  else if (mr == 8)
-    launch(w4a8_skinny_kernel<8>);
-  else
-    launch(w4a8_skinny_kernel<16>);
-  return launch_err("w4a8_skinny_kernel");
+  if (mr == 1) return launch(w4a8_skinny_kernel<1>);
+  if (mr == 4) return launch(w4a8_skinny_kernel<4>);
+  if (mr == 8) return launch(w4a8_skinny_kernel<8>);
+  return launch(w4a8_skinny_kernel<16>);
 }
 
 // Picks the tile width with the fewest (waves x tile width) units.
@@ -316,9 +321,10 @@ static int launch_w8a8_tc(int m, int n, int k, const int8_t* qa, const float* sa
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w8a8_tc_kernel) failed");
   const int tiles = ((m + C::BM - 1) / C::BM) * ((n + BN - 1) / BN);
   const int grid = std::min(tiles, std::max(1, sm_count()));
-  gemm_w8a8_tc_kernel<BN><<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, ty, y_tma, m, n, k, sa, sw, bias, Y, acc_out,
-                                                            device_status_word());
-  return launch_err("gemm_w8a8_tc_kernel");
+  return launch_rc(launch_pdl_ex(gemm_w8a8_tc_kernel<BN>, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tb, ty, y_tma,
+                                 m, n, k, sa, sw, bias, Y, acc_out, device_status_word(),
+                                 static_cast<const int*>(nullptr), 0),
+                   "gemm_w8a8_tc_kernel");
 }
 
 // Grouped GEMM: tiles are scheduled on the device from offs (G+1 row
@@ -348,9 +354,9 @@ int run_grouped_w8a8_tc(int R, int N, int K, const int8_t* xg, const float* sg, 
   // upper bound on tiles: every group adds at most one partial 128-row tile
   const long max_tiles = ((long)(R + 127) / 128 + G) * ((N + BN - 1) / BN);
   const int grid = (int)std::min<long>(max_tiles, std::max(1, sm_count()));
-  kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, ty, y_tma, R, N, K, sg, sw, bias, Y, nullptr, device_status_word(),
-                                         offs, G);
-  return launch_err("grouped gemm_w8a8_tc_kernel");
+  return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tb, ty, y_tma, R, N, K, sg, sw,
+                                 bias, Y, static_cast<int32_t*>(nullptr), device_status_word(), offs, G),
+                   "grouped gemm_w8a8_tc_kernel");
 }
 
 int run_w8a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq, const float* sw,
@@ -378,17 +384,16 @@ int run_w4a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const ui
       return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_tc_kernel) failed");
     const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
     const int grid = std::min(tiles, std::max(1, sm_count()));
-    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tbp, tsc, m, n, k, sa, bias, Y, acc_out, device_status_word());
-    return OC_OK;
+    return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc, m, n, k, sa, bias, Y,
+                                   acc_out, device_status_word()),
+                     "gemm_w4a8_tc_kernel");
   };
-  rc = acc_out ? go(gemm_w4a8_tc_kernel<true>) : go(gemm_w4a8_tc_kernel<false>);
-  if (rc) return rc;
-  return launch_err("gemm_w4a8_tc_kernel");
+  return acc_out ? go(gemm_w4a8_tc_kernel<true>) : go(gemm_w4a8_tc_kernel<false>);
 }
 
 // per-column range factors and f16 activations of the dequantizing W4A8
 // GEMM, one buffer each per (device, stream)
-static StreamScratch g_w4_colscale, g_w4_a16;
+static StreamScratch g_w4_colscale, g_w4_a16, g_w4_part;
 static bool w4_split_ok(int m, int k, int group, const void* sw, const void* wq) {
   return m > kSkinnyM && is_sm100() && group == 32 && k % I4Split::RBK == 0 && aligned16(sw) && aligned16(wq);
 }
@@ -400,9 +405,11 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   float* cs = g_w4_colscale.get((size_t)2 * n, s);
   if (!cs) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
   const int G = k / 32;
-  w4_colscale_kernel<<<(n + 7) / 8, 256, 0, s>>>(sw, n, G, cs);
+  int rc = launch_rc(launch_pdl_ex(w4_colscale_kernel, dim3((n + 7) / 8), dim3(256), 0, s, sw, n, G, cs),
+                     "w4_colscale_kernel");
+  if (rc) return rc;
   CUtensorMap ta, tbp, tsc;
-  int rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
+  rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
                         C::BK, C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tbp, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, (uint64_t)k / 2,
@@ -413,11 +420,24 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   if (rc) return rc;
   if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_split_kernel), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_split_kernel) failed");
+  const int sms = std::max(1, sm_count());
   const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
-  const int grid = std::min(tiles, std::max(1, sm_count()));
-  gemm_w4a8_split_kernel<<<grid, C::THREADS, C::SMEM, s>>>(ta, tbp, tsc, m, n, k, sa, cs, bias, Y,
-                                                           device_status_word());
-  return launch_err("gemm_w4a8_split_kernel");
+  // too few tiles to fill the GPU: split K (deterministic, finished by a reduction kernel)
+  const int ksplit = std::max(1, std::min(k / C::RBK, std::min(8, sms / tiles)));
+  float* part = nullptr;
+  if (ksplit > 1) {
+    part = g_w4_part.get((size_t)ksplit * m * n, s);
+    if (!part) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
+  }
+  const int grid = std::min(tiles * ksplit, sms);
+  rc = launch_rc(launch_pdl_ex(gemm_w4a8_split_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc, m, n, k,
+                               sa, cs, bias, Y, ksplit, part, device_status_word()),
+                 "gemm_w4a8_split_kernel");
+  if (rc || ksplit == 1) return rc;
+  const size_t total = (size_t)m * n;
+  const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
+  return launch_rc(launch_pdl_ex(gemm_w4a8_splitk_reduce, dim3(rb), dim3(256), 0, s, part, ksplit, m, n, cs, sa, bias, Y),
+                   "gemm_w4a8_splitk_reduce");
 }
 
 }  // namespace oc

