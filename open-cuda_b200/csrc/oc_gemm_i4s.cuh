@@ -50,7 +50,9 @@ struct I4Split {
   static constexpr int THREADS = 32 * (3 + CONV_WARPS + EPI_WARPS);
   static constexpr int ACC_COLS = 2 * BM;        // two accumulators (transposed tiles: BM columns)
   static constexpr int TMEM_COLS = 512;
-  static constexpr size_t SMEM = 1024 + (size_t)CSTAGES * A16_BYTES + (size_t)RSTAGES * RSTAGE_BYTES + 512;
+  static constexpr int YSTAGE_BYTES = EPI_WARPS * 2 * 4096;  // two 32x32 f32 output blocks per epilogue warp
+  static constexpr size_t SMEM =
+      1024 + (size_t)CSTAGES * A16_BYTES + (size_t)RSTAGES * RSTAGE_BYTES + YSTAGE_BYTES + 512;
   static constexpr uint32_t IDESC = idesc_f16(BN, BM);  // MMA M = weight rows, N = activation rows
   static_assert(ACC_COLS + CSTAGES * WCOLS <= TMEM_COLS, "tensor memory budget");
   static_assert(RSTAGE_BYTES % 1024 == 0 && A16_BYTES % 1024 == 0, "1024-byte stage alignment");
@@ -112,34 +114,30 @@ struct WorkItem {
 
 // Per-column range factor c_n = 2^(11 - e) with e the exponent of
 // max_j |sw[n][j]|, so |(nib - 8) * sw * c_n| < 8 * 2^(e+1) * 2^(11-e) = 2^15;
-// cs[n] = c_n, cs[N + n] = 1 / c_n (both exact powers of two).  One warp per
-// column.
-__global__ void w4_colscale_kernel(const float* __restrict__ sw, int N, int G, float* __restrict__ cs) {
-  pdl_wait();
-  pdl_launch();
-  const int lane = threadIdx.x & 31;
-  const int col = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (col >= N) return;
+// returns log2(c_n), clamped so that c_n and 1 / c_n are normal floats (0 for
+// an all-zero or non-finite column).  G % 4 == 0 and the row is 16-byte
+// aligned on this path.
+__device__ __forceinline__ int col_range_exp(const float* __restrict__ sw_row, int G) {
+  const float4* r4 = reinterpret_cast<const float4*>(sw_row);
   float mx = 0.0f;
-  for (int j = lane; j < G; j += 32) mx = fmaxf(mx, fabsf(sw[(size_t)col * G + j]));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) {
-    int e = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;  // subnormal or zero: -127
-    int ce = 11 - e;
-    ce = ce < -126 ? -126 : (ce > 126 ? 126 : ce);
-    if (!(mx > 0.0f && mx <= 3.0e38f)) ce = 0;
-    cs[col] = __uint_as_float((uint32_t)(ce + 127) << 23);
-    cs[N + col] = __uint_as_float((uint32_t)(127 - ce) << 23);
+  for (int j = 0; j < G / 4; ++j) {
+    const float4 v = __ldg(r4 + j);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
+  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;  // subnormal or zero: -127
+  const int ce = 11 - e;
+  if (!(mx > 0.0f && mx <= 3.0e38f)) return 0;
+  return ce < -126 ? -126 : (ce > 126 ? 126 : ce);
 }
+__device__ __forceinline__ float exp2_int(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
 __global__ void __launch_bounds__(I4Split::THREADS, 1)
     gemm_w4a8_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBp,
-                           const __grid_constant__ CUtensorMap tmS, int M, int N, int K,
-                           const float* __restrict__ sa, const float* __restrict__ colscale,
+                           const __grid_constant__ CUtensorMap tmS,
+                           const __grid_constant__ CUtensorMap tmOut, int out_tma, int M, int N, int K,
+                           const float* __restrict__ sa, const float* __restrict__ sw,
                            const float* __restrict__ bias, float* __restrict__ Y, int ksplit,
-                           float* __restrict__ part, int* status) {
+                           float* __restrict__ part, int slice_rows, int* status) {
   pdl_wait();
   pdl_launch();
   using C = I4Split;
@@ -150,7 +148,8 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
   auto sA16 = [&](int c) { return cbase + (size_t)c * C::A16_BYTES; };
   auto sBP = [&](int r) { return rbase + (size_t)r * C::RSTAGE_BYTES; };
   auto sS = [&](int r) { return reinterpret_cast<float*>(sBP(r) + C::BP_BYTES); };
-  uint64_t* rfull = reinterpret_cast<uint64_t*>(rbase + (size_t)C::RSTAGES * C::RSTAGE_BYTES);
+  uint8_t* const ystage = rbase + (size_t)C::RSTAGES * C::RSTAGE_BYTES;
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(ystage + C::YSTAGE_BYTES);
   uint64_t* rempty = rfull + C::RSTAGES;
   uint64_t* cfull = rempty + C::RSTAGES;
   uint64_t* cempty = cfull + C::CSTAGES;
@@ -178,6 +177,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmBp);
     prefetch_tmap(&tmS);
+    if (out_tma) prefetch_tmap(&tmOut);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       WorkItem it;
       it.set(w, ksplit, tiles_m, nrb);
       const int col = it.tn * C::BN + cr;
-      const float cval = col < N ? __ldg(colscale + col) : 1.0f;
+      const float cval = col < N ? exp2_int(col_range_exp(sw + (size_t)col * (K / 32), K / 32)) : 1.0f;
       for (int kb = 0; kb < 2 * (it.rb1 - it.rb0); ++kb, ++ci) {
         const int cs = ci % C::CSTAGES;
         const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
@@ -322,15 +322,20 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
   } else {
     // Epilogue: TMEM lane quadrant q = warp % 4 = output columns 32q .. 32q+31
     // of the tile (one per thread); TMEM columns = output rows, half eh of them.
-    const int q = warp & 3, eh = (warp - 3 - C::CONV_WARPS) >> 2;
-    int acc = 0;
+    // Each 32x32 block goes through shared memory to one TMA store (rows and
+    // columns outside the output are clipped by the TMA unit), or, when the
+    // output rows are not 16-byte multiples, straight to global memory.
+    const int ew = warp - 3 - C::CONV_WARPS;
+    const int q = warp & 3, eh = ew >> 2;
+    int acc = 0, ybuf = 0;
     uint32_t aphase = 0;
     for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
       WorkItem it;
       it.set(w, ksplit, tiles_m, nrb);
-      const int col = it.tn * C::BN + q * 32 + lane;
-      // prefetch while the MMAs run
-      const float icn = col < N ? __ldg(colscale + N + col) : 0.0f;  // 1 / c_n, exact
+      const int col0 = it.tn * C::BN + q * 32;
+      const int col = col0 + lane;
+      // prefetch while the MMAs run (1 / c_n: a power of two)
+      const float icn = col < N ? exp2_int(-col_range_exp(sw + (size_t)col * (K / 32), K / 32)) : 0.0f;
       const float bn = (bias && col < N) ? __ldg(bias + col) : 0.0f;
       float sav[2];  // lane l holds sa of row tm*BM + 32c + l, c = 2eh + i
 #pragma unroll
@@ -343,9 +348,11 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         goto done;
       }
       tc_fence_after();
-      // K-split: the raw sum of this slice goes to part[ks] (summed in slice
-      // order and finished by gemm_w4a8_splitk_reduce); else the finished y
-      float* out = ksplit > 1 ? part + (size_t)it.ks * M * N : Y;
+      // K-split: this slice's sum / c_n goes to slice ks of part (rows
+      // [ks * slice_rows, ks * slice_rows + M)), summed in slice order and
+      // finished by gemm_w4a8_splitk_reduce; else the finished y
+      const int out_row = ksplit > 1 ? it.ks * slice_rows : 0;
+      float* out = ksplit > 1 ? part : Y;
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int c = 2 * eh + i;
@@ -354,13 +361,34 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BM + c * 32), r);
         tmem_ld_wait();
-        float* ycol = out + (size_t)row0 * N + col;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           float y = __uint_as_float(r[j]);
-          if (ksplit == 1)
-            y = __fadd_rn(__fmul_rn(__fmul_rn(y, icn), __shfl_sync(0xffffffffu, sav[i], j)), bn);
-          if (col < N && row0 + j < M) ycol[(size_t)j * N] = y;  // a warp writes 32 adjacent columns
+          y = __fmul_rn(y, icn);  // exact: a power of two
+          if (ksplit == 1) y = __fadd_rn(__fmul_rn(y, __shfl_sync(0xffffffffu, sav[i], j)), bn);
+          r[j] = __float_as_uint(y);
+        }
+        if (out_tma) {
+          // block row j = output row row0 + j, 128 bytes, 16-byte chunk cc at
+          // cc ^ (j % 8) (128-byte swizzle); lane = column: conflict-free rows
+          uint8_t* buf = ystage + (size_t)(ew * 2 + (ybuf & 1)) * 4096;
+          if (lane == 0) bulk_wait_read<1>();  // the store that last used buf has read it
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            *reinterpret_cast<uint32_t*>(buf + j * 128 + ((((lane >> 2) ^ j) & 7) << 4) + (lane & 3) * 4) = r[j];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmOut, buf, col0, out_row + row0);
+            bulk_commit();
+          }
+          ++ybuf;
+        } else {
+          float* ycol = out + (size_t)(out_row + row0) * N + col;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)  // a warp writes 32 adjacent columns
+            if (col < N && row0 + j < M) ycol[(size_t)j * N] = __uint_as_float(r[j]);
         }
       }
       tc_fence_before();
@@ -371,6 +399,8 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         aphase ^= 1u;
       }
     }
+    if (out_tma && lane == 0) bulk_wait<0>();  // all output stores complete
+    __syncwarp();
   }
 done:
   tc_fence_before();
@@ -381,19 +411,19 @@ done:
   }
 }
 
-// Finishes a K-split dequantizing GEMM: y = ((sum_s part[s]) / c_n) * sa + bias,
-// the slices added in slice order.
-__global__ void gemm_w4a8_splitk_reduce(const float* __restrict__ part, int ksplit, int M, int N,
-                                        const float* __restrict__ colscale, const float* __restrict__ sa,
+// Finishes a K-split dequantizing GEMM: y = (sum_s part[s]) * sa + bias, the
+// slices (each already divided by c_n, exactly) added in slice order.
+__global__ void gemm_w4a8_splitk_reduce(const float* __restrict__ part, int ksplit, int slice_rows, int M, int N,
+                                        const float* __restrict__ sa,
                                         const float* __restrict__ bias, float* __restrict__ Y) {
   pdl_wait();
   pdl_launch();
-  const size_t total = (size_t)M * N, stride = (size_t)gridDim.x * blockDim.x;
+  const size_t total = (size_t)M * N, slice = (size_t)slice_rows * N, stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += stride) {
     const int row = (int)(i / N), col = (int)(i - (size_t)row * N);
     float v = 0.0f;
-    for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(part + (size_t)s * total + i));
-    const float y = __fmul_rn(__fmul_rn(v, __ldg(colscale + N + col)), __ldg(sa + row));
+    for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(part + (size_t)s * slice + i));
+    const float y = __fmul_rn(v, __ldg(sa + row));
     Y[i] = __fadd_rn(y, bias ? __ldg(bias + col) : 0.0f);
   }
 }

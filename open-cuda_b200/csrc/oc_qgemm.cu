@@ -391,9 +391,9 @@ int run_w4a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const ui
   return acc_out ? go(gemm_w4a8_tc_kernel<true>) : go(gemm_w4a8_tc_kernel<false>);
 }
 
-// per-column range factors and f16 activations of the dequantizing W4A8
-// GEMM, one buffer each per (device, stream)
-static StreamScratch g_w4_colscale, g_w4_a16, g_w4_part;
+// f16 activations and K-split partial sums of the dequantizing W4A8 GEMM,
+// one buffer each per (device, stream)
+static StreamScratch g_w4_a16, g_w4_part;
 static bool w4_split_ok(int m, int k, int group, const void* sw, const void* wq) {
   return m > kSkinnyM && is_sm100() && group == 32 && k % I4Split::RBK == 0 && aligned16(sw) && aligned16(wq);
 }
@@ -402,14 +402,9 @@ static bool w4_split_ok(int m, int k, int group, const void* sw, const void* wq)
 int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq, const float* sw,
                    const float* bias, float* Y, cudaStream_t s) {
   using C = I4Split;
-  float* cs = g_w4_colscale.get((size_t)2 * n, s);
-  if (!cs) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
   const int G = k / 32;
-  int rc = launch_rc(launch_pdl_ex(w4_colscale_kernel, dim3((n + 7) / 8), dim3(256), 0, s, sw, n, G, cs),
-                     "w4_colscale_kernel");
-  if (rc) return rc;
   CUtensorMap ta, tbp, tsc;
-  rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
+  int rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
                         C::BK, C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tbp, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, (uint64_t)k / 2,
@@ -424,19 +419,32 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
   // too few tiles to fill the GPU: split K (deterministic, finished by a reduction kernel)
   const int ksplit = std::max(1, std::min(k / C::RBK, std::min(8, sms / tiles)));
+  const int slice_rows = (m + 31) / 32 * 32;  // a 32-row output block never crosses a slice
   float* part = nullptr;
   if (ksplit > 1) {
-    part = g_w4_part.get((size_t)ksplit * m * n, s);
+    part = g_w4_part.get((size_t)ksplit * slice_rows * n, s);
     if (!part) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
   }
+  // outputs leave through 32x32 TMA stores when rows are 16-byte multiples
+  CUtensorMap tout = tsc;
+  int out_tma = 0;
+  if (n % 4 == 0 && (ksplit > 1 || aligned16(Y))) {
+    float* base = ksplit > 1 ? part : Y;
+    const uint64_t rows = ksplit > 1 ? (uint64_t)ksplit * slice_rows : (uint64_t)m;
+    rc = make_tmap_2d(&tout, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)n, rows, (uint64_t)n * 4, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    out_tma = 1;
+  }
   const int grid = std::min(tiles * ksplit, sms);
-  rc = launch_rc(launch_pdl_ex(gemm_w4a8_split_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc, m, n, k,
-                               sa, cs, bias, Y, ksplit, part, device_status_word()),
+  rc = launch_rc(launch_pdl_ex(gemm_w4a8_split_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc, tout,
+                               out_tma, m, n, k, sa, sw, bias, Y, ksplit, part, slice_rows, device_status_word()),
                  "gemm_w4a8_split_kernel");
   if (rc || ksplit == 1) return rc;
   const size_t total = (size_t)m * n;
   const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
-  return launch_rc(launch_pdl_ex(gemm_w4a8_splitk_reduce, dim3(rb), dim3(256), 0, s, part, ksplit, m, n, cs, sa, bias, Y),
+  return launch_rc(launch_pdl_ex(gemm_w4a8_splitk_reduce, dim3(rb), dim3(256), 0, s, part, ksplit, slice_rows, m, n,
+                                 sa, bias, Y),
                    "gemm_w4a8_splitk_reduce");
 }
 
