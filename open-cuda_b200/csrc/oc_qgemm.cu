@@ -22,10 +22,40 @@ constexpr int kSkinnyM = 16;
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// ---- skinny W8A8: one warp per output column, all m rows at once ---------
-// qa is staged in shared memory; each lane owns 16-byte K chunks
-// lane, lane+32, ...; the exact int32 dot products are reduced with warp
-// shuffles.  Requires k % 16 == 0 and 16-byte aligned qa / Wq.
+// ---- skinny W8A8 (m <= 16): exact int32 dot products on the CUDA cores ----
+// A warp owns COLS = 2 output columns; lane l reads the 16-byte K chunks
+// l, l + 32, ... of both, so each weight byte is loaded once, coalesced, and
+// the next chunk is in flight while the current one is multiplied.  Every
+// lane keeps COLS x MR partial dot products; a transposing butterfly (each
+// exchange step halves the values a lane holds: it keeps one half and adds
+// its partner's copy of that half) leaves lane l with the complete sum of
+// value l >> (5 - H), 2^H = COLS x MR, in 2^H - 1 shuffles instead of
+// 5 x 2^H.  Integer sums are exact, so the result does not depend on the
+// order.  The activation rows are staged in shared memory once per block
+// while the first weight chunks are already on their way.
+constexpr int kSkinnyCols = 2;
+
+template <int V>
+__device__ __forceinline__ int butterfly_sum(int (&v)[V], int lane) {
+  constexpr int H = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : V >= 2 ? 1 : 0;
+  static_assert((1 << H) == V && V <= 32, "power-of-two value count up to 32");
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    const int off = 16 >> h, half = V >> (h + 1);
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const int send = upper ? v[i] : v[i + half];
+      const int keep = upper ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  int s = v[0];
+#pragma unroll
+  for (int off = 16 >> H; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  return s;  // value index lane >> (5 - H)
+}
+
 template <int MR>
 __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, const int8_t* __restrict__ qa,
                                                           const float* __restrict__ sa,
@@ -33,64 +63,65 @@ __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, c
                                                           const float* __restrict__ sw,
                                                           const float* __restrict__ bias, float* __restrict__ Y,
                                                           int32_t* __restrict__ acc_out) {
+  constexpr int COLS = kSkinnyCols, V = COLS * MR;
+  constexpr int H = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : 1;
   pdl_wait();
   pdl_launch();
   extern __shared__ int4 s_qa4[];
   const int nchunk = k >> 4;
-  for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x)
-    s_qa4[i] = __ldg(reinterpret_cast<const int4*>(qa) + i);
-  __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int warps = (gridDim.x * blockDim.x) >> 5;
-  for (int col = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; col < n; col += warps) {
-    const int4* wrow = reinterpret_cast<const int4*>(wq + (size_t)col * k);
-    int acc[MR];
+  const int ngroups = (n + COLS - 1) / COLS;
+  const int gstride = gridDim.x * (blockDim.x >> 5);
+  int cg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  auto load_w = [&](int grp, int c, int4 (&w)[COLS]) {
 #pragma unroll
-    for (int r = 0; r < MR; ++r) acc[r] = 0;
-    int c = lane;
-    for (; c + 32 < nchunk; c += 64) {  // two independent 16-byte loads in flight
-      const int4 w0 = __ldg(wrow + c), w1 = __ldg(wrow + c + 32);
+    for (int j = 0; j < COLS; ++j) {
+      const int col = grp * COLS + j;
+      w[j] = (col < n && c < nchunk) ? __ldg(reinterpret_cast<const int4*>(wq + (size_t)col * k) + c)
+                                      : make_int4(0, 0, 0, 0);
+    }
+  };
+  int4 wc[COLS];
+  load_w(cg, lane, wc);  // in flight during the staging below
+  for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x) s_qa4[i] = __ldg(reinterpret_cast<const int4*>(qa) + i);
+  __syncthreads();
+  for (; cg < ngroups; cg += gstride) {
+    int acc[COLS][MR];
+#pragma unroll
+    for (int j = 0; j < COLS; ++j)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[j][r] = 0;
+    for (int c = lane; c < nchunk; c += 32) {
+      int4 wn[COLS];
+      load_w(cg, c + 32, wn);  // next chunk (zeros past the row)
 #pragma unroll
       for (int r = 0; r < MR; ++r) {
         if (r < m) {
-          const int4 a0 = s_qa4[r * nchunk + c], a1 = s_qa4[r * nchunk + c + 32];
-          acc[r] = __dp4a(w0.x, a0.x, acc[r]);
-          acc[r] = __dp4a(w0.y, a0.y, acc[r]);
-          acc[r] = __dp4a(w0.z, a0.z, acc[r]);
-          acc[r] = __dp4a(w0.w, a0.w, acc[r]);
-          acc[r] = __dp4a(w1.x, a1.x, acc[r]);
-          acc[r] = __dp4a(w1.y, a1.y, acc[r]);
-          acc[r] = __dp4a(w1.z, a1.z, acc[r]);
-          acc[r] = __dp4a(w1.w, a1.w, acc[r]);
+          const int4 a = s_qa4[r * nchunk + c];
+#pragma unroll
+          for (int j = 0; j < COLS; ++j) {
+            acc[j][r] = __dp4a(wc[j].x, a.x, acc[j][r]);
+            acc[j][r] = __dp4a(wc[j].y, a.y, acc[j][r]);
+            acc[j][r] = __dp4a(wc[j].z, a.z, acc[j][r]);
+            acc[j][r] = __dp4a(wc[j].w, a.w, acc[j][r]);
+          }
         }
       }
+#pragma unroll
+      for (int j = 0; j < COLS; ++j) wc[j] = wn[j];
     }
-    for (; c < nchunk; c += 32) {
-      const int4 w0 = __ldg(wrow + c);
+    load_w(cg + gstride, lane, wc);  // first chunk of the next column pair
+    int v[V];
 #pragma unroll
-      for (int r = 0; r < MR; ++r) {
-        if (r < m) {
-          const int4 a0 = s_qa4[r * nchunk + c];
-          acc[r] = __dp4a(w0.x, a0.x, acc[r]);
-          acc[r] = __dp4a(w0.y, a0.y, acc[r]);
-          acc[r] = __dp4a(w0.z, a0.z, acc[r]);
-          acc[r] = __dp4a(w0.w, a0.w, acc[r]);
-        }
-      }
-    }
+    for (int j = 0; j < COLS; ++j)
 #pragma unroll
-    for (int r = 0; r < MR; ++r) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-    }
-    const float swc = __ldg(sw + col);
-    const float bc = bias ? __ldg(bias + col) : 0.0f;
-#pragma unroll
-    for (int r = 0; r < MR; ++r) {
-      if (r < m && lane == r) {
-        Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(acc[r]), sa[r]), swc), bc);
-        if (acc_out) acc_out[(size_t)r * n + col] = acc[r];
-      }
+      for (int r = 0; r < MR; ++r) v[j * MR + r] = acc[j][r];
+    const int sum = butterfly_sum<V>(v, lane);
+    const int idx = lane >> (5 - H), r = idx % MR, col = cg * COLS + idx / MR;
+    if ((lane & ((1 << (5 - H)) - 1)) == 0 && r < m && col < n) {
+      const float bc = bias ? __ldg(bias + col) : 0.0f;
+      Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(sum), __ldg(sa + r)), __ldg(sw + col)), bc);
+      if (acc_out) acc_out[(size_t)r * n + col] = sum;
     }
   }
 }
@@ -118,113 +149,121 @@ __global__ void w8a8_generic_kernel(int m, int n, int k, const int8_t* __restric
   }
 }
 
-// ---- skinny W4A8 -----------------------------------------------------------
+// ---- skinny W4A8 (m <= 16), exact ------------------------------------------
 // Packed row col: k/2 bytes; byte b holds elements 2b (low nibble) and 2b+1
 // (high nibble) as q + 8.  A 16-byte load covers 32 consecutive elements.
-// Activations are staged in shared memory de-interleaved per 8 elements so
-// that dp4a.s32.u32 multiplies signed activations with the raw unsigned
-// nibbles: sum a*(nib-8) = dp(a, nib) - 8*sum(a), with sum(a) per 32-element
-// chunk precomputed.  The group partial sums are exact; the f32 promotion
-// runs in ascending group order per output, as the oracle defines.
+// The activations are staged in shared memory de-interleaved per 8 elements
+// (even elements in one word array, odd in the other) so that dp4a.s32.u32
+// multiplies signed activations with the raw unsigned nibbles:
+// sum a*(nib-8) = dp(a, nib) - 8*sum(a), with sum(a) per 32-element chunk
+// precomputed.  A block owns cb output columns; thread t takes the
+// (column, group) pairs t, t + 256, ... (coalesced 16-byte weight loads),
+// forms the exact int32 group partials of every row and parks them in
+// shared memory; then thread (column, row) promotes its row in ascending
+// group order (s = fma((float)P, sw, s)), the order the oracle defines.
 __device__ __forceinline__ int dp4a_su(int a, uint32_t b, int c) {
   int d;
   asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
 
-// One warp per output column: lane j owns group j (and j+32, ...), loads
-// its 16-byte chunks (a group of 32 INT4 values per chunk, coalesced across
-// lanes), and forms the exact partials P[r][j] for all rows r with
-// dp4a.s32.u32; the partials and the column's group scales go through shared
-// memory, and lane r then runs row r's f32 promotion in ascending group
-// order (s = fma((float)P, sw, s)), the order the oracle defines.
-constexpr int kW4Warps = 8;
 template <int MR>
-__global__ void __launch_bounds__(kW4Warps * 32) w4a8_skinny_kernel(int m, int n, int k, int group,
-                                                                    const int8_t* __restrict__ qa,
-                                                                    const float* __restrict__ sa,
-                                                                    const uint8_t* __restrict__ wq,
-                                                                    const float* __restrict__ sw,
-                                                                    const float* __restrict__ bias,
-                                                                    float* __restrict__ Y,
-                                                                    int32_t* __restrict__ acc_out) {
+__global__ void __launch_bounds__(256) w4a8_skinny_kernel(int m, int n, int k, int group, int cb,
+                                                          const int8_t* __restrict__ qa,
+                                                          const float* __restrict__ sa,
+                                                          const uint8_t* __restrict__ wq,
+                                                          const float* __restrict__ sw,
+                                                          const float* __restrict__ bias, float* __restrict__ Y,
+                                                          int32_t* __restrict__ acc_out) {
   pdl_wait();
   pdl_launch();
-  extern __shared__ int s_dyn[];
-  const int nch = k >> 5;         // 32-element chunks per row
-  const int ng = k / group, cpg = group >> 5;
-  int* s_act = s_dyn;             // [m][nch][8] de-interleaved activation words
-  int* s_sum = s_act + m * nch * 8;  // [m][nch] chunk sums of the activations
-  int* s_warp = s_sum + m * nch;  // per warp: P [MR][ng] then scales [ng]
-  for (int i = threadIdx.x; i < m * nch; i += blockDim.x) {
-    const int r = i / nch, ch = i % nch;
-    const int8_t* a = qa + (size_t)r * k + ch * 32;
+  extern __shared__ int4 s_dyn4[];
+  const int nch = k >> 5;  // 32-element chunks per row
+  const int ng = k / group, cpg = group >> 5, pstride = ng | 1;  // odd stride: conflict-free promotion
+  int4* s_lo = s_dyn4;                                           // [m][nch]: even elements of each 8
+  int4* s_hi = s_lo + m * nch;                                   // [m][nch]: odd elements
+  int* s_sum = reinterpret_cast<int*>(s_hi + m * nch);           // [m][nch] chunk sums
+  int* sP = s_sum + m * nch;                                     // [cb][MR][pstride] group partials
+  const int tid = threadIdx.x;
+  const bool vec = (reinterpret_cast<uintptr_t>(qa) & 15u) == 0;
+  for (int i = tid; i < m * nch; i += blockDim.x) {  // rows are contiguous: chunk i at byte 32 i
+    uint32_t x[8];
+    if (vec) {
+      const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(qa) + 2 * i);
+      const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(qa) + 2 * i + 1);
+      x[0] = a0.x, x[1] = a0.y, x[2] = a0.z, x[3] = a0.w, x[4] = a1.x, x[5] = a1.y, x[6] = a1.z, x[7] = a1.w;
+    } else {
+      const uint8_t* a = reinterpret_cast<const uint8_t*>(qa) + (size_t)i * 32;
+#pragma unroll
+      for (int w = 0; w < 8; ++w)
+        x[w] = (uint32_t)a[4 * w] | ((uint32_t)a[4 * w + 1] << 8) | ((uint32_t)a[4 * w + 2] << 16) |
+               ((uint32_t)a[4 * w + 3] << 24);
+    }
     int sum = 0;
+    uint32_t lo[4], hi[4];
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const int8_t* e = a + 8 * w;
-      uint32_t lo = (uint32_t)(uint8_t)e[0] | ((uint32_t)(uint8_t)e[2] << 8) | ((uint32_t)(uint8_t)e[4] << 16) |
-                    ((uint32_t)(uint8_t)e[6] << 24);
-      uint32_t hi = (uint32_t)(uint8_t)e[1] | ((uint32_t)(uint8_t)e[3] << 8) | ((uint32_t)(uint8_t)e[5] << 16) |
-                    ((uint32_t)(uint8_t)e[7] << 24);
-      s_act[i * 8 + w] = (int)lo;
-      s_act[i * 8 + 4 + w] = (int)hi;
-      for (int t = 0; t < 8; ++t) sum += e[t];
+      lo[w] = __byte_perm(x[2 * w], x[2 * w + 1], 0x6420);
+      hi[w] = __byte_perm(x[2 * w], x[2 * w + 1], 0x7531);
+      sum = __dp4a((int)x[2 * w], 0x01010101, sum);
+      sum = __dp4a((int)x[2 * w + 1], 0x01010101, sum);
     }
+    s_lo[i] = make_int4((int)lo[0], (int)lo[1], (int)lo[2], (int)lo[3]);
+    s_hi[i] = make_int4((int)hi[0], (int)hi[1], (int)hi[2], (int)hi[3]);
     s_sum[i] = sum;
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* sP = s_warp + warp * (MR * ng + ng);
-  float* sS = reinterpret_cast<float*>(sP + MR * ng);
-  const int warps = gridDim.x * kW4Warps;
-  for (int col = blockIdx.x * kW4Warps + warp; col < n; col += warps) {
-    const uint4* wrow = reinterpret_cast<const uint4*>(wq + (size_t)col * (k >> 1));
-    for (int j = lane; j < ng; j += 32) {
+  const uint4* w4 = reinterpret_cast<const uint4*>(wq);
+  for (int c0 = blockIdx.x * cb; c0 < n; c0 += gridDim.x * cb) {
+    for (int p = tid; p < cb * ng; p += blockDim.x) {
+      const int c = p / ng, g = p - c * ng, col = c0 + c;
       int part[MR];
 #pragma unroll
       for (int r = 0; r < MR; ++r) part[r] = 0;
-      for (int cc = 0; cc < cpg; ++cc) {
-        const int ch = j * cpg + cc;
-        const uint4 w = __ldg(wrow + ch);
-        const uint32_t wl[4] = {w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu};
-        const uint32_t wh[4] = {(w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                                (w.w >> 4) & 0x0F0F0F0Fu};
+      if (col < n) {
+        for (int cc = 0; cc < cpg; ++cc) {
+          const int ch = g * cpg + cc;
+          const uint4 w = __ldg(w4 + (size_t)col * nch + ch);
+          const uint32_t wl[4] = {w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu};
+          const uint32_t wh[4] = {(w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                                  (w.w >> 4) & 0x0F0F0F0Fu};
 #pragma unroll
-        for (int r = 0; r < MR; ++r) {
-          if (r < m) {
-            const int4* a4 = reinterpret_cast<const int4*>(s_act + (r * nch + ch) * 8);
-            const int4 alo = a4[0], ahi = a4[1];
-            int p = part[r];
-            p = dp4a_su(alo.x, wl[0], p);
-            p = dp4a_su(alo.y, wl[1], p);
-            p = dp4a_su(alo.z, wl[2], p);
-            p = dp4a_su(alo.w, wl[3], p);
-            p = dp4a_su(ahi.x, wh[0], p);
-            p = dp4a_su(ahi.y, wh[1], p);
-            p = dp4a_su(ahi.z, wh[2], p);
-            p = dp4a_su(ahi.w, wh[3], p);
-            part[r] = p - 8 * s_sum[r * nch + ch];
+          for (int r = 0; r < MR; ++r) {
+            if (r < m) {
+              const int4 alo = s_lo[r * nch + ch], ahi = s_hi[r * nch + ch];
+              int q = 0;
+              q = dp4a_su(alo.x, wl[0], q);
+              q = dp4a_su(alo.y, wl[1], q);
+              q = dp4a_su(alo.z, wl[2], q);
+              q = dp4a_su(alo.w, wl[3], q);
+              q = dp4a_su(ahi.x, wh[0], q);
+              q = dp4a_su(ahi.y, wh[1], q);
+              q = dp4a_su(ahi.z, wh[2], q);
+              q = dp4a_su(ahi.w, wh[3], q);
+              part[r] += q - 8 * s_sum[r * nch + ch];
+            }
           }
         }
       }
 #pragma unroll
       for (int r = 0; r < MR; ++r)
-        if (r < m) sP[r * ng + j] = part[r];
-      sS[j] = __ldg(sw + (size_t)col * ng + j);
+        if (r < m) sP[(c * MR + r) * pstride + g] = part[r];
     }
-    __syncwarp();
-    if (lane < m) {
-      const int r = lane;
-      float acc = 0.0f;
-      for (int j = 0; j < ng; ++j) {
-        const int p = sP[r * ng + j];
-        acc = __fmaf_rn(__int2float_rn(p), sS[j], acc);
-        if (acc_out) acc_out[((size_t)r * n + col) * ng + j] = p;
+    __syncthreads();
+    if (tid < cb * MR) {
+      const int c = tid / MR, r = tid - c * MR, col = c0 + c;
+      if (r < m && col < n) {
+        const int* P = sP + tid * pstride;
+        const float* swc = sw + (size_t)col * ng;
+        float acc = 0.0f;
+        for (int g = 0; g < ng; ++g) {
+          acc = __fmaf_rn(__int2float_rn(P[g]), __ldg(swc + g), acc);
+          if (acc_out) acc_out[((size_t)r * n + col) * ng + g] = P[g];
+        }
+        Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(acc, __ldg(sa + r)), bias ? __ldg(bias + col) : 0.0f);
       }
-      Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(acc, sa[r]), bias ? __ldg(bias + col) : 0.0f);
     }
-    __syncwarp();
+    __syncthreads();
   }
 }
 
@@ -238,25 +277,15 @@ static int launch_rc(cudaError_t e, const char* what) {
   return launch_err(what);
 }
 
-static int grid_cols(int n, int cols_per_block) {
-  int want = (n + cols_per_block - 1) / cols_per_block;
-  int cap = std::max(1, sm_count()) * 8;
-  return std::max(1, std::min(want, cap));
-}
+constexpr size_t kSkinnySmem = 200 * 1024;
 
-int run_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq, const float* sw,
-                    const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
-  const bool vec = (k % 16 == 0) && aligned16(qa) && aligned16(wq);
-  if (!vec || m > kSkinnyM) {
-    return launch_rc(launch_pdl_ex(w8a8_generic_kernel, dim3(std::max(1, sm_count()) * 8), dim3(256), 0, s, m, n, k,
-                                   qa, sa, wq, sw, bias, Y, acc_out),
-                     "w8a8_generic_kernel");
-  }
+static int launch_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq,
+                              const float* sw, const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
   const size_t smem = (size_t)m * k;
-  if (smem > 200 * 1024) return fail(OC_ERR_NOT_SUPPORTED, "w8a8 skinny: m*k too large for shared memory");
-  const int grid = grid_cols(n, 8);
+  const int warps = (n + kSkinnyCols - 1) / kSkinnyCols;
+  const int grid = std::max(1, std::min((warps + 7) / 8, std::max(1, sm_count()) * 16));
   auto launch = [&](auto kern) {
-    smem_attr_once(reinterpret_cast<const void*>(kern), 200 * 1024);
+    smem_attr_once(reinterpret_cast<const void*>(kern), (int)kSkinnySmem);
     return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(256), smem, s, m, n, k, qa, sa, wq, sw, bias, Y, acc_out),
                      "w8a8_skinny_kernel");
   };
@@ -266,24 +295,63 @@ int run_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, cons
   return launch(w8a8_skinny_kernel<16>);
 }
 
+// m <= kSkinnyM rows (more go to the generic kernel); the rows are split
+// into launches whose activations fit in shared memory.
+int run_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq, const float* sw,
+                    const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
+  const bool vec = (k % 16 == 0) && aligned16(qa) && aligned16(wq) && (size_t)k <= kSkinnySmem;
+  if (!vec || m > kSkinnyM) {
+    return launch_rc(launch_pdl_ex(w8a8_generic_kernel, dim3(std::max(1, sm_count()) * 8), dim3(256), 0, s, m, n, k,
+                                   qa, sa, wq, sw, bias, Y, acc_out),
+                     "w8a8_generic_kernel");
+  }
+  const int rows = (int)std::min<size_t>((size_t)m, kSkinnySmem / (size_t)k);
+  for (int r0 = 0; r0 < m; r0 += rows) {
+    const int mr = std::min(rows, m - r0);
+    const int rc = launch_w8a8_skinny(mr, n, k, qa + (size_t)r0 * k, sa + r0, wq, sw, bias, Y + (size_t)r0 * n,
+                                      acc_out ? acc_out + (size_t)r0 * n : nullptr, s);
+    if (rc) return rc;
+  }
+  return OC_OK;
+}
+
+// Shared memory of the W4A8 skinny kernel for m rows, template rows mr and
+// cb columns per block.
+static size_t w4_skinny_smem(int m, int mr, int k, int group, int cb) {
+  const size_t nch = (size_t)k / 32, ng = (size_t)k / group;
+  return (size_t)m * nch * (32 + 4) + (size_t)cb * mr * (ng | 1) * 4;
+}
+
+// m <= kSkinnyM rows; fewer rows and columns per launch when shared memory
+// would not hold them.
 int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const float* sa, const uint8_t* wq,
                     const float* sw, const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
-  const int ng = k / group, nch = k / 32;
-  auto smem_for = [&](int mr) { return ((size_t)m * nch * 9 + (size_t)kW4Warps * (mr * ng + ng)) * sizeof(int); };
-  const int mr = m <= 1 ? 1 : m <= 4 ? 4 : m <= 8 ? 8 : 16;
-  const size_t smem = smem_for(mr);
-  if (smem > 200 * 1024) return fail(OC_ERR_NOT_SUPPORTED, "w4a8 skinny: m*k too large for shared memory");
-  const int grid = std::max(1, std::min((n + kW4Warps - 1) / kW4Warps, std::max(1, sm_count()) * 8));
-  auto launch = [&](auto kern) {
-    smem_attr_once(reinterpret_cast<const void*>(kern), 200 * 1024);
-    return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(kW4Warps * 32), smem, s, m, n, k, group, qa, sa, wq, sw,
-                                   bias, Y, acc_out),
-                     "w4a8_skinny_kernel");
-  };
-  if (mr == 1) return launch(w4a8_skinny_kernel<1>);
-  if (mr == 4) return launch(w4a8_skinny_kernel<4>);
-  if (mr == 8) return launch(w4a8_skinny_kernel<8>);
-  return launch(w4a8_skinny_kernel<16>);
+  const int ng = k / group;
+  int rows = m, cb = 16;
+  auto mr_of = [](int r) { return r <= 1 ? 1 : r <= 4 ? 4 : r <= 8 ? 8 : 16; };
+  while (w4_skinny_smem(rows, mr_of(rows), k, group, cb) > kSkinnySmem) {
+    if (cb > 1) cb >>= 1;
+    else if (rows > 1) rows = (rows + 1) / 2;
+    else return fail(OC_ERR_NOT_SUPPORTED, "w4a8 skinny: k too large for shared memory");
+  }
+  for (int r0 = 0; r0 < m; r0 += rows) {
+    const int mrows = std::min(rows, m - r0), mr = mr_of(mrows);
+    const size_t smem = w4_skinny_smem(mrows, mr, k, group, cb);
+    const int grid = std::max(1, std::min((n + cb - 1) / cb, std::max(1, sm_count()) * 16));
+    auto launch = [&](auto kern) {
+      smem_attr_once(reinterpret_cast<const void*>(kern), (int)kSkinnySmem);
+      return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(256), smem, s, mrows, n, k, group, cb,
+                                     qa + (size_t)r0 * k, sa + r0, wq, sw, bias, Y + (size_t)r0 * n,
+                                     acc_out ? acc_out + (size_t)r0 * n * ng : nullptr),
+                       "w4a8_skinny_kernel");
+    };
+    const int rc = mr == 1   ? launch(w4a8_skinny_kernel<1>)
+                   : mr == 4 ? launch(w4a8_skinny_kernel<4>)
+                   : mr == 8 ? launch(w4a8_skinny_kernel<8>)
+                             : launch(w4a8_skinny_kernel<16>);
+    if (rc) return rc;
+  }
+  return OC_OK;
 }
 
 // Picks the tile width with the fewest (waves x tile width) units.

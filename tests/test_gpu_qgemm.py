@@ -110,6 +110,8 @@ QGEMM_SHAPES = [
     (8, 3584, 512), (64, 3584, 384),
     # enough 128 x 256 tiles to fill the GPU, ragged N
     (1200, 384, 4100),
+    # skinny rows whose activations exceed shared memory: split into launches
+    (16, 16384, 40),
 ]
 
 
