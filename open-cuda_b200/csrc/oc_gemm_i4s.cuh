@@ -1,36 +1,42 @@
 // oc_gemm_i4s.cuh -- persistent tcgen05 GEMM for W4A8 (group-32 scales) that
-// dequantizes the weights in shared memory and accumulates the whole K in
-// TMEM:
-//   x[n][k] = (float)(nib[n][k] - 8) * sw[n][k/32]     (the reference's f32
+// dequantizes the weights on the fly and accumulates the whole K in TMEM:
+//   x[n][k] = (nib[n][k] - 8) * sw[n][k/32]     (the reference's f32
 //             dequantization, dequantize_int4, crates/opencuda-blas/src/lib.rs:922-931)
 //   Y[m][n] = (sum_k qa[m][k] * x[n][k]) * sa[m] + bias[n]
-// x is carried on the tensor core as two f16 terms, hi = f16(x * c_n) and
-// lo = f16(x * c_n - hi) (22 significant bits; c_n = 2^e per output column
-// keeps |x * c_n| < 2^15, inside f16's range), and the quantized activations
-// arrive as f16 (exact integers, written so by the row quantization), so
-// each K-step is two kind::f16 MMAs (hi.A, lo.A) with f32 accumulation; the
-// epilogue divides by c_n (exact).  The result agrees with the exact
-// per-group definition to ~1e-6 relative; the exact int32 group partials,
-// when a caller asks for them, come from oc_gemm_i4.cuh.
+// The weights reach the tensor core as two f16 terms per element.  With c_n
+// = 2^(11 - e) a per-column power of two (e = exponent of the column's
+// largest group scale), s = sw * c_n split as s_hi + s_lo (f16 each, 22
+// significant bits together) and w = nib - 8 (exact in f16):
+//   hi = f16(w * s_hi),   lo = f16(f16(w * s_lo) - (hi - w * s_hi)),
+// where hi - w * s_hi, the rounding error of the product, is exact from one
+// f16 FMA.  hi + lo = w * s to ~2^-20 relative and |w * s| < 2^15 stays in
+// f16's range.  The activations arrive as f16 (exact integers from the row
+// quantization), each K-step is two kind::f16 MMAs (hi, lo) accumulating in
+// f32, and the epilogue divides by c_n (exact).  The output agrees with the
+// exact per-group definition to ~1e-6 relative; the exact int32 group
+// partials, when a caller asks for them, come from oc_gemm_i4.cuh.
 //
-// The converted weights never touch shared memory: the converters store hi
-// and lo into tensor memory (tcgen05.st), where the MMA takes them as its A
-// operand (M = 128 weight rows = output columns), and the f16 activation
-// tile (N = 128 output rows) is the shared-memory B operand.  The
-// accumulator is the output tile transposed: TMEM lane = output column,
-// TMEM column = output row, so the epilogue's stores are coalesced across a
-// warp.  Shared memory then carries only the activation tiles (TMA, read by
-// the MMA) and the packed weights (TMA, read once by the converters).
-// Rings: raw k-blocks of 128 (packed B [128][64 bytes] with the 64-byte
-// swizzle, scales [128][4]) and k-blocks of 64 (activation tile in smem,
-// weight terms in TMEM).  Roles (864 threads):
+// MMA layout: A = the converted weights, stored by the converter warps
+// straight into tensor memory (tcgen05.st; M = 128 weight rows = output
+// columns); B = the f16 activation tile in shared memory (N = bm = 256
+// output rows, 128 for short inputs).  An N = 256 MMA costs about as much
+// as an N = 128 one, so the wide tile halves the tensor time, the
+// conversions and the TMEM stores per output.  The accumulator is the
+// output tile transposed (TMEM lane = output column, TMEM column = output
+// row; 256 columns, one buffer), drained by the same 16 warps that convert:
+// TMEM -> registers (the accumulator is released at once) -> * sa / c_n +
+// bias -> shared memory -> TMA store.  They convert the next tile's first
+// k-blocks before draining, so the MMAs resume as soon as the registers
+// hold the tile.  Rings: raw k-blocks of 128
+// (packed weights [128][64 bytes] with the 64-byte swizzle, scales [128][4])
+// and k-blocks of 64 (activation tile in shared memory, weight terms in
+// TMEM).  Roles (608 threads):
 //   warp 0       TMA producer of the raw ring
-//   warp 1       TMEM allocator + MMA issuer (two 128-column accumulators)
+//   warp 1       TMEM allocator + MMA issuer
 //   warp 2       TMA producer of the f16 activation tiles
-//   warps 3..18  converters: warp = (TMEM lane quadrant, 16-k quarter of
-//                the k-block), thread = one weight row
-//   warps 19..26 epilogue: warp = (TMEM lane quadrant, half of the output
-//                rows): TMEM -> registers, / c_n, * sa, + bias, stores
+//   warps 3..18  converters and drainers: warp = (TMEM lane quadrant q,
+//                16-k quarter cq of the k-block); thread = one weight row;
+//                the drain gives warp (q, cq) output rows [64 cq, 64 cq + 64)
 // Every wait is bounded (oc_ptx.cuh).
 #pragma once
 #include "oc_gemm_i8.cuh"
@@ -39,30 +45,42 @@
 namespace oc {
 
 struct I4Split {
-  static constexpr int BM = 128, BN = 128;  // output rows (activations) x output columns (weights)
+  static constexpr int BN = 128;  // weight rows per tile (MMA M) = output columns
+  static constexpr int BM = 256;  // activation rows per tile (MMA N), at most
   static constexpr int RBK = 128, RGROUPS = RBK / 32, RSTAGES = 4;
   static constexpr int BP_BYTES = BN * RBK / 2, S_BYTES = BN * RGROUPS * 4;
   static constexpr int RSTAGE_BYTES = (BP_BYTES + S_BYTES + 1023) / 1024 * 1024;
-  static constexpr int BK = 64, CSTAGES = 4;
-  static constexpr int A16_BYTES = BM * BK * 2;  // activation tile per k-block (smem)
+  static constexpr int BK = 64, CSTAGES = 3;
+  static constexpr int A16_BYTES = BM * BK * 2;  // activation tile per k-block (shared memory)
   static constexpr int WCOLS = BK;               // TMEM columns per k-block: hi 32 + lo 32
-  static constexpr int CONV_WARPS = 16, EPI_WARPS = 8;
-  static constexpr int THREADS = 32 * (3 + CONV_WARPS + EPI_WARPS);
-  static constexpr int ACC_COLS = 2 * BM;        // two accumulators (transposed tiles: BM columns)
+  static constexpr int CONV_WARPS = 16;
+  static constexpr int THREADS = 32 * (3 + CONV_WARPS);
+  static constexpr int ACC_COLS = BM;  // one accumulator (transposed tile: BM columns)
   static constexpr int TMEM_COLS = 512;
-  static constexpr int YSTAGE_BYTES = EPI_WARPS * 2 * 4096;  // two 32x32 f32 output blocks per epilogue warp
+  static constexpr int YSTAGE_BYTES = CONV_WARPS * 4096;  // one 32x32 f32 output block per warp
+  static constexpr int SA_BYTES = CONV_WARPS * 64 * 4;    // each drainer's 64 row scales
   static constexpr size_t SMEM =
-      1024 + (size_t)CSTAGES * A16_BYTES + (size_t)RSTAGES * RSTAGE_BYTES + YSTAGE_BYTES + 512;
-  static constexpr uint32_t IDESC = idesc_f16(BN, BM);  // MMA M = weight rows, N = activation rows
+      1024 + (size_t)CSTAGES * A16_BYTES + (size_t)RSTAGES * RSTAGE_BYTES + YSTAGE_BYTES + SA_BYTES + 512;
   static_assert(ACC_COLS + CSTAGES * WCOLS <= TMEM_COLS, "tensor memory budget");
   static_assert(RSTAGE_BYTES % 1024 == 0 && A16_BYTES % 1024 == 0, "1024-byte stage alignment");
-  static_assert(CONV_WARPS == 16 && EPI_WARPS == 8, "four converter and two epilogue warps per TMEM lane quadrant");
+  static_assert(CONV_WARPS == 16, "four converter warps per TMEM lane quadrant");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
-// a - b on two f16 lanes (exact for the integers used here)
+// a - b, a * b, a * b + c on two f16 lanes (IEEE round to nearest each)
 __device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
 
@@ -75,27 +93,36 @@ __device__ __forceinline__ uint32_t nib_pair_to_f16(uint32_t w) {
   return hsub2_bits((x & 0x00F0000Fu) | 0x54006400u, 0x54806408u);
 }
 
-__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
-  asm("{\n\t.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
-      : "=f"(lo), "=f"(hi)
-      : "r"(h));
+// f32 -> f16 bits (round to nearest) and back (exact)
+__device__ __forceinline__ uint32_t f32_to_f16_bits(float x) {
+  unsigned short h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(x));
+  return h;
 }
-__device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
-  uint32_t d;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+  float x;
+  asm("{\n\t.reg .f16 t;\n\tmov.b16 t, %1;\n\tcvt.f32.f16 %0, t;\n\t}" : "=f"(x) : "h"((unsigned short)h));
+  return x;
 }
 
-// Two weights (an f16x2 of exact integers w) -> x = w * swc (f32), split into
-// f16x2 hi and lo with hi + lo = x to 22 bits.
-__device__ __forceinline__ void split_pair(uint32_t w2, float swc, uint32_t& hi2, uint32_t& lo2) {
-  float w0, w1;
-  f16x2_to_f32(w2, w0, w1);
-  const float x0 = __fmul_rn(w0, swc), x1 = __fmul_rn(w1, swc);
-  hi2 = f32x2_to_f16x2(x0, x1);
-  float h0, h1;
-  f16x2_to_f32(hi2, h0, h1);
-  lo2 = f32x2_to_f16x2(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+// A scaled group scale s split into f16x2 broadcasts of s_hi, -s_hi, s_lo.
+struct ScaleTerms {
+  uint32_t hi, nhi, lo;
+  __device__ __forceinline__ explicit ScaleTerms(float s) {
+    const uint32_t h = f32_to_f16_bits(s);
+    const uint32_t l = f32_to_f16_bits(__fsub_rn(s, f16_bits_to_f32(h)));  // s - s_hi is exact
+    hi = h | (h << 16);
+    nhi = hi ^ 0x80008000u;
+    lo = l | (l << 16);
+  }
+};
+
+// Two weights (an f16x2 of exact integers w) -> f16x2 hi and lo with
+// hi + lo = w * (s_hi + s_lo) to ~2^-20 relative.
+__device__ __forceinline__ void split_pair(uint32_t w2, const ScaleTerms& st, uint32_t& hi2, uint32_t& lo2) {
+  hi2 = hmul2_bits(w2, st.hi);
+  const uint32_t err = hfma2_bits(w2, st.nhi, hi2);  // hi - w * s_hi, exact
+  lo2 = hsub2_bits(hmul2_bits(w2, st.lo), err);
 }
 
 // Work item w of the dequantizing kernel: tile w / ksplit (tm fastest) and
@@ -134,13 +161,26 @@ __device__ __forceinline__ float exp2_int(int e) { return __uint_as_float((uint3
 __global__ void __launch_bounds__(I4Split::THREADS, 1)
     gemm_w4a8_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBp,
                            const __grid_constant__ CUtensorMap tmS,
-                           const __grid_constant__ CUtensorMap tmOut, int out_tma, int M, int N, int K,
+                           const __grid_constant__ CUtensorMap tmOut, int out_tma, int M, int N, int K, int bm,
                            const float* __restrict__ sa, const float* __restrict__ sw,
                            const float* __restrict__ bias, float* __restrict__ Y, int ksplit,
                            float* __restrict__ part, int slice_rows, int* status) {
+  using C = I4Split;
+  const int tiles_m = (M + bm - 1) / bm;
+  const int tiles_n = (N + C::BN - 1) / C::BN;
+  const int nrb = K / C::RBK;  // K % 128 == 0 on this path
+  const int nitems = tiles_m * tiles_n * ksplit;  // ksplit <= nrb: every item has raw blocks
+  if (threadIdx.x == 0 && (int)blockIdx.x < nitems) {
+    // the first item's packed weights and scales into L2 before the dependency wait
+    WorkItem it;
+    it.set(blockIdx.x, ksplit, tiles_m, nrb);
+    for (int rb = it.rb0; rb < it.rb1; ++rb) {
+      tma_prefetch_2d(&tmBp, rb * (C::RBK / 2), it.tn * C::BN);
+      tma_prefetch_2d(&tmS, rb * C::RGROUPS, it.tn * C::BN);
+    }
+  }
   pdl_wait();
   pdl_launch();
-  using C = I4Split;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* const cbase = smem;
@@ -149,13 +189,14 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
   auto sBP = [&](int r) { return rbase + (size_t)r * C::RSTAGE_BYTES; };
   auto sS = [&](int r) { return reinterpret_cast<float*>(sBP(r) + C::BP_BYTES); };
   uint8_t* const ystage = rbase + (size_t)C::RSTAGES * C::RSTAGE_BYTES;
-  uint64_t* rfull = reinterpret_cast<uint64_t*>(ystage + C::YSTAGE_BYTES);
+  float* const s_sa = reinterpret_cast<float*>(ystage + C::YSTAGE_BYTES);
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(ystage + C::YSTAGE_BYTES + C::SA_BYTES);
   uint64_t* rempty = rfull + C::RSTAGES;
   uint64_t* cfull = rempty + C::RSTAGES;
   uint64_t* cempty = cfull + C::CSTAGES;
   uint64_t* tfull = cempty + C::CSTAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tempty = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -168,10 +209,8 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       mbar_init(&cfull[s], 1 + C::CONV_WARPS);  // activation TMA (with its bytes) + converters
       mbar_init(&cempty[s], 1);                 // MMA commit
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], C::EPI_WARPS);
-    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, C::CONV_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -187,12 +226,6 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
-  const int tiles_m = (M + C::BM - 1) / C::BM;
-  const int tiles_n = (N + C::BN - 1) / C::BN;
-  const int ntiles = tiles_m * tiles_n;
-  const int nrb = K / C::RBK;  // K % 128 == 0 on this path
-  const int nitems = ntiles * ksplit;  // ksplit <= nrb: every item has raw blocks
 
   if (warp == 0) {
     if (lane == 0) {  // raw ring: packed weights and scales
@@ -215,17 +248,17 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int ci = 0, acc = 0;
-      uint32_t aphase = 0;
+      const uint32_t idesc = idesc_f16(C::BN, bm);  // MMA M = weight rows, N = activation rows
+      int ci = 0;
+      uint32_t tphase = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
         WorkItem it;
         it.set(w, ksplit, tiles_m, nrb);
-        if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) {
+        if (!mbar_wait(tempty, tphase ^ 1u, abort_flag)) {  // the previous tile is drained
           kernel_fail(status, abort_flag, kDevTimeoutMma);
           goto done;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(acc * C::BM);
         for (int kb = 0; kb < 2 * (it.rb1 - it.rb0); ++kb, ++ci) {
           const int cs = ci % C::CSTAGES;
           const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
@@ -235,23 +268,21 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a = smem_u32(sA16(cs));
-          const uint32_t w = tmem_base + (uint32_t)(C::ACC_COLS + cs * C::WCOLS);
+          const uint32_t wt = tmem_base + (uint32_t)(C::ACC_COLS + cs * C::WCOLS);
 #pragma unroll
           for (int kk = 0; kk < C::BK / 16; ++kk) {  // K = 16 f16 per MMA: 8 TMEM columns, 32 smem bytes
-            mma_f16_ta(d, w + kk * 8, desc_kmajor_sw128(a + kk * 32), C::IDESC, (kb | kk) != 0 ? 1u : 0u);
-            mma_f16_ta(d, w + 32 + kk * 8, desc_kmajor_sw128(a + kk * 32), C::IDESC, 1u);
+            mma_f16_ta(tmem_base, wt + kk * 8, desc_kmajor_sw128(a + kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
+            mma_f16_ta(tmem_base, wt + 32 + kk * 8, desc_kmajor_sw128(a + kk * 32), idesc, 1u);
           }
           tc_commit(&cempty[cs]);
         }
-        tc_commit(&tfull[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          aphase ^= 1u;
-        }
+        tc_commit(tfull);
+        tphase ^= 1u;
       }
     }
   } else if (warp == 2) {
     if (lane == 0) {  // f16 activation tiles straight into the MMA layout
+      const uint32_t a16_bytes = (uint32_t)bm * C::BK * 2;
       int ci = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
         WorkItem it;
@@ -263,24 +294,130 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
             kernel_fail(status, abort_flag, kDevTimeoutProducer);
             goto done;
           }
-          mbar_arrive_expect_tx(&cfull[cs], C::A16_BYTES);
-          tma_load_2d(sA16(cs), &tmA, cb * C::BK, it.tm * C::BM, &cfull[cs]);
+          mbar_arrive_expect_tx(&cfull[cs], a16_bytes);
+          tma_load_2d(sA16(cs), &tmA, cb * C::BK, it.tm * bm, &cfull[cs]);
         }
       }
     }
-  } else if (warp < 3 + C::CONV_WARPS) {
-    // converter: TMEM lane quadrant q = warp % 4 (the lanes this warp may
-    // write), weight row cr = 32q + lane of the tile, 16-k quarter cq of the
-    // 64-k block (group cq / 2 of the block, half cq % 2 of the group)
-    const int q = warp & 3, cq = (warp - 3) >> 2;
+  } else {
+    // Converter: TMEM lane quadrant q = warp % 4 (the lanes this warp may
+    // access), weight row cr = 32q + lane of the tile, 16-k quarter cq of the
+    // 64-k block (group cq / 2 of the block, half cq % 2 of the group).
+    // Drain: the same lanes, output rows [64 cq, 64 cq + 64) of the tile.
+    const int q = warp & 3, cq = (warp - 3) >> 2, ew = warp - 3;
     const int cr = q * 32 + lane, g = cq >> 1;
-    int ci = 0;
-    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+    const int G = K / 32;
+    uint8_t* const ybuf = ystage + (size_t)ew * 4096;
+    float* const wsa = s_sa + ew * 64;  // this warp's row scales (broadcast reads)
+    // staging: block row j at j * 128, 16-byte chunk (lane / 4) at
+    // (lane / 4) ^ (j % 8) (128-byte swizzle), word lane % 4
+    const uint32_t ylane = (uint32_t)(lane & 3) * 4, yq = (uint32_t)(lane >> 2);
+    uint32_t dphase = 0;
+    // Drain item j of this CTA (work index blockIdx.x + j * gridDim.x).
+    auto drain = [&](int j) -> bool {
+      WorkItem it;
+      it.set(blockIdx.x + j * gridDim.x, ksplit, tiles_m, nrb);
+      const int col0 = it.tn * C::BN + q * 32, col = col0 + lane;
+      // 1 / c_n (a power of two), bias and row scales, loaded while the MMAs finish
+      const float icn = col < N ? exp2_int(-col_range_exp(sw + (size_t)col * G, G)) : 0.0f;
+      const float bn = (bias && col < N) ? __ldg(bias + col) : 0.0f;
+      const int row0 = it.tm * bm + cq * 64;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {  // rows row0 + 32i + lane
+        const int rr = row0 + 32 * i + lane;
+        wsa[i * 32 + lane] = rr < M ? __ldg(sa + rr) : 0.0f;
+      }
+      __syncwarp();
+      if (!mbar_wait(tfull, dphase, abort_flag)) return false;
+      dphase ^= 1u;
+      tc_fence_after();
+      // K-split: this slice's sum / c_n goes to slice ks of part (rows
+      // [ks * slice_rows, ks * slice_rows + M)), summed in slice order and
+      // finished by gemm_w4a8_splitk_reduce; else the finished y
+      const int out_row = ksplit > 1 ? it.ks * slice_rows : 0;
+      float* out = ksplit > 1 ? part : Y;
+      // block 0 is finished and stored, block 1 loaded, and then the
+      // accumulator is released: the next tile's MMAs overlap block 1's work
+      int nblk = 0;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) nblk += (cq * 64 + 32 * i < bm && row0 + 32 * i < M) ? 1 : 0;
+      const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(cq * 64);
+      for (int i = 0; i < 2; ++i) {
+        uint32_t r[32];
+        if (i < nblk) {
+          tmem_ld32(tl + 32 * i, r);
+          tmem_ld_wait();
+        }
+        if (i == nblk - 1 || (i == 1 && nblk == 0)) {  // the last TMEM read of this warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty);
+        }
+        if (i >= nblk) continue;
+        const int rb0 = row0 + 32 * i;
+        if (ksplit == 1) {  // y = acc * (sa / c_n) + bias, one rounding (sa / c_n is exact)
+          const float4* f4 = reinterpret_cast<const float4*>(wsa + i * 32);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 f = f4[j4];
+            r[4 * j4 + 0] = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * j4 + 0]), __fmul_rn(f.x, icn), bn));
+            r[4 * j4 + 1] = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * j4 + 1]), __fmul_rn(f.y, icn), bn));
+            r[4 * j4 + 2] = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * j4 + 2]), __fmul_rn(f.z, icn), bn));
+            r[4 * j4 + 3] = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * j4 + 3]), __fmul_rn(f.w, icn), bn));
+          }
+        } else {  // slice sum / c_n (exact)
+#pragma unroll
+          for (int j2 = 0; j2 < 32; ++j2) r[j2] = __float_as_uint(__fmul_rn(__uint_as_float(r[j2]), icn));
+        }
+        if (out_tma) {
+          // block row j2 = output row rb0 + j2, 128 bytes, 16-byte chunk cc
+          // at cc ^ (j2 % 8) (128-byte swizzle); lane = column: conflict-free
+          if (lane == 0) bulk_wait_read<0>();  // the previous store has read the buffer
+          __syncwarp();
+#pragma unroll
+          for (int j2 = 0; j2 < 32; ++j2)
+            *reinterpret_cast<uint32_t*>(ybuf + j2 * 128 + (((yq ^ j2) & 7) << 4) + ylane) = r[j2];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmOut, ybuf, col0, out_row + rb0);
+            bulk_commit();
+          }
+        } else {
+          float* ycol = out + (size_t)(out_row + rb0) * N + col;
+#pragma unroll
+          for (int j2 = 0; j2 < 32; ++j2)  // a warp writes 32 adjacent columns
+            if (col < N && rb0 + j2 < M) ycol[(size_t)j2 * N] = __uint_as_float(r[j2]);
+        }
+      }
+      __syncwarp();  // wsa is rewritten by the next drain
+      return true;
+    };
+    int ci = 0, jd = 0, jd_next_first = 0;  // next item to drain; first k-block of the item after it
+    {
+      WorkItem it0;
+      it0.set(blockIdx.x, ksplit, tiles_m, nrb);
+      jd_next_first = 2 * (it0.rb1 - it0.rb0);
+    }
+    int j = 0;
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x, ++j) {
       WorkItem it;
       it.set(w, ksplit, tiles_m, nrb);
       const int col = it.tn * C::BN + cr;
-      const float cval = col < N ? exp2_int(col_range_exp(sw + (size_t)col * (K / 32), K / 32)) : 1.0f;
+      const float cval = col < N ? exp2_int(col_range_exp(sw + (size_t)col * G, G)) : 1.0f;
       for (int kb = 0; kb < 2 * (it.rb1 - it.rb0); ++kb, ++ci) {
+        // the stage of k-block ci is freed by the MMA of k-block ci - CSTAGES;
+        // when that one belongs to a later tile, the drains before it come first
+        while (jd < j && ci - C::CSTAGES >= jd_next_first) {
+          if (!drain(jd)) {
+            kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
+            goto done;
+          }
+          ++jd;  // first_kb(jd + 1) = first_kb(jd) + k-blocks of item jd
+          WorkItem nx;
+          nx.set(blockIdx.x + jd * gridDim.x, ksplit, tiles_m, nrb);
+          jd_next_first += 2 * (nx.rb1 - nx.rb0);
+        }
         const int cs = ci % C::CSTAGES;
         const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
         const int ri = ci >> 1, h = ci & 1;
@@ -293,18 +430,18 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         tc_fence_after();
         // 8 packed bytes = 16 nibbles; the raw tile is TMA-swizzled (64 B:
         // 16-byte chunk j of row r at j ^ ((r >> 1) & 3))
-        const uint2 w = *reinterpret_cast<const uint2*>(sBP(rs) + cr * (C::RBK / 2) +
-                                                       (((2 * h + g) ^ ((cr >> 1) & 3)) << 4) + 8 * (cq & 1));
-        const float swc = __fmul_rn(sS(rs)[cr * C::RGROUPS + 2 * h + g], cval);  // exact: cval = 2^e
+        const uint2 wv = *reinterpret_cast<const uint2*>(sBP(rs) + cr * (C::RBK / 2) +
+                                                        (((2 * h + g) ^ ((cr >> 1) & 3)) << 4) + 8 * (cq & 1));
+        const ScaleTerms st(__fmul_rn(sS(rs)[cr * C::RGROUPS + 2 * h + g], cval));  // exact: cval = 2^e
         uint32_t hi[8], lo[8];
-        split_pair(nib_pair_to_f16<0>(w.x), swc, hi[0], lo[0]);
-        split_pair(nib_pair_to_f16<1>(w.x), swc, hi[1], lo[1]);
-        split_pair(nib_pair_to_f16<2>(w.x), swc, hi[2], lo[2]);
-        split_pair(nib_pair_to_f16<3>(w.x), swc, hi[3], lo[3]);
-        split_pair(nib_pair_to_f16<0>(w.y), swc, hi[4], lo[4]);
-        split_pair(nib_pair_to_f16<1>(w.y), swc, hi[5], lo[5]);
-        split_pair(nib_pair_to_f16<2>(w.y), swc, hi[6], lo[6]);
-        split_pair(nib_pair_to_f16<3>(w.y), swc, hi[7], lo[7]);
+        split_pair(nib_pair_to_f16<0>(wv.x), st, hi[0], lo[0]);
+        split_pair(nib_pair_to_f16<1>(wv.x), st, hi[1], lo[1]);
+        split_pair(nib_pair_to_f16<2>(wv.x), st, hi[2], lo[2]);
+        split_pair(nib_pair_to_f16<3>(wv.x), st, hi[3], lo[3]);
+        split_pair(nib_pair_to_f16<0>(wv.y), st, hi[4], lo[4]);
+        split_pair(nib_pair_to_f16<1>(wv.y), st, hi[5], lo[5]);
+        split_pair(nib_pair_to_f16<2>(wv.y), st, hi[6], lo[6]);
+        split_pair(nib_pair_to_f16<3>(wv.y), st, hi[7], lo[7]);
         // k-block columns: hi k = 2c, 2c+1 at column c (c < 32), lo at 32 + c
         const uint32_t taddr =
             tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::ACC_COLS + cs * C::WCOLS + cq * 8);
@@ -319,84 +456,10 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         }
       }
     }
-  } else {
-    // Epilogue: TMEM lane quadrant q = warp % 4 = output columns 32q .. 32q+31
-    // of the tile (one per thread); TMEM columns = output rows, half eh of them.
-    // Each 32x32 block goes through shared memory to one TMA store (rows and
-    // columns outside the output are clipped by the TMA unit), or, when the
-    // output rows are not 16-byte multiples, straight to global memory.
-    const int ew = warp - 3 - C::CONV_WARPS;
-    const int q = warp & 3, eh = ew >> 2;
-    int acc = 0, ybuf = 0;
-    uint32_t aphase = 0;
-    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
-      WorkItem it;
-      it.set(w, ksplit, tiles_m, nrb);
-      const int col0 = it.tn * C::BN + q * 32;
-      const int col = col0 + lane;
-      // prefetch while the MMAs run (1 / c_n: a power of two)
-      const float icn = col < N ? exp2_int(-col_range_exp(sw + (size_t)col * (K / 32), K / 32)) : 0.0f;
-      const float bn = (bias && col < N) ? __ldg(bias + col) : 0.0f;
-      float sav[2];  // lane l holds sa of row tm*BM + 32c + l, c = 2eh + i
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int rr = it.tm * C::BM + (2 * eh + i) * 32 + lane;
-        sav[i] = rr < M ? __ldg(sa + rr) : 0.0f;
-      }
-      if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
+    for (; jd < j; ++jd) {
+      if (!drain(jd)) {
         kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
         goto done;
-      }
-      tc_fence_after();
-      // K-split: this slice's sum / c_n goes to slice ks of part (rows
-      // [ks * slice_rows, ks * slice_rows + M)), summed in slice order and
-      // finished by gemm_w4a8_splitk_reduce; else the finished y
-      const int out_row = ksplit > 1 ? it.ks * slice_rows : 0;
-      float* out = ksplit > 1 ? part : Y;
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int c = 2 * eh + i;
-        const int row0 = it.tm * C::BM + c * 32;
-        if (row0 >= M) break;  // uniform across the warp
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BM + c * 32), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float y = __uint_as_float(r[j]);
-          y = __fmul_rn(y, icn);  // exact: a power of two
-          if (ksplit == 1) y = __fadd_rn(__fmul_rn(y, __shfl_sync(0xffffffffu, sav[i], j)), bn);
-          r[j] = __float_as_uint(y);
-        }
-        if (out_tma) {
-          // block row j = output row row0 + j, 128 bytes, 16-byte chunk cc at
-          // cc ^ (j % 8) (128-byte swizzle); lane = column: conflict-free rows
-          uint8_t* buf = ystage + (size_t)(ew * 2 + (ybuf & 1)) * 4096;
-          if (lane == 0) bulk_wait_read<1>();  // the store that last used buf has read it
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            *reinterpret_cast<uint32_t*>(buf + j * 128 + ((((lane >> 2) ^ j) & 7) << 4) + (lane & 3) * 4) = r[j];
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmOut, buf, col0, out_row + row0);
-            bulk_commit();
-          }
-          ++ybuf;
-        } else {
-          float* ycol = out + (size_t)(out_row + row0) * N + col;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)  // a warp writes 32 adjacent columns
-            if (col < N && row0 + j < M) ycol[(size_t)j * N] = __uint_as_float(r[j]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        aphase ^= 1u;
       }
     }
     if (out_tma && lane == 0) bulk_wait<0>();  // all output stores complete

@@ -139,9 +139,17 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
                         const float* __restrict__ sa, const float* __restrict__ sw, const float* __restrict__ bias,
                         float* __restrict__ Y, int32_t* __restrict__ acc_out, int* status,
                         const int* __restrict__ offs = nullptr, int G = 0) {
+  using C = I8Gemm<BN, GROUPED>;
+  if (!GROUPED && threadIdx.x == 0) {  // the first tile's weight boxes into L2 before the dependency wait
+    const int tiles_m = (M + C::BM - 1) / C::BM, tiles_n = (N + BN - 1) / BN;
+    if ((int)blockIdx.x < tiles_m * tiles_n) {
+      TileInfo ti;
+      map_tile<BN, false>(blockIdx.x, tiles_m, tiles_n, M, N, GroupTable{nullptr, nullptr, 0}, ti);
+      for (int kb = 0; kb < (K + C::BK - 1) / C::BK; ++kb) tma_prefetch_2d(&tmB, kb * C::BK, ti.brow0);
+    }
+  }
   pdl_wait();
   pdl_launch();
-  using C = I8Gemm<BN, GROUPED>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;

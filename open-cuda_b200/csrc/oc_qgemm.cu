@@ -65,6 +65,11 @@ __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, c
                                                           int32_t* __restrict__ acc_out) {
   constexpr int COLS = kSkinnyCols, V = COLS * MR;
   constexpr int H = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : 1;
+  {  // this warp's first two weight rows into L2 while the previous kernel finishes
+    const int cg0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if ((threadIdx.x & 31) == 0 && cg0 * COLS < n)
+      prefetch_l2_bulk(wq + (size_t)cg0 * COLS * k, (uint32_t)(min(COLS, n - cg0 * COLS) * k));
+  }
   pdl_wait();
   pdl_launch();
   extern __shared__ int4 s_qa4[];
@@ -175,11 +180,18 @@ __global__ void __launch_bounds__(256) w4a8_skinny_kernel(int m, int n, int k, i
                                                           const float* __restrict__ sw,
                                                           const float* __restrict__ bias, float* __restrict__ Y,
                                                           int32_t* __restrict__ acc_out) {
+  const int nch = k >> 5;  // 32-element chunks per row
+  const int ng = k / group, cpg = group >> 5, pstride = ng | 1;  // odd stride: conflict-free promotion
+  if (threadIdx.x == 0 && blockIdx.x * cb < n) {  // this block's first weight rows and scales into L2
+    const int c0 = blockIdx.x * cb, cols = min(cb, n - c0);
+    prefetch_l2_bulk(wq + (size_t)c0 * (k >> 1), (uint32_t)cols * (k >> 1));
+    const float* s0 = sw + (size_t)c0 * ng;
+    if ((reinterpret_cast<uintptr_t>(s0) & 15u) == 0 && (cols * ng) % 4 == 0)
+      prefetch_l2_bulk(s0, (uint32_t)cols * ng * 4);
+  }
   pdl_wait();
   pdl_launch();
   extern __shared__ int4 s_dyn4[];
-  const int nch = k >> 5;  // 32-element chunks per row
-  const int ng = k / group, cpg = group >> 5, pstride = ng | 1;  // odd stride: conflict-free promotion
   int4* s_lo = s_dyn4;                                           // [m][nch]: even elements of each 8
   int4* s_hi = s_lo + m * nch;                                   // [m][nch]: odd elements
   int* s_sum = reinterpret_cast<int*>(s_hi + m * nch);           // [m][nch] chunk sums
@@ -471,9 +483,10 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
                    const float* bias, float* Y, cudaStream_t s) {
   using C = I4Split;
   const int G = k / 32;
+  const int bm = m > 128 ? C::BM : 128;  // activation rows per tile (the MMA's N)
   CUtensorMap ta, tbp, tsc;
   int rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
-                        C::BK, C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
+                        C::BK, bm, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tbp, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, (uint64_t)k / 2,
                     C::RBK / 2, C::BN, CU_TENSOR_MAP_SWIZZLE_64B);
@@ -484,7 +497,7 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_split_kernel), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_split_kernel) failed");
   const int sms = std::max(1, sm_count());
-  const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
+  const int tiles = ((m + bm - 1) / bm) * ((n + C::BN - 1) / C::BN);
   // too few tiles to fill the GPU: split K (deterministic, finished by a reduction kernel)
   const int ksplit = std::max(1, std::min(k / C::RBK, std::min(8, sms / tiles)));
   const int slice_rows = (m + 31) / 32 * 32;  // a 32-row output block never crosses a slice
@@ -506,7 +519,7 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   }
   const int grid = std::min(tiles * ksplit, sms);
   rc = launch_rc(launch_pdl_ex(gemm_w4a8_split_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc, tout,
-                               out_tma, m, n, k, sa, sw, bias, Y, ksplit, part, slice_rows, device_status_word()),
+                               out_tma, m, n, k, bm, sa, sw, bias, Y, ksplit, part, slice_rows, device_status_word()),
                  "gemm_w4a8_split_kernel");
   if (rc || ksplit == 1) return rc;
   const size_t total = (size_t)m * n;
