@@ -53,8 +53,8 @@ DATA = "synthetic (SplitMix64-seeded inputs as the reference's tests draw them; 
 # the dominant kernel of each workload, from the ncu captures summarised in
 # profiles/ (same kernels and shapes); None where no capture exists yet.
 NCU_TRAFFIC = {
-    "gemm_w4a8 M=2048": 3128064 + 23808,  # profiles/gemm_w4a8_tc_M2048.md
-    "gemm_w8a8 M=2048": 4012032 + 0,  # profiles/gemm_w8a8_tc_M2048.md
+    "gemm_w4a8 M=2048": 4709376 + 0,  # profiles/gemm_w4a8_split_M2048.md
+    "gemm_w8a8 M=2048": 4015616 + 0,  # profiles/gemm_w8a8_tc_M2048.md
 }
 
 
