@@ -5,14 +5,16 @@
 // A = qa [M][K] int8 and B = qw [N][K] int8 are both K-major, as the
 // reference's per-output-channel quantization of W^T lays them out.
 //
-// One CTA per SM (persistent over 128 x BN output tiles), 192 threads:
+// One CTA per SM (persistent over 128 x BN output tiles), 320 threads:
 //   warp 0      TMA producer: 128-byte-swizzled A/B k-blocks into a
 //               STAGES-deep shared-memory ring (mbarrier full/empty pairs)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //               (M=128, N=BN, K=32 per instruction, s32 accumulate)
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, dequantize,
-//               bias, f32 stores; two TMEM accumulators (2 x BN columns)
-//               let the epilogue of tile i overlap the mainloop of tile i+1.
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant (alternate
+//               32-column chunks): tcgen05.ld 32 columns at a time,
+//               dequantize, bias, f32 TMA stores; two TMEM accumulators
+//               (2 x BN columns) let the epilogue of tile i overlap the
+//               mainloop of tile i+1.
 // Every wait is bounded (oc_ptx.cuh): an expired wait writes the kernel
 // status word and the CTA leaves after releasing its TMEM.
 #pragma once
@@ -27,8 +29,9 @@ struct I8Gemm {
   static constexpr int BM = 128, BN = BN_, BK = 128, STAGES = (BN_ == 256 ? 4 : (GROUPED_ ? 5 : 6));
   static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // power of two, <= 512
-  static constexpr int THREADS = 192;
-  static constexpr int YSTAGE_BYTES = 4 * 2 * 4096;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int YSTAGE_BYTES = EPI_WARPS * 4096;  // one 32x32 f32 block per epilogue warp
   // grouped: clamped row offsets [G+1] and 128-row block prefix [G+1]
   static constexpr int GROUP_BYTES = GROUPED_ ? 2 * 4 * (kMaxGroups + 1) : 0;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + YSTAGE_BYTES + 256 + GROUP_BYTES;
@@ -154,7 +157,7 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint8_t* ystage = sB + C::STAGES * C::B_BYTES;  // 4 warps x 2 x 4 KB output staging
+  uint8_t* ystage = sB + C::STAGES * C::B_BYTES;  // 8 warps x 4 KB output staging
   uint64_t* full = reinterpret_cast<uint64_t*>(ystage + C::YSTAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
@@ -173,7 +176,7 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], C::EPI_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -256,10 +259,11 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
       }
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = tile rows.
-    const int q = warp & 3;
+    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = tile rows, and the
+    // 32-column chunks c with c % 2 == eh.
+    const int q = warp & 3, eh = (warp - 2) >> 2;
+    uint8_t* const buf = ystage + (size_t)(warp - 2) * 4096;
     const bool vec = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15u) == 0);
-    uint32_t ybuf = 0;
     int acc = 0;
     uint32_t aphase = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
@@ -272,12 +276,12 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
       // Prefetch this tile's row scale and the column scales / bias (lane l
       // holds column c*32 + l of chunk c) while the MMAs are still running.
       const float sar = row < row_end ? __ldg(sa + row) : 0.0f;
-      float swv[BN / 32], bv[BN / 32];
+      float swv[BN / 64], bv[BN / 64];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        const int cl = ti.col0 + c * 32 + lane;
-        swv[c] = cl < N ? __ldg(sw + ti.sw_off + cl) : 0.0f;
-        bv[c] = (bias && cl < N) ? __ldg(bias + ti.sw_off + cl) : 0.0f;
+      for (int cc = 0; cc < BN / 64; ++cc) {
+        const int cl = ti.col0 + (2 * cc + eh) * 32 + lane;
+        swv[cc] = cl < N ? __ldg(sw + ti.sw_off + cl) : 0.0f;
+        bv[cc] = (bias && cl < N) ? __ldg(bias + ti.sw_off + cl) : 0.0f;
       }
       if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
         kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
@@ -285,15 +289,15 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
       }
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        const int c0 = c * 32;
+      for (int cc = 0; cc < BN / 64; ++cc) {
+        const int c0 = (2 * cc + eh) * 32;
         const int col0 = ti.col0 + c0;
         if (col0 >= N) break;  // uniform across the warp
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c0), r);
         tmem_ld_wait();
-        const float swl = swv[c];
-        const float bl = bv[c];
+        const float swl = swv[cc];
+        const float bl = bv[cc];
         float y[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -305,8 +309,7 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
           // Stage the warp's 32x32 block in shared memory (128-byte swizzle:
           // 16-byte chunk cc of row t at (cc ^ t%8)) and write it with one
           // TMA store; rows/columns past M/N are clipped by the TMA unit.
-          uint8_t* buf = ystage + (size_t)((q * 2 + (ybuf & 1)) * 4096);
-          if (lane == 0) bulk_wait_read<1>();  // the store that last used buf has read it
+          if (lane == 0) bulk_wait_read<0>();  // the previous store has read buf
           __syncwarp();
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc)
@@ -318,7 +321,6 @@ __global__ void __launch_bounds__(I8Gemm<BN, GROUPED>::THREADS, 1)
             tma_store_2d(&tmY, buf, col0, ti.row0 + q * 32);
             bulk_commit();
           }
-          ++ybuf;
         } else if (row < row_end) {
           float* yrow = Y + (size_t)row * N + col0;
           if (vec && col0 + 32 <= N) {
