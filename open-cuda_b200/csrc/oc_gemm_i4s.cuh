@@ -65,6 +65,7 @@ struct I4Split {
   static_assert(RSTAGE_BYTES % 1024 == 0 && A16_BYTES % 1024 == 0, "1024-byte stage alignment");
   static_assert(CONV_WARPS == 16, "four converter warps per TMEM lane quadrant");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(BN == 128, "the split-K reduction maps a warp to a tile row of 128 columns");
 };
 
 // a - b, a * b, a * b + c on two f16 lanes (IEEE round to nearest each)
@@ -125,17 +126,43 @@ __device__ __forceinline__ void split_pair(uint32_t w2, const ScaleTerms& st, ui
   lo2 = hsub2_bits(hmul2_bits(w2, st.lo), err);
 }
 
-// Work item w of the dequantizing kernel: tile w / ksplit (tm fastest) and
-// K slice w % ksplit, covering raw k-blocks [rb0, rb1).
+// Work schedule of the dequantizing kernel: work items [0, full) are whole
+// tiles (tile w, tm fastest); the remaining nsplit tiles (full .. full +
+// nsplit - 1) are split into ksplit K slices each, item full + u covering
+// slice u % ksplit of tile full + u / ksplit.  Split items write their
+// partial sums to a workspace; gemm_w4a8_splitk_reduce adds them in slice
+// order.  (All tiles split when the tiles do not fill the GPU; only the last
+// round's tiles when they leave most SMs idle.)
+struct SplitPlan {
+  int tiles_m, nrb, full, ksplit, nsplit;
+  __host__ __device__ int items() const { return full + nsplit * ksplit; }
+};
+
+// Work item w: tile (tm, tn), raw k-blocks [rb0, rb1); for a split item its
+// slice ks and the index sidx of its tile among the split tiles.
 struct WorkItem {
-  int tm, tn, ks, rb0, rb1;
-  __device__ __forceinline__ void set(int w, int ksplit, int tiles_m, int nrb) {
-    const int tile = w / ksplit;
-    ks = w - tile * ksplit;
-    tm = tile % tiles_m;
-    tn = tile / tiles_m;
-    rb0 = ks * nrb / ksplit;
-    rb1 = (ks + 1) * nrb / ksplit;
+  int tm, tn, ks, sidx, rb0, rb1;
+  bool split;
+  __device__ __forceinline__ void set(int w, const SplitPlan& sp) {
+    int tile;
+    if (w < sp.full) {
+      tile = w;
+      ks = 0;
+      sidx = 0;
+      rb0 = 0;
+      rb1 = sp.nrb;
+      split = false;
+    } else {
+      const int u = w - sp.full;
+      sidx = u / sp.ksplit;
+      ks = u - sidx * sp.ksplit;
+      tile = sp.full + sidx;
+      rb0 = ks * sp.nrb / sp.ksplit;
+      rb1 = (ks + 1) * sp.nrb / sp.ksplit;
+      split = true;
+    }
+    tm = tile % sp.tiles_m;
+    tn = tile / sp.tiles_m;
   }
 };
 
@@ -161,19 +188,19 @@ __device__ __forceinline__ float exp2_int(int e) { return __uint_as_float((uint3
 __global__ void __launch_bounds__(I4Split::THREADS, 1)
     gemm_w4a8_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBp,
                            const __grid_constant__ CUtensorMap tmS,
-                           const __grid_constant__ CUtensorMap tmOut, int out_tma, int M, int N, int K, int bm,
+                           const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPart,
+                           int out_tma, int M, int N, int K, int bm, int full, int ksplit, int nsplit,
                            const float* __restrict__ sa, const float* __restrict__ sw,
-                           const float* __restrict__ bias, float* __restrict__ Y, int ksplit,
-                           float* __restrict__ part, int slice_rows, int* status) {
+                           const float* __restrict__ bias, float* __restrict__ Y, int* status) {
   using C = I4Split;
   const int tiles_m = (M + bm - 1) / bm;
-  const int tiles_n = (N + C::BN - 1) / C::BN;
   const int nrb = K / C::RBK;  // K % 128 == 0 on this path
-  const int nitems = tiles_m * tiles_n * ksplit;  // ksplit <= nrb: every item has raw blocks
+  const SplitPlan sp{tiles_m, nrb, full, ksplit, nsplit};
+  const int nitems = sp.items();  // ksplit <= nrb: every item has raw blocks
   if (threadIdx.x == 0 && (int)blockIdx.x < nitems) {
     // the first item's packed weights and scales into L2 before the dependency wait
     WorkItem it;
-    it.set(blockIdx.x, ksplit, tiles_m, nrb);
+    it.set(blockIdx.x, sp);
     for (int rb = it.rb0; rb < it.rb1; ++rb) {
       tma_prefetch_2d(&tmBp, rb * (C::RBK / 2), it.tn * C::BN);
       tma_prefetch_2d(&tmS, rb * C::RGROUPS, it.tn * C::BN);
@@ -217,6 +244,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     prefetch_tmap(&tmBp);
     prefetch_tmap(&tmS);
     if (out_tma) prefetch_tmap(&tmOut);
+    if (nsplit) prefetch_tmap(&tmPart);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -232,7 +260,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       int ri = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
         WorkItem it;
-        it.set(w, ksplit, tiles_m, nrb);
+        it.set(w, sp);
         for (int rb = it.rb0; rb < it.rb1; ++rb, ++ri) {
           const int rs = ri % C::RSTAGES;
           const uint32_t rph = (uint32_t)(ri / C::RSTAGES) & 1u;
@@ -253,7 +281,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       uint32_t tphase = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
         WorkItem it;
-        it.set(w, ksplit, tiles_m, nrb);
+        it.set(w, sp);
         if (!mbar_wait(tempty, tphase ^ 1u, abort_flag)) {  // the previous tile is drained
           kernel_fail(status, abort_flag, kDevTimeoutMma);
           goto done;
@@ -286,7 +314,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       int ci = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
         WorkItem it;
-        it.set(w, ksplit, tiles_m, nrb);
+        it.set(w, sp);
         for (int cb = 2 * it.rb0; cb < 2 * it.rb1; ++cb, ++ci) {
           const int cs = ci % C::CSTAGES;
           const uint32_t cph = (uint32_t)(ci / C::CSTAGES) & 1u;
@@ -316,7 +344,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     // Drain item j of this CTA (work index blockIdx.x + j * gridDim.x).
     auto drain = [&](int j) -> bool {
       WorkItem it;
-      it.set(blockIdx.x + j * gridDim.x, ksplit, tiles_m, nrb);
+      it.set(blockIdx.x + j * gridDim.x, sp);
       const int col0 = it.tn * C::BN + q * 32, col = col0 + lane;
       // 1 / c_n (a power of two), bias and row scales, loaded while the MMAs finish
       const float icn = col < N ? exp2_int(-col_range_exp(sw + (size_t)col * G, G)) : 0.0f;
@@ -331,11 +359,9 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
       if (!mbar_wait(tfull, dphase, abort_flag)) return false;
       dphase ^= 1u;
       tc_fence_after();
-      // K-split: this slice's sum / c_n goes to slice ks of part (rows
-      // [ks * slice_rows, ks * slice_rows + M)), summed in slice order and
-      // finished by gemm_w4a8_splitk_reduce; else the finished y
-      const int out_row = ksplit > 1 ? it.ks * slice_rows : 0;
-      float* out = ksplit > 1 ? part : Y;
+      // split item: this slice's sum / c_n goes to the workspace block
+      // [ks][sidx] ([bm][128] f32, through tmPart), summed in slice order by
+      // gemm_w4a8_splitk_reduce; else the finished y
       // block 0 is finished and stored, block 1 loaded, and then the
       // accumulator is released: the next tile's MMAs overlap block 1's work
       int nblk = 0;
@@ -355,7 +381,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         }
         if (i >= nblk) continue;
         const int rb0 = row0 + 32 * i;
-        if (ksplit == 1) {  // y = acc * (sa / c_n) + bias, one rounding (sa / c_n is exact)
+        if (!it.split) {  // y = acc * (sa / c_n) + bias, one rounding (sa / c_n is exact)
           const float4* f4 = reinterpret_cast<const float4*>(wsa + i * 32);
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {
@@ -369,7 +395,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
 #pragma unroll
           for (int j2 = 0; j2 < 32; ++j2) r[j2] = __float_as_uint(__fmul_rn(__uint_as_float(r[j2]), icn));
         }
-        if (out_tma) {
+        if (out_tma || it.split) {
           // block row j2 = output row rb0 + j2, 128 bytes, 16-byte chunk cc
           // at cc ^ (j2 % 8) (128-byte swizzle); lane = column: conflict-free
           if (lane == 0) bulk_wait_read<0>();  // the previous store has read the buffer
@@ -380,11 +406,14 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmOut, ybuf, col0, out_row + rb0);
+            if (it.split)
+              tma_store_2d(&tmPart, ybuf, q * 32, (it.ks * nsplit + it.sidx) * bm + (rb0 - it.tm * bm));
+            else
+              tma_store_2d(&tmOut, ybuf, col0, rb0);
             bulk_commit();
           }
         } else {
-          float* ycol = out + (size_t)(out_row + rb0) * N + col;
+          float* ycol = Y + (size_t)rb0 * N + col;
 #pragma unroll
           for (int j2 = 0; j2 < 32; ++j2)  // a warp writes 32 adjacent columns
             if (col < N && rb0 + j2 < M) ycol[(size_t)j2 * N] = __uint_as_float(r[j2]);
@@ -396,13 +425,13 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
     int ci = 0, jd = 0, jd_next_first = 0;  // next item to drain; first k-block of the item after it
     {
       WorkItem it0;
-      it0.set(blockIdx.x, ksplit, tiles_m, nrb);
+      it0.set(blockIdx.x, sp);
       jd_next_first = 2 * (it0.rb1 - it0.rb0);
     }
     int j = 0;
     for (int w = blockIdx.x; w < nitems; w += gridDim.x, ++j) {
       WorkItem it;
-      it.set(w, ksplit, tiles_m, nrb);
+      it.set(w, sp);
       const int col = it.tn * C::BN + cr;
       const float cval = col < N ? exp2_int(col_range_exp(sw + (size_t)col * G, G)) : 1.0f;
       for (int kb = 0; kb < 2 * (it.rb1 - it.rb0); ++kb, ++ci) {
@@ -415,7 +444,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
           }
           ++jd;  // first_kb(jd + 1) = first_kb(jd) + k-blocks of item jd
           WorkItem nx;
-          nx.set(blockIdx.x + jd * gridDim.x, ksplit, tiles_m, nrb);
+          nx.set(blockIdx.x + jd * gridDim.x, sp);
           jd_next_first += 2 * (nx.rb1 - nx.rb0);
         }
         const int cs = ci % C::CSTAGES;
@@ -462,7 +491,7 @@ __global__ void __launch_bounds__(I4Split::THREADS, 1)
         goto done;
       }
     }
-    if (out_tma && lane == 0) bulk_wait<0>();  // all output stores complete
+    if (lane == 0) bulk_wait<0>();  // all output stores complete
     __syncwarp();
   }
 done:
@@ -474,21 +503,44 @@ done:
   }
 }
 
-// Finishes a K-split dequantizing GEMM: y = (sum_s part[s]) * sa + bias, the
-// slices (each already divided by c_n, exactly) added in slice order.
-__global__ void gemm_w4a8_splitk_reduce(const float* __restrict__ part, int ksplit, int slice_rows, int M, int N,
-                                        const float* __restrict__ sa,
-                                        const float* __restrict__ bias, float* __restrict__ Y) {
+// Finishes the split tiles of the dequantizing GEMM: for split tile sidx and
+// its element (r, c), y = (sum over slices ks, in order, of the workspace
+// block [ks][sidx][r][c] (each already divided by c_n, exactly)) * sa + bias.
+// Block = 8 rows of one split tile, thread = 4 adjacent columns (one 16-byte
+// load per slice, all slices in flight at once).
+constexpr int kReduceRows = 8;
+__global__ void __launch_bounds__(256) gemm_w4a8_splitk_reduce(const float* __restrict__ part, int full, int ksplit,
+                                                               int nsplit, int tiles_m, int bm, int M, int N,
+                                                               const float* __restrict__ sa,
+                                                               const float* __restrict__ bias, float* __restrict__ Y) {
   pdl_wait();
   pdl_launch();
-  const size_t total = (size_t)M * N, slice = (size_t)slice_rows * N, stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int row = (int)(i / N), col = (int)(i - (size_t)row * N);
-    float v = 0.0f;
-    for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(part + (size_t)s * slice + i));
-    const float y = __fmul_rn(v, __ldg(sa + row));
-    Y[i] = __fadd_rn(y, bias ? __ldg(bias + col) : 0.0f);
-  }
+  const int bands = bm / kReduceRows;
+  const int sidx = blockIdx.x / bands, r = (blockIdx.x - sidx * bands) * kReduceRows + (threadIdx.x >> 5);
+  const int c = (threadIdx.x & 31) * 4, tile = full + sidx;
+  const int row = (tile % tiles_m) * bm + r, col = (tile / tiles_m) * I4Split::BN + c;
+  if (row >= M || col >= N) return;
+  const size_t slice = (size_t)nsplit * bm * I4Split::BN;
+  const float4* p = reinterpret_cast<const float4*>(part + ((size_t)sidx * bm + r) * I4Split::BN + c);
+  float4 v[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s)
+    if (s < ksplit) v[s] = __ldg(p + s * (slice / 4));
+  float4 t = v[0];
+#pragma unroll
+  for (int s = 1; s < 8; ++s)
+    if (s < ksplit) {
+      t.x = __fadd_rn(t.x, v[s].x);
+      t.y = __fadd_rn(t.y, v[s].y);
+      t.z = __fadd_rn(t.z, v[s].z);
+      t.w = __fadd_rn(t.w, v[s].w);
+    }
+  const float a = __ldg(sa + row);
+  const float tv[4] = {t.x, t.y, t.z, t.w};
+  float* yr = Y + (size_t)row * N;
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (col + e < N) yr[col + e] = __fadd_rn(__fmul_rn(tv[e], a), bias ? __ldg(bias + col + e) : 0.0f);
 }
 
 int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq, const float* sw,

@@ -497,35 +497,48 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_split_kernel), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_split_kernel) failed");
   const int sms = std::max(1, sm_count());
-  const int tiles = ((m + bm - 1) / bm) * ((n + C::BN - 1) / C::BN);
-  // too few tiles to fill the GPU: split K (deterministic, finished by a reduction kernel)
-  const int ksplit = std::max(1, std::min(k / C::RBK, std::min(8, sms / tiles)));
-  const int slice_rows = (m + 31) / 32 * 32;  // a 32-row output block never crosses a slice
+  const int tiles_m = (m + bm - 1) / bm;
+  const int tiles = tiles_m * ((n + C::BN - 1) / C::BN);
+  const int nrb = k / C::RBK;
+  // Split K where SMs would idle: every tile when the tiles do not fill the
+  // GPU; only the last round's tiles when that round leaves more than half
+  // of the SMs idle.  Partial sums are added in slice order (deterministic).
+  SplitPlan sp{tiles_m, nrb, tiles, 1, 0};
+  if (tiles < sms) {
+    const int ks = std::min(nrb, std::min(8, sms / tiles));
+    if (ks > 1) sp = SplitPlan{tiles_m, nrb, 0, ks, tiles};
+  } else if (tiles % sms != 0 && tiles % sms <= sms / 2) {
+    const int tail = tiles % sms;
+    const int ks = std::min(nrb, std::min(8, sms / tail));
+    if (ks > 1) sp = SplitPlan{tiles_m, nrb, tiles - tail, ks, tail};
+  }
   float* part = nullptr;
-  if (ksplit > 1) {
-    part = g_w4_part.get((size_t)ksplit * slice_rows * n, s);
+  CUtensorMap tout = tsc, tpart = tsc;
+  if (sp.nsplit) {  // workspace [ksplit][nsplit][bm][128] f32
+    const size_t rows = (size_t)sp.ksplit * sp.nsplit * bm;
+    part = g_w4_part.get(rows * C::BN, s);
     if (!part) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
+    rc = make_tmap_2d(&tpart, part, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)C::BN, rows, (uint64_t)C::BN * 4,
+                      32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
   }
   // outputs leave through 32x32 TMA stores when rows are 16-byte multiples
-  CUtensorMap tout = tsc;
   int out_tma = 0;
-  if (n % 4 == 0 && (ksplit > 1 || aligned16(Y))) {
-    float* base = ksplit > 1 ? part : Y;
-    const uint64_t rows = ksplit > 1 ? (uint64_t)ksplit * slice_rows : (uint64_t)m;
-    rc = make_tmap_2d(&tout, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)n, rows, (uint64_t)n * 4, 32, 32,
+  if (n % 4 == 0 && aligned16(Y)) {
+    rc = make_tmap_2d(&tout, Y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)n, (uint64_t)m, (uint64_t)n * 4, 32, 32,
                       CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     out_tma = 1;
   }
-  const int grid = std::min(tiles * ksplit, sms);
+  const int grid = std::min(sp.items(), sms);
   rc = launch_rc(launch_pdl_ex(gemm_w4a8_split_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc, tout,
-                               out_tma, m, n, k, bm, sa, sw, bias, Y, ksplit, part, slice_rows, device_status_word()),
+                               tpart, out_tma, m, n, k, bm, sp.full, sp.ksplit, sp.nsplit, sa, sw, bias, Y,
+                               device_status_word()),
                  "gemm_w4a8_split_kernel");
-  if (rc || ksplit == 1) return rc;
-  const size_t total = (size_t)m * n;
-  const int rb = (int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
-  return launch_rc(launch_pdl_ex(gemm_w4a8_splitk_reduce, dim3(rb), dim3(256), 0, s, part, ksplit, slice_rows, m, n,
-                                 sa, bias, Y),
+  if (rc || !sp.nsplit) return rc;
+  const int rb = sp.nsplit * (bm / kReduceRows);  // bm is 128 or 256
+  return launch_rc(launch_pdl_ex(gemm_w4a8_splitk_reduce, dim3(rb), dim3(256), 0, s, part, sp.full, sp.ksplit,
+                                 sp.nsplit, tiles_m, bm, m, n, sa, bias, Y),
                    "gemm_w4a8_splitk_reduce");
 }
 

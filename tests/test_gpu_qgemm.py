@@ -112,6 +112,9 @@ QGEMM_SHAPES = [
     (1200, 384, 4100),
     # skinny rows whose activations exceed shared memory: split into launches
     (16, 16384, 40),
+    # more tiles than SMs with a ragged last round (its tiles split in K) and
+    # rows that are not 16-byte multiples (no TMA stores)
+    (300, 256, 11522),
 ]
 
 
