@@ -69,8 +69,11 @@ __device__ __forceinline__ void tf_fail(int* status, volatile int* abort_flag, i
 __global__ void __launch_bounds__(448, 1)
     sgemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
                         const __grid_constant__ CUtensorMap tmBl, int M, int N, int K, float alpha, float beta,
-                        float* __restrict__ Cm, int ldc, const float* __restrict__ bias, int* status) {
+                        float* __restrict__ Cm, int ldc, const float* __restrict__ bias, int ksplit,
+                        float* __restrict__ part, int* status) {
   using C = TfGemm;
+  pdl_wait();
+  pdl_launch();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // stage s: [A hi | A lo | B hi | B lo], 16 KB each
@@ -111,17 +114,35 @@ __global__ void __launch_bounds__(448, 1)
 
   const int tiles_m = (M + C::BM - 1) / C::BM;
   const int tiles_n = (N + C::BN - 1) / C::BN;
-  const int ntiles = tiles_m * tiles_n;
   const int nkb = (K + C::BK - 1) / C::BK;
   const int nseg = (nkb + C::SEG_KB - 1) / C::SEG_KB;
+  // work item w: tile w / ksplit (tm fastest), K segments [seg0, seg1) of
+  // slice w % ksplit; a split item leaves its raw sums in part[slice]
+  const int nitems = tiles_m * tiles_n * ksplit;
+  struct Item {
+    int tm, tn, ks, seg0, seg1, kb0, kb1;
+  };
+  auto item = [&](int w) {
+    Item it;
+    const int tile = w / ksplit;
+    it.ks = w - tile * ksplit;
+    it.tm = tile % tiles_m;
+    it.tn = tile / tiles_m;
+    it.seg0 = it.ks * nseg / ksplit;
+    it.seg1 = (it.ks + 1) * nseg / ksplit;
+    it.kb0 = it.seg0 * C::SEG_KB;
+    it.kb1 = min(nkb, it.seg1 * C::SEG_KB);
+    return it;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int tm = tile % tiles_m, tn = tile / tiles_m;
-        for (int kb = 0; kb < nkb; ++kb) {
+      for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+        const Item it = item(w);
+        const int tm = it.tm, tn = it.tn;
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             tf_fail(status, abort_flag, kDevTimeoutProducer);
             goto done;
@@ -142,8 +163,9 @@ __global__ void __launch_bounds__(448, 1)
     if (lane == 0) {
       int stage = 0, acc = 0;
       uint32_t phase = 0, aphase = 0;
-      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        for (int seg = 0; seg < nseg; ++seg) {
+      for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+        const Item it = item(w);
+        for (int seg = it.seg0; seg < it.seg1; ++seg) {
           if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) {
             tf_fail(status, abort_flag, kDevTimeoutMma);
             goto done;
@@ -188,8 +210,9 @@ __global__ void __launch_bounds__(448, 1)
     const int t = threadIdx.x - 64;
     int stage = 0;
     uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      for (int kb = 0; kb < nkb; ++kb) {
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+      const Item it = item(w);
+      for (int kb = it.kb0; kb < it.kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) {
           tf_fail(status, abort_flag, kDevTimeoutProducer);
           goto done;
@@ -213,8 +236,9 @@ __global__ void __launch_bounds__(448, 1)
     const bool vec = ((N & 3) == 0) && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(Cm) & 15u) == 0);
     int acc = 0;
     uint32_t aphase = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const int tm = tile % tiles_m, tn = tile / tiles_m;
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+      const Item it = item(w);
+      const int tm = it.tm, tn = it.tn;
       const int row = tm * C::BM + q * 32 + lane;
       const int colb = tn * C::BN + h * 64;
       float bv[2];
@@ -226,7 +250,7 @@ __global__ void __launch_bounds__(448, 1)
       float s[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) s[i] = 0.0f;
-      for (int seg = 0; seg < nseg; ++seg) {
+      for (int seg = it.seg0; seg < it.seg1; ++seg) {
         if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
           tf_fail(status, abort_flag, kDevTimeoutEpilogue);
           goto done;
@@ -248,6 +272,27 @@ __global__ void __launch_bounds__(448, 1)
           acc = 0;
           aphase ^= 1u;
         }
+      }
+      if (ksplit > 1) {  // raw sums of this slice: part[ks][row][col], dense M x N
+        if (row < M) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int col0 = colb + c * 32;
+            float* prow = part + ((size_t)it.ks * M + row) * N + col0;
+            if (col0 >= N) break;
+            if ((N & 3) == 0 && col0 + 32 <= N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(prow + j) =
+                    make_float4(s[c * 32 + j], s[c * 32 + j + 1], s[c * 32 + j + 2], s[c * 32 + j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) prow[j] = s[c * 32 + j];
+            }
+          }
+        }
+        continue;
       }
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -291,6 +336,8 @@ done:
 // transposes [k][ldb] through a 32x33 shared tile.
 __global__ void split_b_kernel(const float* __restrict__ B, int ldb, int trans_b, int k, int n, int kp,
                                float* __restrict__ hi, float* __restrict__ lo) {
+  pdl_wait();
+  pdl_launch();
   __shared__ float tile[32][33];
   const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
@@ -328,6 +375,8 @@ template <int MR>
 __global__ void __launch_bounds__(256) sgemv_partial_kn(int m, int n, int k, const float* __restrict__ A, int lda,
                                                         const float* __restrict__ B, int ldb,
                                                         float* __restrict__ part) {
+  pdl_wait();
+  pdl_launch();
   __shared__ float sa[MR][kKsl];
   const int k0 = blockIdx.y * kKsl, kn = min(kKsl, k - k0);
   for (int i = threadIdx.x; i < MR * kKsl; i += 256) {
@@ -356,6 +405,8 @@ template <int MR>
 __global__ void __launch_bounds__(256) sgemv_partial_nk(int m, int n, int k, const float* __restrict__ A, int lda,
                                                         const float* __restrict__ B, int ldb,
                                                         float* __restrict__ part) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int col = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (col >= n) return;
@@ -384,6 +435,8 @@ __global__ void __launch_bounds__(256) sgemv_partial_nk(int m, int n, int k, con
 
 __global__ void sgemv_reduce(int m, int n, int slices, const float* __restrict__ part, float alpha, float beta,
                              float* __restrict__ Cm, int ldc, const float* __restrict__ bias) {
+  pdl_wait();
+  pdl_launch();
   const size_t total = (size_t)m * n;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / n), col = (int)(i % n);
@@ -396,42 +449,41 @@ __global__ void sgemv_reduce(int m, int n, int slices, const float* __restrict__
   }
 }
 
-static StreamScratch g_gemv_ws, g_bprep_ws;
+static StreamScratch g_gemv_ws, g_bprep_ws, g_tf_part;
+
+// C = alpha * (sum of the slices of part, in order) + beta * C (+ bias).
+static int launch_reduce(int m, int n, int slices, const float* part, float alpha, float beta, float* Cm, int ldc,
+                         const float* bias, cudaStream_t s) {
+  const int rb = (int)std::min<size_t>(((size_t)m * n + 255) / 256, (size_t)std::max(1, sm_count()) * 8);
+  const cudaError_t e = launch_pdl_ex(sgemv_reduce, dim3(std::max(1, rb)), dim3(256), 0, s, m, n, slices, part, alpha,
+                                      beta, Cm, ldc, bias);
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "sgemv_reduce");
+}
 
 static int launch_gemv(int m, int n, int k, float alpha, const float* A, int lda, const float* B, int ldb,
                        int trans_b, float beta, float* Cm, int ldc, const float* bias, cudaStream_t s) {
   const int slices = trans_b ? (k + 32 * kKsl - 1) / (32 * kKsl) : (k + kKsl - 1) / kKsl;
   float* part = g_gemv_ws.get((size_t)slices * m * n, s);
   if (!part) return fail(OC_ERR_OUT_OF_MEMORY, "sgemv: scratch allocation failed");
+  cudaError_t e;
   if (!trans_b) {
     dim3 grid((n + 255) / 256, slices);
-    if (m <= 1)
-      sgemv_partial_kn<1><<<grid, 256, 0, s>>>(m, n, k, A, lda, B, ldb, part);
-    else if (m <= 4)
-      sgemv_partial_kn<4><<<grid, 256, 0, s>>>(m, n, k, A, lda, B, ldb, part);
-    else
-      sgemv_partial_kn<8><<<grid, 256, 0, s>>>(m, n, k, A, lda, B, ldb, part);
+    auto kern = m <= 1 ? sgemv_partial_kn<1> : m <= 4 ? sgemv_partial_kn<4> : sgemv_partial_kn<8>;
+    e = launch_pdl_ex(kern, grid, dim3(256), 0, s, m, n, k, A, lda, B, ldb, part);
   } else {
     dim3 grid((n + 7) / 8, slices);
-    if (m <= 1)
-      sgemv_partial_nk<1><<<grid, 256, 0, s>>>(m, n, k, A, lda, B, ldb, part);
-    else if (m <= 4)
-      sgemv_partial_nk<4><<<grid, 256, 0, s>>>(m, n, k, A, lda, B, ldb, part);
-    else
-      sgemv_partial_nk<8><<<grid, 256, 0, s>>>(m, n, k, A, lda, B, ldb, part);
+    auto kern = m <= 1 ? sgemv_partial_nk<1> : m <= 4 ? sgemv_partial_nk<4> : sgemv_partial_nk<8>;
+    e = launch_pdl_ex(kern, grid, dim3(256), 0, s, m, n, k, A, lda, B, ldb, part);
   }
-  const int rb = (int)std::min<size_t>(((size_t)m * n + 255) / 256, (size_t)std::max(1, sm_count()) * 8);
-  sgemv_reduce<<<std::max(1, rb), 256, 0, s>>>(m, n, slices, part, alpha, beta, Cm, ldc, bias);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? OC_OK : from_cuda(e, "sgemv kernels");
+  if (e != cudaSuccess) return from_cuda(e, "sgemv_partial kernel");
+  return launch_reduce(m, n, slices, part, alpha, beta, Cm, ldc, bias, s);
 }
 
 static int kpad(int k) { return (k + 3) & ~3; }
 
 int launch_split_b(const float* B, int ldb, int trans_b, int k, int n, float* hi, float* lo, cudaStream_t s) {
   dim3 grid((n + 31) / 32, (kpad(k) + 31) / 32);
-  split_b_kernel<<<grid, 256, 0, s>>>(B, ldb, trans_b, k, n, kpad(k), hi, lo);
-  cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl_ex(split_b_kernel, grid, dim3(256), 0, s, B, ldb, trans_b, k, n, kpad(k), hi, lo);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "split_b_kernel");
 }
 
@@ -450,12 +502,23 @@ int launch_tf32_gemm(int m, int n, int k, float alpha, const float* A, int lda, 
   if (rc) return rc;
   if (!smem_attr_once(reinterpret_cast<const void*>(sgemm_tf32x3_kernel), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(sgemm_tf32x3_kernel) failed");
+  const int sms = std::max(1, sm_count());
   const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
-  const int grid = std::min(tiles, std::max(1, sm_count()));
-  sgemm_tf32x3_kernel<<<grid, C::THREADS, C::SMEM, s>>>(ta, tbh, tbl, m, n, k, alpha, beta, Cm, ldc, bias,
-                                                        device_status_word());
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? OC_OK : from_cuda(e, "sgemm_tf32x3_kernel");
+  // tiles for at most half of the SMs: split the K segments across CTAs and
+  // add the slices in order afterwards (with the alpha/beta/bias epilogue)
+  const int nseg = ((k + C::BK - 1) / C::BK + C::SEG_KB - 1) / C::SEG_KB;
+  const int ksplit = 2 * tiles <= sms ? std::max(1, std::min(nseg, std::min(4, sms / tiles))) : 1;
+  float* part = nullptr;
+  if (ksplit > 1) {
+    part = g_tf_part.get((size_t)ksplit * m * n, s);
+    if (!part) return fail(OC_ERR_OUT_OF_MEMORY, "sgemm: scratch allocation failed");
+  }
+  const int grid = std::min(tiles * ksplit, sms);
+  cudaError_t e = launch_pdl_ex(sgemm_tf32x3_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbh, tbl, m, n, k,
+                                alpha, beta, Cm, ldc, bias, ksplit, part, device_status_word());
+  if (e != cudaSuccess) return from_cuda(e, "sgemm_tf32x3_kernel");
+  if (ksplit == 1) return OC_OK;
+  return launch_reduce(m, n, ksplit, part, alpha, beta, Cm, ldc, bias, s);
 }
 
 }  // namespace oc
@@ -501,10 +564,7 @@ int oc_sgemm(int m, int n, int k, float alpha, const float* A, int lda, const fl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (k == 0) {
     // acc = 0 for every element: C = alpha*0 + beta*C (+ bias); no operand reads
-    const int rb = (int)std::min<size_t>(((size_t)m * n + 255) / 256, (size_t)std::max(1, sm_count()) * 8);
-    sgemv_reduce<<<std::max(1, rb), 256, 0, s>>>(m, n, 0, nullptr, alpha, beta, C, ldc, bias);
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? OC_OK : from_cuda(e, "sgemv_reduce");
+    return launch_reduce(m, n, 0, nullptr, alpha, beta, C, ldc, bias, s);
   }
   OC_REQUIRE(A && B, "sgemm: NULL pointer");
   const bool tma_ok = is_sm100() && aligned16(A) && (lda % 4 == 0);
