@@ -748,6 +748,10 @@ static void launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
   launch_pdl(kern, dim3(p.tiles, p.slices), dim3(256), p.smem, s, a);
 }
 
+// Rows up to which a linear runs as the fused split-K GEMV; more rows go to
+// the 3xTF32 tensor-core GEMM (split-K when its tiles are few).
+constexpr int kGptGemvRows = 16;
+
 // out[rows][L.out] = epilogue(x[rows][L.in] . W + b) (GemvEpi); *n += kernels
 // launched.  Up to 32 rows: one split-K GEMV with the epilogue fused; more
 // rows: the tensor-core GEMM, then the epilogue as its own kernel.
@@ -758,12 +762,12 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
                const float* ln_b = nullptr) {
   cudaStream_t s = g->stream;
   const int H = (int)g->cfg.hidden_size, ms = (int)g->cfg.max_seq_len;
-  if (rows > 32 && ln_w) {
+  if (rows > kGptGemvRows && ln_w) {
     layernorm_kernel<<<rows, 256, 0, s>>>(x, L.in, g->normed, L.in, ln_w, ln_b, g->cfg.layer_norm_eps);
     *n += 1;
     x = g->normed;
   }
-  if (rows > 32) {
+  if (rows > kGptGemvRows) {
     float* dst = epi == kEpiResidual ? g->tmp : out;
     int rc = oc_sgemm_prepared(rows, L.out, L.in, 1.0f, x, L.in, L.prep, 0.0f, dst, L.out, L.b, s);
     if (rc) return rc;
@@ -780,8 +784,7 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
     if (rows <= 1) launch_gemv<1, 4>(p, a, s);
     else if (rows <= 4) launch_gemv<4, 4>(p, a, s);
     else if (rows <= 8) launch_gemv<8, 4>(p, a, s);
-    else if (rows <= 16) launch_gemv<16, 2>(p, a, s);
-    else launch_gemv<32, 2>(p, a, s);
+    else launch_gemv<16, 2>(p, a, s);
     *n += 1;
   }
   cudaError_t e = launch_status();
@@ -873,9 +876,9 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
   // decode GEMV scratch: per-slice partials [slices][rows][out] and the
   // column-tile counters, for every row bucket the GEMV path serves
   // (rows <= min(R, 32))
-  const int gemv_rows = (int)std::min<size_t>(R, 32);
+  const int gemv_rows = (int)std::min<size_t>(R, kGptGemvRows);
   for (const GptLinear* L : {&g->lm, &g->layers[0].qkv, &g->layers[0].ao, &g->layers[0].fc, &g->layers[0].pj}) {
-    for (int bucket : {1, 4, 8, 16, 32}) {
+    for (int bucket : {1, 4, 8, 16}) {
       const GemvPlan p = gemv_plan(L->in, L->out, bucket);
       g->part_floats = std::max(g->part_floats, (size_t)p.slices * std::min(bucket, gemv_rows) * L->out);
       g->counter_count = std::max(g->counter_count, (size_t)p.tiles);

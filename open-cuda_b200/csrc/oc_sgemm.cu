@@ -507,7 +507,7 @@ int launch_tf32_gemm(int m, int n, int k, float alpha, const float* A, int lda, 
   // tiles for at most half of the SMs: split the K segments across CTAs and
   // add the slices in order afterwards (with the alpha/beta/bias epilogue)
   const int nseg = ((k + C::BK - 1) / C::BK + C::SEG_KB - 1) / C::SEG_KB;
-  const int ksplit = 2 * tiles <= sms ? std::max(1, std::min(nseg, std::min(4, sms / tiles))) : 1;
+  const int ksplit = 2 * tiles <= sms ? std::max(1, std::min(nseg, std::min(8, sms / tiles))) : 1;
   float* part = nullptr;
   if (ksplit > 1) {
     part = g_tf_part.get((size_t)ksplit * m * n, s);
