@@ -19,6 +19,7 @@
 #include <cstring>
 #include <vector>
 
+#include "oc_gemm_epi.cuh"
 #include "oc_internal.h"
 #include "oc_ptx.cuh"
 
@@ -104,37 +105,6 @@ __global__ void layernorm_kernel(const float* __restrict__ x, size_t x_stride, f
   const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(var, eps)));
   for (int c = threadIdx.x; c < H; c += blockDim.x)
     yr[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[c], mean), inv), w[c]), b[c]);
-}
-
-// gelu_new in f64, cast to f32 (llm:268-275).
-__global__ void gelu_kernel(float* __restrict__ x, size_t n) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    const double xf = (double)x[i];
-    const double inner = 0.7978845608028654 * (xf + 0.044715 * (xf * xf * xf));
-    x[i] = (float)(0.5 * xf * (1.0 + tanh(inner)));
-  }
-}
-
-__global__ void add_kernel(float* __restrict__ acc, const float* __restrict__ d, size_t n) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    acc[i] = __fadd_rn(acc[i], d[i]);
-}
-
-// Writes the k and v columns of qkv rows into the cache at positions
-// pos0 + i (rows r = b * L + i).
-__global__ void kv_store_kernel(const float* __restrict__ qkv, int L, const int* __restrict__ pos0, int H,
-                                float* __restrict__ kc, float* __restrict__ vc, int max_seq, int rows) {
-  const int r = blockIdx.x;
-  if (r >= rows) return;
-  const int b = r / L, i = r % L;
-  const int p = *pos0 + i;
-  const float* src = qkv + (size_t)r * 3 * H;
-  float* kd = kc + ((size_t)b * max_seq + p) * H;
-  float* vd = vc + ((size_t)b * max_seq + p) * H;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    kd[c] = src[H + c];
-    vd[c] = src[2 * H + c];
-  }
 }
 
 // Attention of one query row per (row, head) CTA over the cached keys
@@ -366,13 +336,6 @@ __global__ void __launch_bounds__(kArgThreads)
   }
 }
 
-// gelu_new in f64, cast to f32 (llm:268-275), for the GEMV epilogue.
-__device__ __forceinline__ float gelu_new_dev(float v) {
-  const double xf = (double)v;
-  const double inner = 0.7978845608028654 * (xf + 0.044715 * (xf * xf * xf));
-  return (float)(0.5 * xf * (1.0 + tanh(inner)));
-}
-
 // Epilogues fused into the decode GEMV (y = x.W + bias, the reference's
 // sgemm then host bias add, llm:227-238):
 //   kEpiPlain     out = y
@@ -402,7 +365,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int r, int col,
   float* o = a.out + (size_t)r * a.n + col;
   switch (a.epi) {
     case kEpiGelu:
-      *o = gelu_new_dev(y);
+      *o = gelu_new_f64(y);
       break;
     case kEpiResidual:
       *o = __fadd_rn(*o, y);
@@ -663,7 +626,7 @@ struct oc_gpt {
   std::vector<GptLayer> layers;
   GptLinear lm;
   // activations
-  float *hidden, *normed, *qkv, *ctx, *tmp, *inter, *logits, *part;
+  float *hidden, *normed, *qkv, *ctx, *inter, *logits, *part;
   size_t part_floats = 0;
   unsigned* counters = nullptr;  // decode GEMV column-tile counters
   size_t counter_count = 0;
@@ -768,15 +731,19 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
     x = g->normed;
   }
   if (rows > kGptGemvRows) {
-    float* dst = epi == kEpiResidual ? g->tmp : out;
-    int rc = oc_sgemm_prepared(rows, L.out, L.in, 1.0f, x, L.in, L.prep, 0.0f, dst, L.out, L.b, s);
+    // tensor-core GEMM with the epilogue fused where its sums are finished
+    GemmEpi ge;
+    ge.mode = epi == kEpiGelu ? kGemmEpiGelu : epi == kEpiResidual ? kGemmEpiResidual
+              : epi == kEpiQkv ? kGemmEpiQkv : kGemmEpiPlain;
+    ge.kc = kc;
+    ge.vc = vc;
+    ge.pos = g->pos;
+    ge.L = seq_rows;
+    ge.H = H;
+    ge.max_seq = ms;
+    int rc = sgemm_prepared_epi(rows, L.out, L.in, x, L.in, L.prep, out, L.out, L.b, ge, s);
     if (rc) return rc;
-    *n += 1;  // one tensor-core GEMM launch
-    const size_t total = (size_t)rows * L.out;
-    if (epi == kEpiGelu) gelu_kernel<<<ew_blocks(total), 256, 0, s>>>(out, total);
-    if (epi == kEpiResidual) add_kernel<<<ew_blocks(total), 256, 0, s>>>(out, g->tmp, total);
-    if (epi == kEpiQkv) kv_store_kernel<<<rows, 256, 0, s>>>(out, seq_rows, g->pos, H, kc, vc, ms, rows);
-    if (epi != kEpiPlain) *n += 1;
+    *n += 1;  // one tensor-core GEMM launch (plus its split-K reduction when split)
   } else {
     const GemvPlan p = gemv_plan(L.in, L.out, rows);
     GemvArgs a{rows, L.out, L.in, p.ks, p.slices, epi, x, L.w, L.b, g->part, g->counters, out,
@@ -886,7 +853,7 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
   }
   if ((rc = galloc_t(g, R * H, &g->hidden)) || (rc = galloc_t(g, R * H, &g->normed)) ||
       (rc = galloc_t(g, R * 3 * H, &g->qkv)) || (rc = galloc_t(g, R * H, &g->ctx)) ||
-      (rc = galloc_t(g, R * H, &g->tmp)) || (rc = galloc_t(g, R * I, &g->inter)) ||
+      (rc = galloc_t(g, R * I, &g->inter)) ||
       (rc = galloc_t(g, (size_t)max_batch * V, &g->logits)) || (rc = galloc_t(g, g->part_floats, &g->part)) ||
       (rc = galloc_t(g, cfg->num_layers * (size_t)max_batch * ms * H, &g->kc)) ||
       (rc = galloc_t(g, cfg->num_layers * (size_t)max_batch * ms * H, &g->vc)) ||

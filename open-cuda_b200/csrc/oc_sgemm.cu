@@ -25,6 +25,7 @@
 #include <map>
 #include <mutex>
 
+#include "oc_gemm_epi.cuh"
 #include "oc_internal.h"
 #include "oc_ptx.cuh"
 
@@ -70,7 +71,7 @@ __global__ void __launch_bounds__(448, 1)
     sgemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
                         const __grid_constant__ CUtensorMap tmBl, int M, int N, int K, float alpha, float beta,
                         float* __restrict__ Cm, int ldc, const float* __restrict__ bias, int ksplit,
-                        float* __restrict__ part, int* status) {
+                        float* __restrict__ part, const GemmEpi epi, int* status) {
   using C = TfGemm;
   pdl_wait();
   pdl_launch();
@@ -305,9 +306,9 @@ __global__ void __launch_bounds__(448, 1)
           float y[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            float v = __fmul_rn(alpha, s[c * 32 + j]);
-            if (beta != 0.0f && col0 + j < N) v = __fadd_rn(v, __fmul_rn(beta, crow[j]));
-            y[j] = __fadd_rn(v, bj[j]);
+            const float v = __fmul_rn(alpha, s[c * 32 + j]);
+            y[j] = col0 + j < N ? gemm_epi_value(epi, v, beta, bj[j], crow + j) : 0.0f;
+            if (col0 + j < N) gemm_epi_kv(epi, row, col0 + j, y[j]);
           }
           if (vec && col0 + 32 <= N) {
 #pragma unroll
@@ -434,18 +435,35 @@ __global__ void __launch_bounds__(256) sgemv_partial_nk(int m, int n, int k, con
 }
 
 __global__ void sgemv_reduce(int m, int n, int slices, const float* __restrict__ part, float alpha, float beta,
-                             float* __restrict__ Cm, int ldc, const float* __restrict__ bias) {
+                             float* __restrict__ Cm, int ldc, const float* __restrict__ bias, const GemmEpi epi) {
   pdl_wait();
   pdl_launch();
-  const size_t total = (size_t)m * n;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int r = (int)(i / n), col = (int)(i % n);
+  const size_t total = (size_t)m * n, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int r = total < 0x7fffffffull ? (int)((unsigned)i / (unsigned)n) : (int)(i / n);
+    const int col = (int)(i - (size_t)r * n);
+    const float* p = part + i;
     float s = 0.0f;
-    for (int sl = 0; sl < slices; ++sl) s = __fadd_rn(s, part[((size_t)sl * m + r) * n + col]);
-    float v = __fmul_rn(alpha, s);
+    int sl = 0;
+    for (; sl + 8 <= slices; sl += 8) {  // eight loads in flight, added in slice order
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __ldg(p + (size_t)(sl + j) * total);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[j]);
+    }
+    if (sl < slices) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = sl + j < slices ? __ldg(p + (size_t)(sl + j) * total) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (sl + j < slices) s = __fadd_rn(s, v[j]);
+    }
     float* cp = Cm + (size_t)r * ldc + col;
-    if (beta != 0.0f) v = __fadd_rn(v, __fmul_rn(beta, *cp));
-    *cp = __fadd_rn(v, bias ? bias[col] : 0.0f);
+    const float y = gemm_epi_value(epi, __fmul_rn(alpha, s), beta, bias ? __ldg(bias + col) : 0.0f, cp);
+    *cp = y;
+    gemm_epi_kv(epi, r, col, y);
   }
 }
 
@@ -453,10 +471,10 @@ static StreamScratch g_gemv_ws, g_bprep_ws, g_tf_part;
 
 // C = alpha * (sum of the slices of part, in order) + beta * C (+ bias).
 static int launch_reduce(int m, int n, int slices, const float* part, float alpha, float beta, float* Cm, int ldc,
-                         const float* bias, cudaStream_t s) {
+                         const float* bias, cudaStream_t s, const GemmEpi& epi = GemmEpi()) {
   const int rb = (int)std::min<size_t>(((size_t)m * n + 255) / 256, (size_t)std::max(1, sm_count()) * 8);
   const cudaError_t e = launch_pdl_ex(sgemv_reduce, dim3(std::max(1, rb)), dim3(256), 0, s, m, n, slices, part, alpha,
-                                      beta, Cm, ldc, bias);
+                                      beta, Cm, ldc, bias, epi);
   return e == cudaSuccess ? OC_OK : from_cuda(e, "sgemv_reduce");
 }
 
@@ -488,7 +506,8 @@ int launch_split_b(const float* B, int ldb, int trans_b, int k, int n, float* hi
 }
 
 int launch_tf32_gemm(int m, int n, int k, float alpha, const float* A, int lda, const float* Bhi, const float* Blo,
-                     int ldbp, float beta, float* Cm, int ldc, const float* bias, cudaStream_t s) {
+                     int ldbp, float beta, float* Cm, int ldc, const float* bias, cudaStream_t s,
+                     const GemmEpi& epi = GemmEpi()) {
   using C = TfGemm;
   CUtensorMap ta, tbh, tbl;
   int rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k, (uint64_t)m, (uint64_t)lda * 4,
@@ -515,10 +534,20 @@ int launch_tf32_gemm(int m, int n, int k, float alpha, const float* A, int lda, 
   }
   const int grid = std::min(tiles * ksplit, sms);
   cudaError_t e = launch_pdl_ex(sgemm_tf32x3_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbh, tbl, m, n, k,
-                                alpha, beta, Cm, ldc, bias, ksplit, part, device_status_word());
+                                alpha, beta, Cm, ldc, bias, ksplit, part, epi, device_status_word());
   if (e != cudaSuccess) return from_cuda(e, "sgemm_tf32x3_kernel");
   if (ksplit == 1) return OC_OK;
-  return launch_reduce(m, n, ksplit, part, alpha, beta, Cm, ldc, bias, s);
+  return launch_reduce(m, n, ksplit, part, alpha, beta, Cm, ldc, bias, s, epi);
+}
+
+static int kpad_k(int k) { return (k + 3) & ~3; }
+
+// C = epilogue(alpha * A . B) with B prepared (oc_sgemm_prepare_b); the GPT
+// linears' fused epilogues (oc_gemm_epi.cuh).
+int sgemm_prepared_epi(int m, int n, int k, const float* A, int lda, const float* prepared, float* C, int ldc,
+                       const float* bias, const GemmEpi& epi, cudaStream_t s) {
+  const int kp = kpad_k(k);
+  return launch_tf32_gemm(m, n, k, 1.0f, A, lda, prepared, prepared + (size_t)n * kp, kp, 0.0f, C, ldc, bias, s, epi);
 }
 
 }  // namespace oc
