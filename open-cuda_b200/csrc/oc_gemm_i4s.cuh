@@ -170,7 +170,14 @@ struct WorkItem {
 // max_j |sw[n][j]|, so |(nib - 8) * sw * c_n| < 8 * 2^(e+1) * 2^(11-e) = 2^15;
 // returns log2(c_n), clamped so that c_n and 1 / c_n are normal floats (0 for
 // an all-zero or non-finite column).  G % 4 == 0 and the row is 16-byte
-// aligned on this path.
+// aligned on this path.  range_exp_of_max maps the column's max |sw| (NaN
+// scales ignored, as fmaxf does) to log2(c_n).
+__device__ __forceinline__ int range_exp_of_max(float mx) {
+  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;  // subnormal or zero: -127
+  const int ce = 11 - e;
+  if (!(mx > 0.0f && mx <= 3.0e38f)) return 0;
+  return ce < -126 ? -126 : (ce > 126 ? 126 : ce);
+}
 __device__ __forceinline__ int col_range_exp(const float* __restrict__ sw_row, int G) {
   const float4* r4 = reinterpret_cast<const float4*>(sw_row);
   float mx = 0.0f;
@@ -178,10 +185,7 @@ __device__ __forceinline__ int col_range_exp(const float* __restrict__ sw_row, i
     const float4 v = __ldg(r4 + j);
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
-  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;  // subnormal or zero: -127
-  const int ce = 11 - e;
-  if (!(mx > 0.0f && mx <= 3.0e38f)) return 0;
-  return ce < -126 ? -126 : (ce > 126 ? 126 : ce);
+  return range_exp_of_max(mx);
 }
 __device__ __forceinline__ float exp2_int(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 

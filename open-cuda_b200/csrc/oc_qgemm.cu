@@ -12,6 +12,7 @@
 
 #include "oc_gemm_i4.cuh"
 #include "oc_gemm_i4s.cuh"
+#include "oc_gemm_i4x.cuh"
 #include "oc_gemm_i8.cuh"
 #include "oc_internal.h"
 #include "oc_quant.cuh"
@@ -471,11 +472,68 @@ int run_w4a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const ui
   return acc_out ? go(gemm_w4a8_tc_kernel<true>) : go(gemm_w4a8_tc_kernel<false>);
 }
 
-// f16 activations and K-split partial sums of the dequantizing W4A8 GEMM,
-// one buffer each per (device, stream)
-static StreamScratch g_w4_a16, g_w4_part;
+// f16 activations, K-split partial sums, expanded weight terms and split-tile
+// ready counters of the W4A8 tensor-core GEMMs, one buffer each per (device,
+// stream)
+static StreamScratch g_w4_a16, g_w4_part, g_w4_wx, g_w4_ready;
 static bool w4_split_ok(int m, int k, int group, const void* sw, const void* wq) {
   return m > kSkinnyM && is_sm100() && group == 32 && k % I4Split::RBK == 0 && aligned16(sw) && aligned16(wq);
+}
+
+// Work plan, partial-sum workspace and output map shared by the two W4A8
+// tensor-core kernels (tiles of 128 output columns x bm rows, nrb k-blocks).
+struct W4Launch {
+  SplitPlan sp;
+  float* part = nullptr;
+  CUtensorMap tout, tpart;
+  int out_tma = 0;
+};
+
+static int w4_prepare(int m, int n, int bm, int nrb, float* Y, const CUtensorMap& any_map, cudaStream_t s,
+                      W4Launch& L, bool split_tail = true) {
+  const int sms = std::max(1, sm_count());
+  const int tiles_m = (m + bm - 1) / bm;
+  const int tiles = tiles_m * ((n + I4Split::BN - 1) / I4Split::BN);
+  // Split K where SMs would idle: every tile when the tiles do not fill the
+  // GPU; only the last round's tiles when that round leaves more than half
+  // of the SMs idle.  Partial sums are added in slice order (deterministic).
+  L.sp = SplitPlan{tiles_m, nrb, tiles, 1, 0};
+  if (tiles < sms) {
+    const int ks = std::min(nrb, std::min(8, sms / tiles));
+    if (ks > 1) L.sp = SplitPlan{tiles_m, nrb, 0, ks, tiles};
+  } else if (split_tail && tiles % sms != 0 && tiles % sms <= sms / 2) {
+    const int tail = tiles % sms;
+    const int ks = std::min(nrb, std::min(8, sms / tail));
+    if (ks > 1) L.sp = SplitPlan{tiles_m, nrb, tiles - tail, ks, tail};
+  }
+  L.tout = any_map;  // unused maps still travel as valid kernel parameters
+  L.tpart = any_map;
+  if (L.sp.nsplit) {  // workspace [ksplit][nsplit][bm][128] f32
+    const size_t rows = (size_t)L.sp.ksplit * L.sp.nsplit * bm;
+    L.part = g_w4_part.get(rows * I4Split::BN, s);
+    if (!L.part) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
+    const int rc = make_tmap_2d(&L.tpart, L.part, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)I4Split::BN, rows,
+                                (uint64_t)I4Split::BN * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  // outputs leave through 32x32 TMA stores when rows are 16-byte multiples
+  if (n % 4 == 0 && aligned16(Y)) {
+    const int rc = make_tmap_2d(&L.tout, Y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)n, (uint64_t)m,
+                                (uint64_t)n * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    L.out_tma = 1;
+  }
+  return OC_OK;
+}
+
+// Finishes the split tiles (no-op without any).
+static int w4_reduce(const W4Launch& L, int bm, int m, int n, const float* sa, const float* bias, float* Y,
+                     cudaStream_t s) {
+  if (!L.sp.nsplit) return OC_OK;
+  const int rb = L.sp.nsplit * (bm / kReduceRows);  // bm is 128 or 256
+  return launch_rc(launch_pdl_ex(gemm_w4a8_splitk_reduce, dim3(rb), dim3(256), 0, s, L.part, L.sp.full,
+                                 L.sp.ksplit, L.sp.nsplit, L.sp.tiles_m, bm, m, n, sa, bias, Y),
+                   "gemm_w4a8_splitk_reduce");
 }
 
 // Y = dequantizing W4A8 GEMM on f16 activations qa16 [m][k] (exact integers).
@@ -496,50 +554,74 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   if (rc) return rc;
   if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_split_kernel), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_split_kernel) failed");
-  const int sms = std::max(1, sm_count());
-  const int tiles_m = (m + bm - 1) / bm;
-  const int tiles = tiles_m * ((n + C::BN - 1) / C::BN);
-  const int nrb = k / C::RBK;
-  // Split K where SMs would idle: every tile when the tiles do not fill the
-  // GPU; only the last round's tiles when that round leaves more than half
-  // of the SMs idle.  Partial sums are added in slice order (deterministic).
-  SplitPlan sp{tiles_m, nrb, tiles, 1, 0};
-  if (tiles < sms) {
-    const int ks = std::min(nrb, std::min(8, sms / tiles));
-    if (ks > 1) sp = SplitPlan{tiles_m, nrb, 0, ks, tiles};
-  } else if (tiles % sms != 0 && tiles % sms <= sms / 2) {
-    const int tail = tiles % sms;
-    const int ks = std::min(nrb, std::min(8, sms / tail));
-    if (ks > 1) sp = SplitPlan{tiles_m, nrb, tiles - tail, ks, tail};
-  }
-  float* part = nullptr;
-  CUtensorMap tout = tsc, tpart = tsc;
-  if (sp.nsplit) {  // workspace [ksplit][nsplit][bm][128] f32
-    const size_t rows = (size_t)sp.ksplit * sp.nsplit * bm;
-    part = g_w4_part.get(rows * C::BN, s);
-    if (!part) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
-    rc = make_tmap_2d(&tpart, part, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)C::BN, rows, (uint64_t)C::BN * 4,
-                      32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  // outputs leave through 32x32 TMA stores when rows are 16-byte multiples
-  int out_tma = 0;
-  if (n % 4 == 0 && aligned16(Y)) {
-    rc = make_tmap_2d(&tout, Y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)n, (uint64_t)m, (uint64_t)n * 4, 32, 32,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-    out_tma = 1;
-  }
-  const int grid = std::min(sp.items(), sms);
-  rc = launch_rc(launch_pdl_ex(gemm_w4a8_split_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc, tout,
-                               tpart, out_tma, m, n, k, bm, sp.full, sp.ksplit, sp.nsplit, sa, sw, bias, Y,
-                               device_status_word()),
+  W4Launch L;
+  rc = w4_prepare(m, n, bm, k / C::RBK, Y, tsc, s, L);
+  if (rc) return rc;
+  const int grid = std::min(L.sp.items(), std::max(1, sm_count()));
+  rc = launch_rc(launch_pdl_ex(gemm_w4a8_split_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbp, tsc,
+                               L.tout, L.tpart, L.out_tma, m, n, k, bm, L.sp.full, L.sp.ksplit, L.sp.nsplit, sa, sw,
+                               bias, Y, device_status_word()),
                  "gemm_w4a8_split_kernel");
-  if (rc || !sp.nsplit) return rc;
-  const int rb = sp.nsplit * (bm / kReduceRows);  // bm is 128 or 256
-  return launch_rc(launch_pdl_ex(gemm_w4a8_splitk_reduce, dim3(rb), dim3(256), 0, s, part, sp.full, sp.ksplit,
-                                 sp.nsplit, tiles_m, bm, m, n, sa, bias, Y),
-                   "gemm_w4a8_splitk_reduce");
+  if (rc) return rc;
+  return w4_reduce(L, bm, m, n, sa, bias, Y, s);
+}
+
+// The weights go through w4_expand_kernel once per call when they are reused
+// by at least eight 256-row tiles (below that the extra pass costs more than
+// the in-kernel conversion saves: 20.2 vs 17.2 us at 1024 x 768 x 3072,
+// 29.2 vs 30.6 us at 2048 x 768 x 3072) and their f16 terms (4 bytes per
+// weight) stay well inside L2; otherwise the dequantizing kernel converts
+// them in place.
+static bool w4_staged_ok(int m, int n, int k) {
+  return m > 7 * I4Staged::BM && (size_t)n * k * 4 <= ((size_t)64 << 20) && k % I4Staged::BK == 0;
+}
+
+// Y = W4A8 GEMM on f16 activations qa16 [m][k] through the expanded weight
+// terms (oc_gemm_i4x.cuh); the split tiles are finished inside the GEMM.
+int run_w4a8_staged(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq, const float* sw,
+                    const float* bias, float* Y, cudaStream_t s) {
+  using C = I4Staged;
+  float* buf = g_w4_wx.get((size_t)n * k + (size_t)n, s);  // wx [n][2k] f16, then icn [n]
+  if (!buf) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
+  __half* wx = reinterpret_cast<__half*>(buf);
+  float* icn = buf + (size_t)n * k;
+  CUtensorMap ta, tw;
+  int rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
+                        C::BK, C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tw, wx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)n, (uint64_t)k * 4, C::BK,
+                    C::BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_staged_kernel), C::SMEM))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_staged_kernel) failed");
+  W4Launch L;
+  // No K split of a last round: its partial sums would add writes to the
+  // output burst that bounds this kernel (the split of every tile stays
+  // for grids that do not fill the GPU).
+  rc = w4_prepare(m, n, C::BM, k / C::BK, Y, tw, s, L, /*split_tail=*/false);
+  if (rc) return rc;
+  int* ready = nullptr;
+  if (L.sp.nsplit) {
+    ready = reinterpret_cast<int*>(g_w4_ready.get((size_t)L.sp.nsplit, s));
+    if (!ready) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
+  }
+  rc = launch_rc(launch_pdl_ex(w4_expand_kernel, dim3((unsigned)((n + 7) / 8)), dim3(256), 0, s, wq, sw, n, k, wx,
+                               icn, ready, L.sp.nsplit),
+                 "w4_expand_kernel");
+  if (rc) return rc;
+  const int grid = std::min(L.sp.items(), std::max(1, sm_count()));
+  return launch_rc(launch_pdl_ex(gemm_w4a8_staged_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tw, L.tout,
+                                 L.tpart, L.out_tma, m, n, k, L.sp.full, L.sp.ksplit, L.sp.nsplit, sa, icn, bias, Y,
+                                 L.part, ready, device_status_word()),
+                   "gemm_w4a8_staged_kernel");
+}
+
+// The W4A8 tensor-core GEMM on f16 activations: expanded weight terms for
+// many rows, in-kernel dequantization otherwise.
+static int run_w4a8_f16(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq,
+                        const float* sw, const float* bias, float* Y, cudaStream_t s) {
+  if (w4_staged_ok(m, n, k)) return run_w4a8_staged(m, n, k, qa16, sa, wq, sw, bias, Y, s);
+  return run_w4a8_split(m, n, k, qa16, sa, wq, sw, bias, Y, s);
 }
 
 }  // namespace oc
@@ -601,7 +683,7 @@ int oc_igemm_w4a8(int m, int n, int k, int group, const int8_t* qa, const float*
     if (!a16) return fail(OC_ERR_OUT_OF_MEMORY, "igemm_w4a8: scratch allocation failed");
     int rc = launch_i8_to_f16(qa, (size_t)m * k, a16, s);
     if (rc) return rc;
-    return run_w4a8_split(m, n, k, a16, sa, Wq, w_scales, bias, Y, s);
+    return run_w4a8_f16(m, n, k, a16, sa, Wq, w_scales, bias, Y, s);
   }
   if (m > kSkinnyM && is_sm100() && group == 32 && k % 128 == 0 && aligned16(w_scales) && aligned16(qa))
     return run_w4a8_tc(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
@@ -632,7 +714,7 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float* A, const uint8_t*
     __half* qa16 = static_cast<__half*>(workspace);
     float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k * 2));
     int rc = launch_quantize_rows_f16(A, m, k, qa16, sa, s);
-    if (rc == OC_OK) return run_w4a8_split(m, n, k, qa16, sa, Wq, w_scales, bias, Y, s);
+    if (rc == OC_OK) return run_w4a8_f16(m, n, k, qa16, sa, Wq, w_scales, bias, Y, s);
     if (rc != OC_ERR_NOT_SUPPORTED) return rc;
   }
   int8_t* qa = static_cast<int8_t*>(workspace);

@@ -115,6 +115,10 @@ QGEMM_SHAPES = [
     # more tiles than SMs with a ragged last round (its tiles split in K) and
     # rows that are not 16-byte multiples (no TMA stores)
     (300, 256, 11522),
+    # many rows (W4A8 through the expanded weight terms): every tile split in
+    # K and finished in the GEMM, ragged rows and columns; the same with rows
+    # that are not 16-byte multiples; more tiles than SMs, ragged columns
+    (1800, 256, 1000), (2000, 256, 1002), (1900, 384, 4100),
 ]
 
 
@@ -170,10 +174,13 @@ def test_qgemm_no_bias_and_host_slices(oc, oracle):
     dev.close()
 
 
+@pytest.mark.parametrize("m", [64, 1800])
 @pytest.mark.parametrize("scale", [1e-30, 1e-6, 1.0, 1e6])
-def test_w4a8_dequantizing_kernel_range(oc, oracle, scale):
-    # per-column range factors keep the f16 terms in range for any scale magnitude
-    m, k, n = 64, 256, 160
+def test_w4a8_dequantizing_kernel_range(oc, oracle, scale, m):
+    # per-column range factors keep the f16 terms in range for any scale
+    # magnitude, in the dequantizing kernel (64 rows) and in the expanded
+    # weight terms (1800 rows)
+    k, n = 256, 160
     A, WT, bias = synth.qgemm_case(m, k, n, 11, 12, 13)
     WT = (WT * np.float32(scale)).astype(np.float32)
     WT[7] *= np.float32(1e-3)  # one column far smaller than the rest
