@@ -25,11 +25,83 @@ Arena& arena_of(const oc_device* d) {
 
 static size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
+void release_arena(const oc_device* d) {
+  Arena* a = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_arena_mu);
+    auto it = g_arenas.find(d);
+    if (it == g_arenas.end()) return;
+    a = it->second;
+    g_arenas.erase(it);
+  }
+  {
+    std::lock_guard<std::mutex> lk(a->mu);  // no call of this device object is running
+    if (a->h2d) cudaStreamSynchronize(a->h2d);
+    if (a->d2h) cudaStreamSynchronize(a->d2h);
+    if (a->ptr) cudaFree(a->ptr);
+    for (auto& e : a->ev)
+      if (e) cudaEventDestroy(e);
+    if (a->h2d) cudaStreamDestroy(a->h2d);
+    if (a->d2h) cudaStreamDestroy(a->d2h);
+    if (a->status_h) cudaFreeHost(a->status_h);
+  }
+  delete a;
+}
+
+int arena_pipeline(Arena& a) {
+  if (a.h2d) return OC_OK;
+  cudaStream_t h = nullptr, d = nullptr;
+  cudaEvent_t ev[Arena::kEvents] = {};
+  bool ok = cudaStreamCreateWithFlags(&h, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&d, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; ok && i < Arena::kEvents; ++i)
+    ok = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    for (auto& e : ev)
+      if (e) cudaEventDestroy(e);
+    if (h) cudaStreamDestroy(h);
+    if (d) cudaStreamDestroy(d);
+    return fail(OC_ERR_LAUNCH_FAILED, "copy stream / event creation failed");
+  }
+  for (int i = 0; i < Arena::kEvents; ++i) a.ev[i] = ev[i];
+  a.h2d = h;
+  a.d2h = d;
+  return OC_OK;
+}
+
+int arena_finish(Arena& a, cudaStream_t s) {
+  int* w = device_status_word();
+  if (!w) return fail(OC_ERR_LAUNCH_FAILED, "device status word unavailable");
+  if (!a.status_h) {
+    if (cudaHostAlloc(reinterpret_cast<void**>(&a.status_h), sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
+      cudaGetLastError();
+      a.status_h = nullptr;
+      OC_CHECK_CUDA(cudaStreamSynchronize(s));
+      return check_device_status(s);
+    }
+  }
+  *a.status_h = 0;
+  OC_CHECK_CUDA(cudaMemcpyAsync(a.status_h, w, sizeof(int), cudaMemcpyDeviceToHost, s));
+  OC_CHECK_CUDA(cudaStreamSynchronize(s));
+  const int v = *a.status_h;
+  if (v != 0) {
+    int zero = 0;
+    cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    char buf[128];
+    snprintf(buf, sizeof buf, "a kernel reported status %d (bounded wait expired)", v);
+    return fail(OC_ERR_TIMEOUT, buf);
+  }
+  return OC_OK;
+}
+
 // Returns a device pointer with at least `bytes` bytes (caller holds mu).
 int arena_get(Arena& a, size_t bytes, cudaStream_t s, uint8_t** out) {
   if (a.bytes < bytes) {
     if (a.ptr) {
       cudaStreamSynchronize(s);
+      if (a.h2d) cudaStreamSynchronize(a.h2d);
+      if (a.d2h) cudaStreamSynchronize(a.d2h);
       cudaFree(a.ptr);
       a.ptr = nullptr;
       a.bytes = 0;
@@ -135,20 +207,45 @@ static int blas_qgemm(oc_device* dev, int bits, size_t m, size_t n, size_t k, si
   float* dy = reinterpret_cast<float*>(p);
   p += al(m * n * 4);
   void* dws = p;
-  OC_CHECK_CUDA(cudaMemcpyAsync(da, a, m * k * 4, cudaMemcpyHostToDevice, s));
-  OC_CHECK_CUDA(cudaMemcpyAsync(dw, wq, wbytes, cudaMemcpyHostToDevice, s));
-  OC_CHECK_CUDA(cudaMemcpyAsync(dsc, w_scales, ng * 4, cudaMemcpyHostToDevice, s));
-  if (bias) OC_CHECK_CUDA(cudaMemcpyAsync(db, bias, n * 4, cudaMemcpyHostToDevice, s));
-  if (bits == 8)
-    rc = oc_qgemm_w8a8((int)m, (int)n, (int)k, da, static_cast<const int8_t*>(dw), dsc, bias ? db : nullptr, dy,
-                       dws, ws, nullptr, s);
-  else
-    rc = oc_qgemm_w4a8((int)m, (int)n, (int)k, (int)group, da, static_cast<const uint8_t*>(dw), dsc,
-                       bias ? db : nullptr, dy, dws, ws, nullptr, s);
+  rc = arena_pipeline(ar);
   if (rc) return rc;
-  OC_CHECK_CUDA(cudaMemcpyAsync(y, dy, m * n * 4, cudaMemcpyDeviceToHost, s));
-  OC_CHECK_CUDA(cudaStreamSynchronize(s));
-  return check_device_status(s);
+  // Row chunks of at least 512 rows (at most 16 chunks) when the output copy
+  // is long: chunk c's input copy (host -> device stream), matmul (device
+  // stream) and output copy (device -> host stream) overlap the neighbouring
+  // chunks', and the two copy directions run at once.  Rows are quantized
+  // independently, so a chunk is the same computation on fewer rows.
+  size_t rows = m;
+  if (m * n * 4 >= ((size_t)8 << 20) && m >= 1024) rows = std::max<size_t>(512, (m + 15) / 16);
+  const int nch = (int)((m + rows - 1) / rows);  // 1 + 2 * nch <= Arena::kEvents
+  cudaStream_t sh = ar.h2d, sd = ar.d2h;
+  OC_CHECK_CUDA(cudaMemcpyAsync(dw, wq, wbytes, cudaMemcpyHostToDevice, sh));
+  OC_CHECK_CUDA(cudaMemcpyAsync(dsc, w_scales, ng * 4, cudaMemcpyHostToDevice, sh));
+  if (bias) OC_CHECK_CUDA(cudaMemcpyAsync(db, bias, n * 4, cudaMemcpyHostToDevice, sh));
+  OC_CHECK_CUDA(cudaEventRecord(ar.ev[0], sh));
+  OC_CHECK_CUDA(cudaStreamWaitEvent(s, ar.ev[0], 0));
+  for (int c = 0; c < nch; ++c) {
+    const size_t r0 = (size_t)c * rows, mc = std::min(rows, m - r0);
+    OC_CHECK_CUDA(cudaMemcpyAsync(da + r0 * k, a + r0 * k, mc * k * 4, cudaMemcpyHostToDevice, sh));
+    OC_CHECK_CUDA(cudaEventRecord(ar.ev[1 + 2 * c], sh));
+    OC_CHECK_CUDA(cudaStreamWaitEvent(s, ar.ev[1 + 2 * c], 0));
+    if (bits == 8)
+      rc = oc_qgemm_w8a8((int)mc, (int)n, (int)k, da + r0 * k, static_cast<const int8_t*>(dw), dsc,
+                         bias ? db : nullptr, dy + r0 * n, dws, ws, nullptr, s);
+    else
+      rc = oc_qgemm_w4a8((int)mc, (int)n, (int)k, (int)group, da + r0 * k, static_cast<const uint8_t*>(dw), dsc,
+                         bias ? db : nullptr, dy + r0 * n, dws, ws, nullptr, s);
+    if (rc) {  // nothing queued may still touch the arena or the caller's buffers
+      cudaStreamSynchronize(sh);
+      cudaStreamSynchronize(s);
+      cudaStreamSynchronize(sd);
+      return rc;
+    }
+    OC_CHECK_CUDA(cudaEventRecord(ar.ev[2 + 2 * c], s));
+    OC_CHECK_CUDA(cudaStreamWaitEvent(sd, ar.ev[2 + 2 * c], 0));
+    OC_CHECK_CUDA(cudaMemcpyAsync(y + r0 * n, dy + r0 * n, mc * n * 4, cudaMemcpyDeviceToHost, sd));
+  }
+  // every output copy follows its matmul (events), so one synchronization covers the call
+  return arena_finish(ar, sd);
 }
 
 int oc_blas_qgemm_w8a8(oc_device* dev, size_t m, size_t n, size_t k, const float* a, const int8_t* wq,

@@ -66,14 +66,29 @@ cudaStream_t device_stream(const oc_device* d);
 bool device_owns(oc_device* d, uint64_t addr, size_t bytes);
 
 // Grow-only device scratch, one per device object; callers hold `mu` for
-// the whole host-slice call (so calls on one device object serialize).
+// the whole host-slice call (so calls on one device object serialize).  The
+// pipelined calls also use two copy streams (host -> device, device -> host),
+// events between the three streams and a pinned word that receives the
+// device status, all created on first use and released with the device.
 struct Arena {
+  static constexpr int kEvents = 40;
   std::mutex mu;
   void* ptr = nullptr;
   size_t bytes = 0;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev[kEvents] = {};
+  int* status_h = nullptr;
 };
 Arena& arena_of(const oc_device* d);
 int arena_get(Arena& a, size_t bytes, cudaStream_t s, uint8_t** out);
+// Creates the copy streams and events (caller holds mu, device current).
+int arena_pipeline(Arena& a);
+// Reads the device status word into the pinned word behind the work queued
+// on `s`, synchronizes `s` once and returns OC_ERR_TIMEOUT if a kernel
+// reported an expired wait (the word is then reset).
+int arena_finish(Arena& a, cudaStream_t s);
+// Frees a device object's arena (called when the device object closes).
+void release_arena(const oc_device* d);
 
 // Grow-only scratch buffers, one per (device, stream) and reused in stream
 // order: a call's kernels finish before the next call's kernels on that

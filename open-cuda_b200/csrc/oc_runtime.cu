@@ -232,6 +232,7 @@ int oc_device_close(oc_device* dev) {
   {
     DeviceGuard g(dev->ordinal);
     cudaStreamSynchronize(dev->stream);
+    oc::release_arena(dev);  // host-slice scratch, copy streams and events of this device object
     for (auto& kv : dev->allocs) cudaFree(reinterpret_cast<void*>(kv.first));
     cudaStreamDestroy(dev->stream);
   }

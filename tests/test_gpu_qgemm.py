@@ -174,6 +174,33 @@ def test_qgemm_no_bias_and_host_slices(oc, oracle):
     dev.close()
 
 
+@pytest.mark.parametrize("pinned", [False, True])
+def test_host_slice_qgemm_row_chunks(oc, oracle, pinned):
+    # outputs of >= 8 MB and >= 1024 rows go through row chunks whose copies
+    # and matmuls overlap on three streams (3 chunks here: 512, 512, 76 rows);
+    # pinned host buffers let the copies run asynchronously.  Opening and
+    # closing the device object again releases and rebuilds its scratch.
+    m, k, n = 1100, 256, 2048
+    A, WT, bias = synth.qgemm_case(m, k, n, 21, 22, 23)
+    wq, ws = _weights(oracle, WT, 8, k)
+    wq4, ws4 = _weights(oracle, WT, 4, 32)
+    y_ref = oracle.qgemm_w8a8(m, k, n, A, wq, ws, bias)
+    y4_ref = oracle.qgemm_w4a8(m, k, n, 32, A, wq4, ws4, bias)
+    if pinned:
+        Ah = torch.from_numpy(A).pin_memory().numpy()
+        y8 = torch.zeros(m * n).pin_memory().numpy()
+        y4 = torch.zeros(m * n).pin_memory().numpy()
+    else:
+        Ah, y8, y4 = A, np.zeros(m * n, np.float32), np.zeros(m * n, np.float32)
+    for _ in range(2):
+        dev = oc.Device(0)
+        dev.qgemm_w8a8(m, n, k, Ah, wq, ws, bias, out=y8)
+        bits_equal(y8, y_ref)
+        dev.qgemm_w4a8(m, n, k, 32, Ah, wq4, ws4, bias, out=y4)
+        assert rel_fro(y4, y4_ref) <= W4_REL_FRO
+        dev.close()
+
+
 @pytest.mark.parametrize("m", [64, 1800])
 @pytest.mark.parametrize("scale", [1e-30, 1e-6, 1.0, 1e6])
 def test_w4a8_dequantizing_kernel_range(oc, oracle, scale, m):
