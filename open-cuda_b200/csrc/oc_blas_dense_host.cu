@@ -59,8 +59,7 @@ int oc_blas_sgemm(oc_device* dev, size_t m, size_t k, size_t n, float alpha, con
                 nullptr, s);
   if (rc) return rc;
   OC_CHECK_CUDA(cudaMemcpyAsync(c, dc, m * n * 4, cudaMemcpyDeviceToHost, s));
-  OC_CHECK_CUDA(cudaStreamSynchronize(s));
-  return check_device_status(s);
+  return arena_finish(ar, s);
 }
 
 int oc_blas_softmax_rows(oc_device* dev, size_t rows, size_t cols, const float* data, float* out) {
@@ -149,8 +148,7 @@ static int blas_mla(oc_device* dev, int compress, size_t seq_len, size_t d_in, s
                 : oc_mla_decompress_kv((int)seq_len, (int)d_in, (int)d_out, dx, dp, dy, s);
   if (rc) return rc;
   OC_CHECK_CUDA(cudaMemcpyAsync(y, dy, seq_len * d_out * 4, cudaMemcpyDeviceToHost, s));
-  OC_CHECK_CUDA(cudaStreamSynchronize(s));
-  return check_device_status(s);
+  return arena_finish(ar, s);
 }
 
 int oc_blas_mla_compress_kv(oc_device* dev, size_t seq_len, size_t d_h, size_t d_c, const float* kv,

@@ -115,10 +115,13 @@ QGEMM_SHAPES = [
     # more tiles than SMs with a ragged last round (its tiles split in K) and
     # rows that are not 16-byte multiples (no TMA stores)
     (300, 256, 11522),
-    # many rows (W4A8 through the expanded weight terms): every tile split in
-    # K and finished in the GEMM, ragged rows and columns; the same with rows
-    # that are not 16-byte multiples; more tiles than SMs, ragged columns
-    (1800, 256, 1000), (2000, 256, 1002), (1900, 384, 4100),
+    # many rows (W4A8 through the expanded weight terms): long K, every tile
+    # split in K and finished in the GEMM, ragged rows and columns; the same
+    # with rows that are not 16-byte multiples; more tiles than SMs, ragged
+    # columns
+    (1800, 2048, 200), (1850, 2048, 202), (1900, 384, 4100),
+    # short K, tiles filling half the GPU: not split
+    (600, 256, 3000),
 ]
 
 
