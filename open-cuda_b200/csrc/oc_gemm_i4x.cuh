@@ -5,9 +5,11 @@
 // The dequantizing kernel of oc_gemm_i4s.cuh converts every weight tile once
 // per 256-row activation tile; with M = 2048 that is eight conversions of
 // each weight, and the converter warps' ALU work slows the MMA stream.  Here
-// w4_expand_kernel writes, per weight row n, the same hi / lo f16 terms
-// (hi = f16(w * s_hi), lo = f16(f16(w * s_lo) - (hi - w * s_hi)), s = sw *
-// c_n, c_n = 2^range_exp) into wx [N][2K] -- k-block kb of 64 holds hi at
+// the expansion (expand_weight_row, run by the launch that also prepares the
+// f16 activations: w4_prep_kernel or w4_prep_i8_kernel) writes, per weight
+// row n, the same hi / lo f16 terms (hi = f16(w * s_hi), lo = f16(f16(w *
+// s_lo) - (hi - w * s_hi)), s = sw * c_n, c_n = 2^range_exp) into wx [N][2K]
+// -- k-block kb of 64 holds hi at
 // columns [128 kb, 128 kb + 64) and lo at [128 kb + 64, 128 kb + 128) -- and
 // 1 / c_n into icn [N].  For the shapes routed here wx fits in L2, so the GEMM
 // reads it from there.
@@ -36,6 +38,7 @@
 // bounded (oc_ptx.cuh).
 #pragma once
 #include "oc_gemm_i4s.cuh"
+#include "oc_quant.cuh"
 
 namespace oc {
 
@@ -57,40 +60,21 @@ struct I4Staged {
   static_assert(BN == I4Split::BN, "the split-K workspace and reduction are shared with the dequantizing kernel");
 };
 
-// One warp per weight row n (K % 64 == 0, group 32): icn[n] = 1 / c_n and the
-// row's hi / lo terms, 8 weights (one packed word) per lane and step.  The
-// column factor and the first packed words are read before the dependency
-// wait (they are inputs of this call); wx, icn and the GEMM's split-tile
-// ready counters (zeroed by block 0) are written after it (the previous
-// call's GEMM may still use them).
-__global__ void __launch_bounds__(256) w4_expand_kernel(const uint8_t* __restrict__ wq,
-                                                        const float* __restrict__ sw, int N, int K,
-                                                        __half* __restrict__ wx, float* __restrict__ icn,
-                                                        int* __restrict__ ready, int nready) {
-  const int n = (int)((blockIdx.x * 256u + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-  const int G = K / 32;
-  const bool live = n < N;
-  const float* srow = sw + (size_t)(live ? n : 0) * G;
-  const uint32_t* wrow = reinterpret_cast<const uint32_t*>(wq + (size_t)(live ? n : 0) * (K / 2));
-  float mx = 0.0f;
-  uint32_t w = 0;
-  if (live) {
-    for (int j = lane; j < G; j += 32) mx = fmaxf(mx, fabsf(__ldg(srow + j)));
-    if (lane < K / 8) w = __ldg(wrow + lane);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  pdl_wait();
-  pdl_launch();
-  if (blockIdx.x == 0)  // the GEMM that follows counts its split slices from zero
-    for (int i = threadIdx.x; i < nready; i += 256) ready[i] = 0;
-  if (!live) return;
+// Weight row n's 1 / c_n and hi / lo terms by one warp (K % 64 == 0, group
+// 32), 8 weights (one packed word) per lane and step; `w0` is the row's
+// packed word `lane` (read by the caller, 0 if lane >= K / 8) and `mx` the
+// row's max |scale| (warp-reduced by the caller).
+__device__ __forceinline__ void expand_weight_row(const uint8_t* __restrict__ wq, const float* __restrict__ sw, int K,
+                                                  __half* __restrict__ wx, float* __restrict__ icn, int n, int lane,
+                                                  float mx, uint32_t w0) {
+  const float* srow = sw + (size_t)n * (K / 32);
+  const uint32_t* wrow = reinterpret_cast<const uint32_t*>(wq + (size_t)n * (K / 2));
   const int ce = range_exp_of_max(mx);
   const float cval = exp2_int(ce);
   if (lane == 0) icn[n] = exp2_int(-ce);
   __half* xrow = wx + (size_t)n * 2 * K;
   for (int u = lane; u < K / 8; u += 32) {
-    if (u != lane) w = __ldg(wrow + u);  // weights k0 .. k0 + 7, even k in the low nibble
+    const uint32_t w = u == lane ? w0 : __ldg(wrow + u);  // weights k0 .. k0 + 7, even k in the low nibble
     const int k0 = 8 * u;
     const ScaleTerms st(__fmul_rn(__ldg(srow + k0 / 32), cval));  // exact: cval = 2^ce
     uint4 hi, lo;
@@ -102,6 +86,47 @@ __global__ void __launch_bounds__(256) w4_expand_kernel(const uint8_t* __restric
     *reinterpret_cast<uint4*>(dst) = hi;
     *reinterpret_cast<uint4*>(dst + 64) = lo;
   }
+}
+
+// Max |scale| of weight row n and its packed word `lane`, read by one warp.
+__device__ __forceinline__ void weight_row_head(const uint8_t* __restrict__ wq, const float* __restrict__ sw, int K,
+                                                int n, int lane, float& mx, uint32_t& w0) {
+  const float* srow = sw + (size_t)n * (K / 32);
+  mx = 0.0f;
+  for (int j = lane; j < K / 32; j += 32) mx = fmaxf(mx, fabsf(__ldg(srow + j)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  w0 = lane < K / 8 ? __ldg(reinterpret_cast<const uint32_t*>(wq + (size_t)n * (K / 2)) + lane) : 0u;
+}
+
+// The row quantization of the f32 activations (blocks [0, m): one row per
+// CTA, as quantize_rows_i8_kernel<VPT, true>) and the weight expansion
+// (blocks [m, m + ceil(N / 4)): one weight row per warp) in one launch, so
+// the GEMM waits on one kernel instead of two.  Everything is read after the
+// dependency wait (the activations and the weights may come from the kernel
+// just before).
+template <int VPT>
+__global__ void __launch_bounds__(128) w4_prep_kernel(const float* __restrict__ A, int m, int k,
+                                                      __half* __restrict__ qa16, float* __restrict__ sa,
+                                                      const uint8_t* __restrict__ wq, const float* __restrict__ sw,
+                                                      int N, __half* __restrict__ wx, float* __restrict__ icn,
+                                                      int* __restrict__ ready, int nready) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float red[4];
+  if ((int)blockIdx.x < m) {
+    quantize_row_block<VPT, true>(A, k, qa16, sa, blockIdx.x, red);
+    return;
+  }
+  const int b = (int)blockIdx.x - m, lane = threadIdx.x & 31;
+  if (b == 0)  // the GEMM that follows counts its split slices from zero
+    for (int i = threadIdx.x; i < nready; i += 128) ready[i] = 0;
+  const int n = 4 * b + (threadIdx.x >> 5);
+  if (n >= N) return;
+  float mx;
+  uint32_t w0;
+  weight_row_head(wq, sw, k, n, lane, mx, w0);
+  expand_weight_row(wq, sw, k, wx, icn, n, lane, mx, w0);
 }
 
 // Ready counters of the split tiles: acquire load and bounded wait.
@@ -391,7 +416,50 @@ done:
   }
 }
 
-int run_w4a8_staged(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq, const float* sw,
-                    const float* bias, float* Y, cudaStream_t s);
+// The same launch for activations that are already int8 (the pre-quantized
+// entry point): blocks [0, nconv) convert qa to f16 (exact), 1024 elements
+// per block, 8 per thread; the rest expand the weights, one row per warp.
+// n_act % 8 == 0, qa 8-byte and qa16 16-byte aligned.
+__global__ void __launch_bounds__(128) w4_prep_i8_kernel(const int8_t* __restrict__ qa, size_t n_act, int nconv,
+                                                         __half* __restrict__ qa16, const uint8_t* __restrict__ wq,
+                                                         const float* __restrict__ sw, int N, int K,
+                                                         __half* __restrict__ wx, float* __restrict__ icn,
+                                                         int* __restrict__ ready, int nready) {
+  pdl_wait();
+  pdl_launch();
+  if ((int)blockIdx.x < nconv) {
+    const size_t i = (size_t)blockIdx.x * 128 + threadIdx.x;  // 8-element chunk
+    if (i < n_act / 8) {
+      const uint2 w = reinterpret_cast<const uint2*>(qa)[i];
+      const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+      __half2 h[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn((float)b[2 * e], (float)b[2 * e + 1]);
+      uint4 o;
+      o.x = *reinterpret_cast<const uint32_t*>(&h[0]);
+      o.y = *reinterpret_cast<const uint32_t*>(&h[1]);
+      o.z = *reinterpret_cast<const uint32_t*>(&h[2]);
+      o.w = *reinterpret_cast<const uint32_t*>(&h[3]);
+      reinterpret_cast<uint4*>(qa16)[i] = o;
+    }
+    return;
+  }
+  const int b = (int)blockIdx.x - nconv, lane = threadIdx.x & 31;
+  if (b == 0)  // the GEMM that follows counts its split slices from zero
+    for (int j = threadIdx.x; j < nready; j += 128) ready[j] = 0;
+  const int n = 4 * b + (threadIdx.x >> 5);
+  if (n >= N) return;
+  float mx;
+  uint32_t w0;
+  weight_row_head(wq, sw, K, n, lane, mx, w0);
+  expand_weight_row(wq, sw, K, wx, icn, n, lane, mx, w0);
+}
+
+// The activations are prepared by the launch that expands the weights:
+// quantized from A_f32 (quantize_rows_f16_ok must hold; qa16 and sa are
+// written), or, with A_f32 == nullptr, converted from the int8 rows qa_i8
+// (n = m * k % 8 == 0, 8-byte aligned; qa16 is written, sa read).
+int run_w4a8_staged(int m, int n, int k, __half* qa16, float* sa, const uint8_t* wq, const float* sw,
+                    const float* bias, float* Y, cudaStream_t s, const float* A_f32, const int8_t* qa_i8);
 
 }  // namespace oc

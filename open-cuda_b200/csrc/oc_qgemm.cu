@@ -570,20 +570,20 @@ int run_w4a8_split(int m, int n, int k, const __half* qa16, const float* sa, con
   return w4_reduce(L, bm, m, n, sa, bias, Y, s);
 }
 
-// The weights go through w4_expand_kernel once per call when they are reused
-// by at least eight 256-row tiles (below that the extra pass costs more than
-// the in-kernel conversion saves: 20.2 vs 17.2 us at 1024 x 768 x 3072,
-// 29.2 vs 30.6 us at 2048 x 768 x 3072) and their f16 terms (4 bytes per
-// weight) stay well inside L2; otherwise the dequantizing kernel converts
-// them in place.
+// The weights are expanded once per call (in the launch that prepares the
+// activations) when they are reused by at least eight 256-row tiles (below
+// that the extra pass costs more than the in-kernel conversion saves: 20.2
+// vs 17.2 us at 1024 x 768 x 3072, 29.2 vs 30.6 us at 2048 x 768 x 3072) and
+// their f16 terms (4 bytes per weight) stay well inside L2; otherwise the
+// dequantizing kernel converts them in place.
 static bool w4_staged_ok(int m, int n, int k) {
   return m > 7 * I4Staged::BM && (size_t)n * k * 4 <= ((size_t)64 << 20) && k % I4Staged::BK == 0;
 }
 
 // Y = W4A8 GEMM on f16 activations qa16 [m][k] through the expanded weight
 // terms (oc_gemm_i4x.cuh); the split tiles are finished inside the GEMM.
-int run_w4a8_staged(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq, const float* sw,
-                    const float* bias, float* Y, cudaStream_t s) {
+int run_w4a8_staged(int m, int n, int k, __half* qa16, float* sa, const uint8_t* wq, const float* sw,
+                    const float* bias, float* Y, cudaStream_t s, const float* A_f32, const int8_t* qa_i8) {
   using C = I4Staged;
   float* buf = g_w4_wx.get((size_t)n * k + (size_t)n, s);  // wx [n][2k] f16, then icn [n]
   if (!buf) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
@@ -609,23 +609,25 @@ int run_w4a8_staged(int m, int n, int k, const __half* qa16, const float* sa, co
     ready = reinterpret_cast<int*>(g_w4_ready.get((size_t)L.sp.nsplit, s));
     if (!ready) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
   }
-  rc = launch_rc(launch_pdl_ex(w4_expand_kernel, dim3((unsigned)((n + 7) / 8)), dim3(256), 0, s, wq, sw, n, k, wx,
-                               icn, ready, L.sp.nsplit),
-                 "w4_expand_kernel");
+  if (A_f32) {
+    const int n4 = k / 4;
+    auto kern = n4 <= 128 * 2 ? w4_prep_kernel<2> : n4 <= 128 * 4 ? w4_prep_kernel<4> : w4_prep_kernel<8>;
+    rc = launch_rc(launch_pdl_ex(kern, dim3((unsigned)(m + (n + 3) / 4)), dim3(128), 0, s, A_f32, m, k, qa16, sa, wq,
+                                 sw, n, wx, icn, ready, L.sp.nsplit),
+                   "w4_prep_kernel");
+  } else {
+    const size_t n_act = (size_t)m * k;
+    const int nconv = (int)((n_act / 8 + 127) / 128);
+    rc = launch_rc(launch_pdl_ex(w4_prep_i8_kernel, dim3((unsigned)(nconv + (n + 3) / 4)), dim3(128), 0, s, qa_i8,
+                                 n_act, nconv, qa16, wq, sw, n, k, wx, icn, ready, L.sp.nsplit),
+                   "w4_prep_i8_kernel");
+  }
   if (rc) return rc;
   const int grid = std::min(L.sp.items(), std::max(1, sm_count()));
   return launch_rc(launch_pdl_ex(gemm_w4a8_staged_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tw, L.tout,
                                  L.tpart, L.out_tma, m, n, k, L.sp.full, L.sp.ksplit, L.sp.nsplit, sa, icn, bias, Y,
                                  L.part, ready, device_status_word()),
                    "gemm_w4a8_staged_kernel");
-}
-
-// The W4A8 tensor-core GEMM on f16 activations: expanded weight terms for
-// many rows, in-kernel dequantization otherwise.
-static int run_w4a8_f16(int m, int n, int k, const __half* qa16, const float* sa, const uint8_t* wq,
-                        const float* sw, const float* bias, float* Y, cudaStream_t s) {
-  if (w4_staged_ok(m, n, k)) return run_w4a8_staged(m, n, k, qa16, sa, wq, sw, bias, Y, s);
-  return run_w4a8_split(m, n, k, qa16, sa, wq, sw, bias, Y, s);
 }
 
 }  // namespace oc
@@ -685,9 +687,11 @@ int oc_igemm_w4a8(int m, int n, int k, int group, const int8_t* qa, const float*
     // no int32 partials requested: the dequantizing GEMM on f16 activations
     __half* a16 = reinterpret_cast<__half*>(g_w4_a16.get(((size_t)m * k + 1) / 2, s));
     if (!a16) return fail(OC_ERR_OUT_OF_MEMORY, "igemm_w4a8: scratch allocation failed");
+    if (w4_staged_ok(m, n, k))  // int8 -> f16 conversion and weight expansion in one launch
+      return run_w4a8_staged(m, n, k, a16, const_cast<float*>(sa), Wq, w_scales, bias, Y, s, nullptr, qa);
     int rc = launch_i8_to_f16(qa, (size_t)m * k, a16, s);
     if (rc) return rc;
-    return run_w4a8_f16(m, n, k, a16, sa, Wq, w_scales, bias, Y, s);
+    return run_w4a8_split(m, n, k, a16, sa, Wq, w_scales, bias, Y, s);
   }
   if (m > kSkinnyM && is_sm100() && group == 32 && k % 128 == 0 && aligned16(w_scales) && aligned16(qa))
     return run_w4a8_tc(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s);
@@ -717,8 +721,10 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float* A, const uint8_t*
     // activations quantized straight to f16 for the dequantizing tensor-core GEMM
     __half* qa16 = static_cast<__half*>(workspace);
     float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k * 2));
+    if (w4_staged_ok(m, n, k) && quantize_rows_f16_ok(A, k, qa16))  // quantization and expansion in one launch
+      return run_w4a8_staged(m, n, k, qa16, sa, Wq, w_scales, bias, Y, s, A, nullptr);
     int rc = launch_quantize_rows_f16(A, m, k, qa16, sa, s);
-    if (rc == OC_OK) return run_w4a8_f16(m, n, k, qa16, sa, Wq, w_scales, bias, Y, s);
+    if (rc == OC_OK) return run_w4a8_split(m, n, k, qa16, sa, Wq, w_scales, bias, Y, s);
     if (rc != OC_ERR_NOT_SUPPORTED) return rc;
   }
   int8_t* qa = static_cast<int8_t*>(workspace);

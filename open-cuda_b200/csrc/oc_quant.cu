@@ -12,19 +12,6 @@
 
 namespace oc {
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-__device__ __forceinline__ int quant_one(float x, float s, float qmax) {
-  if (s == 0.0f) return 0;
-  float q = roundf(__fdiv_rn(x, s));
-  if (q != q) return 0;  // Rust: NaN.clamp(..) as i8 == 0
-  return (int)fminf(fmaxf(q, -qmax), qmax);
-}
-
 // One warp per group: scale of group g (blas:797-809).
 __global__ void group_scales_kernel(const float* __restrict__ x, size_t len, size_t group, float qmax,
                                     float* __restrict__ scales, size_t ngroups) {
@@ -85,11 +72,8 @@ __global__ void dequantize_i4_kernel(const uint8_t* __restrict__ q, const float*
 }
 
 // Row quantization of activations, quantize_int8(A, group = k): one CTA of
-// 128 threads per row, the row held in registers (VPT float4 per thread),
-// a block max-reduction, then int8 stores.  Requires k % 4 == 0 and a
-// 16-byte aligned A; k <= 128 * 4 * VPT.
-// quantize_int8(A row, group = k); F16: the quantized integers are written as
-// f16 (exact, |q| <= 127) for the f16 tensor-core path, else as int8.
+// 128 threads per row (quantize_row_block, oc_quant.cuh); F16: the integers
+// are written as f16 for the f16 tensor-core path, else as int8.
 template <int VPT, bool F16 = false>
 __global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __restrict__ A, int m, int k,
                                                                void* __restrict__ qout, float* __restrict__ sa) {
@@ -98,50 +82,7 @@ __global__ void __launch_bounds__(128) quantize_rows_i8_kernel(const float* __re
   __shared__ float red[4];
   const int row = blockIdx.x;
   if (row >= m) return;
-  const float4* a4 = reinterpret_cast<const float4*>(A + (size_t)row * k);
-  const int n4 = k >> 2;
-  float4 v[VPT];
-  float mx = 0.0f;
-#pragma unroll
-  for (int j = 0; j < VPT; j++) {
-    int idx = threadIdx.x + j * 128;
-    if (idx < n4) {
-      v[j] = __ldg(a4 + idx);
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
-    }
-  }
-  mx = warp_max(mx);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  const float s = (mx == 0.0f) ? 0.0f : __fdiv_rn(mx, 127.0f);
-  if (threadIdx.x == 0) sa[row] = s;
-  if (F16) {
-    uint2* h4 = reinterpret_cast<uint2*>(static_cast<__half*>(qout) + (size_t)row * k);
-#pragma unroll
-    for (int j = 0; j < VPT; j++) {
-      int idx = threadIdx.x + j * 128;
-      if (idx < n4) {
-        const __half2 a = __floats2half2_rn((float)quant_one(v[j].x, s, 127.0f), (float)quant_one(v[j].y, s, 127.0f));
-        const __half2 b = __floats2half2_rn((float)quant_one(v[j].z, s, 127.0f), (float)quant_one(v[j].w, s, 127.0f));
-        h4[idx] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
-      }
-    }
-    return;
-  }
-  char4* q4 = reinterpret_cast<char4*>(static_cast<int8_t*>(qout) + (size_t)row * k);
-#pragma unroll
-  for (int j = 0; j < VPT; j++) {
-    int idx = threadIdx.x + j * 128;
-    if (idx < n4) {
-      char4 o;
-      o.x = (signed char)quant_one(v[j].x, s, 127.0f);
-      o.y = (signed char)quant_one(v[j].y, s, 127.0f);
-      o.z = (signed char)quant_one(v[j].z, s, 127.0f);
-      o.w = (signed char)quant_one(v[j].w, s, 127.0f);
-      q4[idx] = o;
-    }
-  }
+  quantize_row_block<VPT, F16>(A, k, qout, sa, row, red);
 }
 
 // int8 -> f16 (exact), 8 elements per thread per step.
@@ -187,7 +128,7 @@ int launch_quantize_i8(const float* x, size_t len, const float* scales, size_t g
 int launch_quantize_rows_f16(const float* A, int m, int k, __half* qa16, float* sa, cudaStream_t s) {
   if (m <= 0) return OC_OK;
   const int n4 = k / 4;
-  if (k % 8 || !aligned16(A) || !aligned16(qa16) || n4 > 128 * 8) return OC_ERR_NOT_SUPPORTED;
+  if (!quantize_rows_f16_ok(A, k, qa16)) return OC_ERR_NOT_SUPPORTED;
   auto kern = n4 <= 128 * 2 ? quantize_rows_i8_kernel<2, true>
               : n4 <= 128 * 4 ? quantize_rows_i8_kernel<4, true>
                               : quantize_rows_i8_kernel<8, true>;
