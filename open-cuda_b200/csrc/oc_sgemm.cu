@@ -67,6 +67,10 @@ __device__ __forceinline__ void tf_fail(int* status, volatile int* abort_flag, i
   *abort_flag = 1;
 }
 
+// PLAIN: the sgemm epilogue (alpha * acc (+ beta * C) + bias); else the GPT
+// linears' fused epilogues (epi.mode, oc_gemm_epi.cuh).  Separate
+// instantiations keep the plain epilogue free of per-element mode tests.
+template <bool PLAIN>
 __global__ void __launch_bounds__(448, 1)
     sgemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
                         const __grid_constant__ CUtensorMap tmBl, int M, int N, int K, float alpha, float beta,
@@ -304,11 +308,20 @@ __global__ void __launch_bounds__(448, 1)
         if (row < M && col0 < N) {
           float* crow = Cm + (size_t)row * ldc + col0;
           float y[32];
+          if (PLAIN) {  // sgemm: alpha * acc (+ beta * C) + bias
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float v = __fmul_rn(alpha, s[c * 32 + j]);
-            y[j] = col0 + j < N ? gemm_epi_value(epi, v, beta, bj[j], crow + j) : 0.0f;
-            if (col0 + j < N) gemm_epi_kv(epi, row, col0 + j, y[j]);
+            for (int j = 0; j < 32; ++j) {
+              float v = __fmul_rn(alpha, s[c * 32 + j]);
+              if (beta != 0.0f && col0 + j < N) v = __fadd_rn(v, __fmul_rn(beta, crow[j]));
+              y[j] = __fadd_rn(v, bj[j]);
+            }
+          } else {  // the GPT linears' fused epilogues
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float v = __fmul_rn(alpha, s[c * 32 + j]);
+              y[j] = col0 + j < N ? gemm_epi_value(epi, v, beta, bj[j], crow + j) : 0.0f;
+              if (col0 + j < N) gemm_epi_kv(epi, row, col0 + j, y[j]);
+            }
           }
           if (vec && col0 + 32 <= N) {
 #pragma unroll
@@ -519,7 +532,9 @@ int launch_tf32_gemm(int m, int n, int k, float alpha, const float* A, int lda, 
   rc = make_tmap_2d(&tbl, Blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k, (uint64_t)n, (uint64_t)ldbp * 4,
                     C::BK, C::BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (!smem_attr_once(reinterpret_cast<const void*>(sgemm_tf32x3_kernel), C::SMEM))
+  const bool plain = epi.mode == kGemmEpiPlain;
+  auto kern = plain ? sgemm_tf32x3_kernel<true> : sgemm_tf32x3_kernel<false>;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(sgemm_tf32x3_kernel) failed");
   const int sms = std::max(1, sm_count());
   const int tiles = ((m + C::BM - 1) / C::BM) * ((n + C::BN - 1) / C::BN);
@@ -533,7 +548,7 @@ int launch_tf32_gemm(int m, int n, int k, float alpha, const float* A, int lda, 
     if (!part) return fail(OC_ERR_OUT_OF_MEMORY, "sgemm: scratch allocation failed");
   }
   const int grid = std::min(tiles * ksplit, sms);
-  cudaError_t e = launch_pdl_ex(sgemm_tf32x3_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbh, tbl, m, n, k,
+  cudaError_t e = launch_pdl_ex(kern, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tbh, tbl, m, n, k,
                                 alpha, beta, Cm, ldc, bias, ksplit, part, epi, device_status_word());
   if (e != cudaSuccess) return from_cuda(e, "sgemm_tf32x3_kernel");
   if (ksplit == 1) return OC_OK;
