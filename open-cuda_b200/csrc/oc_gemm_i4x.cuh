@@ -42,9 +42,13 @@
 
 namespace oc {
 
-struct I4Staged {
+// BM_ activation rows per tile: 256, or 192 where 256-row tiles would leave
+// a short last round (an N=192 MMA costs ~85 % of an N=256 one, measured).
+template <int BM_>
+struct I4StagedT {
   static constexpr int BN = 128;  // weight rows per tile (MMA M) = output columns
-  static constexpr int BM = 256;  // activation rows per tile (MMA N)
+  static constexpr int BM = BM_;  // activation rows per tile (MMA N)
+  static constexpr int HALF = BM / 2, NBH = HALF / 32;  // rows and 32-row blocks per epilogue half
   static constexpr int BK = 64;   // k per stage: 128-byte f16 rows
   static constexpr int STAGES = 3;
   static constexpr int A_BYTES = BM * BK * 2;  // activation tile
@@ -52,13 +56,16 @@ struct I4Staged {
   static constexpr int STAGE_BYTES = A_BYTES + 2 * W_BYTES;
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int TMEM_COLS = 2 * BM;  // two accumulators (transposed tiles)
+  static constexpr int TMEM_COLS = 512;  // two accumulators of BM columns (transposed tiles)
   static constexpr int YSTAGE_BYTES = EPI_WARPS * 4096;  // one 32 x 32 f32 block per epilogue warp
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + YSTAGE_BYTES + 256;
+  static_assert(BM == 256 || BM == 192, "tile heights of the expanded-weight GEMM");
+  static_assert(A_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1024-byte operand alignment");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  static_assert(TMEM_COLS <= 512, "tensor memory budget");
+  static_assert(2 * BM <= TMEM_COLS, "tensor memory budget");
   static_assert(BN == I4Split::BN, "the split-K workspace and reduction are shared with the dequantizing kernel");
 };
+using I4Staged = I4StagedT<256>;
 
 // Weight row n's 1 / c_n and hi / lo terms by one warp (K % 64 == 0, group
 // 32), 8 weights (one packed word) per lane and step; `w0` is the row's
@@ -99,12 +106,12 @@ __device__ __forceinline__ void weight_row_head(const uint8_t* __restrict__ wq, 
   w0 = lane < K / 8 ? __ldg(reinterpret_cast<const uint32_t*>(wq + (size_t)n * (K / 2)) + lane) : 0u;
 }
 
-// The row quantization of the f32 activations (blocks [0, m): one row per
-// CTA, as quantize_rows_i8_kernel<VPT, true>) and the weight expansion
-// (blocks [m, m + ceil(N / 4)): one weight row per warp) in one launch, so
-// the GEMM waits on one kernel instead of two.  Everything is read after the
-// dependency wait (the activations and the weights may come from the kernel
-// just before).
+// The weight expansion (blocks [0, eb), eb = ceil(N / 4): one weight row per
+// warp; first, so the longer rows of work start first) and the row
+// quantization of the f32 activations (blocks [eb, eb + m): one row per CTA,
+// as quantize_rows_i8_kernel<VPT, true>) in one launch, so the GEMM waits on
+// one kernel instead of two.  Everything is read after the dependency wait
+// (the activations and the weights may come from the kernel just before).
 template <int VPT>
 __global__ void __launch_bounds__(128) w4_prep_kernel(const float* __restrict__ A, int m, int k,
                                                       __half* __restrict__ qa16, float* __restrict__ sa,
@@ -114,14 +121,15 @@ __global__ void __launch_bounds__(128) w4_prep_kernel(const float* __restrict__ 
   pdl_wait();
   pdl_launch();
   __shared__ float red[4];
-  if ((int)blockIdx.x < m) {
-    quantize_row_block<VPT, true>(A, k, qa16, sa, blockIdx.x, red);
+  const int eb = (N + 3) / 4;
+  if ((int)blockIdx.x >= eb) {
+    quantize_row_block<VPT, true>(A, k, qa16, sa, (int)blockIdx.x - eb, red);
     return;
   }
-  const int b = (int)blockIdx.x - m, lane = threadIdx.x & 31;
-  if (b == 0)  // the GEMM that follows counts its split slices from zero
+  const int lane = threadIdx.x & 31;
+  if (blockIdx.x == 0)  // the GEMM that follows counts its split slices from zero
     for (int i = threadIdx.x; i < nready; i += 128) ready[i] = 0;
-  const int n = 4 * b + (threadIdx.x >> 5);
+  const int n = 4 * (int)blockIdx.x + (threadIdx.x >> 5);
   if (n >= N) return;
   float mx;
   uint32_t w0;
@@ -148,6 +156,7 @@ __device__ __forceinline__ bool wait_count(const int* p, int target, volatile in
   }
 }
 
+template <int BM>
 __global__ void __launch_bounds__(I4Staged::THREADS, 1)
     gemm_w4a8_staged_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                             const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPart,
@@ -155,7 +164,7 @@ __global__ void __launch_bounds__(I4Staged::THREADS, 1)
                             const float* __restrict__ sa, const float* __restrict__ icn,
                             const float* __restrict__ bias, float* __restrict__ Y, float* __restrict__ part,
                             int* __restrict__ ready, int* status) {
-  using C = I4Staged;
+  using C = I4StagedT<BM>;
   pdl_wait();  // wx, icn and the zeroed ready counters come from the kernel just before this one
   pdl_launch();
   const int tiles_m = (M + C::BM - 1) / C::BM;
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(I4Staged::THREADS, 1)
     }
   } else {
     // Epilogue warp: TMEM lanes 32 q .. 32 q + 31 = output columns, tile
-    // rows [128 eh, 128 eh + 128) = four 32 x 32 blocks, read from TMEM two
+    // rows [HALF eh, HALF eh + HALF) = NBH 32 x 32 blocks, read from TMEM two
     // at a time (the accumulator is released after the last read), finished
     // in registers and stored through the warp's 4 KB staging buffer by TMA.
     const int q = warp & 3, eh = (warp - 2) >> 2, ew = warp - 2;
@@ -283,23 +292,23 @@ __global__ void __launch_bounds__(I4Staged::THREADS, 1)
       WorkItem it;
       it.set(w, sp);
       const int col0 = it.tn * C::BN + q * 32, col = col0 + lane;
-      const int trow0 = it.tm * C::BM, brow0 = trow0 + eh * 128;
+      const int trow0 = it.tm * C::BM, brow0 = trow0 + eh * C::HALF;
       // column factor, bias and this lane's row scales, loaded while the MMAs run
       const float ic = col < N ? __ldg(icn + col) : 0.0f;
       const float bn = (bias && col < N) ? __ldg(bias + col) : 0.0f;
-      float sar[4];
+      float sar[C::NBH];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < C::NBH; ++i) {
         const int rr = brow0 + 32 * i + lane;
         sar[i] = rr < M ? __ldg(sa + rr) : 0.0f;
       }
-      const int nblk = min(4, max(0, (M - brow0 + 31) / 32));  // blocks holding rows < M
+      const int nblk = min(C::NBH, max(0, (M - brow0 + 31) / 32));  // blocks holding rows < M
       if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
         kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
         goto done;
       }
       tc_fence_after();
-      const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BM + eh * 128);
+      const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BM + eh * C::HALF);
       // The last slice of a split tile finishes it: the other slices' partial
       // sums (each acc / c_n, exact) are added in slice order, then its own.
       const bool finisher = it.split && it.ks == ksplit - 1;
@@ -310,8 +319,8 @@ __global__ void __launch_bounds__(I4Staged::THREADS, 1)
       }
       // two blocks at a time; the accumulator is released after the last TMEM read
 #pragma unroll 1
-      for (int hp = 0; hp < 2; ++hp) {
-        const int nb = min(2, nblk - 2 * hp);  // blocks of this half holding rows < M
+      for (int hp = 0; hp < (C::NBH + 1) / 2; ++hp) {
+        const int nb = min(2, nblk - 2 * hp);  // blocks of this pair holding rows < M
         uint32_t r[2][32];
         float t[2][32];
         if (finisher && nb > 0) {
@@ -341,7 +350,7 @@ __global__ void __launch_bounds__(I4Staged::THREADS, 1)
         for (int i = 0; i < 2; ++i)
           if (i < nb) tmem_ld32(tl + 32 * (2 * hp + i), r[i]);
         tmem_ld_wait();
-        if (hp == (nblk > 2 ? 1 : 0)) {  // after this warp's last TMEM read of the item
+        if (hp == (nblk > 0 ? (nblk - 1) / 2 : 0)) {  // after this warp's last TMEM read of the item
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -358,12 +367,12 @@ __global__ void __launch_bounds__(I4Staged::THREADS, 1)
 #pragma unroll
             for (int j2 = 0; j2 < 32; ++j2) {
               const float tt = __fadd_rn(t[i][j2], __fmul_rn(__uint_as_float(r[i][j2]), ic));
-              r[i][j2] = __float_as_uint(__fadd_rn(__fmul_rn(tt, __shfl_sync(0xffffffffu, sar[bi], j2)), bn));
+              r[i][j2] = __float_as_uint(__fadd_rn(__fmul_rn(tt, __shfl_sync(0xffffffffu, sar[min(bi, C::NBH - 1)], j2)), bn));
             }
           } else {  // y = acc * (sa / c_n) + bias, one rounding (sa / c_n is exact)
 #pragma unroll
             for (int j2 = 0; j2 < 32; ++j2) {
-              const float sc = __fmul_rn(__shfl_sync(0xffffffffu, sar[bi], j2), ic);
+              const float sc = __fmul_rn(__shfl_sync(0xffffffffu, sar[min(bi, C::NBH - 1)], j2), ic);
               r[i][j2] = __float_as_uint(__fmaf_rn(__uint_as_float(r[i][j2]), sc, bn));
             }
           }
@@ -417,9 +426,10 @@ done:
 }
 
 // The same launch for activations that are already int8 (the pre-quantized
-// entry point): blocks [0, nconv) convert qa to f16 (exact), 1024 elements
-// per block, 8 per thread; the rest expand the weights, one row per warp.
-// n_act % 8 == 0, qa 8-byte and qa16 16-byte aligned.
+// entry point): blocks [0, ceil(N / 4)) expand the weights, one row per warp;
+// the `nconv` blocks after them convert qa to f16 (exact), 8 elements per
+// thread and step, grid-stride.  n_act % 8 == 0, qa 8-byte and qa16 16-byte
+// aligned.
 __global__ void __launch_bounds__(128) w4_prep_i8_kernel(const int8_t* __restrict__ qa, size_t n_act, int nconv,
                                                          __half* __restrict__ qa16, const uint8_t* __restrict__ wq,
                                                          const float* __restrict__ sw, int N, int K,
@@ -427,9 +437,10 @@ __global__ void __launch_bounds__(128) w4_prep_i8_kernel(const int8_t* __restric
                                                          int* __restrict__ ready, int nready) {
   pdl_wait();
   pdl_launch();
-  if ((int)blockIdx.x < nconv) {
-    const size_t i = (size_t)blockIdx.x * 128 + threadIdx.x;  // 8-element chunk
-    if (i < n_act / 8) {
+  const int eb = (N + 3) / 4;
+  if ((int)blockIdx.x >= eb) {
+    const size_t n8 = n_act / 8, stride = (size_t)nconv * 128;
+    for (size_t i = (size_t)((int)blockIdx.x - eb) * 128 + threadIdx.x; i < n8; i += stride) {
       const uint2 w = reinterpret_cast<const uint2*>(qa)[i];
       const int8_t* b = reinterpret_cast<const int8_t*>(&w);
       __half2 h[4];
@@ -444,10 +455,10 @@ __global__ void __launch_bounds__(128) w4_prep_i8_kernel(const int8_t* __restric
     }
     return;
   }
-  const int b = (int)blockIdx.x - nconv, lane = threadIdx.x & 31;
-  if (b == 0)  // the GEMM that follows counts its split slices from zero
+  const int lane = threadIdx.x & 31;
+  if (blockIdx.x == 0)  // the GEMM that follows counts its split slices from zero
     for (int j = threadIdx.x; j < nready; j += 128) ready[j] = 0;
-  const int n = 4 * b + (threadIdx.x >> 5);
+  const int n = 4 * (int)blockIdx.x + (threadIdx.x >> 5);
   if (n >= N) return;
   float mx;
   uint32_t w0;

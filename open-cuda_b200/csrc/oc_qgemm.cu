@@ -589,20 +589,29 @@ int run_w4a8_staged(int m, int n, int k, __half* qa16, float* sa, const uint8_t*
   if (!buf) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm_w4a8: scratch allocation failed");
   __half* wx = reinterpret_cast<__half*>(buf);
   float* icn = buf + (size_t)n * k;
+  // Tile height: 192 rows instead of 256 when that takes fewer MMA cycles on
+  // the busiest SM (rounds of tiles x cycles per 64-k block: ~875 at N=192,
+  // ~1030 at N=256, measured); grids that do not fill the GPU keep 256.
+  const int sms = std::max(1, sm_count()), tiles_n = (n + C::BN - 1) / C::BN;
+  auto rounds = [&](int bm) { return ((m + bm - 1) / bm * tiles_n + sms - 1) / sms; };
+  const int tiles256 = (m + 255) / 256 * tiles_n;
+  const int bm = tiles256 >= sms && rounds(192) * 875 < rounds(256) * 1030 ? 192 : 256;
   CUtensorMap ta, tw;
   int rc = make_tmap_2d(&ta, qa16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2,
-                        C::BK, C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
+                        C::BK, bm, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tw, wx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)n, (uint64_t)k * 4, C::BK,
                     C::BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (!smem_attr_once(reinterpret_cast<const void*>(gemm_w4a8_staged_kernel), C::SMEM))
+  auto gemm = bm == 192 ? gemm_w4a8_staged_kernel<192> : gemm_w4a8_staged_kernel<256>;
+  const size_t smem = bm == 192 ? I4StagedT<192>::SMEM : I4StagedT<256>::SMEM;
+  if (!smem_attr_once(reinterpret_cast<const void*>(gemm), smem))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_w4a8_staged_kernel) failed");
   W4Launch L;
   // No K split of a last round: its partial sums would add writes to the
   // output burst that bounds this kernel (the split of every tile stays
   // for grids that do not fill the GPU).
-  rc = w4_prepare(m, n, k, C::BM, k / C::BK, Y, tw, s, L, /*split_tail=*/false);
+  rc = w4_prepare(m, n, k, bm, k / C::BK, Y, tw, s, L, /*split_tail=*/false);
   if (rc) return rc;
   int* ready = nullptr;
   if (L.sp.nsplit) {
@@ -617,14 +626,14 @@ int run_w4a8_staged(int m, int n, int k, __half* qa16, float* sa, const uint8_t*
                    "w4_prep_kernel");
   } else {
     const size_t n_act = (size_t)m * k;
-    const int nconv = (int)((n_act / 8 + 127) / 128);
+    const int nconv = (int)std::min<size_t>((n_act / 8 + 127) / 128, (size_t)sms * 8);
     rc = launch_rc(launch_pdl_ex(w4_prep_i8_kernel, dim3((unsigned)(nconv + (n + 3) / 4)), dim3(128), 0, s, qa_i8,
                                  n_act, nconv, qa16, wq, sw, n, k, wx, icn, ready, L.sp.nsplit),
                    "w4_prep_i8_kernel");
   }
   if (rc) return rc;
   const int grid = std::min(L.sp.items(), std::max(1, sm_count()));
-  return launch_rc(launch_pdl_ex(gemm_w4a8_staged_kernel, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tw, L.tout,
+  return launch_rc(launch_pdl_ex(gemm, dim3(grid), dim3(C::THREADS), smem, s, ta, tw, L.tout,
                                  L.tpart, L.out_tma, m, n, k, L.sp.full, L.sp.ksplit, L.sp.nsplit, sa, icn, bias, Y,
                                  L.part, ready, device_status_word()),
                    "gemm_w4a8_staged_kernel");

@@ -122,6 +122,9 @@ QGEMM_SHAPES = [
     (1800, 2048, 200), (1850, 2048, 202), (1900, 384, 4100),
     # short K, tiles filling half the GPU: not split
     (600, 256, 3000),
+    # many rows on 192-row tiles (fewer MMA cycles on the busiest SM than
+    # 256-row tiles): ragged rows and columns; columns not 16-byte multiples
+    (2000, 256, 3000), (2050, 384, 3070),
 ]
 
 
