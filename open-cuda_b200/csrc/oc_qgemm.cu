@@ -367,15 +367,22 @@ int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const floa
   return OC_OK;
 }
 
-// Picks the tile width with the fewest (waves x tile width) units.
-static int pick_bn(int m, int n) {
+// Picks the tile width (128, 192 or 256 output columns) with the fewest
+// bytes through the busiest SM: waves x (operand tiles loaded + output tile
+// stored) per tile, the SM's load and store rates being what bounds these
+// short-K tiles (~100 GB/s in, ~45 GB/s out per SM, measured; a store byte
+// weighs about two loaded ones).
+static int pick_bn(int m, int n, int k) {
   const int sms = std::max(1, sm_count());
   auto cost = [&](int bn) {
-    long tiles = (long)((m + 127) / 128) * ((n + bn - 1) / bn);
-    long waves = (tiles + sms - 1) / sms;
-    return waves * bn;
+    const long tiles = (long)((m + 127) / 128) * ((n + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    return waves * ((long)k * (128 + bn) + 2L * 128 * bn * 4);
   };
-  return cost(256) < cost(128) ? 256 : 128;
+  int best = 128;
+  for (int bn : {192, 256})
+    if (cost(bn) < cost(best)) best = bn;
+  return best;
 }
 
 template <int BN>
@@ -442,8 +449,10 @@ int run_grouped_w8a8_tc(int R, int N, int K, const int8_t* xg, const float* sg, 
 
 int run_w8a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq, const float* sw,
                 const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
-  return pick_bn(m, n) == 256 ? launch_w8a8_tc<256>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s)
-                              : launch_w8a8_tc<128>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s);
+  const int bn = pick_bn(m, n, k);
+  return bn == 256   ? launch_w8a8_tc<256>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s)
+         : bn == 192 ? launch_w8a8_tc<192>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s)
+                     : launch_w8a8_tc<128>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s);
 }
 
 int run_w4a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const uint8_t* wq, const float* sw,
