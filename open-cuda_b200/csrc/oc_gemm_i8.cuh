@@ -29,7 +29,7 @@ struct I8Gemm {
   static constexpr int BM = 128, BN = BN_, BK = 128;
   static constexpr int STAGES = BN_ >= 192 ? 4 : (GROUPED_ ? 5 : 6);
   static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = BN == 128 ? 256 : 512;  // two accumulators of BN columns (a power of two)
+  static constexpr int TMEM_COLS = BN <= 64 ? 128 : (BN == 128 ? 256 : 512);  // two accumulators of BN columns (a power of two)
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS);
   static constexpr int YSTAGE_BYTES = EPI_WARPS * 4096;  // one 32x32 f32 block per epilogue warp
@@ -37,7 +37,7 @@ struct I8Gemm {
   static constexpr int GROUP_BYTES = GROUPED_ ? 2 * 4 * (kMaxGroups + 1) : 0;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + YSTAGE_BYTES + 256 + GROUP_BYTES;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
-  static_assert(BN == 128 || BN == 192 || BN == 256, "tile widths");
+  static_assert(BN == 64 || BN == 128 || BN == 192 || BN == 256, "tile widths");
   static_assert(2 * BN <= TMEM_COLS && SMEM <= 227 * 1024, "tensor / shared memory budget");
 };
 

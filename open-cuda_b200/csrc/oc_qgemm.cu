@@ -367,7 +367,7 @@ int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const floa
   return OC_OK;
 }
 
-// Picks the tile width (128, 192 or 256 output columns) with the fewest
+// Picks the tile width (64, 128, 192 or 256 output columns) with the fewest
 // bytes through the busiest SM: waves x (operand tiles loaded + output tile
 // stored) per tile, the SM's load and store rates being what bounds these
 // short-K tiles (~100 GB/s in, ~45 GB/s out per SM, measured; a store byte
@@ -380,7 +380,7 @@ static int pick_bn(int m, int n, int k) {
     return waves * ((long)k * (128 + bn) + 2L * 128 * bn * 4);
   };
   int best = 128;
-  for (int bn : {192, 256})
+  for (int bn : {64, 192, 256})
     if (cost(bn) < cost(best)) best = bn;
   return best;
 }
@@ -452,6 +452,7 @@ int run_w8a8_tc(int m, int n, int k, const int8_t* qa, const float* sa, const in
   const int bn = pick_bn(m, n, k);
   return bn == 256   ? launch_w8a8_tc<256>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s)
          : bn == 192 ? launch_w8a8_tc<192>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s)
+         : bn == 64  ? launch_w8a8_tc<64>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s)
                      : launch_w8a8_tc<128>(m, n, k, qa, sa, wq, sw, bias, Y, acc_out, s);
 }
 
