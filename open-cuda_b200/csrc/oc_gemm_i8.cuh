@@ -27,7 +27,7 @@ constexpr int kMaxGroups = 1024;  // grouped GEMM: groups per launch
 template <int BN_, bool GROUPED_ = false>
 struct I8Gemm {
   static constexpr int BM = 128, BN = BN_, BK = 128;
-  static constexpr int STAGES = BN_ >= 192 ? 4 : (GROUPED_ ? 5 : 6);
+  static constexpr int STAGES = BN_ >= 192 ? (GROUPED_ ? 3 : 4) : (GROUPED_ ? 5 : 6);
   static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = BN <= 64 ? 128 : (BN == 128 ? 256 : 512);  // two accumulators of BN columns (a power of two)
   static constexpr int EPI_WARPS = 8;
