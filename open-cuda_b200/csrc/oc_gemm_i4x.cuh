@@ -9,31 +9,30 @@
 // f16 activations: w4_prep_kernel or w4_prep_i8_kernel) writes, per weight
 // row n, the same hi / lo f16 terms (hi = f16(w * s_hi), lo = f16(f16(w *
 // s_lo) - (hi - w * s_hi)), s = sw * c_n, c_n = 2^range_exp) into wx [N][2K]
-// -- k-block kb of 64 holds hi at
-// columns [128 kb, 128 kb + 64) and lo at [128 kb + 64, 128 kb + 128) -- and
-// 1 / c_n into icn [N].  For the shapes routed here wx fits in L2, so the GEMM
-// reads it from there.
+// (k-block kb of 64 holds hi at columns [128 kb, 128 kb + 64) and lo at
+// [128 kb + 64, 128 kb + 128)) and 1 / c_n into icn [N].  For the shapes
+// routed here wx fits in L2, so the GEMM reads it from there.
 //
-// GEMM: the same tile, MMA layout and numerics as the dequantizing kernel
-// (A = 128 weight rows, B = 256 activation rows, two kind::f16 MMAs per
+// GEMM: the same MMA layout and numerics as the dequantizing kernel (A = 128
+// weight rows, B = BM = 256 or 192 activation rows, two kind::f16 MMAs per
 // K = 16 step: hi then lo, f32 accumulation in TMEM; y = acc * (sa / c_n) +
 // bias), so both kernels give the same sums.  Without converter warps TMEM
 // holds two accumulators and the epilogue of tile i overlaps the MMAs of
 // tile i + 1.  Persistent, one CTA per SM, 320 threads:
-//   warp 0      TMA producer: activation tile [256][64] and the hi / lo
+//   warp 0      TMA producer: activation tile [BM][64] and the hi / lo
 //               weight tiles [128][64] of each k-block (128-byte swizzle)
 //               into a 3-stage ring
 //   warp 1      TMEM allocator + MMA issuer
 //   warps 2..9  epilogue: warp = (TMEM lane quadrant q = warp % 4, row half
-//               eh); four 32 x 32 blocks TMEM -> registers -> * sa / c_n +
-//               bias -> shared memory (transposed) -> TMA store
-// Work items follow SplitPlan (oc_gemm_i4s.cuh): whole tiles, then the last
-// round's tiles split in K.  A CTA runs its split item first.  The epilogue
-// warps of slices 0 .. ksplit - 2 store the slice's partial sums and count
-// them on the tile's ready counter; the CTA of the last slice waits for the
-// count (its siblings run at the same time) and finishes the tile in slice
-// order, the arithmetic of gemm_w4a8_splitk_reduce, while its MMAs already
-// run the next tile.  All CTAs of the grid (at most one per SM) are
+//               eh); BM / 64 blocks of 32 x 32: TMEM -> registers -> * sa /
+//               c_n + bias -> shared memory (transposed) -> TMA store
+// Work items follow SplitPlan (oc_gemm_i4s.cuh): whole tiles, then (for
+// grids that do not fill the GPU) tiles split in K.  A CTA runs its split
+// item first.  The epilogue warps of slices 0 .. ksplit - 2 store the
+// slice's partial sums and count them on the tile's ready counter; the CTA
+// of the last slice waits for the count (its siblings run at the same time)
+// and finishes the tile in slice order, the arithmetic of
+// gemm_w4a8_splitk_reduce.  All CTAs of the grid (at most one per SM) are
 // resident together, and every wait, the ready-counter wait included, is
 // bounded (oc_ptx.cuh).
 #pragma once
