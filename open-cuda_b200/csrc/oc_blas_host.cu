@@ -209,14 +209,19 @@ static int blas_qgemm(oc_device* dev, int bits, size_t m, size_t n, size_t k, si
   void* dws = p;
   rc = arena_pipeline(ar);
   if (rc) return rc;
-  // Row chunks of at least 512 rows (at most 16 chunks) when the output copy
+  // Row chunks of at least 512 rows (at most 17 chunks) when the output copy
   // is long: chunk c's input copy (host -> device stream), matmul (device
   // stream) and output copy (device -> host stream) overlap the neighbouring
   // chunks', and the two copy directions run at once.  Rows are quantized
   // independently, so a chunk is the same computation on fewer rows.
-  size_t rows = m;
-  if (m * n * 4 >= ((size_t)8 << 20) && m >= 1024) rows = std::max<size_t>(512, (m + 15) / 16);
-  const int nch = (int)((m + rows - 1) / rows);  // 1 + 2 * nch <= Arena::kEvents
+  // The first chunk is short (128 rows) so that the output copy, the
+  // bottleneck, starts as early as possible.
+  size_t rows = m, first = m;
+  if (m * n * 4 >= ((size_t)8 << 20) && m >= 1024) {
+    rows = std::max<size_t>(512, (m + 15) / 16);
+    first = 128;
+  }
+  const int nch = 1 + (int)((m - first + rows - 1) / rows);  // 1 + 2 * nch <= Arena::kEvents
   cudaStream_t sh = ar.h2d, sd = ar.d2h;
   OC_CHECK_CUDA(cudaMemcpyAsync(dw, wq, wbytes, cudaMemcpyHostToDevice, sh));
   OC_CHECK_CUDA(cudaMemcpyAsync(dsc, w_scales, ng * 4, cudaMemcpyHostToDevice, sh));
@@ -224,7 +229,8 @@ static int blas_qgemm(oc_device* dev, int bits, size_t m, size_t n, size_t k, si
   OC_CHECK_CUDA(cudaEventRecord(ar.ev[0], sh));
   OC_CHECK_CUDA(cudaStreamWaitEvent(s, ar.ev[0], 0));
   for (int c = 0; c < nch; ++c) {
-    const size_t r0 = (size_t)c * rows, mc = std::min(rows, m - r0);
+    const size_t r0 = c == 0 ? 0 : first + (size_t)(c - 1) * rows;
+    const size_t mc = std::min(c == 0 ? first : rows, m - r0);
     OC_CHECK_CUDA(cudaMemcpyAsync(da + r0 * k, a + r0 * k, mc * k * 4, cudaMemcpyHostToDevice, sh));
     OC_CHECK_CUDA(cudaEventRecord(ar.ev[1 + 2 * c], sh));
     OC_CHECK_CUDA(cudaStreamWaitEvent(s, ar.ev[1 + 2 * c], 0));

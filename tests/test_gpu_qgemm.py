@@ -183,7 +183,7 @@ def test_qgemm_no_bias_and_host_slices(oc, oracle):
 @pytest.mark.parametrize("pinned", [False, True])
 def test_host_slice_qgemm_row_chunks(oc, oracle, pinned):
     # outputs of >= 8 MB and >= 1024 rows go through row chunks whose copies
-    # and matmuls overlap on three streams (3 chunks here: 512, 512, 76 rows);
+    # and matmuls overlap on three streams (3 chunks here: 128, 512, 460 rows);
     # pinned host buffers let the copies run asynchronously.  Opening and
     # closing the device object again releases and rebuilds its scratch.
     m, k, n = 1100, 256, 2048
