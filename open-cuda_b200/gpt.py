@@ -139,3 +139,123 @@ class GptModel:
             lg = lg[:, :n]
             return (toks[0], lg[0]) if single else (toks, lg)
         return toks[0] if single else toks
+
+
+# ---- checkpoint loading (llm:661-731) -------------------------------------
+
+def read_safetensors(data: bytes) -> dict:
+    """Tensors of a safetensors file: {name: (dtype, shape, bytes)}.
+
+    The format: an 8-byte little-endian header length N, N bytes of JSON
+    ({name: {"dtype", "shape", "data_offsets": [begin, end]}}, plus an
+    optional "__metadata__" entry), then the tensor bytes, offsets relative
+    to the end of the header."""
+    import json
+    import struct
+
+    if len(data) < 8:
+        raise ValueError("open-cuda-llm: failed to parse model.safetensors (truncated header)")
+    (n,) = struct.unpack("<Q", data[:8])
+    if 8 + n > len(data):
+        raise ValueError("open-cuda-llm: failed to parse model.safetensors (header length past the end)")
+    header = json.loads(data[8:8 + n].decode("utf-8"))
+    base = 8 + n
+    out = {}
+    for name, info in header.items():
+        if name == "__metadata__":
+            continue
+        b, e = info["data_offsets"]
+        if not (0 <= b <= e <= len(data) - base):
+            raise ValueError(f"open-cuda-llm: failed to parse model.safetensors (tensor '{name}' out of range)")
+        out[name] = (info["dtype"], tuple(info["shape"]), memoryview(data)[base + b:base + e])
+    return out
+
+
+def _tensor_f32(tensors: dict, name: str) -> np.ndarray:
+    """tensor_f32 (llm:112-126): an F32 tensor's values, little-endian."""
+    if name not in tensors:
+        raise ValueError(f"open-cuda-llm: missing tensor '{name}'")
+    dtype, _, raw = tensors[name]
+    if dtype != "F32":
+        raise ValueError(f"open-cuda-llm: tensor '{name}' has unexpected dtype {dtype} (expected F32)")
+    if len(raw) % 4:
+        raise ValueError(f"open-cuda-llm: tensor '{name}' byte length not a multiple of 4")
+    return np.frombuffer(raw, dtype="<f4").astype(np.float32)
+
+
+def gpt2_config_from_json(text: str) -> GptConfig:
+    """GPT2Config::into_gpt_config (llm:76-110): n_positions (else n_ctx) is
+    the context length, intermediate size 4 * n_embd, eps 1e-5 by default."""
+    import json
+
+    raw = json.loads(text)
+    ctx = raw.get("n_positions") if raw.get("n_positions") is not None else raw.get("n_ctx")
+    if ctx is None:
+        raise ValueError("open-cuda-llm: config.json must have n_positions or n_ctx")
+    h, heads = int(raw["n_embd"]), int(raw["n_head"])
+    if h % heads:
+        raise ValueError(f"open-cuda-llm: n_embd {h} not divisible by n_head {heads}")
+    eps = raw.get("layer_norm_epsilon")
+    return GptConfig(int(raw["vocab_size"]), h, int(raw["n_layer"]), heads, 4 * h, int(ctx),
+                     1e-5 if eps is None else float(eps))
+
+
+def gpt2_checkpoint_plan(directory) -> tuple[GptConfig, list]:
+    """GptModel::load (llm:661-731) up to the weights: the config and the
+    list of (weight name, layer, values) to upload.  Tensor names may carry
+    the `transformer.` prefix (detected from wte.weight, llm:681-687); the
+    Conv1D weights are already [in][out]; lm_head is tied to wte, transposed
+    to [hidden][vocab] with a zero bias (llm:722-728)."""
+    from pathlib import Path
+
+    d = Path(directory)
+    try:
+        cfg_text = (d / "config.json").read_text()
+    except OSError as e:
+        raise ValueError(f"open-cuda-llm: failed to read config.json in {d}: {e}") from e
+    cfg = gpt2_config_from_json(cfg_text)
+    try:
+        data = (d / "model.safetensors").read_bytes()
+    except OSError as e:
+        raise ValueError(f"open-cuda-llm: failed to read model.safetensors in {d}: {e}") from e
+    t = read_safetensors(data)
+    prefix = "" if "wte.weight" in t else ("transformer." if "transformer.wte.weight" in t else "")
+    H, V, I, ctx = cfg.hidden_size, cfg.vocab_size, cfg.intermediate_size, cfg.max_seq_len
+    plan = []
+
+    def sized(name, count, what):
+        v = _tensor_f32(t, prefix + name)
+        if v.size != count:
+            raise ValueError(f"open-cuda-llm: '{prefix}{name}' has {v.size} elements, expected {what}")
+        return v
+
+    wte = sized("wte.weight", V * H, f"{V}x{H}")
+    plan.append(("wte", 0, wte))
+    plan.append(("wpe", 0, sized("wpe.weight", ctx * H, f"{ctx}x{H}")))
+    for i in range(cfg.num_layers):
+        p = f"h.{i}."
+        for key, (tensor, n_in, n_out) in {"qkv": ("attn.c_attn", H, 3 * H), "attn_out": ("attn.c_proj", H, H),
+                                           "fc": ("mlp.c_fc", H, I), "proj": ("mlp.c_proj", I, H)}.items():
+            plan.append((key + "_w", i, sized(p + tensor + ".weight", n_in * n_out, f"{n_in}x{n_out}")))
+            plan.append((key + "_b", i, _tensor_f32(t, prefix + p + tensor + ".bias")))
+        for key, ln in (("ln1", "ln_1"), ("ln2", "ln_2")):
+            plan.append((key + "_w", i, _tensor_f32(t, prefix + p + ln + ".weight")))
+            plan.append((key + "_b", i, _tensor_f32(t, prefix + p + ln + ".bias")))
+    plan.append(("lnf_w", 0, _tensor_f32(t, prefix + "ln_f.weight")))
+    plan.append(("lnf_b", 0, _tensor_f32(t, prefix + "ln_f.bias")))
+    plan.append(("lm_head_w", 0, np.ascontiguousarray(wte.reshape(V, H).T).ravel()))
+    plan.append(("lm_head_b", 0, np.zeros(V, np.float32)))
+    return cfg, plan
+
+
+def load_gpt2(directory, device: int = 0, max_batch: int = 1, max_prompt_len: int = 64) -> GptModel:
+    """GptModel::load (llm:661-731) onto the device: config.json and
+    model.safetensors of a Hugging Face GPT-2 checkpoint in `directory`."""
+    cfg, plan = gpt2_checkpoint_plan(directory)
+    m = GptModel(cfg, None, device=device, max_batch=max_batch, max_prompt_len=max_prompt_len)
+    for name, layer, values in plan:
+        m.set_weight(name, values, layer)
+    return m
+
+
+GptModel.load = staticmethod(load_gpt2)

@@ -92,3 +92,51 @@ def test_gpt2_124m_batch1_matches_oracle(gptmod, oracle):
     for b in range(4):
         assert bt[b].tolist() == ref.generate(prompts[b], 6).tolist(), b
     dev.close()
+
+
+def test_gpt2_checkpoint_matches_oracle(gptmod, oracle):
+    """GptModel::load (llm:661-731): a Hugging Face-style checkpoint (the
+    `transformer.` naming, lm_head tied to wte) written from the oracle's
+    weights, loaded onto the device: greedy tokens identical and logits
+    within 1e-4 of the oracle running the same weights."""
+    import json
+    import shutil
+    from pathlib import Path
+
+    st = pytest.importorskip("safetensors.numpy")
+    cfg = gptmod.GptConfig(oracle.BYTE_VOCAB_SIZE, 32, 2, 4, 128, 256, 1e-5)  # intermediate = 4 * hidden
+    V, H, L, ctx = cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.max_seq_len
+    ref = oracle.GptModel(_oracle_cfg(oracle, cfg), 99)
+    wte = ref.weight("wte").reshape(V, H)
+    ref.weight("lm_head_w")[:] = np.ascontiguousarray(wte.T).ravel()  # tied, as in a GPT-2 checkpoint
+    ref.weight("lm_head_b")[:] = 0.0
+    t = {"transformer.wte.weight": wte.copy(), "transformer.wpe.weight": ref.weight("wpe").reshape(ctx, H).copy(),
+         "transformer.ln_f.weight": ref.weight("lnf_w").copy(), "transformer.ln_f.bias": ref.weight("lnf_b").copy()}
+    for i in range(L):
+        p = f"transformer.h.{i}."
+        for key, name, shape in (("qkv", "attn.c_attn", (H, 3 * H)), ("attn_out", "attn.c_proj", (H, H)),
+                                 ("fc", "mlp.c_fc", (H, 4 * H)), ("proj", "mlp.c_proj", (4 * H, H))):
+            t[p + name + ".weight"] = ref.weight(key + "_w", i).reshape(shape).copy()
+            t[p + name + ".bias"] = ref.weight(key + "_b", i).copy()
+        for key, ln in (("ln1", "ln_1"), ("ln2", "ln_2")):
+            t[p + ln + ".weight"] = ref.weight(key + "_w", i).copy()
+            t[p + ln + ".bias"] = ref.weight(key + "_b", i).copy()
+    d = Path(__file__).parent / "_tmp" / "gpt2_checkpoint"
+    if d.exists():
+        shutil.rmtree(d)
+    d.mkdir(parents=True)
+    try:
+        (d / "config.json").write_text(json.dumps({"vocab_size": V, "n_embd": H, "n_layer": L, "n_head": 4,
+                                                   "n_positions": ctx, "layer_norm_epsilon": 1e-5}))
+        st.save_file({k: np.ascontiguousarray(v, np.float32) for k, v in t.items()}, str(d / "model.safetensors"))
+        dev = gptmod.GptModel.load(d)
+    finally:
+        shutil.rmtree(d)
+    prompt = oracle.byte_encode("checkpoint")
+    ref.set_attention(flash=True, block=4)
+    rt, rl = ref.generate(prompt, 8, want_logits=True)
+    dt, dl = dev.generate(prompt, 8, want_logits=True)
+    assert dt.tolist() == rt.tolist()
+    assert np.max(np.abs(dl - rl)) < LOGIT_TOL
+    assert np.array_equal(dev.weight("lm_head_w"), ref.weight("lm_head_w"))
+    dev.close()
