@@ -94,6 +94,30 @@ int oc_device_memcpy_d2h(oc_device *dev, void *dst, uint64_t src, size_t bytes);
 int oc_device_memcpy_d2d(oc_device *dev, uint64_t dst, uint64_t src, size_t bytes);
 /* GpuDevice::synchronize (core:106); also reports kernel status words. */
 int oc_device_synchronize(oc_device *dev);
+
+/* ---- multi-device (crates/opencuda-multidev/src/lib.rs) ----------------- */
+
+/* DevicePartition (multidev:17-22): layers [layer_start, layer_end) on the
+ * device at index device_id of the list. */
+typedef struct {
+  size_t device_id, layer_start, layer_end;
+} oc_device_partition;
+/* partition_layers (multidev:28-74): device i < n-1 gets
+ * floor(total_layers * mem_i / sum(mem)) layers, the last device the rest;
+ * when every device reports 0 bytes, total_layers / n each and the rest to
+ * the last.  An empty list is OC_ERR_INVALID_VALUE ("no devices to partition
+ * across").  out receives num_devices entries.  No GPU work. */
+int oc_partition_layers_by_memory(const uint64_t *total_memory, size_t num_devices, size_t total_layers,
+                                  oc_device_partition *out);
+/* The same over device objects (their oc_device_info total_memory). */
+int oc_partition_layers(oc_device *const *devices, size_t num_devices, size_t total_layers,
+                        oc_device_partition *out);
+/* transfer_between_devices (multidev:78-83, a stub in the reference): copies
+ * bytes from src_addr (an allocation of src) to dst_addr (an allocation of
+ * dst), over NVLink as a peer copy when the two GPUs can access each other,
+ * else staged through pinned host memory; returns when the copy is done.
+ * Unknown addresses or sizes past either allocation are OC_ERR_INVALID_VALUE. */
+int oc_transfer_between_devices(oc_device *src, uint64_t src_addr, oc_device *dst, uint64_t dst_addr, size_t bytes);
 /* GpuDevice::launch_kernel (core:99-104), routed by kernel name the way the
  * Vulkan backend routes SPIR-V entry points
  * (crates/opencuda-vulkan/src/real.rs:868-887).  Names and argument

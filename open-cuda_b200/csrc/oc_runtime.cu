@@ -3,6 +3,7 @@
 // error strings, tensor-map encoding and the per-device kernel status word.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -325,6 +326,100 @@ int oc_device_synchronize(oc_device* dev) {
   DeviceGuard g(dev->ordinal);
   OC_CHECK_CUDA(cudaStreamSynchronize(dev->stream));
   return oc::check_device_status(dev->stream);
+}
+
+int oc_partition_layers_by_memory(const uint64_t* total_memory, size_t num_devices, size_t total_layers,
+                                  oc_device_partition* out) {
+  if (num_devices == 0) return oc::fail(OC_ERR_INVALID_VALUE, "no devices to partition across");
+  if (!total_memory || !out) return oc::fail(OC_ERR_INVALID_VALUE, "NULL argument");
+  unsigned __int128 total = 0;
+  for (size_t i = 0; i < num_devices; ++i) total += total_memory[i];
+  size_t offset = 0;
+  for (size_t i = 0; i < num_devices; ++i) {
+    size_t n;
+    if (i + 1 == num_devices)
+      n = total_layers - offset;
+    else if (total == 0)
+      n = total_layers / num_devices;
+    else
+      n = (size_t)((unsigned __int128)total_layers * total_memory[i] / total);
+    const size_t end = std::min(offset + n, total_layers);
+    out[i] = oc_device_partition{i, offset, end};
+    offset = end;
+  }
+  return OC_OK;
+}
+
+int oc_partition_layers(oc_device* const* devices, size_t num_devices, size_t total_layers,
+                        oc_device_partition* out) {
+  if (num_devices == 0) return oc::fail(OC_ERR_INVALID_VALUE, "no devices to partition across");
+  if (!devices || !out) return oc::fail(OC_ERR_INVALID_VALUE, "NULL argument");
+  std::vector<uint64_t> mem(num_devices);
+  for (size_t i = 0; i < num_devices; ++i) {
+    oc_device_info info;
+    const int rc = oc_device_get_info(devices[i], &info);
+    if (rc) return rc;
+    mem[i] = info.total_memory;
+  }
+  return oc_partition_layers_by_memory(mem.data(), num_devices, total_layers, out);
+}
+
+int oc_transfer_between_devices(oc_device* src, uint64_t src_addr, oc_device* dst, uint64_t dst_addr,
+                                size_t bytes) {
+  if (!src || !dst) return oc::fail(OC_ERR_INVALID_VALUE, "NULL device");
+  const size_t cs = lookup(src, src_addr), cd = lookup(dst, dst_addr);
+  if (cs == 0 || cd == 0 || bytes > cs || bytes > cd) return oc::fail(OC_ERR_INVALID_VALUE, "invalid device pointer");
+  if (bytes == 0) return OC_OK;
+  // queued work on either device that touches the buffers finishes first
+  {
+    DeviceGuard g(src->ordinal);
+    OC_CHECK_CUDA(cudaStreamSynchronize(src->stream));
+  }
+  {
+    DeviceGuard g(dst->ordinal);
+    OC_CHECK_CUDA(cudaStreamSynchronize(dst->stream));
+  }
+  void* sp = reinterpret_cast<void*>(src_addr);
+  void* dp = reinterpret_cast<void*>(dst_addr);
+  if (src->ordinal == dst->ordinal) {
+    DeviceGuard g(src->ordinal);
+    OC_CHECK_CUDA(cudaMemcpyAsync(dp, sp, bytes, cudaMemcpyDeviceToDevice, src->stream));
+    OC_CHECK_CUDA(cudaStreamSynchronize(src->stream));
+    return OC_OK;
+  }
+  int can = 0;
+  OC_CHECK_CUDA(cudaDeviceCanAccessPeer(&can, dst->ordinal, src->ordinal));
+  if (can) {  // NVLink / NVSwitch peer copy, issued on the destination's stream
+    DeviceGuard g(dst->ordinal);
+    const cudaError_t e = cudaDeviceEnablePeerAccess(src->ordinal, 0);
+    if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) return oc::from_cuda(e, "cudaDeviceEnablePeerAccess");
+    cudaGetLastError();
+    OC_CHECK_CUDA(cudaMemcpyPeerAsync(dp, dst->ordinal, sp, src->ordinal, bytes, dst->stream));
+    OC_CHECK_CUDA(cudaStreamSynchronize(dst->stream));
+    return OC_OK;
+  }
+  // no peer path: device -> pinned host -> device in 8 MiB pieces
+  const size_t piece = std::min(bytes, (size_t)8 << 20);
+  void* host = nullptr;
+  OC_CHECK_CUDA(cudaMallocHost(&host, piece));
+  int rc = OC_OK;
+  for (size_t off = 0; off < bytes && rc == OC_OK; off += piece) {
+    const size_t n = std::min(piece, bytes - off);
+    {
+      DeviceGuard g(src->ordinal);
+      if (cudaMemcpyAsync(host, static_cast<uint8_t*>(sp) + off, n, cudaMemcpyDeviceToHost, src->stream) !=
+              cudaSuccess ||
+          cudaStreamSynchronize(src->stream) != cudaSuccess)
+        rc = oc::from_cuda(cudaGetLastError(), "transfer_between_devices (device to host)");
+    }
+    if (rc) break;
+    DeviceGuard g(dst->ordinal);
+    if (cudaMemcpyAsync(static_cast<uint8_t*>(dp) + off, host, n, cudaMemcpyHostToDevice, dst->stream) != cudaSuccess ||
+        cudaStreamSynchronize(dst->stream) != cudaSuccess)
+      rc = oc::from_cuda(cudaGetLastError(), "transfer_between_devices (host to device)");
+  }
+  cudaFreeHost(host);
+  return rc;
 }
 
 int oc_get_device_status(int* status) {

@@ -79,6 +79,9 @@ _SIGS = {
     "oc_device_memcpy_d2h": (ci, [vp, vp, C.c_uint64, sz]),
     "oc_device_memcpy_d2d": (ci, [vp, C.c_uint64, C.c_uint64, sz]),
     "oc_device_synchronize": (ci, [vp]),
+    "oc_partition_layers_by_memory": (ci, [C.POINTER(C.c_uint64), sz, sz, vp]),
+    "oc_partition_layers": (ci, [C.POINTER(vp), sz, sz, vp]),
+    "oc_transfer_between_devices": (ci, [vp, C.c_uint64, vp, C.c_uint64, sz]),
     "oc_device_stream": (vp, [vp]),
     "oc_get_device_status": (ci, [C.POINTER(ci)]),
     "oc_sgemm": (ci, [ci, ci, ci, cf, vp, ci, vp, ci, ci, cf, vp, ci, vp, vp]),
@@ -521,6 +524,37 @@ class Device:
                                        _np_ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
                                        _np_ptr(y)))
         return y
+
+
+class DevicePartition(C.Structure):
+    """DevicePartition (crates/opencuda-multidev/src/lib.rs:17-22)."""
+
+    _fields_ = [("device_id", sz), ("layer_start", sz), ("layer_end", sz)]
+
+
+def partition_layers_by_memory(total_memory, total_layers: int) -> list[tuple[int, int, int]]:
+    """partition_layers (multidev:28-74) on a list of device memory sizes:
+    [(device_id, layer_start, layer_end)]."""
+    n = len(total_memory)
+    mem = (C.c_uint64 * max(n, 1))(*[int(x) for x in total_memory])
+    out = (DevicePartition * max(n, 1))()
+    check(lib().oc_partition_layers_by_memory(mem, n, total_layers, out))
+    return [(p.device_id, p.layer_start, p.layer_end) for p in out[:n]]
+
+
+def partition_layers(devices, total_layers: int) -> list[tuple[int, int, int]]:
+    """partition_layers (multidev:28-74) over Device objects."""
+    n = len(devices)
+    hs = (vp * max(n, 1))(*[d.handle for d in devices])
+    out = (DevicePartition * max(n, 1))()
+    check(lib().oc_partition_layers(hs, n, total_layers, out))
+    return [(p.device_id, p.layer_start, p.layer_end) for p in out[:n]]
+
+
+def transfer_between_devices(src: "Device", src_addr: int, dst: "Device", dst_addr: int, nbytes: int) -> None:
+    """transfer_between_devices (multidev:78-83): allocation to allocation,
+    NVLink peer copy or staged through host memory; synchronous."""
+    check(lib().oc_transfer_between_devices(src.handle, src_addr, dst.handle, dst_addr, nbytes))
 
 
 class LaunchConfig(C.Structure):
