@@ -438,6 +438,11 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
       const int kk = warp + 8 * u;
       if (kk < kn) pre[u] = __ldg(reinterpret_cast<const VT*>(wp + (size_t)kk * a.n));
     }
+    // the rest of this CTA's weight rows into L2 (the weights are not written
+    // by any kernel, so this may run before the dependency wait)
+    if ((a.n & 3) == 0 && (reinterpret_cast<uintptr_t>(a.W) & 15u) == 0 && tile * TN + TN <= a.n)
+      for (int kk = 64 + threadIdx.x; kk < kn; kk += 256)
+        prefetch_l2_bulk(a.W + (size_t)(k0 + kk) * a.n + tile * TN, TN * 4);
   }
   pdl_wait();  // x, out, the KV cache and the counters belong to the predecessors until here
   pdl_launch();
