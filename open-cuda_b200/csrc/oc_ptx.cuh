@@ -25,7 +25,6 @@ enum : int {
   kDevTimeoutProducer = 1,
   kDevTimeoutMma = 2,
   kDevTimeoutEpilogue = 3,
-  kDevTimeoutRows = 4,  // a skinny GEMM waited for its quantized activation rows
 };
 
 // Wall-clock bound on any spin-wait inside a kernel: a wait that has not

@@ -9,8 +9,6 @@
 //  * larger m, W4A8: oc_gemm_i4.cuh (INT4 widened to int8 in shared memory,
 //    per-group TMEM partials promoted to f32 in the epilogue warps).
 #include <algorithm>
-#include <map>
-#include <mutex>
 
 #include "oc_gemm_i4.cuh"
 #include "oc_gemm_i4s.cuh"
@@ -59,83 +57,13 @@ __device__ __forceinline__ int butterfly_sum(int (&v)[V], int lane) {
   return s;  // value index lane >> (5 - H)
 }
 
-// ---- activation rows quantized inside a skinny GEMM -------------------------
-// quantize_int8(row, group = k) of each of the m rows (the arithmetic of
-// quantize_rows_i8_kernel: max |x| over the row, s = max / 127, q =
-// round(x / s) clamped) without a launch of its own: block b quantizes rows
-// b, b + gridDim.x, ... into qa / sa and counts each finished row in
-// flags[0]; every block then waits (bounded) for all m rows, which it reads
-// through L2 (they are written during this launch, so never through the
-// read-only path).  flags[1] counts the blocks that are done; the last one
-// zeroes both words for the next launch on this stream, which reads them only
-// after its dependency wait, i.e. after this grid has completed.
-struct RowQuant {
-  const float* A;  // [m][k] f32, 16-byte aligned, k % 4 == 0; nullptr: qa / sa are inputs
-  int* flags;      // [2], zero at launch
-  int* status;     // device status word
-};
-
-__device__ __forceinline__ bool wait_rows(const int* p, int target) {
-  if (ld_acquire_gpu(p) >= target) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    __nanosleep(32);
-    if (ld_acquire_gpu(p) >= target) return true;
-    if ((it & 15u) == 15u && globaltimer_ns() - t0 > kWaitLimitNs) return false;
-  }
-}
-
-// Every thread of the (256-thread) block calls it.
-__device__ __forceinline__ void quantize_rows_in_grid(const RowQuant& rq, int m, int k, int8_t* qa, float* sa) {
-  __shared__ float red[8];
-  const int n4 = k >> 2;
-  for (int row = blockIdx.x; row < m; row += gridDim.x) {
-    const float4* a4 = reinterpret_cast<const float4*>(rq.A + (size_t)row * k);
-    float mx = 0.0f;
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-      const float4 v = __ldg(a4 + i);
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-    mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-#pragma unroll
-    for (int w = 0; w < 8; ++w) mx = fmaxf(mx, red[w]);
-    const float s = (mx == 0.0f) ? 0.0f : __fdiv_rn(mx, 127.0f);
-    if (threadIdx.x == 0) sa[row] = s;
-    char4* q4 = reinterpret_cast<char4*>(qa + (size_t)row * k);
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-      const float4 v = __ldg(a4 + i);
-      q4[i] = make_char4((signed char)quant_one(v.x, s, 127.0f), (signed char)quant_one(v.y, s, 127.0f),
-                         (signed char)quant_one(v.z, s, 127.0f), (signed char)quant_one(v.w, s, 127.0f));
-    }
-    __threadfence();
-    __syncthreads();  // every store of the row is visible; red may be reused
-    if (threadIdx.x == 0) atomicAdd(rq.flags, 1);
-  }
-  if (threadIdx.x == 0) {
-    if (!wait_rows(rq.flags, m)) atomicCAS(rq.status, 0, kDevTimeoutRows);
-    __threadfence();
-  }
-  __syncthreads();
-}
-
-// End of a launch that quantized its rows: the last block resets the flags.
-__device__ __forceinline__ void rows_launch_done(const RowQuant& rq) {
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(rq.flags + 1, 1) == (int)gridDim.x - 1) {
-    rq.flags[0] = 0;
-    rq.flags[1] = 0;
-  }
-}
-
 template <int MR>
 __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, const int8_t* __restrict__ qa,
                                                           const float* __restrict__ sa,
                                                           const int8_t* __restrict__ wq,
                                                           const float* __restrict__ sw,
                                                           const float* __restrict__ bias, float* __restrict__ Y,
-                                                          int32_t* __restrict__ acc_out, const RowQuant rq) {
+                                                          int32_t* __restrict__ acc_out) {
   constexpr int COLS = kSkinnyCols, V = COLS * MR;
   constexpr int H = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : 1;
   {  // this warp's first two weight rows into L2 while the previous kernel finishes
@@ -161,12 +89,7 @@ __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, c
   };
   int4 wc[COLS];
   load_w(cg, lane, wc);  // in flight during the staging below
-  if (rq.A) {
-    quantize_rows_in_grid(rq, m, k, const_cast<int8_t*>(qa), const_cast<float*>(sa));
-    for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x) s_qa4[i] = __ldcg(reinterpret_cast<const int4*>(qa) + i);
-  } else {
-    for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x) s_qa4[i] = __ldg(reinterpret_cast<const int4*>(qa) + i);
-  }
+  for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x) s_qa4[i] = __ldg(reinterpret_cast<const int4*>(qa) + i);
   __syncthreads();
   for (; cg < ngroups; cg += gstride) {
     int acc[COLS][MR];
@@ -203,12 +126,10 @@ __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, c
     const int idx = lane >> (5 - H), r = idx % MR, col = cg * COLS + idx / MR;
     if ((lane & ((1 << (5 - H)) - 1)) == 0 && r < m && col < n) {
       const float bc = bias ? __ldg(bias + col) : 0.0f;
-      const float sr = rq.A ? __ldcg(sa + r) : __ldg(sa + r);
-      Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(sum), sr), __ldg(sw + col)), bc);
+      Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(sum), __ldg(sa + r)), __ldg(sw + col)), bc);
       if (acc_out) acc_out[(size_t)r * n + col] = sum;
     }
   }
-  if (rq.A) rows_launch_done(rq);
 }
 
 // Exact dot products of any shape (scalar loads); used when k is not a
@@ -259,7 +180,7 @@ __global__ void __launch_bounds__(256) w4a8_skinny_kernel(int m, int n, int k, i
                                                           const uint8_t* __restrict__ wq,
                                                           const float* __restrict__ sw,
                                                           const float* __restrict__ bias, float* __restrict__ Y,
-                                                          int32_t* __restrict__ acc_out, const RowQuant rq) {
+                                                          int32_t* __restrict__ acc_out) {
   const int nch = k >> 5;  // 32-element chunks per row
   const int ng = k / group, cpg = group >> 5, pstride = ng | 1;  // odd stride: conflict-free promotion
   if (threadIdx.x == 0 && blockIdx.x * cb < n) {  // this block's first weight rows and scales into L2
@@ -278,14 +199,9 @@ __global__ void __launch_bounds__(256) w4a8_skinny_kernel(int m, int n, int k, i
   int* sP = s_sum + m * nch;                                     // [cb][MR][pstride] group partials
   const int tid = threadIdx.x;
   const bool vec = (reinterpret_cast<uintptr_t>(qa) & 15u) == 0;
-  if (rq.A) quantize_rows_in_grid(rq, m, k, const_cast<int8_t*>(qa), const_cast<float*>(sa));
   for (int i = tid; i < m * nch; i += blockDim.x) {  // rows are contiguous: chunk i at byte 32 i
     uint32_t x[8];
-    if (vec && rq.A) {  // written in this launch: through L2
-      const uint4 a0 = __ldcg(reinterpret_cast<const uint4*>(qa) + 2 * i);
-      const uint4 a1 = __ldcg(reinterpret_cast<const uint4*>(qa) + 2 * i + 1);
-      x[0] = a0.x, x[1] = a0.y, x[2] = a0.z, x[3] = a0.w, x[4] = a1.x, x[5] = a1.y, x[6] = a1.z, x[7] = a1.w;
-    } else if (vec) {
+    if (vec) {
       const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(qa) + 2 * i);
       const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(qa) + 2 * i + 1);
       x[0] = a0.x, x[1] = a0.y, x[2] = a0.z, x[3] = a0.w, x[4] = a1.x, x[5] = a1.y, x[6] = a1.z, x[7] = a1.w;
@@ -357,13 +273,11 @@ __global__ void __launch_bounds__(256) w4a8_skinny_kernel(int m, int n, int k, i
           acc = __fmaf_rn(__int2float_rn(P[g]), __ldg(swc + g), acc);
           if (acc_out) acc_out[((size_t)r * n + col) * ng + g] = P[g];
         }
-        const float sr = rq.A ? __ldcg(sa + r) : __ldg(sa + r);
-        Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(acc, sr), bias ? __ldg(bias + col) : 0.0f);
+        Y[(size_t)r * n + col] = __fadd_rn(__fmul_rn(acc, __ldg(sa + r)), bias ? __ldg(bias + col) : 0.0f);
       }
     }
     __syncthreads();
   }
-  if (rq.A) rows_launch_done(rq);
 }
 
 static int launch_err(const char* what) {
@@ -378,41 +292,15 @@ static int launch_rc(cudaError_t e, const char* what) {
 
 constexpr size_t kSkinnySmem = 200 * 1024;
 
-// Two zeroed words per (device, stream) for the row quantization fused into
-// the skinny kernels (each launch leaves them zero again).
-static int* rowquant_flags(cudaStream_t s) {
-  static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, int*> words;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lk(mu);
-  int*& w = words[std::make_pair(dev, s)];
-  if (!w) {
-    int* p = nullptr;
-    if (cudaMalloc(&p, 256) != cudaSuccess || cudaMemsetAsync(p, 0, 256, s) != cudaSuccess) {
-      cudaGetLastError();
-      if (p) cudaFree(p);
-      return nullptr;
-    }
-    w = p;
-  }
-  return w;
-}
-
-// The row quantization of A can run inside the skinny kernels (float4 rows).
-static bool rowquant_ok(const float* A, int k) { return A && k % 4 == 0 && aligned16(A); }
-
 static int launch_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq,
-                              const float* sw, const float* bias, float* Y, int32_t* acc_out, const RowQuant& rq,
-                              cudaStream_t s) {
+                              const float* sw, const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
   const size_t smem = (size_t)m * k;
   const int warps = (n + kSkinnyCols - 1) / kSkinnyCols;
   const int grid = std::max(1, std::min((warps + 7) / 8, std::max(1, sm_count()) * 16));
   auto launch = [&](auto kern) {
     smem_attr_once(reinterpret_cast<const void*>(kern), (int)kSkinnySmem);
-    return launch_rc(
-        launch_pdl_ex(kern, dim3(grid), dim3(256), smem, s, m, n, k, qa, sa, wq, sw, bias, Y, acc_out, rq),
-        "w8a8_skinny_kernel");
+    return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(256), smem, s, m, n, k, qa, sa, wq, sw, bias, Y, acc_out),
+                     "w8a8_skinny_kernel");
   };
   if (m <= 1) return launch(w8a8_skinny_kernel<1>);
   if (m <= 4) return launch(w8a8_skinny_kernel<4>);
@@ -421,17 +309,10 @@ static int launch_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float
 }
 
 // m <= kSkinnyM rows (more go to the generic kernel); the rows are split
-// into launches whose activations fit in shared memory.  With A (f32 rows)
-// the kernels quantize the rows into qa / sa themselves.
+// into launches whose activations fit in shared memory.
 int run_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, const int8_t* wq, const float* sw,
-                    const float* bias, float* Y, int32_t* acc_out, cudaStream_t s, const float* A = nullptr) {
+                    const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
   const bool vec = (k % 16 == 0) && aligned16(qa) && aligned16(wq) && (size_t)k <= kSkinnySmem;
-  RowQuant rq{nullptr, nullptr, device_status_word()};
-  if (A && vec && m <= kSkinnyM && rowquant_ok(A, k)) rq.flags = rowquant_flags(s);
-  if (A && !rq.flags) {
-    const int rc = launch_quantize_rows_i8(A, m, k, const_cast<int8_t*>(qa), const_cast<float*>(sa), s);
-    if (rc) return rc;
-  }
   if (!vec || m > kSkinnyM) {
     return launch_rc(launch_pdl_ex(w8a8_generic_kernel, dim3(std::max(1, sm_count()) * 8), dim3(256), 0, s, m, n, k,
                                    qa, sa, wq, sw, bias, Y, acc_out),
@@ -440,9 +321,8 @@ int run_w8a8_skinny(int m, int n, int k, const int8_t* qa, const float* sa, cons
   const int rows = (int)std::min<size_t>((size_t)m, kSkinnySmem / (size_t)k);
   for (int r0 = 0; r0 < m; r0 += rows) {
     const int mr = std::min(rows, m - r0);
-    const RowQuant rq_c{rq.flags ? A + (size_t)r0 * k : nullptr, rq.flags, rq.status};
     const int rc = launch_w8a8_skinny(mr, n, k, qa + (size_t)r0 * k, sa + r0, wq, sw, bias, Y + (size_t)r0 * n,
-                                      acc_out ? acc_out + (size_t)r0 * n : nullptr, rq_c, s);
+                                      acc_out ? acc_out + (size_t)r0 * n : nullptr, s);
     if (rc) return rc;
   }
   return OC_OK;
@@ -456,18 +336,10 @@ static size_t w4_skinny_smem(int m, int mr, int k, int group, int cb) {
 }
 
 // m <= kSkinnyM rows; fewer rows and columns per launch when shared memory
-// would not hold them.  With A (f32 rows) the kernels quantize the rows into
-// qa / sa themselves.
+// would not hold them.
 int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const float* sa, const uint8_t* wq,
-                    const float* sw, const float* bias, float* Y, int32_t* acc_out, cudaStream_t s,
-                    const float* A = nullptr) {
+                    const float* sw, const float* bias, float* Y, int32_t* acc_out, cudaStream_t s) {
   const int ng = k / group;
-  RowQuant rq{nullptr, nullptr, device_status_word()};
-  if (A && aligned16(qa) && rowquant_ok(A, k)) rq.flags = rowquant_flags(s);
-  if (A && !rq.flags) {
-    const int rc = launch_quantize_rows_i8(A, m, k, const_cast<int8_t*>(qa), const_cast<float*>(sa), s);
-    if (rc) return rc;
-  }
   int rows = m, cb = 16;
   auto mr_of = [](int r) { return r <= 1 ? 1 : r <= 4 ? 4 : r <= 8 ? 8 : 16; };
   while (w4_skinny_smem(rows, mr_of(rows), k, group, cb) > kSkinnySmem) {
@@ -481,10 +353,9 @@ int run_w4a8_skinny(int m, int n, int k, int group, const int8_t* qa, const floa
     const int grid = std::max(1, std::min((n + cb - 1) / cb, std::max(1, sm_count()) * 16));
     auto launch = [&](auto kern) {
       smem_attr_once(reinterpret_cast<const void*>(kern), (int)kSkinnySmem);
-      const RowQuant rq_c{rq.flags ? A + (size_t)r0 * k : nullptr, rq.flags, rq.status};
       return launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(256), smem, s, mrows, n, k, group, cb,
                                      qa + (size_t)r0 * k, sa + r0, wq, sw, bias, Y + (size_t)r0 * n,
-                                     acc_out ? acc_out + (size_t)r0 * n * ng : nullptr, rq_c),
+                                     acc_out ? acc_out + (size_t)r0 * n * ng : nullptr),
                        "w4a8_skinny_kernel");
     };
     const int rc = mr == 1   ? launch(w4a8_skinny_kernel<1>)
@@ -829,10 +700,7 @@ int oc_qgemm_w8a8(int m, int n, int k, const float* A, const int8_t* Wq, const f
   OC_REQUIRE(aligned16(workspace), "qgemm_w8a8: workspace must be 16-byte aligned");
   int8_t* qa = static_cast<int8_t*>(workspace);
   float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (m <= kSkinnyM)  // the rows are quantized inside the GEMV launch
-    return run_w8a8_skinny(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, s, A);
-  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, s);
+  int rc = launch_quantize_rows_i8(A, m, k, qa, sa, static_cast<cudaStream_t>(stream));
   if (rc) return rc;
   return oc_igemm_w8a8(m, n, k, qa, sa, Wq, w_scales, bias, Y, acc_out, stream);
 }
@@ -892,8 +760,6 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float* A, const uint8_t*
   }
   int8_t* qa = static_cast<int8_t*>(workspace);
   float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)m * k * 2));
-  if (m <= kSkinnyM && aligned16(Wq))  // the rows are quantized inside the GEMV launch
-    return run_w4a8_skinny(m, n, k, group, qa, sa, Wq, w_scales, bias, Y, acc_out, s, A);
   int rc = launch_quantize_rows_i8(A, m, k, qa, sa, s);
   if (rc) return rc;
   return oc_igemm_w4a8(m, n, k, group, qa, sa, Wq, w_scales, bias, Y, acc_out, stream);

@@ -4,8 +4,6 @@ W8A8 output, and the W4A8 output whenever the exact group partials are
 requested (the per-group kernel).  The W4A8 output of the dequantizing
 kernel (no partials requested, M > 16, k % 128 == 0) is f32 work and is held
 to the dequantized-output tolerance: relative Frobenius error <= 1e-5."""
-import ctypes as C
-
 import numpy as np
 import pytest
 
@@ -167,47 +165,6 @@ def test_qgemm_w4a8_bit_exact(oc, oracle, m, k, n):
     else:
         assert rel_fro(y2, y_ref) <= W4_REL_FRO, rel_fro(y2, y_ref)
         bits_equal(y3, y2)  # int8 entry point: the same kernel on the same integers
-
-
-def test_skinny_row_quantization_in_launch(oc, oracle):
-    """m <= 16: the f32 rows are quantized inside the GEMV launch.  A chain of
-    calls on one stream without a synchronization between them (each launch
-    leaves its ready counters at zero for the next), rows of every count
-    including ones that do not fill a block, zero rows (scale 0), and rows
-    that are not 16-byte aligned (quantized by their own launch instead)."""
-    k, n = 768, 520
-    _, WT, bias = synth.qgemm_case(1, k, n, 1, 40, 41)
-    wq, ws = _weights(oracle, WT, 8, k)
-    wq4, ws4 = _weights(oracle, WT, 4, 32)
-    W8 = (torch.from_numpy(wq).cuda().view(n, k), torch.from_numpy(ws).cuda())
-    W4 = (torch.from_numpy(wq4).cuda(), torch.from_numpy(ws4).cuda())
-    bd = torch.from_numpy(bias).cuda()
-    runs = []
-    for i, (m, aligned) in enumerate([(1, True), (5, True), (16, True), (2, False), (16, False), (1, True), (7, True)]):
-        A = synth.qgemm_case(m, k, n, 50 + i, 40, 41)[0]
-        if i == 6:
-            A[3] = 0.0  # an all-zero row: scale 0, every integer 0
-        buf = torch.empty(m * k + 4, dtype=torch.float32, device="cuda")
-        off = 0 if aligned else 1
-        Ad = buf[off:off + m * k].view(m, k)
-        Ad.copy_(torch.from_numpy(A))
-        assert (Ad.data_ptr() % 16 == 0) == aligned
-        y8 = oc.qgemm_w8a8(Ad, *W8, bd)
-        y4 = oc.qgemm_w4a8(Ad, *W4, 32, bd)
-        runs.append((m, A, y8, y4))
-    torch.cuda.synchronize()
-    for m, A, y8, y4 in runs:
-        bits_equal(y8.cpu().numpy().ravel(), oracle.qgemm_w8a8(m, k, n, A, wq, ws, bias))
-        bits_equal(y4.cpu().numpy().ravel(), oracle.qgemm_w4a8(m, k, n, 32, A, wq4, ws4, bias))
-    # the quantized rows the launches wrote match the row quantization kernel's
-    A = torch.from_numpy(runs[2][1]).cuda()
-    qa, sa = oc.quantize_rows_int8(A)
-    oc.qgemm_w8a8(A, *W8, bd)
-    ws_bytes = oc.workspace(16, k, A.device)
-    torch.cuda.synchronize()
-    assert torch.equal(ws_bytes[:16 * k].view(torch.int8).view(16, k).cpu(), qa.cpu())
-    st = C.c_int(-1)
-    assert oc.lib().oc_get_device_status(C.byref(st)) == 0 and st.value == 0  # no wait ran out
 
 
 def test_qgemm_no_bias_and_host_slices(oc, oracle):
