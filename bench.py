@@ -439,8 +439,7 @@ def run_qgemm(ctx):
            "d2h_bytes_per_step": sum(m * Q_N * 4 for m in Q_M) * 2, "ms_per_step": round(t_e2e * 1e3, 3)}
     dev.close()
     cpu = cpu_qgemm() if ctx.rank == 0 and not args.no_cpu_baseline else None
-    config = {"workload": "config-2 quantized GEMM sweep: M in {1,16,128,2048}, K=768, N=3072, "
-                          "W8A8 per-channel + W4A8 group-32, f32 bias and output",
+    config = {"workload": WORKLOADS["qgemm"],
               "parallelism": f"replicas x{ctx.world}",
               "l2": f"{Q_SETS} rotating device input sets (~300 MB) > 126 MB L2",
               "graph": "one CUDA graph per set (row quantization + GEMM per matmul)"}
@@ -562,7 +561,7 @@ def run_sgemm(ctx):
            "d2h_bytes_per_step": 4 * S_M * S_N, "ms_per_step": round(t_e2e * 1e3, 4)}
     dev.close()
     cpu = cpu_sgemm() if ctx.rank == 0 and not args.no_cpu_baseline else None
-    config = {"workload": "config-1 sgemm: A[512x768] . B[768x2304] + bias, N(0,0.02) seed 0, 3xTF32",
+    config = {"workload": WORKLOADS["sgemm"],
               "parallelism": f"replicas x{ctx.world}", "l2": f"{S_SETS} rotating sets (213 MB) > 126 MB L2",
               "graph": "one CUDA graph per set"}
     emit(ctx, "sgemm TFLOP/s (f32 via 3xTF32, 512x768x2304 + bias)", value, "TFLOP/s", ms_step,
@@ -647,8 +646,7 @@ def run_gpt2(ctx):
     e2e = {"value": r["e2e_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 32 * G_PROMPT * 4,
            "d2h_bytes_per_step": 32 * G_NEW * 4, "ms_per_step": round(r["e2e_ms"], 3)}
     cpu = cpu_gpt2() if ctx.rank == 0 and not args.no_cpu_baseline else None
-    config = {"workload": "config-3 GPT-2 124M random-init (load_random seed 3), prompt 32, 128 greedy tokens, "
-                          "batch 32 (32 independent sequences)", "parallelism": f"replicas x{ctx.world}",
+    config = {"workload": WORKLOADS["gpt2"], "parallelism": f"replicas x{ctx.world}",
               "graph": "decode step captured once, replayed per token", "l2": "weights 497 MB > 126 MB L2"}
     extra = {"batch1": {"tok_s": res[1]["tok_s"], "ms_per_generate": res[1]["ms"],
                         "e2e_tok_s": res[1]["e2e_tok_s"], "gpu_launches": res[1]["launches"]}}
@@ -800,7 +798,7 @@ def run_int4(ctx):
            "note": "host-slice oc_blas_qgemm_w4a8 per rank shard (no gather on the host path)"}
     dev.close()
     cpu = cpu_int4() if ctx.rank == 0 and not args.no_cpu_baseline else None
-    config = {"workload": "config-4 INT4 group-32 sweep K=3584, N in {3584,18944,152064}, M in {1,8,64,512,4096}",
+    config = {"workload": WORKLOADS["int4"],
               "parallelism": f"column shard x{ctx.world} + NCCL all-gather" if ctx.world > 1 else "1 GPU",
               "l2": "weights rotated over copies so every step reads > 126 MB"}
     emit(ctx, "INT4 g32 GEMM TOPS (K=3584 sweep)", value, "TOPS", ms_step, "int4 x int8 -> int32 (f32 in/out)",
@@ -916,8 +914,7 @@ def run_moe(ctx):
            "d2h_bytes_per_step": T * E_D * 4, "ms_per_step": round(t_e2e * 1e3, 2)}
     cpu = cpu_moe() if ctx.rank == 0 and not args.no_cpu_baseline else None
     launches = 13 if g == 1 else 13 + 3  # + dispatch by rank, regroup by expert, gather back
-    config = {"workload": "config-5 MoE: 8192 tokens x d 7168, 256 experts (d_ff 2048, INT8 per-channel) + 1 "
-                          "shared, top-8 over N(0,1) router logits, grouped W8A8 GEMMs",
+    config = {"workload": WORKLOADS["moe"],
               "parallelism": f"expert parallel x{g} (32 experts per GPU at 8), NCCL all-to-all" if g > 1
               else "1 GPU, all experts local",
               "l2": "expert weights 7.5 GB > 126 MB L2"}
@@ -1021,8 +1018,7 @@ def run_mla(ctx):
            "d2h_bytes_per_step": 4 * (L_SEQ * L_DC + 2 * L_SEQ * L_UP), "ms_per_step": round(t_e2e * 1e3, 2)}
     dev.close()
     cpu = cpu_mla() if ctx.rank == 0 and not args.no_cpu_baseline else None
-    config = {"workload": "config-5 MLA: KV[16384x7168] . down[7168x512] -> latent; latent . up_K/up_V "
-                          "[512x16384], N(0,0.02) weights", "parallelism": f"replicas x{ctx.world}",
+    config = {"workload": WORKLOADS["mla"], "parallelism": f"replicas x{ctx.world}",
               "l2": "operands 0.5-1 GB > 126 MB L2"}
     emit(ctx, "MLA compress+decompress TFLOP/s (3xTF32)", value, "TFLOP/s", ms_step,
          "f32 (3xTF32 tensor cores, f32 accumulate)", config, launches * steps, roof, clk, e2e, cpu,
@@ -1033,6 +1029,19 @@ def run_mla(ctx):
 # ----------------------------------------------------------------------------
 # reference arm
 # ----------------------------------------------------------------------------
+
+WORKLOADS = {
+    "qgemm": "config-2 quantized GEMM sweep: M in {1,16,128,2048}, K=768, N=3072, W8A8 per-channel + W4A8 group-32, "
+             "f32 bias and output",
+    "sgemm": "config-1 sgemm: A[512x768] . B[768x2304] + bias, N(0,0.02) seed 0, 3xTF32",
+    "gpt2": "config-3 GPT-2 124M random-init (load_random seed 3), prompt 32, 128 greedy tokens, "
+            "batch 32 (32 independent sequences)",
+    "int4": "config-4 INT4 group-32 sweep K=3584, N in {3584,18944,152064}, M in {1,8,64,512,4096}",
+    "moe": "config-5 MoE: 8192 tokens x d 7168, 256 experts (d_ff 2048, INT8 per-channel) + 1 shared, top-8 over "
+           "N(0,1) router logits, grouped W8A8 GEMMs",
+    "mla": "config-5 MLA: KV[16384x7168] . down[7168x512] -> latent; latent . up_K/up_V [512x16384], N(0,0.02) weights",
+}
+
 
 REF = {
     "qgemm": (cpu_qgemm, Q_METRIC, "TOPS", lambda v: q_ops() / (v * 1e12) * 1e3),
@@ -1052,18 +1061,21 @@ def run_reference(args):
         return
     fn, metric, unit, ms_of = REF[args.workload]
     vals, last = [], None
-    n = max(1, min(args.steps, 3)) if args.workload in ("gpt2", "moe", "int4") else args.steps
-    for i in range(min(args.warmup, 1) + n):
+    heavy = args.workload in ("gpt2", "moe", "int4")  # samples of 10 s and more: fewer of them
+    n = max(1, min(args.steps, 3)) if heavy else args.steps
+    w = min(args.warmup, 3) if heavy else args.warmup
+    for i in range(w + n):
         r = fn()
-        if i >= min(args.warmup, 1):
+        if i >= w:
             vals.append(r["value"])
             last = r
     v = statistics.median(vals)
     line = {
         "impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": args.gpus,
-        "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": ms_of(v), "higher_is_better": True,
+        "steps": n, "warmup": w, "ms_per_step": ms_of(v), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA,
-        "config": {"workload": f"{args.workload} on the reference CPU path (restated in C, all host cores)"},
+        "config": {"workload": WORKLOADS[args.workload],
+                   "parallelism": f"reference CPU path restated in C, {last['cores']} host threads, rank 0"},
         "cpu_baseline": {"value": v, "unit": unit, "cores": last["cores"], "kind": last["kind"],
                          "sample": last["sample"]},
         "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
