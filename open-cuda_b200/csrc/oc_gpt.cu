@@ -444,14 +444,53 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
       for (int kk = 64 + threadIdx.x; kk < kn; kk += 256)
         prefetch_l2_bulk(a.W + (size_t)(k0 + kk) * a.n + tile * TN, TN * 4);
   }
+  // this thread's first LayerNorm gain and shift (constant parameters) ahead
+  // of the wait as well
+  const bool ln_pre = a.ln_w && (int)threadIdx.x < min(a.ks, kn);
+  float lw0 = 0.0f, lb0 = 0.0f;
+  if (ln_pre) {
+    lw0 = __ldg(a.ln_w + k0 + threadIdx.x);
+    lb0 = __ldg(a.ln_b + k0 + threadIdx.x);
+  }
   pdl_wait();  // x, out, the KV cache and the counters belong to the predecessors until here
   pdl_launch();
   if (a.ln_w) {
     // LayerNorm statistics of each x row (warp per row): mean = sum / k,
-    // var = sum (x - mean)^2 / k, inv = 1 / sqrt(var + eps)
+    // var = sum (x - mean)^2 / k, inv = 1 / sqrt(var + eps).  Rows of up to
+    // 1024 floats stay in registers between the two sums (one read of x).
     for (int r = warp; r < a.m; r += 8) {
       const float* xr = a.x + (size_t)r * a.k;
       float sm = 0.0f;
+      if ((a.k & 3) == 0 && a.k <= 1024) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = lane * 4 + 128 * j;
+          v[j] = c < a.k ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (lane * 4 + 128 * j < a.k) sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v[j].x), v[j].y), v[j].z), v[j].w);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+        const float mean = __fdiv_rn(sm, (float)a.k);
+        float vs = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (lane * 4 + 128 * j < a.k) {
+            const float d0 = __fsub_rn(v[j].x, mean), d1 = __fsub_rn(v[j].y, mean);
+            const float d2 = __fsub_rn(v[j].z, mean), d3 = __fsub_rn(v[j].w, mean);
+            vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+        if (lane == 0) {
+          ln_mean[r] = mean;
+          ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)a.k), a.ln_eps)));
+        }
+        continue;
+      }
       if ((a.k & 3) == 0) {
 #pragma unroll 4
         for (int c = lane * 4; c < a.k; c += 128) {
@@ -483,8 +522,11 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
     float v = 0.0f;
     if (r < a.m && kk < kn) {
       v = a.x[(size_t)r * a.k + k0 + kk];
-      if (a.ln_w)
-        v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, ln_mean[r]), ln_inv[r]), a.ln_w[k0 + kk]), a.ln_b[k0 + kk]);
+      if (a.ln_w) {
+        const bool pre = ln_pre && kk == (int)threadIdx.x;
+        const float lw = pre ? lw0 : a.ln_w[k0 + kk], lb = pre ? lb0 : a.ln_b[k0 + kk];
+        v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, ln_mean[r]), ln_inv[r]), lw), lb);
+      }
     }
     xs[i] = v;
   }
