@@ -122,6 +122,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // rows j0 .. j0+cnt-1 of a [*, row stride H] cache slice -> dst [cnt][d];
 // one commit group per call (empty when cnt == 0)
@@ -183,13 +184,18 @@ __global__ void __launch_bounds__(kAttnThreads)
   const bool vec = (d & 3) == 0 && (H & 3) == 0;
   const int ntiles = (n + kAttnTile - 1) / kAttnTile;
   const int tile_f = kAttnTile * d;
+  // one tile of keys: V goes into the second buffer together with K, so its
+  // loads are in flight during the scores (K waits alone below)
+  const bool one = ntiles == 1;
   attn_stage(buf, kb, 0, min(kAttnTile, n), d, H, vec);
+  if (one) attn_stage(buf + tile_f, vb, 0, n, d, H, vec);
   for (int c = threadIdx.x; c < d; c += kAttnThreads) qs[c] = q[c];
   // pass 1: scores
   float mx = -INFINITY;
   for (int t = 0; t < ntiles; ++t) {
     const int nj = (t + 1) * kAttnTile;
-    attn_stage(buf + ((t + 1) & 1) * tile_f, kb, nj, t + 1 < ntiles ? min(kAttnTile, n - nj) : 0, d, H, vec);
+    if (!one)
+      attn_stage(buf + ((t + 1) & 1) * tile_f, kb, nj, t + 1 < ntiles ? min(kAttnTile, n - nj) : 0, d, H, vec);
     cp_async_wait1();
     __syncthreads();
     const float* kt = buf + (t & 1) * tile_f;
@@ -221,8 +227,16 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int G = kAttnThreads / d >= 1 ? kAttnThreads / d : 1;
   const int dim = threadIdx.x % d, g = threadIdx.x / d;
   float acc = 0.0f;
-  attn_stage(buf, vb, 0, min(kAttnTile, n), d, H, vec);
-  for (int t = 0; t < ntiles; ++t) {
+  if (one) {
+    cp_async_wait0();
+    __syncthreads();
+    const float* vt = buf + tile_f;
+    if (g < G && threadIdx.x < G * d)
+      for (int j = g; j < n; j += G) acc = __fmaf_rn(s[j], vt[j * d + dim], acc);
+  } else {
+    attn_stage(buf, vb, 0, min(kAttnTile, n), d, H, vec);
+  }
+  for (int t = 0; t < (one ? 0 : ntiles); ++t) {
     const int nj = (t + 1) * kAttnTile;
     attn_stage(buf + ((t + 1) & 1) * tile_f, vb, nj, t + 1 < ntiles ? min(kAttnTile, n - nj) : 0, d, H, vec);
     cp_async_wait1();
