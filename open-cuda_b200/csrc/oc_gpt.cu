@@ -374,15 +374,17 @@ struct GemvArgs {
   float ln_eps;
 };
 
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int r, int col, float s) {
-  const float y = __fadd_rn(s, a.bias[col]);
+// bias = a.bias[col] and old = the output's previous value (kEpiResidual),
+// both loaded by the caller ahead of the sum they are combined with
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int r, int col, float s, float bias, float old) {
+  const float y = __fadd_rn(s, bias);
   float* o = a.out + (size_t)r * a.n + col;
   switch (a.epi) {
     case kEpiGelu:
       *o = gelu_new_f64(y);
       break;
     case kEpiResidual:
-      *o = __fadd_rn(*o, y);
+      *o = __fadd_rn(old, y);
       break;
     case kEpiQkv: {
       *o = y;
@@ -603,7 +605,8 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
   if (a.slices == 1) {
     for (int e = threadIdx.x; e < MR * TN; e += 256) {
       const int r = e / TN, col = col_base + e % TN;
-      if (r < a.m && col < a.n) gemv_epilogue(a, r, col, red[e]);
+      if (r < a.m && col < a.n)
+        gemv_epilogue(a, r, col, red[e], a.bias[col], a.epi == kEpiResidual ? a.out[(size_t)r * a.n + col] : 0.0f);
     }
     return;
   }
@@ -622,6 +625,9 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
     if (r >= a.m || col >= a.n) continue;
     const float* pp = a.part + (size_t)r * a.n + col;
     const size_t stride = (size_t)a.m * a.n;
+    // the epilogue's operands in flight with the partial sums
+    const float bias = a.bias[col];
+    const float old = a.epi == kEpiResidual ? a.out[(size_t)r * a.n + col] : 0.0f;
     float t = 0.0f;
     int sl = 0;
     for (; sl + 8 <= a.slices; sl += 8) {  // eight loads in flight, added in slice order
@@ -632,7 +638,7 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
       for (int j = 0; j < 8; ++j) t = __fadd_rn(t, v[j]);
     }
     for (; sl < a.slices; ++sl) t = __fadd_rn(t, __ldcg(pp + (size_t)sl * stride));
-    gemv_epilogue(a, r, col, t);
+    gemv_epilogue(a, r, col, t, bias, old);
   }
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
 }
