@@ -614,12 +614,18 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
     const int r = e / TN, col = col_base + e % TN;
     if (r < a.m && col < a.n) a.part[((size_t)slice * a.m + r) * a.n + col] = red[e];
   }
-  __threadfence();
+  // the CTA's partial stores, ordered before thread 0's counter update by the
+  // barrier, are released by that acq_rel atomic; the finishing CTA's
+  // acquire (same atomic) and the second barrier order its loads after all
+  // slices' stores
   __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(a.slices - 1);
+  if (threadIdx.x == 0) {
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counters + tile) : "memory");
+    is_last = prev == (unsigned)(a.slices - 1);
+  }
   __syncthreads();
   if (!is_last) return;
-  __threadfence();
   for (int e = threadIdx.x; e < MR * TN; e += 256) {
     const int r = e / TN, col = col_base + e % TN;
     if (r >= a.m || col >= a.n) continue;
