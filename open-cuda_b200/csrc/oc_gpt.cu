@@ -859,22 +859,13 @@ int forward(oc_gpt* g, int batch, int L, const uint32_t* tokens, uint32_t* out, 
     if ((rc = linear_fwd(g, Ly.pj, g->inter, rows, g->hidden, kEpiResidual, n))) return rc;
     *n += 1;  // the attention (+ the linears, their layer norms and epilogues above)
   }
-  if (L == 1) {
-    // decode: the rows are the sequences' last rows; the final layer norm
-    // goes with the lm_head linear (fused into its GEMV)
-    if ((rc = linear_fwd(g, g->lm, g->hidden, batch, g->logits, kEpiPlain, n, nullptr, nullptr, 1,
-                         (const float*)g->lnfw, (const float*)g->lnfb)))
-      return rc;
-  } else {
-    // last row of each sequence (rows b*L + L-1) -> normed[b], one launch
-    launch_pdl(layernorm_kernel, dim3(batch), dim3(256), 0, s, (const float*)(g->hidden + (size_t)(L - 1) * H),
-               (size_t)L * H, g->normed, H, (const float*)g->lnfw, (const float*)g->lnfb, c.layer_norm_eps);
-    *n += 1;
-    if ((rc = linear_fwd(g, g->lm, g->normed, batch, g->logits, kEpiPlain, n))) return rc;
-  }
+  // last row of each sequence (rows b*L + L-1) -> normed[b], one launch
+  launch_pdl(layernorm_kernel, dim3(batch), dim3(256), 0, s, (const float*)(g->hidden + (size_t)(L - 1) * H),
+             (size_t)L * H, g->normed, H, (const float*)g->lnfw, (const float*)g->lnfb, c.layer_norm_eps);
+  if ((rc = linear_fwd(g, g->lm, g->normed, batch, g->logits, kEpiPlain, n))) return rc;
   launch_pdl(argmax_kernel, dim3((V + kArgChunk - 1) / kArgChunk, batch), dim3(kArgThreads), 0, s,
              (const float*)g->logits, V, g->next, out, out_stride, g->step, g->pos, L, keep, g->arg);
-  *n += 1 + 1;  // embed, argmax (which also advances step and pos)
+  *n += 1 + 1 + 1;  // embed, final layer norm, argmax (which also advances step and pos)
   cudaError_t e = launch_status();
   return e == cudaSuccess ? OC_OK : from_cuda(e, "gpt forward");
 }
