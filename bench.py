@@ -43,7 +43,7 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-for p in (ROOT, os.path.join(ROOT, "open-cuda_b200"), os.path.join(ROOT, "oracle")):
+for p in (ROOT, os.path.join(ROOT, "open-cuda_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 

@@ -13,7 +13,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-for p in (os.path.join(ROOT, "oracle"), os.path.join(ROOT, "open-cuda_b200")):
+for p in (os.path.join(ROOT, "oracle"), os.path.join(ROOT, "open-cuda_b200"), os.path.join(ROOT, "tests")):
     sys.path.insert(0, p)
 
 import oracle  # noqa: E402

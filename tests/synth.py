@@ -1,4 +1,5 @@
-"""Seeded synthetic inputs for the benchmark workloads and parity tests.
+"""Seeded synthetic inputs for the benchmark workloads and parity tests
+(test and benchmark input generation; not part of the library).
 
 Streams come from SplitMix64 (the generator of the reference's
 GptModel::load_random, crates/open-cuda-llm/src/lib.rs:178-206), vectorised
