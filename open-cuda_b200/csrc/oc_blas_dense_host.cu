@@ -205,8 +205,20 @@ int oc_device_launch(oc_device* dev, const char* name, const oc_launch_config* c
       return fail(OC_ERR_INVALID_VALUE, "launch " + kname + ": m, k, n must be usize");
     if (naive && (!arg_f32(&args[6], &alpha) || !arg_f32(&args[7], &beta)))
       return fail(OC_ERR_INVALID_VALUE, "launch sgemm_naive: alpha, beta must be f32");
+    // The reference's sgemm_naive closure captures transpose_b (blas:206-210)
+    // instead of passing it, so its 8-argument launch (blas:222-232) does not
+    // say whether B is k x n or n x k, and SDPA launches it with
+    // transpose_b = true (blas:517).  Guessing would silently compute Q*K for
+    // Q*K^T, so the 8-argument form is refused ("UnsupportedKernel", code 8)
+    // and only an explicit 9th u32 transpose_b proceeds.
     uint32_t tb = 0;
-    if (naive && nargs > 8 && args[8].kind == OC_ARG_U32) tb = args[8].v.u32;
+    if (naive) {
+      if (nargs < 9 || args[8].kind != OC_ARG_U32 || args[8].v.u32 > 1)
+        return fail(OC_ERR_LAUNCH_FAILED,
+                    "launch sgemm_naive: transpose_b is not among the reference's 8 arguments; pass it as a 9th "
+                    "u32 argument (0 or 1), or call oc_blas_sgemm / oc_blas_sdpa");
+      tb = args[8].v.u32;
+    }
     void *A, *B, *Cm;
     if ((rc = arg_ptr(dev, &args[0], m * k * 4, &A)) || (rc = arg_ptr(dev, &args[1], k * n * 4, &B)) ||
         (rc = arg_ptr(dev, &args[2], m * n * 4, &Cm)))

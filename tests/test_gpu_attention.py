@@ -150,12 +150,28 @@ def test_launch_kernel_by_name(oc, oracle):
     dev.memcpy_h2d(pa, a)
     dev.memcpy_h2d(pb, b)
     dev.memcpy_h2d(pc, np.zeros(m * n, np.float32))
-    dev.launch_kernel("sgemm_naive", [K.ptr(pa), K.ptr(pb), K.ptr(pc), K.usize(m), K.usize(k), K.usize(n),
-                                      K.f32(1.0), K.f32(0.0)])
+    base = [K.ptr(pa), K.ptr(pb), K.ptr(pc), K.usize(m), K.usize(k), K.usize(n), K.f32(1.0), K.f32(0.0)]
+    # the reference's own 8-argument launch (blas:222-232) leaves transpose_b
+    # inside the closure; its SDPA caller needs B transposed (blas:517), so the
+    # backend refuses it rather than guess, before touching C
+    sentinel = np.full(m * n, 7.0, np.float32)
+    dev.memcpy_h2d(pc, sentinel)
+    with pytest.raises(oc.OcError) as e:
+        dev.launch_kernel("sgemm_naive", base)
+    assert e.value.code == oc.OC_ERR_LAUNCH_FAILED and "transpose_b" in str(e.value)
+    with pytest.raises(oc.OcError):
+        dev.launch_kernel("sgemm_naive", base + [K.u32(2)])
     dev.synchronize()
     c = np.zeros(m * n, np.float32)
     dev.memcpy_d2h(c, pc)
-    assert rel(c, oracle.sgemm(m, k, n, 1.0, a, b, 0.0, np.zeros(m * n))) < TOL
+    assert np.array_equal(c, sentinel)
+    for tb in (0, 1):
+        dev.memcpy_h2d(pc, np.zeros(m * n, np.float32))
+        dev.launch_kernel("sgemm_naive", base + [K.u32(tb)])
+        dev.synchronize()
+        dev.memcpy_d2h(c, pc)
+        # with transpose_b, b holds B as n x k (the Q.K^T form of blas:517)
+        assert rel(c, oracle.sgemm(m, k, n, 1.0, a, b, 0.0, np.zeros(m * n), transpose_b=bool(tb))) < TOL, tb
     # quantize_symmetric: bit-exact with scales from group_scales
     x = synth.normal(3, 100, 0, 1)
     t = oracle.quantize_int8(x, 25)
