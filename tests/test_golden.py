@@ -79,3 +79,19 @@ def test_moe_golden(oracle):
     y = oracle.moe_forward(g["x"], g["logits"], g["w1"], g["s1"], g["w2"], g["s2"], g["sw1"], g["ss1"], g["sw2"],
                            g["ss2"], k)
     assert np.array_equal(bits(y), bits(g["y"]))
+
+
+def test_gpt2_124m_golden_prefix(oracle):
+    """The GPT-2 124M decode fixture (tests/golden/make_gpt2_golden.py): the
+    oracle reproduces the first 12 tokens of sequence 0 and their logits at
+    the stored vocabulary ids bit for bit; the fixture's prompts are the
+    workload's prompts."""
+    import synth
+    g = load("gpt2_124m_seed3_128tok.npz")
+    assert np.array_equal(g["prompts"], synth.gpt_prompts(32, 32))
+    model = oracle.GptModel(oracle.GptConfig.gpt2_124m(), int(g["seed"]))
+    model.set_attention(flash=True, block=int(g["block"]))
+    toks, lg = model.generate(g["prompts"][0], 12, want_logits=True)
+    assert toks.tolist() == g["tokens"][0][:12].tolist()
+    assert np.array_equal(bits(lg[:, g["sub_idx"]]), bits(g["sub_seq0"][:12]))
+    assert np.all(g["margin"] > 0) and np.array_equal(g["tokens"][:, :12][0], toks)

@@ -94,6 +94,51 @@ def test_gpt2_124m_batch1_matches_oracle(gptmod, oracle):
     dev.close()
 
 
+def _first_mismatch_report(g, b, dt):
+    """Where device tokens first leave the oracle's, with the oracle's top-1 /
+    top-2 margin at that step (a near-tie flips under an ulp-level logit
+    difference)."""
+    ref = g["tokens"][b]
+    bad = np.nonzero(np.asarray(dt, np.uint32) != ref)[0]
+    if bad.size == 0:
+        return ""
+    t = int(bad[0])
+    return (f"sequence {b}: first mismatch at step {t}: device {int(dt[t])}, oracle {int(ref[t])} "
+            f"(oracle runner-up {int(g['top2'][b, t])}, top-1/top-2 margin {float(g['margin'][b, t]):.3g})")
+
+
+def test_gpt2_124m_128_tokens_batch1_and_32(gptmod):
+    """The GPT-2 decode workload at its configured size: GPT-2 124M
+    load_random(seed 3), fused flash attention, greedy generate of 128 new
+    tokens (llm:910-929) from 32-token prompts, at batch 1 and batch 32 (32
+    independent sequences).  Oracle outputs are the committed fixture
+    tests/golden/gpt2_124m_seed3_128tok.npz (tests/golden/make_gpt2_golden.py):
+    every token identical; logits within 1e-4 at the stored points (every
+    step of sequence 0 at 256 fixed vocabulary ids, sequence 0's full last
+    step, every sequence's last step at those ids)."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "gpt2_124m_seed3_128tok.npz"))
+    prompts, idx = g["prompts"], g["sub_idx"]
+    cfg = gptmod.GptConfig.gpt2_124m()
+    dev = gptmod.GptModel.load_random(cfg, 3, max_batch=32, max_prompt_len=32)
+    # batch 1 (the CUDA-core GEMV decode path)
+    t1, l1 = dev.generate(prompts[0], 128, want_logits=True)
+    assert len(t1) == 128
+    assert t1.tolist() == g["tokens"][0].tolist(), _first_mismatch_report(g, 0, t1)
+    assert np.max(np.abs(l1[:, idx] - g["sub_seq0"])) < LOGIT_TOL
+    assert np.max(np.abs(l1[-1] - g["full_seq0_last"])) < LOGIT_TOL
+    del l1
+    # batch 32 (the tensor-core GEMM decode path)
+    tb, lb = dev.generate(prompts, 128, want_logits=True)
+    assert tb.shape == (32, 128)
+    reports = [_first_mismatch_report(g, b, tb[b]) for b in range(32)]
+    assert not any(reports), "; ".join(r for r in reports if r)
+    assert np.max(np.abs(lb[0][:, idx] - g["sub_seq0"])) < LOGIT_TOL
+    assert np.max(np.abs(lb[:, -1][:, idx] - g["sub_last"])) < LOGIT_TOL
+    assert np.max(np.abs(lb[0, -1] - g["full_seq0_last"])) < LOGIT_TOL
+    dev.close()
+
+
 def test_gpt2_checkpoint_matches_oracle(gptmod, oracle):
     """GptModel::load (llm:661-731): a Hugging Face-style checkpoint (the
     `transformer.` naming, lm_head tied to wte) written from the oracle's
