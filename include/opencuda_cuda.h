@@ -122,8 +122,13 @@ int oc_transfer_between_devices(oc_device *src, uint64_t src_addr, oc_device *ds
  * Vulkan backend routes SPIR-V entry points
  * (crates/opencuda-vulkan/src/real.rs:868-887).  Names and argument
  * contracts (the reference's KernelArg lists):
- *   "sgemm_naive"        [A,B,C ptr; m,k,n usize; alpha,beta f32] plus an
- *                        optional trailing u32 transpose_b (blas:183-232)
+ *   "sgemm_naive"        [A,B,C ptr; m,k,n usize; alpha,beta f32; u32
+ *                        transpose_b] (blas:183-232).  The reference captures
+ *                        transpose_b in the kernel closure (blas:206-210) and
+ *                        launches only the first 8; that 8-argument form is
+ *                        refused (OC_ERR_LAUNCH_FAILED) because its SDPA
+ *                        caller needs B transposed (blas:517): route
+ *                        scaled_dot_product_attention* to oc_blas_sdpa
  *   "matmul"             [A,B,C ptr; m,k,n usize], C = A.B (blas:335-348)
  *   "quantize_symmetric" [in,scales,out ptr; len,group usize; qmin,qmax f32]
  *                        (blas:834-868), one int8 per element
@@ -301,6 +306,28 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float *A, const uint8_t 
                   const float *bias, float *Y, void *workspace, size_t workspace_bytes, int32_t *acc_out,
                   void *stream);
 
+/* Weight-only quantized matmul: f32 activations, quantized weights, the
+ * product the reference forms as Linear::forward over dequantized weights
+ * (sgemm(A, dequantize(Wq)^T) + bias; llm:227-238 with blas:922-945):
+ *   Y[m][n] = sum_k A[m][k] * x[n][k] + bias[n],
+ *   x = q * w_scales[n]                    (oc_qgemm_w8: quantize_int8 of
+ *                                           W^T with group = k)
+ *   x = (nib - 8) * w_scales[(n*k + k') / group]   (oc_qgemm_w4: quantize_int4
+ *                                           of W^T, packed two per byte)
+ * f32 work, within 1e-5 relative Frobenius of the f32 reference.  m <= 16
+ * streams the weights once on the CUDA cores; larger m runs a tcgen05 GEMM
+ * on f16 terms of both operands (~22 significant bits each, f32
+ * accumulation), in column chunks whose expanded weights fit in L2.
+ * Scratch for the expanded terms and K-split partial sums is kept per
+ * (device, stream) inside the library and grows on first use of a larger
+ * shape (that first call synchronizes the device: make it before any stream
+ * capture).  bias may be NULL.  Any group > 0 is accepted for INT4 (groups
+ * may straddle rows as in the reference's flat quantization). */
+int oc_qgemm_w8(int m, int n, int k, const float *A, const int8_t *Wq, const float *w_scales, const float *bias,
+                float *Y, void *stream);
+int oc_qgemm_w4(int m, int n, int k, int group, const float *A, const uint8_t *Wq, const float *w_scales,
+                const float *bias, float *Y, void *stream);
+
 /* The same products on activations that are already quantized, as
  * quantize_int8(A, group = k) returns them: qa [m][k] int8 and sa [m] f32
  * (for example tokens that arrive quantized).  No workspace needed. */
@@ -396,6 +423,14 @@ int oc_blas_qgemm_w8a8(oc_device *dev, size_t m, size_t n, size_t k, const float
                        const float *w_scales, const float *bias, float *y);
 int oc_blas_qgemm_w4a8(oc_device *dev, size_t m, size_t n, size_t k, size_t group, const float *a,
                        const uint8_t *wq, const float *w_scales, const float *bias, float *y);
+/* The weight-only matmuls (oc_qgemm_w8 / oc_qgemm_w4) on host memory, the
+ * host-slice form of Linear::forward over dequantized weights (llm:227-238):
+ * A [m][k] f32, W^T quantized as the reference quantizes it, bias [n] (may
+ * be NULL), Y [m][n]; copies in, multiplies, copies out, synchronizes. */
+int oc_blas_qgemm_w8(oc_device *dev, size_t m, size_t n, size_t k, const float *a, const int8_t *wq,
+                     const float *w_scales, const float *bias, float *y);
+int oc_blas_qgemm_w4(oc_device *dev, size_t m, size_t n, size_t k, size_t group, const float *a,
+                     const uint8_t *wq, const float *w_scales, const float *bias, float *y);
 
 #ifdef __cplusplus
 }

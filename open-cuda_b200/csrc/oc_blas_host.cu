@@ -175,9 +175,11 @@ int oc_blas_quantize_int4(oc_device* dev, const float* input, size_t len, size_t
   return OC_OK;
 }
 
-// Shared body of the two host-slice quantized matmuls.
-static int blas_qgemm(oc_device* dev, int bits, size_t m, size_t n, size_t k, size_t group, const float* a,
-                      const void* wq, const float* w_scales, const float* bias, float* y) {
+// Shared body of the host-slice quantized matmuls: W8A8 / W4A8, or the
+// weight-only products (wonly) whose row chunks reuse the weight terms the
+// first chunk expanded.
+static int blas_qgemm(oc_device* dev, int bits, bool wonly, size_t m, size_t n, size_t k, size_t group,
+                      const float* a, const void* wq, const float* w_scales, const float* bias, float* y) {
   OC_REQUIRE(dev, "NULL device");
   OC_REQUIRE(m > 0 && n > 0 && k > 0, "qgemm: m, n, k must be > 0");
   OC_REQUIRE(a && wq && w_scales && y, "qgemm: NULL pointer");
@@ -186,8 +188,8 @@ static int blas_qgemm(oc_device* dev, int bits, size_t m, size_t n, size_t k, si
   cudaStream_t s = device_stream(dev);
   Arena& ar = arena_of(dev);
   std::lock_guard<std::mutex> lk(ar.mu);
-  const size_t wbytes = bits == 8 ? n * k : n * k / 2;
-  const size_t ng = bits == 8 ? n : n * (k / group);
+  const size_t wbytes = bits == 8 ? n * k : (n * k + 1) / 2;
+  const size_t ng = bits == 8 ? n : (n * k + group - 1) / group;
   size_t ws = 0;
   int rc = oc_qgemm_workspace_size((int)m, (int)k, &ws);
   if (rc) return rc;
@@ -234,7 +236,10 @@ static int blas_qgemm(oc_device* dev, int bits, size_t m, size_t n, size_t k, si
     OC_CHECK_CUDA(cudaMemcpyAsync(da + r0 * k, a + r0 * k, mc * k * 4, cudaMemcpyHostToDevice, sh));
     OC_CHECK_CUDA(cudaEventRecord(ar.ev[1 + 2 * c], sh));
     OC_CHECK_CUDA(cudaStreamWaitEvent(s, ar.ev[1 + 2 * c], 0));
-    if (bits == 8)
+    if (wonly)
+      rc = run_qgemm_wo(bits, (int)mc, (int)n, (int)k, (int)group, da + r0 * k, dw, dsc, bias ? db : nullptr,
+                        dy + r0 * n, s, c > 0);
+    else if (bits == 8)
       rc = oc_qgemm_w8a8((int)mc, (int)n, (int)k, da + r0 * k, static_cast<const int8_t*>(dw), dsc,
                          bias ? db : nullptr, dy + r0 * n, dws, ws, nullptr, s);
     else
@@ -256,13 +261,24 @@ static int blas_qgemm(oc_device* dev, int bits, size_t m, size_t n, size_t k, si
 
 int oc_blas_qgemm_w8a8(oc_device* dev, size_t m, size_t n, size_t k, const float* a, const int8_t* wq,
                        const float* w_scales, const float* bias, float* y) {
-  return blas_qgemm(dev, 8, m, n, k, k, a, wq, w_scales, bias, y);
+  return blas_qgemm(dev, 8, false, m, n, k, k, a, wq, w_scales, bias, y);
 }
 
 int oc_blas_qgemm_w4a8(oc_device* dev, size_t m, size_t n, size_t k, size_t group, const float* a,
                        const uint8_t* wq, const float* w_scales, const float* bias, float* y) {
   OC_REQUIRE(group > 0 && k % group == 0, "qgemm_w4a8: group must divide k");
-  return blas_qgemm(dev, 4, m, n, k, group, a, wq, w_scales, bias, y);
+  return blas_qgemm(dev, 4, false, m, n, k, group, a, wq, w_scales, bias, y);
+}
+
+int oc_blas_qgemm_w8(oc_device* dev, size_t m, size_t n, size_t k, const float* a, const int8_t* wq,
+                     const float* w_scales, const float* bias, float* y) {
+  return blas_qgemm(dev, 8, true, m, n, k, k, a, wq, w_scales, bias, y);
+}
+
+int oc_blas_qgemm_w4(oc_device* dev, size_t m, size_t n, size_t k, size_t group, const float* a,
+                     const uint8_t* wq, const float* w_scales, const float* bias, float* y) {
+  OC_REQUIRE(group > 0, "qgemm_w4: group_size must be > 0");
+  return blas_qgemm(dev, 4, true, m, n, k, group, a, wq, w_scales, bias, y);
 }
 
 }  // extern "C"

@@ -136,25 +136,6 @@ __global__ void __launch_bounds__(128) w4_prep_kernel(const float* __restrict__ 
   expand_weight_row(wq, sw, k, wx, icn, n, lane, mx, w0);
 }
 
-// Ready counters of the split tiles: acquire load and bounded wait.
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ bool wait_count(const int* p, int target, volatile int* abort_flag) {
-  if (ld_acquire_gpu(p) >= target) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    __nanosleep(64);
-    if (ld_acquire_gpu(p) >= target) return true;
-    if ((it & 15u) == 15u) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-    }
-  }
-}
-
 template <int BM>
 __global__ void __launch_bounds__(I4Staged::THREADS, 1)
     gemm_w4a8_staged_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,

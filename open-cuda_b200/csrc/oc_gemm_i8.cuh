@@ -41,11 +41,6 @@ struct I8Gemm {
   static_assert(2 * BN <= TMEM_COLS && SMEM <= 227 * 1024, "tensor / shared memory budget");
 };
 
-__device__ __forceinline__ void kernel_fail(int* status, volatile int* abort_flag, int code) {
-  if (status) atomicCAS(status, 0, code);
-  *abort_flag = 1;
-}
-
 // Tile -> rows/columns.  Plain GEMM: tile t covers rows tm*128.. (tm = t %
 // tiles_m) and columns tn*BN.. of one matrix.  Grouped GEMM (GROUPED): the
 // rows of A / Y are the concatenation of G groups (group g = rows

@@ -1,0 +1,708 @@
+// oc_gemm_wo.cuh -- weight-only quantized matmul: f32 activations times
+// INT8 (per-output-channel scales) or INT4 (group scales) weights, f32 out,
+//   Y[m][n] = sum_k A[m][k] * x[n][k] + bias[n],
+//   x = q * sw[n] (INT8, dequantize_int8) or (nib - 8) * sw[n][k / group]
+//   (INT4, dequantize_int4), crates/opencuda-blas/src/lib.rs:922-945,
+// the product the reference forms as sgemm(A, dequantize(W)^T) + bias in
+// Linear::forward (crates/open-cuda-llm/src/lib.rs:227-238).  All of it is
+// f32 work, held to the f32 tolerance (1e-5 relative Frobenius).
+//
+// Tensor-core path (more than 16 rows, K % 64 == 0): the operands reach
+// kind::f16 MMAs as f16 terms whose sums carry ~22 significant bits:
+//  * activations: per row a power of two c_m = 2^(14 - e) (e = exponent of
+//    the row's max |a|), t = a * c_m (exact), hi = f16(t), lo = f16(t - hi)
+//    (t - hi exact), so hi + lo = t to 2^-22 relative and |hi| < 2^15;
+//  * INT8 weights: q itself (exact in f16), one term;
+//  * INT4 weights: the two f16 terms of the W4A8 kernels, hi + lo =
+//    x * c_n to ~2^-20 (c_n a per-column power of two, oc_gemm_common.cuh).
+// Each K = 16 step issues q.hi_a, q.lo_a (INT8) or w_hi.hi_a, w_lo.hi_a,
+// w_hi.lo_a (INT4; the lo.lo product is below 2^-22), f32 accumulation in
+// TMEM, and the epilogue multiplies by the exact factor 1 / c_m times sw[n]
+// (INT8) or 1 / c_n (INT4) and adds the bias.  Per K = 16 step that is two
+// or three f16 MMAs, where a 3xTF32 GEMM of the dequantized weights would
+// take three TF32 MMAs of half the K each (six f16-MMA times).
+//
+// A preparation launch (wo_prep_kernel) writes both operands' terms in the
+// layout the GEMM streams with TMA: per 64-k block kb, the hi term at
+// columns [128 kb, 128 kb + 64) and the lo term at [128 kb + 64, 128 kb +
+// 128) of a [rows][2K] f16 matrix (INT4 weights and activations), or the
+// plain [N][K] f16 copy of the INT8 weights.  Large N is processed in column
+// chunks whose weight terms fit in L2, so the terms are written and read
+// back without reaching HBM.
+//
+// GEMM roles (persistent, one CTA per SM, 320 threads), as in the
+// expanded-weight W4A8 kernel (oc_gemm_i4x.cuh): warp 0 TMA producer, warp 1
+// TMEM allocator + MMA issuer, warps 2..9 epilogue (TMEM -> registers ->
+// scale + bias -> swizzled shared memory -> TMA store); two TMEM
+// accumulators; tiles split in K for grids that do not fill the GPU, the
+// last slice's CTA finishing the tile in slice order after a bounded wait on
+// the tile's ready counter.
+//
+// Skinny path (at most 16 rows): CUDA-core dot products that stream each
+// weight row once with 16-byte loads; the activation rows sit in shared
+// memory, laid out so that a warp's 16-byte reads are conflict-free; the
+// weights are converted to f32 exactly in registers (INT8: byte + 2^23 + 128
+// as float bits, minus 2^23 + 128; INT4: nibble likewise, minus 2^23 + 8),
+// and products and sums run on f32x2 pairs.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "oc_gemm_common.cuh"
+#include "oc_ptx.cuh"
+
+namespace oc {
+
+// ---- tensor-core GEMM ---------------------------------------------------------
+
+template <int BM_, int WT_>
+struct WoGemmT {
+  static constexpr int BN = 128;   // weight rows per tile (MMA M) = output columns
+  static constexpr int BM = BM_;   // activation rows per tile (MMA N)
+  static constexpr int WT = WT_;   // weight terms: 1 (INT8 values) or 2 (INT4 hi / lo)
+  static constexpr int HALF = BM / 2, NBH = HALF / 32;  // rows and 32-row blocks per epilogue half
+  static constexpr int BK = 64;    // k per stage: 128-byte f16 rows
+  static constexpr int A_BYTES = BM * BK * 2;  // one activation-term tile
+  static constexpr int W_BYTES = BN * BK * 2;  // one weight-term tile
+  static constexpr int STAGE_BYTES = 2 * A_BYTES + WT * W_BYTES;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int TMEM_COLS = 512;  // two accumulators of BM columns (transposed tiles)
+  static constexpr int YSTAGE_BYTES = EPI_WARPS * 4096;  // one 32 x 32 f32 block per epilogue warp
+  static constexpr size_t FIXED = 1024 + YSTAGE_BYTES + 256;
+  static constexpr int STAGES_FIT = (int)((227 * 1024 - FIXED) / STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+  static constexpr size_t SMEM = FIXED + (size_t)STAGES * STAGE_BYTES;
+  static_assert(BM == 256 || BM == 192, "tile heights");
+  static_assert(WT == 1 || WT == 2, "weight terms");
+  static_assert(STAGES >= 2, "at least a double-buffered ring");
+  static_assert(A_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1024-byte operand alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(2 * BM <= TMEM_COLS, "tensor memory budget");
+};
+
+// v * rf * cf + b with one rounding: fma(v, rf * cf, b) while rf * cf (a
+// power of two times the INT8 scale, or a product of two powers of two) is a
+// normal float; when it is not (activations and weights both far from 1),
+// the row's power of two is applied first (exact: v * rf stays in range for
+// the sums this kernel forms), then fma(v * rf, cf, b).
+__device__ __forceinline__ float wo_scale(float v, float rf, float cf, float b) {
+  const float sc = __fmul_rn(rf, cf);
+  const float asc = fabsf(sc);
+  const float y1 = __fmaf_rn(v, sc, b);
+  const float y2 = __fmaf_rn(__fmul_rn(v, rf), cf, b);
+  return (asc >= 1.17549435e-38f && asc <= 3.40282347e38f) ? y1 : y2;
+}
+
+// tmA: activation terms [M][2K] f16 (box 64 x BM); tmW: weight terms, [N][2K]
+// (WT = 2) or [N][K] (WT = 1) f16 (box 64 x 128); tmOut: Y [M][N] f32 (box
+// 32 x 32, when out_tma); tmPart: split-K partial sums [rows][128] f32.
+// colf[n]: sw[n] (INT8) or 1 / c_n (INT4); rowf[m]: 1 / c_m.
+template <int BM, int WT>
+__global__ void __launch_bounds__(WoGemmT<BM, WT>::THREADS, 1)
+    gemm_wo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPart, int out_tma,
+                   int M, int N, int K, int full, int ksplit, int nsplit, const float* __restrict__ rowf,
+                   const float* __restrict__ colf, const float* __restrict__ bias, float* __restrict__ Y, int ldy,
+                   float* __restrict__ part, int* __restrict__ ready, int* status) {
+  using C = WoGemmT<BM, WT>;
+  pdl_wait();  // the operand terms and the zeroed ready counters come from the kernel just before this one
+  pdl_launch();
+  const int tiles_m = (M + C::BM - 1) / C::BM;
+  const SplitPlan sp{tiles_m, K / C::BK, full, ksplit, nsplit};
+  const int nitems = sp.items();
+  // this CTA's items in descending order: its split item (if any) first
+  const int first = (int)blockIdx.x + ((nitems - 1 - (int)blockIdx.x) / (int)gridDim.x) * (int)gridDim.x;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto sAh = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
+  auto sAl = [&](int s) { return sAh(s) + C::A_BYTES; };
+  auto sW = [&](int s, int t) { return sAh(s) + 2 * C::A_BYTES + t * C::W_BYTES; };
+  uint8_t* const ystage = smem + (size_t)C::STAGES * C::STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(ystage + C::YSTAGE_BYTES);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* tfull = empty_bar + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], C::EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+    if (out_tma) prefetch_tmap(&tmOut);
+    if (nsplit) prefetch_tmap(&tmPart);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int w = first; w >= 0; w -= gridDim.x) {
+        WorkItem it;
+        it.set(w, sp);
+        for (int kb = it.rb0; kb < it.rb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+            kernel_fail(status, abort_flag, kDevTimeoutProducer);
+            goto done;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+          tma_load_2d(sAh(stage), &tmA, 2 * kb * C::BK, it.tm * C::BM, &full_bar[stage]);
+          tma_load_2d(sAl(stage), &tmA, 2 * kb * C::BK + C::BK, it.tm * C::BM, &full_bar[stage]);
+          if (WT == 2) {
+            tma_load_2d(sW(stage, 0), &tmW, 2 * kb * C::BK, it.tn * C::BN, &full_bar[stage]);
+            tma_load_2d(sW(stage, 1), &tmW, 2 * kb * C::BK + C::BK, it.tn * C::BN, &full_bar[stage]);
+          } else {
+            tma_load_2d(sW(stage, 0), &tmW, kb * C::BK, it.tn * C::BN, &full_bar[stage]);
+          }
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(C::BN, C::BM);  // MMA M = weight rows, N = activation rows
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, aphase = 0;
+      for (int w = first; w >= 0; w -= gridDim.x) {
+        WorkItem it;
+        it.set(w, sp);
+        if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) {
+          kernel_fail(status, abort_flag, kDevTimeoutMma);
+          goto done;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * C::BM);
+        for (int kb = 0; kb < it.rb1 - it.rb0; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+            kernel_fail(status, abort_flag, kDevTimeoutMma);
+            goto done;
+          }
+          tc_fence_after();
+          const uint32_t ah = smem_u32(sAh(stage)), al = smem_u32(sAl(stage));
+          const uint32_t w0 = smem_u32(sW(stage, 0)), w1 = smem_u32(sW(stage, WT - 1));
+#pragma unroll
+          for (int kk = 0; kk < C::BK / 16; ++kk) {  // K = 16 f16 per MMA: 32 bytes of each row
+            const uint64_t dah = desc_kmajor_sw128(ah + kk * 32), dal = desc_kmajor_sw128(al + kk * 32);
+            const uint64_t dw0 = desc_kmajor_sw128(w0 + kk * 32);
+            mma_f16(d, dw0, dah, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if (WT == 2) mma_f16(d, desc_kmajor_sw128(w1 + kk * 32), dah, idesc, 1u);
+            mma_f16(d, dw0, dal, idesc, 1u);
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          aphase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // Epilogue warp: TMEM lanes 32 q .. 32 q + 31 = output columns, tile
+    // rows [HALF eh, HALF eh + HALF) = NBH 32 x 32 blocks, read from TMEM two
+    // at a time (the accumulator is released after the last read).
+    const int q = warp & 3, eh = (warp - 2) >> 2, ew = warp - 2;
+    uint8_t* const ybuf = ystage + (size_t)ew * 4096;
+    // staging: block row j at j * 128, 16-byte chunk (lane / 4) at
+    // (lane / 4) ^ (j % 8) (128-byte swizzle), word lane % 4
+    const uint32_t ylane = (uint32_t)(lane & 3) * 4, yq = (uint32_t)(lane >> 2);
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int w = first; w >= 0; w -= gridDim.x) {
+      WorkItem it;
+      it.set(w, sp);
+      const int col0 = it.tn * C::BN + q * 32, col = col0 + lane;
+      const int trow0 = it.tm * C::BM, brow0 = trow0 + eh * C::HALF;
+      // column factor, bias and this lane's row factors, loaded while the MMAs run
+      const float cf = col < N ? __ldg(colf + col) : 0.0f;
+      const float bn = (bias && col < N) ? __ldg(bias + col) : 0.0f;
+      float rfr[C::NBH];
+#pragma unroll
+      for (int i = 0; i < C::NBH; ++i) {
+        const int rr = brow0 + 32 * i + lane;
+        rfr[i] = rr < M ? __ldg(rowf + rr) : 0.0f;
+      }
+      const int nblk = min(C::NBH, max(0, (M - brow0 + 31) / 32));  // blocks holding rows < M
+      if (!mbar_wait(&tfull[acc], aphase, abort_flag)) {
+        kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
+        goto done;
+      }
+      tc_fence_after();
+      const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BM + eh * C::HALF);
+      // The last slice of a split tile finishes it: the other slices' scaled
+      // partial sums are added in slice order, then its own, then the bias.
+      const bool finisher = it.split && it.ks == ksplit - 1;
+      const bool writer = it.split && !finisher;
+      if (finisher && !wait_count(ready + it.sidx, (ksplit - 1) * C::EPI_WARPS, abort_flag)) {
+        kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
+        goto done;
+      }
+#pragma unroll 1
+      for (int hp = 0; hp < (C::NBH + 1) / 2; ++hp) {
+        const int nb = min(2, nblk - 2 * hp);  // blocks of this pair holding rows < M
+        uint32_t r[2][32];
+        float t[2][32];
+        if (finisher && nb > 0) {
+          // partial sums of slices 0 .. ksplit - 2 at (row rb0 + j2, column col): lane = column
+          const float* pc = part + ((size_t)it.sidx * C::BM + (brow0 - trow0) + 64 * hp) * C::BN + q * 32 + lane;
+          const size_t slice = (size_t)nsplit * C::BM * C::BN;
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            if (i < nb)
+#pragma unroll
+              for (int j2 = 0; j2 < 32; ++j2) t[i][j2] = __ldcg(pc + (size_t)(32 * i + j2) * C::BN);
+          for (int s2 = 1; s2 < ksplit - 1; ++s2) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+              if (i < nb)
+#pragma unroll
+                for (int j2 = 0; j2 < 32; ++j2)
+                  r[i][j2] = __float_as_uint(__ldcg(pc + s2 * slice + (size_t)(32 * i + j2) * C::BN));
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+              if (i < nb)
+#pragma unroll
+                for (int j2 = 0; j2 < 32; ++j2) t[i][j2] = __fadd_rn(t[i][j2], __uint_as_float(r[i][j2]));
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (i < nb) tmem_ld32(tl + 32 * (2 * hp + i), r[i]);
+        tmem_ld_wait();
+        if (hp == (nblk > 0 ? (nblk - 1) / 2 : 0)) {  // after this warp's last TMEM read of the item
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (i >= nb) break;
+          const int bi = 2 * hp + i;
+          const int rb0 = brow0 + 32 * bi;  // output row of r[i][0]
+#pragma unroll
+          for (int j2 = 0; j2 < 32; ++j2) {
+            const float rf = __shfl_sync(0xffffffffu, rfr[min(bi, C::NBH - 1)], j2);
+            const float v = __uint_as_float(r[i][j2]);
+            const float y = writer ? wo_scale(v, rf, cf, 0.0f)
+                                   : (finisher ? __fadd_rn(__fadd_rn(t[i][j2], wo_scale(v, rf, cf, 0.0f)), bn)
+                                               : wo_scale(v, rf, cf, bn));
+            r[i][j2] = __float_as_uint(y);
+          }
+          if (out_tma || writer) {
+            if (lane == 0) bulk_wait_read<0>();  // the previous store has read the buffer
+            __syncwarp();
+#pragma unroll
+            for (int j2 = 0; j2 < 32; ++j2)
+              *reinterpret_cast<uint32_t*>(ybuf + j2 * 128 + (((yq ^ j2) & 7) << 4) + ylane) = r[i][j2];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (writer)
+                tma_store_2d(&tmPart, ybuf, q * 32, (it.ks * nsplit + it.sidx) * C::BM + (rb0 - trow0));
+              else
+                tma_store_2d(&tmOut, ybuf, col0, rb0);
+              bulk_commit();
+            }
+          } else if (col < N) {
+            float* ycol = Y + (size_t)rb0 * ldy + col;
+#pragma unroll
+            for (int j2 = 0; j2 < 32; ++j2)  // a warp writes 32 adjacent columns
+              if (rb0 + j2 < M) ycol[(size_t)j2 * ldy] = __uint_as_float(r[i][j2]);
+          }
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        aphase ^= 1u;
+      }
+      if (writer) {  // this warp's share of the slice is in memory: count it
+        if (lane == 0) {
+          bulk_wait<0>();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          __threadfence();
+          atomicAdd(ready + it.sidx, 1);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) bulk_wait<0>();  // all output stores complete
+    __syncwarp();
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---- operand preparation --------------------------------------------------------
+
+// log2(c_m) for an activation row with max |a| = mx: |a * c_m| < 2^15
+// (f16's range), clamped so that c_m and 1 / c_m are normal floats; 0 for an
+// all-zero or non-finite row.
+__device__ __forceinline__ int act_range_exp(float mx) {
+  if (!(mx > 0.0f && mx <= 3.0e38f)) return 0;
+  const int e = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;  // subnormal: -127
+  const int ce = 14 - e;
+  return ce < -126 ? -126 : (ce > 126 ? 126 : ce);
+}
+
+// f32 pair -> (hi, lo) f16x2 pairs: hi = f16(t), lo = f16(t - hi), t = x * c.
+__device__ __forceinline__ void split_act_pair(float x0, float x1, float c, uint32_t& hi2, uint32_t& lo2) {
+  const float t0 = __fmul_rn(x0, c), t1 = __fmul_rn(x1, c);  // exact: c = 2^ce
+  const uint32_t h0 = f32_to_f16_bits(t0), h1 = f32_to_f16_bits(t1);
+  const uint32_t l0 = f32_to_f16_bits(__fsub_rn(t0, f16_bits_to_f32(h0)));
+  const uint32_t l1 = f32_to_f16_bits(__fsub_rn(t1, f16_bits_to_f32(h1)));
+  hi2 = h0 | (h1 << 16);
+  lo2 = l0 | (l1 << 16);
+}
+
+// Activation row `row` by one CTA of 128 threads: row max, then the hi / lo
+// terms into ax [m][2k] (64-k blocks: hi, then lo) and 1 / c_m into icm.
+// k % 64 == 0, A 16-byte aligned.
+__device__ __forceinline__ void split_act_row(const float* __restrict__ A, int k, __half* __restrict__ ax,
+                                              float* __restrict__ icm, int row, float* red) {
+  const float4* a4 = reinterpret_cast<const float4*>(A + (size_t)row * k);
+  const int n4 = k >> 2;
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < n4; i += 128) {
+    const float4 v = __ldg(a4 + i);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const int ce = act_range_exp(mx);
+  const float c = exp2_int(ce);
+  if (threadIdx.x == 0) icm[row] = exp2_int(-ce);
+  __half* xrow = ax + (size_t)row * 2 * k;
+  for (int i = threadIdx.x; i < n4; i += 128) {  // elements 4i .. 4i + 3
+    const float4 v = __ldg(a4 + i);
+    uint2 hi, lo;
+    split_act_pair(v.x, v.y, c, hi.x, lo.x);
+    split_act_pair(v.z, v.w, c, hi.y, lo.y);
+    const int k0 = 4 * i;
+    __half* dst = xrow + 128 * (k0 >> 6) + (k0 & 63);
+    *reinterpret_cast<uint2*>(dst) = hi;
+    *reinterpret_cast<uint2*>(dst + 64) = lo;
+  }
+}
+
+// INT4 weight row n (packed [N][K/2], scales [N][K/group], group % 8 == 0)
+// -> hi / lo terms into wx row nr ([rows][2K]) and 1 / c_n into icn[nr], by
+// one warp.
+__device__ __forceinline__ void expand_w4_row(const uint8_t* __restrict__ wq, const float* __restrict__ sw, int K,
+                                              int group, __half* __restrict__ wx, float* __restrict__ icn, int n,
+                                              int nr, int lane) {
+  const int G = K / group;
+  const float* srow = sw + (size_t)n * G;
+  float mx = 0.0f;
+  for (int j = lane; j < G; j += 32) mx = fmaxf(mx, fabsf(__ldg(srow + j)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int ce = range_exp_of_max(mx);
+  const float cval = exp2_int(ce);
+  if (lane == 0) icn[nr] = exp2_int(-ce);
+  const uint32_t* wrow = reinterpret_cast<const uint32_t*>(wq + (size_t)n * (K / 2));
+  __half* xrow = wx + (size_t)nr * 2 * K;
+  for (int u = lane; u < K / 8; u += 32) {
+    const uint32_t w = __ldg(wrow + u);  // weights k0 .. k0 + 7, even k in the low nibble
+    const int k0 = 8 * u;
+    const ScaleTerms st(__fmul_rn(__ldg(srow + k0 / group), cval));  // exact: cval = 2^ce
+    uint4 hi, lo;
+    split_pair(nib_pair_to_f16<0>(w), st, hi.x, lo.x);
+    split_pair(nib_pair_to_f16<1>(w), st, hi.y, lo.y);
+    split_pair(nib_pair_to_f16<2>(w), st, hi.z, lo.z);
+    split_pair(nib_pair_to_f16<3>(w), st, hi.w, lo.w);
+    __half* dst = xrow + 128 * (k0 / 64) + (k0 % 64);
+    *reinterpret_cast<uint4*>(dst) = hi;
+    *reinterpret_cast<uint4*>(dst + 64) = lo;
+  }
+}
+
+// INT8 weight row n ([N][K]) -> f16 values (exact) into w16 row nr, by one warp.
+__device__ __forceinline__ void expand_w8_row(const int8_t* __restrict__ wq, int K, __half* __restrict__ w16, int n,
+                                              int nr, int lane) {
+  const int4* wrow = reinterpret_cast<const int4*>(wq + (size_t)n * K);
+  uint4* xrow = reinterpret_cast<uint4*>(w16 + (size_t)nr * K);
+  for (int u = lane; u < K / 16; u += 32) {
+    const int4 w = __ldg(wrow + u);
+    const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+    uint32_t h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const __half2 p = __floats2half2_rn((float)b[2 * e], (float)b[2 * e + 1]);
+      h[e] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    xrow[2 * u] = make_uint4(h[0], h[1], h[2], h[3]);
+    xrow[2 * u + 1] = make_uint4(h[4], h[5], h[6], h[7]);
+  }
+}
+
+// One launch prepares a column chunk: blocks [0, eb) expand weight rows n0 ..
+// n0 + nc - 1 (a warp per row, eb = ceil(nc / 4)); blocks [eb, eb + ma) split
+// the activation rows (ma = m for the first chunk of a call, else 0); block 0
+// zeroes the ready counters of the GEMM that follows.
+template <int WT>
+__global__ void __launch_bounds__(128) wo_prep_kernel(const float* __restrict__ A, int ma, int k,
+                                                      __half* __restrict__ ax, float* __restrict__ icm,
+                                                      const void* __restrict__ wq, const float* __restrict__ sw,
+                                                      int group, int n0, int nc, __half* __restrict__ wx,
+                                                      float* __restrict__ icn, int* __restrict__ ready, int nready) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float red[4];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nready; i += 128) ready[i] = 0;
+  const int eb = (nc + 3) / 4;
+  if ((int)blockIdx.x >= eb) {
+    if ((int)blockIdx.x - eb < ma) split_act_row(A, k, ax, icm, (int)blockIdx.x - eb, red);
+    return;
+  }
+  const int nr = 4 * (int)blockIdx.x + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (nr >= nc) return;
+  if (WT == 2)
+    expand_w4_row(static_cast<const uint8_t*>(wq), sw, k, group, wx, icn, n0 + nr, nr, lane);
+  else
+    expand_w8_row(static_cast<const int8_t*>(wq), k, wx, n0 + nr, nr, lane);
+}
+
+// ---- skinny path (m <= 16) -----------------------------------------------------
+
+// Float sums of V values per lane across the warp: a transposing butterfly
+// leaves lane l with the complete sum of value l >> (5 - H), 2^H = V.  The
+// order of the additions is fixed, so the result is deterministic.
+template <int V>
+__device__ __forceinline__ float butterfly_sum_f(float (&v)[V], int lane) {
+  constexpr int H = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : V >= 2 ? 1 : 0;
+  static_assert((1 << H) == V && V <= 32, "power-of-two value count up to 32");
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    const int off = 16 >> h, half = V >> (h + 1);
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = upper ? v[i] : v[i + half];
+      const float keep = upper ? v[i + half] : v[i];
+      v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
+    }
+  }
+  float s = v[0];
+#pragma unroll
+  for (int off = 16 >> H; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+  return s;
+}
+
+// 16 weights of one 16-byte chunk half -> 8 pairs of f32 (exact), pair e =
+// elements (2e, 2e + 1): INT8, the chunk's 4 words; INT4, the 8 nibbles of
+// words (2h, 2h + 1).  A byte b becomes the float 2^23 + b through its bits
+// (0x4B000000 | b), and one f32x2 subtraction of (2^23 + 128) or (2^23 + 8)
+// per pair leaves q or nib - 8.
+__device__ __forceinline__ uint32_t byte_as_f32_bits(uint32_t x, uint32_t sel) {
+  return __byte_perm(x, 0x4B000000u, 0x7650u | sel);
+}
+template <int BITS>
+__device__ __forceinline__ void weights_to_f2(const int4& w, int h, uint64_t (&p)[8]) {
+  if (BITS == 8) {
+    const uint64_t off = f2_pack(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+    const uint32_t u[4] = {(uint32_t)w.x ^ 0x80808080u, (uint32_t)w.y ^ 0x80808080u, (uint32_t)w.z ^ 0x80808080u,
+                           (uint32_t)w.w ^ 0x80808080u};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      p[2 * i] = f2_add(u2_pack(byte_as_f32_bits(u[i], 0), byte_as_f32_bits(u[i], 1)), off);
+      p[2 * i + 1] = f2_add(u2_pack(byte_as_f32_bits(u[i], 2), byte_as_f32_bits(u[i], 3)), off);
+    }
+  } else {
+    const uint64_t off = f2_pack(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
+    const uint32_t wa = (uint32_t)(h ? w.z : w.x), wb = (uint32_t)(h ? w.w : w.y);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t ww = i ? wb : wa;
+      const uint32_t lo = ww & 0x0F0F0F0Fu, hi = (ww >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+      for (int b = 0; b < 4; ++b)  // byte b holds elements 2b (low nibble) and 2b + 1 (high)
+        p[4 * i + b] = f2_add(u2_pack(byte_as_f32_bits(lo, b), byte_as_f32_bits(hi, b)), off);
+    }
+  }
+}
+
+// Warp = COLS output columns; lane = the 16-byte weight chunks lane, lane +
+// 32, ... of each column (16 INT8 or 32 INT4 weights), the next chunk in
+// flight while the current one is multiplied.  Shared memory holds the m
+// activation rows as float4 (r, c, j) at ((r * J + j) * nch + c), J = float4
+// per chunk, so that a warp's reads of (r, j) are consecutive.  Products
+// and sums run as f32x2 pairs (even and odd elements in separate partial
+// sums, added at the end).  A block of 256 threads covers 8 * COLS columns,
+// grid-stride.
+template <int BITS, int MR, int COLS>
+__global__ void __launch_bounds__(256) wo_skinny_kernel(int m, int n, int k, int group, const float* __restrict__ A,
+                                                        const uint8_t* __restrict__ wq, const float* __restrict__ sw,
+                                                        const float* __restrict__ bias, float* __restrict__ Y) {
+  constexpr int J = BITS == 8 ? 4 : 8;  // float4 of activations per 16-byte weight chunk
+  constexpr int V = COLS * MR;
+  constexpr int H = V >= 32 ? 5 : V >= 16 ? 4 : V >= 8 ? 3 : V >= 4 ? 2 : V >= 2 ? 1 : 0;
+  const size_t rowb = BITS == 8 ? (size_t)k : (size_t)k / 2;  // bytes per weight row
+  {  // this warp's first weight rows into L2 while the previous kernel finishes
+    const int cg0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if ((threadIdx.x & 31) == 0 && cg0 * COLS < n)
+      prefetch_l2_bulk(wq + (size_t)cg0 * COLS * rowb, (uint32_t)(min(COLS, n - cg0 * COLS) * rowb));
+  }
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ float4 s_a4[];
+  const int nch = (int)(rowb >> 4);  // 16-byte chunks per weight row
+  const int lane = threadIdx.x & 31;
+  const int ngroups = (n + COLS - 1) / COLS;
+  const int gstride = gridDim.x * (blockDim.x >> 5);
+  const int G = BITS == 8 ? 1 : k / group;
+  int cg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  auto load_w = [&](int grp, int c, int4 (&w)[COLS]) {
+#pragma unroll
+    for (int j = 0; j < COLS; ++j) {
+      const int col = grp * COLS + j;
+      w[j] = (col < n && c < nch) ? __ldg(reinterpret_cast<const int4*>(wq + (size_t)col * rowb) + c)
+                                  : make_int4(0, 0, 0, 0);
+    }
+  };
+  int4 wc[COLS];
+  load_w(cg, lane, wc);  // in flight during the staging below
+  {
+    const float4* a4 = reinterpret_cast<const float4*>(A);
+    const int per_row = nch * J;
+    for (int i = threadIdx.x; i < m * per_row; i += blockDim.x) {
+      const int r = i / per_row, rem = i - r * per_row, c = rem / J, j = rem - c * J;
+      s_a4[(r * J + j) * nch + c] = __ldg(a4 + i);
+    }
+  }
+  __syncthreads();
+  const uint64_t zero2 = f2_pack(0.0f, 0.0f);
+  for (; cg < ngroups; cg += gstride) {
+    uint64_t acc[COLS][MR];
+#pragma unroll
+    for (int j = 0; j < COLS; ++j)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[j][r] = zero2;
+    for (int c = lane; c < nch; c += 32) {
+      int4 wn[COLS];
+      load_w(cg, c + 32, wn);  // next chunk (zeros past the row)
+#pragma unroll
+      for (int h = 0; h < (BITS == 8 ? 1 : 2); ++h) {  // 16-weight halves of the chunk
+        uint64_t wf[COLS][8];
+        uint64_t sc[COLS];
+#pragma unroll
+        for (int j = 0; j < COLS; ++j) {
+          weights_to_f2<BITS>(wc[j], h, wf[j]);
+          if (BITS == 4) {
+            const int col = min(cg * COLS + j, n - 1);
+            const float s1 = __ldg(sw + (size_t)col * G + (32 * c + 16 * h) / group);
+            sc[j] = f2_pack(s1, s1);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          if (r < m) {
+            uint64_t a[8];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              const float4 v = s_a4[(r * J + 4 * h + jj) * nch + c];
+              a[2 * jj] = f2_pack(v.x, v.y);
+              a[2 * jj + 1] = f2_pack(v.z, v.w);
+            }
+#pragma unroll
+            for (int j = 0; j < COLS; ++j) {
+              if (BITS == 8) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[j][r] = f2_fma(a[e], wf[j][e], acc[j][r]);
+              } else {
+                uint64_t d = zero2;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d = f2_fma(a[e], wf[j][e], d);
+                acc[j][r] = f2_fma(d, sc[j], acc[j][r]);  // the half's group scale
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < COLS; ++j) wc[j] = wn[j];
+    }
+    load_w(cg + gstride, lane, wc);  // first chunk of the next column group
+    float v[V];
+#pragma unroll
+    for (int j = 0; j < COLS; ++j)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        float lo, hi;
+        f2_unpack(acc[j][r], lo, hi);
+        v[j * MR + r] = __fadd_rn(lo, hi);
+      }
+    const float sum = butterfly_sum_f<V>(v, lane);
+    const int idx = lane >> (5 - H), r = idx % MR, col = cg * COLS + idx / MR;
+    if ((lane & ((1 << (5 - H)) - 1)) == 0 && r < m && col < n) {
+      const float bc = bias ? __ldg(bias + col) : 0.0f;
+      Y[(size_t)r * n + col] = BITS == 8 ? __fmaf_rn(sum, __ldg(sw + col), bc) : __fadd_rn(sum, bc);
+    }
+  }
+}
+
+// Any shape: one warp per output element, lane-strided k, each weight
+// dequantized as the reference does (flattened group index for INT4).
+template <int BITS>
+__global__ void wo_generic_kernel(int m, int n, int k, int group, const float* __restrict__ A,
+                                  const uint8_t* __restrict__ wq, const float* __restrict__ sw,
+                                  const float* __restrict__ bias, float* __restrict__ Y) {
+  pdl_wait();
+  pdl_launch();
+  const int lane = threadIdx.x & 31;
+  const size_t warps = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t o = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < (size_t)m * n; o += warps) {
+    const int r = (int)(o / n), col = (int)(o % n);
+    float acc = 0.0f;
+    for (int t = lane; t < k; t += 32) {
+      const size_t fi = (size_t)col * k + t;  // index in the flattened W^T
+      float x;
+      if (BITS == 8) {
+        x = __fmul_rn((float)reinterpret_cast<const int8_t*>(wq)[fi], sw[col]);
+      } else {
+        const uint8_t b = wq[fi >> 1];
+        const int nib = (fi & 1) ? (b >> 4) : (b & 15);
+        x = __fmul_rn((float)(nib - 8), sw[fi / group]);
+      }
+      acc = __fmaf_rn(A[(size_t)r * k + t], x, acc);
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, s));
+    if (lane == 0) Y[o] = __fadd_rn(acc, bias ? bias[col] : 0.0f);
+  }
+}
+
+}  // namespace oc

@@ -120,6 +120,12 @@ struct StreamScratch {
   }
 };
 
+// Weight-only quantized matmul (oc_qgemm_w8 / oc_qgemm_w4, bits 8 or 4) on
+// `s`.  weights_ready: the previous weight-only call on `s` used the same
+// weights, so the terms it expanded may be reused (checked inside).
+int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
+                 const float* bias, float* Y, cudaStream_t s, bool weights_ready);
+
 // Launches `kern` with programmatic stream serialization (the kernel must
 // begin with pdl_wait(), oc_ptx.cuh); returns the launch status.
 template <typename... KArgs, typename... Args>

@@ -32,6 +32,13 @@ enum : int {
 // pipeline returns an error status instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 
+// Records `code` in the status word (first error wins) and tells the CTA's
+// other roles to stop waiting.
+__device__ __forceinline__ void kernel_fail(int* status, volatile int* abort_flag, int code) {
+  if (status) atomicCAS(status, 0, code);
+  *abort_flag = 1;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

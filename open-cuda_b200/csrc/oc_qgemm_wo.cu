@@ -1,0 +1,276 @@
+// oc_qgemm_wo.cu -- weight-only quantized matmul entry points: f32
+// activations, INT8 (per-output-channel) or INT4 (group) weights in the
+// reference's quantized layout, f32 output equal to the reference's
+// composition sgemm(A, dequantize(W)^T) + bias (Linear::forward,
+// crates/open-cuda-llm/src/lib.rs:227-238, over dequantize_int8 / int4,
+// crates/opencuda-blas/src/lib.rs:922-945) within the f32 tolerance.
+//
+// Paths (kernels in oc_gemm_wo.cuh):
+//  * m <= 16: wo_skinny_kernel, CUDA-core dot products streaming the weights
+//    once (HBM-bound for decode-sized inputs);
+//  * larger m, K % 64 == 0: wo_prep_kernel + gemm_wo_kernel, the tcgen05
+//    f16-term GEMM, in column chunks whose expanded weight terms fit in L2;
+//  * other shapes: the skinny kernel over 16-row chunks, or the scalar
+//    wo_generic_kernel.
+#include <algorithm>
+#include <map>
+#include <mutex>
+
+#include "oc_gemm_wo.cuh"
+#include "oc_internal.h"
+
+namespace oc {
+
+constexpr int kWoSkinnyM = 16;
+// Expanded weight terms of one column chunk stay below this many bytes, so
+// that they are written and read back in L2.
+constexpr size_t kWoChunkBytes = (size_t)40 << 20;
+
+static int wo_launch_rc(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return from_cuda(e, what);
+  return OC_OK;
+}
+
+// ---- skinny --------------------------------------------------------------------
+
+static bool wo_skinny_ok(int bits, int k, int group, const void* A, const void* wq) {
+  if (!aligned16(A) || !aligned16(wq)) return false;
+  if (bits == 8) return k % 16 == 0;
+  return k % 32 == 0 && group % 16 == 0 && k % group == 0;
+}
+
+template <int BITS, int MR>
+static int launch_wo_skinny_mr(int m, int n, int k, int group, const float* A, const uint8_t* wq, const float* sw,
+                               const float* bias, float* Y, cudaStream_t s) {
+  constexpr int COLS = (MR == 4 || MR == 8) ? 4 : 2;
+  auto kern = wo_skinny_kernel<BITS, MR, COLS>;
+  const size_t smem = (size_t)m * k * 4;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), smem))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(wo_skinny_kernel) failed");
+  const int groups = (n + COLS - 1) / COLS, blocks = (groups + 7) / 8;
+  const int per_sm = (int)std::max<size_t>(1, std::min<size_t>(8, (200u << 10) / std::max<size_t>(smem, 1)));
+  const int grid = std::max(1, std::min(blocks, sm_count() * per_sm));
+  return wo_launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(256), smem, s, m, n, k, group, A, wq, sw, bias, Y),
+                      "wo_skinny_kernel");
+}
+
+// Up to 16 rows per launch; fewer when the rows' activations exceed the
+// shared-memory budget (200 KB).
+template <int BITS>
+static int run_wo_skinny(int m, int n, int k, int group, const float* A, const uint8_t* wq, const float* sw,
+                         const float* bias, float* Y, cudaStream_t s) {
+  const int fit = (int)std::max<size_t>(1, ((size_t)200 << 10) / ((size_t)k * 4));
+  const int step = std::min(kWoSkinnyM, fit);
+  for (int r0 = 0; r0 < m; r0 += step) {
+    const int mr = std::min(step, m - r0);
+    const float* Ar = A + (size_t)r0 * k;
+    float* Yr = Y + (size_t)r0 * n;
+    int rc;
+    if (mr <= 1)
+      rc = launch_wo_skinny_mr<BITS, 1>(mr, n, k, group, Ar, wq, sw, bias, Yr, s);
+    else if (mr <= 2)
+      rc = launch_wo_skinny_mr<BITS, 2>(mr, n, k, group, Ar, wq, sw, bias, Yr, s);
+    else if (mr <= 4)
+      rc = launch_wo_skinny_mr<BITS, 4>(mr, n, k, group, Ar, wq, sw, bias, Yr, s);
+    else if (mr <= 8)
+      rc = launch_wo_skinny_mr<BITS, 8>(mr, n, k, group, Ar, wq, sw, bias, Yr, s);
+    else
+      rc = launch_wo_skinny_mr<BITS, 16>(mr, n, k, group, Ar, wq, sw, bias, Yr, s);
+    if (rc) return rc;
+  }
+  return OC_OK;
+}
+
+// ---- tensor-core GEMM ----------------------------------------------------------
+
+// Activation terms (ax [m][2k] f16, then icm [m]), weight terms of one column
+// chunk (wx, then icn), split-K partial sums and ready counters; one buffer
+// each per (device, stream).
+static StreamScratch g_wo_ax, g_wo_wx, g_wo_part, g_wo_ready;
+
+// The weights whose terms the (device, stream) scratch holds, when one chunk
+// covered all columns: a later call with weights_ready on the same stream
+// and the same weights skips the expansion.
+struct WoExpanded {
+  const void* wq = nullptr;
+  const float* sw = nullptr;
+  int bits = 0, n = 0, k = 0, group = 0;
+};
+static std::mutex g_wo_mu;
+static std::map<std::pair<int, cudaStream_t>, WoExpanded> g_wo_expanded;
+
+static bool wo_tc_ok(int bits, int m, int k, int group, const void* A) {
+  return m > kWoSkinnyM && is_sm100() && k % 64 == 0 && aligned16(A) && (bits == 8 || (group % 8 == 0 && k % group == 0));
+}
+
+template <int BM, int WT>
+static int launch_wo_gemm(const CUtensorMap& ta, const CUtensorMap& tw, int m, int nc, int k, int ldy,
+                          const float* icm, const float* colf, const float* bias, float* Yc, cudaStream_t s) {
+  using C = WoGemmT<BM, WT>;
+  auto kern = gemm_wo_kernel<BM, WT>;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_wo_kernel) failed");
+  const int sms = std::max(1, sm_count());
+  const int tiles_m = (m + BM - 1) / BM, tiles = tiles_m * ((nc + C::BN - 1) / C::BN);
+  const int nrb = k / C::BK;
+  // Split K only where the tiles do not fill the GPU: every tile then, in
+  // up to 8 slices (the last slice's CTA adds the others in slice order).
+  // Short K splits only grids that fill at most a quarter of the GPU: a
+  // slice writes a whole tile of partial sums at the SM's store rate.
+  SplitPlan sp{tiles_m, nrb, tiles, 1, 0};
+  if (tiles < sms && (k >= 2048 || 4 * tiles <= sms)) {
+    const int ks = std::min(nrb, std::min(8, sms / tiles));
+    if (ks > 1) sp = SplitPlan{tiles_m, nrb, 0, ks, tiles};
+  }
+  CUtensorMap tout = tw, tpart = tw;  // unused maps still travel as valid kernel parameters
+  float* part = nullptr;
+  int* ready = nullptr;
+  int rc;
+  if (sp.nsplit) {
+    const size_t rows = (size_t)sp.ksplit * sp.nsplit * BM;
+    part = g_wo_part.get(rows * C::BN, s);
+    ready = reinterpret_cast<int*>(g_wo_ready.get((size_t)sp.nsplit, s));
+    if (!part || !ready) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm (weight-only): scratch allocation failed");
+    rc = make_tmap_2d(&tpart, part, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)C::BN, rows, (uint64_t)C::BN * 4, 32,
+                      32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  int out_tma = 0;
+  if (ldy % 4 == 0 && aligned16(Yc)) {  // 32 x 32 TMA stores when rows are 16-byte multiples
+    rc = make_tmap_2d(&tout, Yc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)nc, (uint64_t)m, (uint64_t)ldy * 4, 32,
+                      32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    out_tma = 1;
+  }
+  // the preparation launch just before zeroes `ready` (its nready argument)
+  const int grid = std::min(sp.items(), sms);
+  return wo_launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(C::THREADS), C::SMEM, s, ta, tw, tout, tpart, out_tma, m,
+                                    nc, k, sp.full, sp.ksplit, sp.nsplit, icm, colf, bias, Yc, ldy, part, ready,
+                                    device_status_word()),
+                      "gemm_wo_kernel");
+}
+
+// Number of split tiles the GEMM of a chunk will use (to size and zero the
+// ready counters in the preparation launch): the same rule as launch_wo_gemm.
+static int wo_nsplit(int m, int nc, int k, int bm) {
+  const int sms = std::max(1, sm_count());
+  const int tiles = (m + bm - 1) / bm * ((nc + 127) / 128), nrb = k / 64;
+  if (tiles < sms && (k >= 2048 || 4 * tiles <= sms) && std::min(nrb, std::min(8, sms / tiles)) > 1) return tiles;
+  return 0;
+}
+
+template <int WT>
+static int run_wo_gemm(int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
+                       const float* bias, float* Y, cudaStream_t s, bool weights_ready) {
+  const size_t col_bytes = (size_t)k * 2 * WT + 4;  // expanded terms (+ 1 / c_n) per weight row
+  int nc = (int)std::min<size_t>((size_t)n, std::max<size_t>(128, kWoChunkBytes / col_bytes / 128 * 128));
+  float* axb = g_wo_ax.get((size_t)m * k + (size_t)m, s);  // ax [m][2k] f16, then icm [m]
+  float* wxb = g_wo_wx.get(((size_t)nc * k * 2 * WT + 3) / 4 + (size_t)nc, s);  // terms, then icn [nc]
+  if (!axb || !wxb) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm (weight-only): scratch allocation failed");
+  __half* ax = reinterpret_cast<__half*>(axb);
+  float* icm = axb + (size_t)m * k;
+  __half* wx = reinterpret_cast<__half*>(wxb);
+  float* icn = wxb + ((size_t)nc * k * 2 * WT + 3) / 4;
+  // Tile height: 192 rows where that takes fewer MMA cycles on the busiest
+  // SM (rounds of tiles x ~875 vs ~1030 cycles per k-block), else 256.
+  const int sms = std::max(1, sm_count()), tiles_n = (nc + 127) / 128;
+  auto rounds = [&](int bm) { return ((m + bm - 1) / bm * tiles_n + sms - 1) / sms; };
+  const int tiles256 = (m + 255) / 256 * tiles_n;
+  const int bm = tiles256 >= sms && rounds(192) * 875 < rounds(256) * 1030 ? 192 : 256;
+  CUtensorMap ta;
+  int rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
+                        64, bm, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_pair(dev, s);
+  bool skip_expand = false;
+  if (weights_ready && nc == n) {
+    std::lock_guard<std::mutex> lk(g_wo_mu);
+    const WoExpanded& e = g_wo_expanded[key];
+    skip_expand = e.wq == wq && e.sw == sw && e.bits == (WT == 2 ? 4 : 8) && e.n == n && e.k == k && e.group == group;
+  }
+  if (!skip_expand) {  // the scratch is about to be overwritten: no reuse until this call completes
+    std::lock_guard<std::mutex> lk(g_wo_mu);
+    g_wo_expanded[key] = WoExpanded{};
+  }
+  for (int n0 = 0; n0 < n; n0 += nc) {
+    const int ncur = std::min(nc, n - n0);
+    const int nsplit = wo_nsplit(m, ncur, k, bm);
+    int* ready = nullptr;
+    if (nsplit) {
+      ready = reinterpret_cast<int*>(g_wo_ready.get((size_t)nsplit, s));
+      if (!ready) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm (weight-only): scratch allocation failed");
+    }
+    const int ncx = skip_expand ? 0 : ncur;
+    const int ma = n0 == 0 ? m : 0;
+    // at least one block when there are ready counters to zero
+    const unsigned blocks = (unsigned)std::max((ncx + 3) / 4 + ma, nsplit ? 1 : 0);
+    if (blocks > 0) {
+      rc = wo_launch_rc(launch_pdl_ex(wo_prep_kernel<WT>, dim3(blocks), dim3(128), 0, s, A, ma, k, ax, icm, wq, sw,
+                                      group, n0, ncx, wx, icn, ready, nsplit),
+                        "wo_prep_kernel");
+      if (rc) return rc;
+    }
+    CUtensorMap tw;
+    rc = make_tmap_2d(&tw, wx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * WT, (uint64_t)ncur,
+                      (uint64_t)k * WT * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const float* colf = WT == 2 ? icn : sw + n0;
+    const float* bc = bias ? bias + n0 : nullptr;
+    float* Yc = Y + n0;
+    if (bm == 192)
+      rc = launch_wo_gemm<192, WT>(ta, tw, m, ncur, k, n, icm, colf, bc, Yc, s);
+    else
+      rc = launch_wo_gemm<256, WT>(ta, tw, m, ncur, k, n, icm, colf, bc, Yc, s);
+    if (rc) return rc;
+  }
+  if (nc == n && !skip_expand) {
+    std::lock_guard<std::mutex> lk(g_wo_mu);
+    g_wo_expanded[key] = WoExpanded{wq, sw, WT == 2 ? 4 : 8, n, k, group};
+  }
+  return OC_OK;
+}
+
+int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
+                 const float* bias, float* Y, cudaStream_t s, bool weights_ready) {
+  const uint8_t* w8 = static_cast<const uint8_t*>(wq);
+  if (wo_tc_ok(bits, m, k, group, A) && aligned16(wq))
+    return bits == 8 ? run_wo_gemm<1>(m, n, k, group, A, wq, sw, bias, Y, s, weights_ready)
+                     : run_wo_gemm<2>(m, n, k, group, A, wq, sw, bias, Y, s, weights_ready);
+  if (wo_skinny_ok(bits, k, group, A, wq))
+    return bits == 8 ? run_wo_skinny<8>(m, n, k, group, A, w8, sw, bias, Y, s)
+                     : run_wo_skinny<4>(m, n, k, group, A, w8, sw, bias, Y, s);
+  const size_t warps = (size_t)m * n;
+  const int grid = (int)std::min<size_t>((warps + 7) / 8, (size_t)std::max(1, sm_count()) * 16);
+  if (bits == 8)
+    return wo_launch_rc(launch_pdl_ex(wo_generic_kernel<8>, dim3(grid), dim3(256), 0, s, m, n, k, group, A, w8, sw,
+                                      bias, Y),
+                        "wo_generic_kernel");
+  return wo_launch_rc(launch_pdl_ex(wo_generic_kernel<4>, dim3(grid), dim3(256), 0, s, m, n, k, group, A, w8, sw,
+                                    bias, Y),
+                      "wo_generic_kernel");
+}
+
+}  // namespace oc
+
+using namespace oc;
+
+extern "C" {
+
+int oc_qgemm_w8(int m, int n, int k, const float* A, const int8_t* Wq, const float* w_scales, const float* bias,
+                float* Y, void* stream) {
+  OC_REQUIRE(m > 0 && n > 0 && k > 0, "qgemm_w8: m, n, k must be > 0");
+  OC_REQUIRE(A && Wq && w_scales && Y, "qgemm_w8: NULL pointer");
+  return run_qgemm_wo(8, m, n, k, k, A, Wq, w_scales, bias, Y, static_cast<cudaStream_t>(stream), false);
+}
+
+int oc_qgemm_w4(int m, int n, int k, int group, const float* A, const uint8_t* Wq, const float* w_scales,
+                const float* bias, float* Y, void* stream) {
+  OC_REQUIRE(m > 0 && n > 0 && k > 0, "qgemm_w4: m, n, k must be > 0");
+  OC_REQUIRE(group > 0, "qgemm_w4: group_size must be > 0");
+  OC_REQUIRE(A && Wq && w_scales && Y, "qgemm_w4: NULL pointer");
+  return run_qgemm_wo(4, m, n, k, group, A, Wq, w_scales, bias, Y, static_cast<cudaStream_t>(stream), false);
+}
+
+}  // extern "C"

@@ -121,12 +121,16 @@ _SIGS = {
     "oc_igemm_w8a8": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
     "oc_igemm_w4a8": (ci, [ci, ci, ci, ci, vp, vp, vp, vp, vp, vp, vp, vp]),
     "oc_quantize_rows_int8": (ci, [vp, ci, ci, vp, vp, vp]),
+    "oc_qgemm_w8": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp]),
+    "oc_qgemm_w4": (ci, [ci, ci, ci, ci, vp, vp, vp, vp, vp, vp]),
     "oc_qgemm_w8a8_noalloc": (ci, [ci, ci, ci, vp, vp, vp, vp, vp, vp]),
     "oc_qgemm_w8a8_noalloc_max_bytes": (ci, [C.POINTER(sz)]),
     "oc_blas_quantize_int8": (ci, [vp, vp, sz, sz, vp, vp]),
     "oc_blas_quantize_int4": (ci, [vp, vp, sz, sz, vp, vp]),
     "oc_blas_qgemm_w8a8": (ci, [vp, sz, sz, sz, vp, vp, vp, vp, vp]),
     "oc_blas_qgemm_w4a8": (ci, [vp, sz, sz, sz, sz, vp, vp, vp, vp, vp]),
+    "oc_blas_qgemm_w8": (ci, [vp, sz, sz, sz, vp, vp, vp, vp, vp]),
+    "oc_blas_qgemm_w4": (ci, [vp, sz, sz, sz, sz, vp, vp, vp, vp, vp]),
 }
 
 
@@ -386,6 +390,35 @@ def qgemm_w4a8(A, Wq, w_scales, group: int, bias=None, out=None, want_acc=False)
     return (Y, acc) if want_acc else Y
 
 
+def qgemm_w8(A, Wq, w_scales, bias=None, out=None):
+    """Weight-only INT8: Y = A . dequantize_int8(Wq)^T + bias in f32.
+
+    A [m, k] f32, Wq [n, k] int8 (quantize_int8 of W^T, group = k),
+    w_scales [n] f32.  Linear::forward over the dequantized weights
+    (crates/open-cuda-llm/src/lib.rs:227-238)."""
+    torch = _torch()
+    _need_cuda(A, Wq, w_scales, bias)
+    m, k = A.shape
+    n = Wq.numel() // k
+    Y = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=A.device)
+    check(lib().oc_qgemm_w8(m, n, k, _ptr(A), _ptr(Wq), _ptr(w_scales), _ptr(bias), _ptr(Y), _stream()))
+    return Y
+
+
+def qgemm_w4(A, Wq, w_scales, group: int, bias=None, out=None):
+    """Weight-only INT4: Y = A . dequantize_int4(Wq)^T + bias in f32.
+
+    Wq packed as quantize_int4 packs W^T ([n*k/2] bytes), w_scales
+    [ceil(n*k/group)] f32."""
+    torch = _torch()
+    _need_cuda(A, Wq, w_scales, bias)
+    m, k = A.shape
+    n = Wq.numel() * 2 // k
+    Y = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=A.device)
+    check(lib().oc_qgemm_w4(m, n, k, group, _ptr(A), _ptr(Wq), _ptr(w_scales), _ptr(bias), _ptr(Y), _stream()))
+    return Y
+
+
 def quantize_rows_int8(A):
     """quantize_int8(A, group = k) of a [m, k] f32 matrix: (qa [m, k] int8, sa [m] f32)."""
     torch = _torch()
@@ -523,6 +556,26 @@ class Device:
                                        _np_ptr(np.ascontiguousarray(w_scales, np.float32)),
                                        _np_ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
                                        _np_ptr(y)))
+        return y
+
+    def qgemm_w8(self, m, n, k, a, wq, w_scales, bias=None, out=None):
+        """Weight-only INT8 on host slices (oc_blas_qgemm_w8)."""
+        a = np.ascontiguousarray(a, np.float32)
+        y = out if out is not None else np.zeros(m * n, np.float32)
+        check(lib().oc_blas_qgemm_w8(self._h, m, n, k, _np_ptr(a), _np_ptr(np.ascontiguousarray(wq)),
+                                     _np_ptr(np.ascontiguousarray(w_scales, np.float32)),
+                                     _np_ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
+                                     _np_ptr(y)))
+        return y
+
+    def qgemm_w4(self, m, n, k, group, a, wq, w_scales, bias=None, out=None):
+        """Weight-only INT4 on host slices (oc_blas_qgemm_w4)."""
+        a = np.ascontiguousarray(a, np.float32)
+        y = out if out is not None else np.zeros(m * n, np.float32)
+        check(lib().oc_blas_qgemm_w4(self._h, m, n, k, group, _np_ptr(a), _np_ptr(np.ascontiguousarray(wq)),
+                                     _np_ptr(np.ascontiguousarray(w_scales, np.float32)),
+                                     _np_ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
+                                     _np_ptr(y)))
         return y
 
 

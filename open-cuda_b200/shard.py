@@ -81,3 +81,19 @@ def sharded_qgemm_w4a8(A, wq_full, ws_full, group: int, bias_full, plan: ColumnS
     bias = None if bias_full is None else (bias_full[r0:r1] if bias_full.numel() == plan.n else bias_full)
     local = oc.qgemm_w4a8(A, wq, ws, group, bias)
     return gather_columns(local, plan, pg)
+
+
+def sharded_qgemm_w4(A, wq_full, ws_full, group: int, bias_full, plan: ColumnShard, rank: int, pg=None):
+    """Weight-only INT4 (f32 activations, oc_qgemm_w4) with this rank's column
+    block computed locally and the rest gathered; arguments as
+    sharded_qgemm_w4a8."""
+    import opencuda_cuda as oc
+
+    k = A.shape[1]
+    (b0, b1), (s0, s1) = plan.w4_slices(rank, k, group)
+    r0, r1 = plan.rows(rank)
+    wq = wq_full[b0:b1] if wq_full.numel() * 2 // k == plan.n else wq_full
+    ws = ws_full[s0:s1] if ws_full.numel() * group // k == plan.n else ws_full
+    bias = None if bias_full is None else (bias_full[r0:r1] if bias_full.numel() == plan.n else bias_full)
+    local = oc.qgemm_w4(A, wq, ws, group, bias=bias)
+    return gather_columns(local, plan, pg)
