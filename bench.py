@@ -49,16 +49,6 @@ for p in (ROOT, os.path.join(ROOT, "open-cuda_b200"), os.path.join(ROOT, "oracle
 
 DATA = "synthetic (SplitMix64-seeded inputs as the reference's tests draw them; no dataset, no checkpoint)"
 
-# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
-# the dominant kernel of each workload, from the ncu captures summarised in
-# profiles/ (same kernels and shapes); None where no capture exists yet.
-NCU_TRAFFIC = {
-    "gemm_w4a8 M=2048": 12684032 + 6656,  # profiles/gemm_w4a8_staged_M2048.md (cold L2)
-    "gemm_w8a8 M=2048": 4006912 + 0,  # profiles/gemm_w8a8_tc_M2048.md
-    "sgemm_tf32x3 512x768x2304": 15784960 + 0,  # profiles/sgemm_tf32x3_512x768x2304.md
-}
-
-
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -143,7 +133,7 @@ def roofline(kernel: str, ops: float, nbytes: float, us: float, peaks, ops_unit=
     tensor_peak = int8 if ops_unit == "TOPS" else tf32 / 3.0  # 3xTF32: three MMAs per product
     t_tensor = ops / (tensor_peak * 1e12)
     t_hbm = nbytes / (hbm * 1e9)
-    tr = NCU_TRAFFIC.get(kernel)
+    tr = None  # DRAM traffic comes from ncu captures, never from a timed run
     if t_hbm >= t_tensor:
         ach = nbytes / (us * 1e-6) / 1e9
         return {"bound": "hbm", "kernel": kernel, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
@@ -250,12 +240,17 @@ class Ctx:
         del g
         return statistics.median(samples)
 
-    def close(self, *graphs):
+    def close(self, *graphs, finish=True):
         for g in graphs:
             del g
+        if finish:
+            self.finish()
+
+    def finish(self):
         if self.dist:
             self.dist.barrier()
             self.dist.destroy_process_group()
+            self.dist = None
 
 
 def emit(ctx, metric, value, unit, ms_step, dtype, config, launches, roof, clk, e2e, cpu, extra=None,
@@ -279,19 +274,67 @@ def emit(ctx, metric, value, unit, ms_step, dtype, config, launches, roof, clk, 
 
 Q_K, Q_N, Q_G = 768, 3072, 32
 Q_M = (1, 16, 128, 2048)
-Q_SETS = 8
+Q_SETS = 48  # rotating input sets: 48 x 3.85 MB of quantized weights + scales (185 MB) > 126 MB L2
 Q_METRIC = "INT8/INT4 weight-quantized GEMM TOPS (M in {1,16,128,2048}, K=768, N=3072)"
+# config-4 cold-HBM decode GEMV: one activation row against the 7B-class vocabulary projection
+V_K, V_N = 3584, 152064
 
 
 def q_ops() -> int:
     return 2 * sum(2 * m * Q_K * Q_N for m in Q_M)  # two weight types
 
 
-def q_bytes(kind: str, m: int) -> int:
-    """Algorithmic bytes of one GEMM launch: qa + sa + weights + scales + bias + Y."""
+def wo_bytes(kind: str, m: int, k: int, n: int, group: int = Q_G) -> int:
+    """Algorithmic bytes of one weight-only call: f32 A + quantized weights +
+    f32 scales + bias + f32 Y."""
+    w = n * k if kind == "w8" else n * k // 2
+    sc = n * 4 if kind == "w8" else n * (k // group) * 4
+    return m * k * 4 + w + sc + n * 4 + m * n * 4
+
+
+def a8_bytes(kind: str, m: int) -> int:
+    """Algorithmic bytes of one int8-activation GEMM launch: qa + sa + weights + scales + bias + Y."""
     w = Q_N * Q_K if kind == "w8" else Q_N * Q_K // 2
     sc = Q_N * 4 if kind == "w8" else Q_N * (Q_K // Q_G) * 4
     return m * Q_K + m * 4 + w + sc + Q_N * 4 + m * Q_N * 4
+
+
+def wo_chunk_cols(k: int, wt: int = 2) -> int:
+    """Columns per chunk of the weight-only GEMM (expanded terms <= 40 MB)."""
+    return max(128, (40 << 20) // (k * 2 * wt + 4) // 128 * 128)
+
+
+def wo_launches(m: int, k: int) -> int:
+    """Kernels one weight-only call launches: the skinny kernel (m <= 16, one
+    launch while the rows fit its shared memory) or preparation + GEMM."""
+    if m <= 16:
+        step = max(1, min(16, (200 << 10) // (k * 4)))
+        return -(-m // step)
+    return 2
+
+
+def roofline_wo(kind: str, m: int, k: int, n: int, us: float, peaks, what: str):
+    """Roofline of a weight-only call.  Its products run as f16 terms on the
+    tensor cores: 2 kind::f16 MMAs per product step for INT8 weights, 3 for
+    INT4, so the tensor ceiling is the measured bf16 dense rate / 2 or / 3 in
+    f32-equivalent FLOP/s; the HBM ceiling is the algorithmic bytes at the
+    measured copy bandwidth.  The bound is the longer of the two times."""
+    hbm, _, _, src = peaks
+    bf16 = 2.0 * peaks[2]
+    terms = 2 if kind == "w8" else 3
+    peak_t = bf16 / terms
+    ops, nbytes = 2 * m * k * n, wo_bytes(kind, m, k, n)
+    t_t, t_h = ops / (peak_t * 1e12), nbytes / (hbm * 1e9)
+    common = {"kernel": what, "algorithmic_bytes": int(nbytes), "algorithmic_ops": int(ops),
+              "us_per_launch": round(us, 3), "traffic": None}
+    if t_h >= t_t:
+        ach = nbytes / (us * 1e-6) / 1e9
+        return dict(common, bound="hbm", achieved=round(ach, 1), peak=hbm, unit="GB/s", frac=round(ach / hbm, 4),
+                    peak_source=f"{src} hbm_gbs (copy bandwidth)")
+    ach = ops / (us * 1e-6) / 1e12
+    return dict(common, bound="tensor", achieved=round(ach, 2), peak=round(peak_t, 1), unit="TFLOP/s",
+                frac=round(ach / peak_t, 4),
+                peak_source=f"{src} bf16_tflops / {terms} (f16 MMAs per f32 product step)")
 
 
 def cpu_qgemm(target_s: float = 6.0):
@@ -333,6 +376,142 @@ def cpu_qgemm(target_s: float = 6.0):
     return {"value": v, "unit": "TOPS", "cores": cores, "kind": "port", "sample": desc}
 
 
+def _rotating_us(ctx, launch_of, nsets: int, reps: int = 32) -> float:
+    """kernel_us of a launch that walks `nsets` input sets round robin."""
+    ctr = [0]
+
+    def launch():
+        launch_of(ctr[0] % nsets)
+        ctr[0] += 1
+
+    return ctx.kernel_us(launch, reps=reps)
+
+
+def qgemm_cold_gemv(ctx):
+    """Config-4 decode GEMV from cold HBM: M=1, K=3584, N=152064, weight-only
+    INT8 (545 MB of weights) and INT4 g32 (272 MB packed + 68 MB scales)."""
+    torch, oc = ctx.torch, ctx.oc
+    g = torch.Generator(device=ctx.device).manual_seed(5)
+    W = torch.randn(V_N, V_K, generator=g, device=ctx.device) * 0.02
+    q8, s8 = oc.quantize_int8(W.view(-1), V_K)
+    q4, s4 = oc.quantize_int4(W.view(-1), Q_G)
+    del W
+    A = torch.rand(1, V_K, generator=g, device=ctx.device) * 2 - 1
+    b = torch.zeros(V_N, device=ctx.device)
+    Y = torch.empty(1, V_N, device=ctx.device)
+    out = {}
+    for kind in ("w8", "w4"):
+        def launch():
+            if kind == "w8":
+                oc.qgemm_w8(A, q8, s8, bias=b, out=Y)
+            else:
+                oc.qgemm_w4(A, q4, s4, Q_G, bias=b, out=Y)
+
+        us = ctx.kernel_us(launch, reps=8)
+        nb = wo_bytes(kind, 1, V_K, V_N)
+        out[f"{kind}_M1_K{V_K}_N{V_N}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1),
+                                           "frac_hbm": round(nb / us / 1e3 / ctx.peaks[0], 4),
+                                           "bytes": nb, "kernel": "wo_skinny_kernel"}
+    del q8, s8, q4, s4
+    torch.cuda.empty_cache()
+    return out
+
+
+def qgemm_gpt2_batch1(ctx):
+    """GPT-2 124M greedy decode at batch 1 (load_random seed 3, 32-token
+    prompt, 128 new tokens): tok/s and the decode step's weight bytes per
+    second against HBM."""
+    import gpt
+    import synth
+
+    torch = ctx.torch
+    m = gpt.GptModel.load_random(gpt.GptConfig.gpt2_124m(), 3, device=ctx.local, max_batch=1,
+                                 max_prompt_len=G_PROMPT)
+    p = synth.gpt_prompts(1, G_PROMPT)[0]
+    ext = torch.cuda.ExternalStream(m.stream(), device=ctx.device)
+    for _ in range(3):
+        m.generate(p, G_NEW)
+    torch.cuda.synchronize()
+    n0 = m.kernel_launches()
+    steps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(steps):
+        m.generate(p, G_NEW)
+    e1.record(ext)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    launches = (m.kernel_launches() - n0) // steps
+    m.close()
+    H, V, I = 768, 50257, 3072
+    step_bytes = 12 * 4 * (H * 3 * H + H * H + H * I + I * H) + 4 * H * V
+    per_tok_us = ms * 1e3 / G_NEW
+    gbs = step_bytes / (per_tok_us * 1e-6) / 1e9
+    return {"tok_s": round(G_NEW / (ms * 1e-3), 1), "us_per_token": round(per_tok_us, 2),
+            "weight_bytes_per_token": step_bytes, "GB/s": round(gbs, 1), "frac_hbm": round(gbs / ctx.peaks[0], 4),
+            "gpu_launches_per_generate": launches,
+            "note": "per-token time includes the amortised 32-token prefill"}
+
+
+def qgemm_sharded(ctx):
+    """N > 1: the config-4 column-sharded INT4 g32 weight-only GEMM (K=3584,
+    N=152064): each rank computes its N/g columns, one NCCL all-gather plus
+    oc_gather_columns lay them out as [M][N] on every rank.  Timed per M with
+    the exchange inside (max over ranks), the all-gather alone beside it;
+    rank 0 checks the gathered result bit for bit against every shard's
+    product computed on its own GPU."""
+    import shard
+
+    torch, oc = ctx.torch, ctx.oc
+    plan = shard.ColumnShard(V_N, ctx.world)
+    g = torch.Generator(device=ctx.device).manual_seed(5)
+    W = torch.randn(V_N, V_K, generator=g, device=ctx.device) * 0.02  # the same matrix on every rank
+    q4, s4 = oc.quantize_int4(W.view(-1), Q_G)
+    del W
+    bias = torch.randn(V_N, generator=g, device=ctx.device) * 0.02
+    (b0, b1), (c0, c1) = plan.w4_slices(ctx.rank, V_K, Q_G)
+    r0, r1 = plan.rows(ctx.rank)
+    wl, sl, bl = q4[b0:b1].clone(), s4[c0:c1].clone(), bias[r0:r1].clone()
+    out = {"ranks": ctx.world, "columns_per_rank": plan.cols, "collective": "NCCL all_gather_into_tensor",
+           "per_M": {}}
+    identical = True
+    for m in (1, 512, 4096):
+        A = torch.rand(m, V_K, generator=g, device=ctx.device) * 2 - 1
+
+        def step(_i):
+            local = oc.qgemm_w4(A, wl, sl, Q_G, bias=bl)
+            return shard.gather_columns(local, plan)
+
+        local = oc.qgemm_w4(A, wl, sl, Q_G, bias=bl)
+        flat = torch.empty(ctx.world * local.numel(), device=ctx.device)
+        with torch.cuda.stream(ctx.stream):
+            for i in range(3):
+                y = step(i)
+                ctx.dist.all_gather_into_tensor(flat, local.view(-1))
+        torch.cuda.synchronize()
+        reps = 10 if m < 4096 else 5
+        ms, _ = ctx.timed(step, reps)
+        ms_ag, _ = ctx.timed(lambda _i: ctx.dist.all_gather_into_tensor(flat, local.view(-1)), reps)
+        with torch.cuda.stream(ctx.stream):
+            y = step(0)
+        torch.cuda.synchronize()
+        if ctx.rank == 0:  # every shard's product on this GPU, laid side by side
+            ref = torch.empty(m, V_N, device=ctx.device)
+            for r in range(ctx.world):
+                (x0, x1), (y0, y1) = plan.w4_slices(r, V_K, Q_G)
+                s0_, s1_ = plan.rows(r)
+                ref[:, s0_:s1_] = oc.qgemm_w4(A, q4[x0:x1], s4[y0:y1], Q_G, bias=bias[s0_:s1_])
+            torch.cuda.synchronize()
+            identical = identical and bool(torch.equal(ref.view(torch.int32), y.view(torch.int32)))
+            del ref
+        ops = 2 * m * V_K * V_N
+        out["per_M"][f"M{m}"] = {"ms": round(ms, 4), "allgather_ms": round(ms_ag, 4),
+                                 "allgather_share": round(ms_ag / ms, 3), "TOPS": round(ops / (ms * 1e-3) / 1e12, 2),
+                                 "gathered_MB": round(m * V_N * 4 / 2 ** 20, 1)}
+    out["bit_identical_to_shards_on_one_gpu"] = identical
+    return out
+
+
 def run_qgemm(ctx):
     torch, oc, args = ctx.torch, ctx.oc, ctx.args
     import synth
@@ -341,26 +520,27 @@ def run_qgemm(ctx):
     Wd = torch.from_numpy(WT).to(ctx.device)
     q8, s8 = oc.quantize_int8(Wd, Q_K)       # per output channel
     q4, s4 = oc.quantize_int4(Wd, Q_G)      # group 32, packed
+    Ad = torch.from_numpy(A).to(ctx.device)
+    bd = torch.from_numpy(bias).to(ctx.device)
     torch.cuda.synchronize()
     sets = []
     for _ in range(Q_SETS):
         sets.append({
-            "A": {m: torch.from_numpy(A[:m]).to(ctx.device) for m in Q_M},
+            "A": {m: Ad[:m].clone() for m in Q_M},
             "q8": q8.clone().view(Q_N, Q_K), "s8": s8.clone(), "q4": q4.clone(), "s4": s4.clone(),
-            "bias": torch.from_numpy(bias).to(ctx.device),
+            "bias": bd.clone(),
             "Y": {m: torch.empty(m, Q_N, dtype=torch.float32, device=ctx.device) for m in Q_M},
         })
 
     def step(i):
         s = sets[i % Q_SETS]
         for m in Q_M:
-            oc.qgemm_w8a8(s["A"][m], s["q8"], s["s8"], s["bias"], out=s["Y"][m])
-            oc.qgemm_w4a8(s["A"][m], s["q4"], s["s4"], Q_G, s["bias"], out=s["Y"][m])
-        return 4 * len(Q_M)  # row quantization + GEMM per matmul
+            oc.qgemm_w8(s["A"][m], s["q8"], s["s8"], bias=s["bias"], out=s["Y"][m])
+            oc.qgemm_w4(s["A"][m], s["q4"], s["s4"], Q_G, bias=s["bias"], out=s["Y"][m])
+        return 2 * sum(wo_launches(m, Q_K) for m in Q_M)
 
-    oc.workspace(max(Q_M), Q_K, ctx.device)
     with torch.cuda.stream(ctx.stream):
-        for i in range(Q_SETS):
+        for i in range(Q_SETS):  # scratch sized before capture
             step(i)
     ctx.stream.synchronize()
     graphs = []
@@ -381,35 +561,47 @@ def run_qgemm(ctx):
     ms_step, clk = ctx.timed(lambda i: graphs[i % Q_SETS].replay(), args.steps)
     value = q_ops() * ctx.world / (ms_step * 1e-3) / 1e12
 
-    # each GEMM kernel alone on pre-quantized activations
+    # each weight-only call alone (rotating sets: cold weights)
     per = {}
-    pre = []
-    for s in sets:
-        pre.append({m: oc.quantize_rows_int8(s["A"][m]) for m in Q_M})
+    for kind in ("w8", "w4"):
+        for m in Q_M:
+            def call(j, kind=kind, m=m):
+                s = sets[j]
+                if kind == "w8":
+                    oc.qgemm_w8(s["A"][m], s["q8"], s["s8"], bias=s["bias"], out=s["Y"][m])
+                else:
+                    oc.qgemm_w4(s["A"][m], s["q4"], s["s4"], Q_G, bias=s["bias"], out=s["Y"][m])
+
+            us = _rotating_us(ctx, call, Q_SETS)
+            ops = 2 * m * Q_K * Q_N
+            per[f"{kind}_M{m}"] = {"us": round(us, 3), "TFLOP/s": round(ops / us / 1e6, 2),
+                                   "GB/s": round(wo_bytes(kind, m, Q_K, Q_N) / us / 1e3, 1),
+                                   "launches": wo_launches(m, Q_K)}
+    dom = max(per, key=lambda key: per[key]["us"])
+    dkind, dm = dom.split("_M")
+    dm = int(dm)
+    what = ("wo_skinny_kernel" if dm <= 16 else "wo_prep_kernel + gemm_wo_kernel (one call)") + f" {dkind} M={dm}"
+    roof = roofline_wo(dkind, dm, Q_K, Q_N, per[dom]["us"], ctx.peaks, what)
+
+    # the int8-activation kernels (W8A8 / W4A8, exact int32) on the same sets
+    per_a8 = {}
+    pre = [{m: oc.quantize_rows_int8(s["A"][m]) for m in Q_M} for s in sets]
     torch.cuda.synchronize()
     for kind in ("w8", "w4"):
         for m in Q_M:
-            ctr = [0]
-
-            def launch():
-                j = ctr[0] % Q_SETS
-                ctr[0] += 1
+            def call(j, kind=kind, m=m):
                 s, (qa, sa) = sets[j], pre[j][m]
                 if kind == "w8":
                     oc.igemm_w8a8(qa, sa, s["q8"], s["s8"], s["bias"], out=s["Y"][m])
                 else:
                     oc.igemm_w4a8(qa, sa, s["q4"], s["s4"], Q_G, s["bias"], out=s["Y"][m])
 
-            us = ctx.kernel_us(launch, reps=32)
-            ops = 2 * m * Q_K * Q_N
-            per[f"{kind}a8_M{m}"] = {"us": round(us, 3), "TOPS": round(ops / us / 1e6, 2),
-                                     "GB/s": round(q_bytes(kind, m) / us / 1e3, 1)}
-    dom = max(per, key=lambda k: per[k]["us"])
-    dkind, dm = dom.split("a8_M")
-    dm = int(dm)
-    roof = roofline(f"gemm_{dkind}a8 M={dm}", 2 * dm * Q_K * Q_N, q_bytes(dkind, dm), per[dom]["us"], ctx.peaks)
+            us = _rotating_us(ctx, call, Q_SETS)
+            per_a8[f"{kind}a8_M{m}"] = {"us": round(us, 3), "TOPS": round(2 * m * Q_K * Q_N / us / 1e6, 2),
+                                        "GB/s": round(a8_bytes(kind, m) / us / 1e3, 1)}
+    del pre
 
-    # e2e through the host-slice C ABI (oc_blas_qgemm_*) with pinned host buffers
+    # e2e through the host-slice C ABI (oc_blas_qgemm_w8 / _w4) with pinned host buffers
     dev = oc.Device(ctx.local)
     s0 = sets[0]
     hA = {m: torch.from_numpy(A[:m]).pin_memory() for m in Q_M}
@@ -421,10 +613,10 @@ def run_qgemm(ctx):
 
     def e2e_step():
         for m in Q_M:
-            oc.check(L.oc_blas_qgemm_w8a8(dev.handle, m, Q_N, Q_K, hA[m].data_ptr(), hq8.data_ptr(),
-                                          hs8.data_ptr(), hb.data_ptr(), hY[m].data_ptr()))
-            oc.check(L.oc_blas_qgemm_w4a8(dev.handle, m, Q_N, Q_K, Q_G, hA[m].data_ptr(), hq4.data_ptr(),
-                                          hs4.data_ptr(), hb.data_ptr(), hY[m].data_ptr()))
+            oc.check(L.oc_blas_qgemm_w8(dev.handle, m, Q_N, Q_K, hA[m].data_ptr(), hq8.data_ptr(),
+                                        hs8.data_ptr(), hb.data_ptr(), hY[m].data_ptr()))
+            oc.check(L.oc_blas_qgemm_w4(dev.handle, m, Q_N, Q_K, Q_G, hA[m].data_ptr(), hq4.data_ptr(),
+                                        hs4.data_ptr(), hb.data_ptr(), hY[m].data_ptr()))
 
     for _ in range(max(2, args.warmup)):
         e2e_step()
@@ -438,14 +630,21 @@ def run_qgemm(ctx):
            "h2d_bytes_per_step": sum(2 * m * Q_K * 4 + per_m_w for m in Q_M),
            "d2h_bytes_per_step": sum(m * Q_N * 4 for m in Q_M) * 2, "ms_per_step": round(t_e2e * 1e3, 3)}
     dev.close()
+    extra = {"per_kernel": per, "per_kernel_int8_activations": per_a8}
+    ctx.close(*graphs, finish=False)  # the extras below still use the process group
+    graphs = []
+    extra["gemv_cold_hbm"] = qgemm_cold_gemv(ctx)
+    extra["gpt2_batch1"] = qgemm_gpt2_batch1(ctx)
+    if ctx.world > 1:
+        extra["sharded"] = qgemm_sharded(ctx)
     cpu = cpu_qgemm() if ctx.rank == 0 and not args.no_cpu_baseline else None
     config = {"workload": WORKLOADS["qgemm"],
               "parallelism": f"replicas x{ctx.world}",
-              "l2": f"{Q_SETS} rotating device input sets (~300 MB) > 126 MB L2",
-              "graph": "one CUDA graph per set (row quantization + GEMM per matmul)"}
-    emit(ctx, Q_METRIC, value, "TOPS", ms_step, "int8 x int8 -> int32 (f32 in/out)", config,
-         launches * args.steps, roof, clk, e2e, cpu, {"per_kernel": per})
-    ctx.close(*graphs)
+              "l2": f"{Q_SETS} rotating device input sets (weights alone 185 MB) > 126 MB L2",
+              "graph": "one CUDA graph per set (8 weight-only matmuls)"}
+    emit(ctx, Q_METRIC, value, "TOPS", ms_step, "f32 (f32 activations x dequantized int8 / int4 weights)", config,
+         launches * args.steps, roof, clk, e2e, cpu, extra)
+    ctx.finish()
 
 
 # ----------------------------------------------------------------------------
@@ -725,8 +924,8 @@ def run_int4(ctx):
             c = cases[n]
             q4, s4 = c["w"][i % len(c["w"])]
             for m in I_M:
-                y = oc.qgemm_w4a8(c["A"][m], q4, s4, I_G, c["bias"])
-                n_l += 2
+                y = oc.qgemm_w4(c["A"][m], q4, s4, I_G, bias=c["bias"])
+                n_l += wo_launches(m, I_K) * (1 if m <= 16 else -(-c["plan"].cols // wo_chunk_cols(I_K)))
                 if ctx.world > 1:
                     shard.gather_columns(y, c["plan"])
                     n_l += 1  # gather kernel (plus the NCCL all-gather)
@@ -743,28 +942,25 @@ def run_int4(ctx):
             step(i)
     ms_step, clk = ctx.timed(step, args.steps)
     value = i_ops() / (ms_step * 1e-3) / 1e12
-    # the dominant kernel: time each local GEMM alone
+    # the dominant call: time each local GEMM alone
     per = {}
     for n in I_N:
         c = cases[n]
+        nl = c["plan"].cols
+        Y = {m: torch.empty(m, nl, dtype=torch.float32, device=d) for m in I_M}
         for m in I_M:
-            ctr = [0]
-            qa, sa = oc.quantize_rows_int8(c["A"][m])
-            nl = c["plan"].cols
-            Y = torch.empty(m, nl, dtype=torch.float32, device=d)
+            def call(j, c=c, m=m):
+                q4, s4 = c["w"][j]
+                oc.qgemm_w4(c["A"][m], q4, s4, I_G, bias=c["bias"], out=Y[m])
 
-            def launch():
-                q4, s4 = c["w"][ctr[0] % len(c["w"])]
-                ctr[0] += 1
-                oc.igemm_w4a8(qa, sa, q4, s4, I_G, c["bias"], out=Y)
-
-            us = ctx.kernel_us(launch, reps=8)
-            per[f"M{m}_N{n}"] = {"us": round(us, 2), "TOPS": round(2 * m * I_K * nl / us / 1e6, 2)}
+            us = _rotating_us(ctx, call, len(c["w"]), reps=8)
+            per[f"M{m}_N{n}"] = {"us": round(us, 2), "TFLOP/s": round(2 * m * I_K * nl / us / 1e6, 2),
+                                 "GB/s": round(wo_bytes("w4", m, I_K, nl, I_G) / us / 1e3, 1)}
     dom = max(per, key=lambda k: per[k]["us"])
     dm, dn = [int(x[1:]) for x in dom.split("_")]
     nl = cases[dn]["plan"].cols
-    nbytes = dm * I_K + dm * 4 + nl * I_K // 2 + nl * (I_K // I_G) * 4 + nl * 4 + dm * nl * 4
-    roof = roofline(f"gemm_w4a8 M={dm} N={nl} K={I_K}", 2 * dm * I_K * nl, nbytes, per[dom]["us"], ctx.peaks)
+    what = ("wo_skinny_kernel" if dm <= 16 else "wo_prep_kernel + gemm_wo_kernel (one call)") + f" M={dm} N={nl}"
+    roof = roofline_wo("w4", dm, I_K, nl, per[dom]["us"], ctx.peaks, what)
     # e2e: rank 0 runs the host-slice call for its shard (weights copied per call, as blas does)
     dev = oc.Device(ctx.local)
     L = oc.lib()
@@ -781,8 +977,8 @@ def run_int4(ctx):
             hq, hs, hb, hA, hY = hosts[n]
             nl = cases[n]["plan"].cols
             for m in I_M:
-                oc.check(L.oc_blas_qgemm_w4a8(dev.handle, m, nl, I_K, I_G, hA[m].data_ptr(), hq.data_ptr(),
-                                              hs.data_ptr(), hb.data_ptr(), hY[m].data_ptr()))
+                oc.check(L.oc_blas_qgemm_w4(dev.handle, m, nl, I_K, I_G, hA[m].data_ptr(), hq.data_ptr(),
+                                            hs.data_ptr(), hb.data_ptr(), hY[m].data_ptr()))
 
     e2e_step()
     t0 = time.perf_counter()
@@ -795,13 +991,14 @@ def run_int4(ctx):
     d2h = sum(m * cases[n]["plan"].cols * 4 for m in I_M for n in I_N)
     e2e = {"value": i_ops() / t_e2e / 1e12, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
            "ms_per_step": round(t_e2e * 1e3, 2),
-           "note": "host-slice oc_blas_qgemm_w4a8 per rank shard (no gather on the host path)"}
+           "note": "host-slice oc_blas_qgemm_w4 per rank shard (no gather on the host path)"}
     dev.close()
     cpu = cpu_int4() if ctx.rank == 0 and not args.no_cpu_baseline else None
     config = {"workload": WORKLOADS["int4"],
               "parallelism": f"column shard x{ctx.world} + NCCL all-gather" if ctx.world > 1 else "1 GPU",
               "l2": "weights rotated over copies so every step reads > 126 MB"}
-    emit(ctx, "INT4 g32 GEMM TOPS (K=3584 sweep)", value, "TOPS", ms_step, "int4 x int8 -> int32 (f32 in/out)",
+    emit(ctx, "INT4 g32 GEMM TOPS (K=3584 sweep)", value, "TOPS", ms_step,
+         "f32 (f32 activations x dequantized int4 weights)",
          config, launches * args.steps, roof, clk, e2e, cpu, {"per_kernel": per}, scaling="strong")
     ctx.close()
 
@@ -1031,12 +1228,13 @@ def run_mla(ctx):
 # ----------------------------------------------------------------------------
 
 WORKLOADS = {
-    "qgemm": "config-2 quantized GEMM sweep: M in {1,16,128,2048}, K=768, N=3072, W8A8 per-channel + W4A8 group-32, "
-             "f32 bias and output",
+    "qgemm": "config-2 quantized GEMM sweep: M in {1,16,128,2048}, K=768, N=3072, f32 activations, INT8 per-channel "
+             "and INT4 group-32 weights (weight-only: sgemm(A, dequantize(W)^T) + bias), f32 bias and output",
     "sgemm": "config-1 sgemm: A[512x768] . B[768x2304] + bias, N(0,0.02) seed 0, 3xTF32",
     "gpt2": "config-3 GPT-2 124M random-init (load_random seed 3), prompt 32, 128 greedy tokens, "
             "batch 32 (32 independent sequences)",
-    "int4": "config-4 INT4 group-32 sweep K=3584, N in {3584,18944,152064}, M in {1,8,64,512,4096}",
+    "int4": "config-4 INT4 group-32 sweep K=3584, N in {3584,18944,152064}, M in {1,8,64,512,4096}, f32 activations "
+            "(weight-only)",
     "moe": "config-5 MoE: 8192 tokens x d 7168, 256 experts (d_ff 2048, INT8 per-channel) + 1 shared, top-8 over "
            "N(0,1) router logits, grouped W8A8 GEMMs",
     "mla": "config-5 MLA: KV[16384x7168] . down[7168x512] -> latent; latent . up_K/up_V [512x16384], N(0,0.02) weights",
