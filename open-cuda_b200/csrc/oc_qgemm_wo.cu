@@ -113,12 +113,14 @@ static int launch_wo_gemm(const CUtensorMap& ta, const CUtensorMap& tw, int m, i
   const int sms = std::max(1, sm_count());
   const int tiles_m = (m + BM - 1) / BM, tiles = tiles_m * ((nc + C::BN - 1) / C::BN);
   const int nrb = k / C::BK;
-  // Split K only where the tiles do not fill the GPU: every tile then, in
-  // up to 8 slices (the last slice's CTA adds the others in slice order).
-  // Short K splits only grids that fill at most a quarter of the GPU: a
-  // slice writes a whole tile of partial sums at the SM's store rate.
+  // Split K only for long K where the tiles do not fill the GPU: every tile
+  // then, in up to 8 slices (the last slice's CTA adds the others in slice
+  // order).  Short K is not split: a slice writes a whole tile of partial
+  // sums at the SM's store rate and the last slice reads them back, which
+  // measured slower than the unsplit tiles (128 x 768 x 3072: 19 us unsplit,
+  // 26-31 us in 2-6 slices).
   SplitPlan sp{tiles_m, nrb, tiles, 1, 0};
-  if (tiles < sms && (k >= 2048 || 4 * tiles <= sms)) {
+  if (tiles < sms && k >= 2048) {
     const int ks = std::min(nrb, std::min(8, sms / tiles));
     if (ks > 1) sp = SplitPlan{tiles_m, nrb, 0, ks, tiles};
   }
@@ -155,7 +157,7 @@ static int launch_wo_gemm(const CUtensorMap& ta, const CUtensorMap& tw, int m, i
 static int wo_nsplit(int m, int nc, int k, int bm) {
   const int sms = std::max(1, sm_count());
   const int tiles = (m + bm - 1) / bm * ((nc + 127) / 128), nrb = k / 64;
-  if (tiles < sms && (k >= 2048 || 4 * tiles <= sms) && std::min(nrb, std::min(8, sms / tiles)) > 1) return tiles;
+  if (tiles < sms && k >= 2048 && std::min(nrb, std::min(8, sms / tiles)) > 1) return tiles;
   return 0;
 }
 
@@ -172,11 +174,12 @@ static int run_wo_gemm(int m, int n, int k, int group, const float* A, const voi
   __half* wx = reinterpret_cast<__half*>(wxb);
   float* icn = wxb + ((size_t)nc * k * 2 * WT + 3) / 4;
   // Tile height: 192 rows where that takes fewer MMA cycles on the busiest
-  // SM (rounds of tiles x ~875 vs ~1030 cycles per k-block), else 256.
+  // SM (rounds of tiles x ~875 vs ~1030 cycles per k-block), else 256.  A
+  // short input fits one 192-row tile at a lower cost than a 256-row one
+  // (128 x 768 x 3072: 19 vs 25 us; 512 rows: 20 vs 26 us).
   const int sms = std::max(1, sm_count()), tiles_n = (nc + 127) / 128;
   auto rounds = [&](int bm) { return ((m + bm - 1) / bm * tiles_n + sms - 1) / sms; };
-  const int tiles256 = (m + 255) / 256 * tiles_n;
-  const int bm = tiles256 >= sms && rounds(192) * 875 < rounds(256) * 1030 ? 192 : 256;
+  const int bm = rounds(192) * 875 < rounds(256) * 1030 ? 192 : 256;
   CUtensorMap ta;
   int rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
                         64, bm, CU_TENSOR_MAP_SWIZZLE_128B);
