@@ -135,6 +135,10 @@ int oc_transfer_between_devices(oc_device *src, uint64_t src_addr, oc_device *ds
  *   "softmax"            [data ptr; rows,cols usize], in place (blas:383-385)
  *   "flash_attention"    [q,k,v,o ptr; seq,head_dim,block usize; scale f32]
  *                        (blas:745-760)
+ *   "qgemm_w8"           [A,Wq,scales,bias,Y ptr; m,n,k usize]: oc_qgemm_w8
+ *   "qgemm_w4"           [A,Wq,scales,bias,Y ptr; m,n,k,group usize]:
+ *                        oc_qgemm_w4 (new blas functions launch these; no
+ *                        counterpart kernel in the reference)
  * Pointer arguments must be allocations of this device large enough for
  * the shapes.  Other names: OC_ERR_LAUNCH_FAILED ("kernel source not
  * supported by this backend").  Asynchronous until oc_device_synchronize. */
@@ -348,7 +352,10 @@ int oc_quantize_rows_int8(const float *A, int m, int k, int8_t *qa, float *sa, v
  * 16 MiB, else OC_ERR_INVALID_VALUE.  Every GPU that loads the library
  * keeps the array until exit; concurrent calls on one device that overlap
  * on the GPU race on it, so order them on one stream.  The first call on a
- * device looks up the array's address; make it before any stream capture. */
+ * device looks up the array's address; make it before any stream capture.
+ * The address is kept for the life of the process (as the library keeps its
+ * other per-device state): do not call cudaDeviceReset on a device while the
+ * library is in use on it. */
 int oc_qgemm_w8a8_noalloc(int m, int n, int k, const float *A, const int8_t *Wq, const float *w_scales,
                           const float *bias, float *Y, void *stream);
 /* The size of that array in bytes (16 MiB). */

@@ -267,6 +267,30 @@ int oc_device_launch(oc_device* dev, const char* name, const oc_launch_config* c
     return oc_flash_attention_fwd((const float*)q, (const float*)k, (const float*)v, (float*)o, 1, (int)seq, (int)seq,
                                   (int)d, scale, 0, s);
   }
+  if (kname == "qgemm_w8" || kname == "qgemm_w4") {
+    // The weight-only matmuls (oc_qgemm_w8 / _w4) for blas functions that
+    // launch them by name: [A, Wq, scales, bias, Y ptr; m, n, k usize] plus a
+    // group usize for INT4.
+    const bool w8 = kname == "qgemm_w8";
+    if (nargs < (w8 ? 8u : 9u)) return fail(OC_ERR_INVALID_VALUE, "launch " + kname + ": too few arguments");
+    size_t m, n, k, group = 0;
+    if (!arg_usize(&args[5], &m) || !arg_usize(&args[6], &n) || !arg_usize(&args[7], &k) ||
+        (!w8 && !arg_usize(&args[8], &group)))
+      return fail(OC_ERR_INVALID_VALUE, "launch " + kname + ": m, n, k (and group) must be usize");
+    if (w8) group = k;
+    if (m == 0 || n == 0 || k == 0 || group == 0 || m >= (1u << 31) || n >= (1u << 31) || k >= (1u << 31))
+      return fail(OC_ERR_INVALID_VALUE, "launch " + kname + ": bad shape");
+    const size_t wbytes = w8 ? n * k : (n * k + 1) / 2, nscales = w8 ? n : (n * k + group - 1) / group;
+    void *A, *W, *S, *B, *Y;
+    if ((rc = arg_ptr(dev, &args[0], m * k * 4, &A)) || (rc = arg_ptr(dev, &args[1], wbytes, &W)) ||
+        (rc = arg_ptr(dev, &args[2], nscales * 4, &S)) || (rc = arg_ptr(dev, &args[3], n * 4, &B)) ||
+        (rc = arg_ptr(dev, &args[4], m * n * 4, &Y)))
+      return rc;
+    return w8 ? oc_qgemm_w8((int)m, (int)n, (int)k, (const float*)A, (const int8_t*)W, (const float*)S,
+                            (const float*)B, (float*)Y, s)
+              : oc_qgemm_w4((int)m, (int)n, (int)k, (int)group, (const float*)A, (const uint8_t*)W,
+                            (const float*)S, (const float*)B, (float*)Y, s);
+  }
   return fail(OC_ERR_LAUNCH_FAILED, "kernel source not supported by this backend: " + kname);
 }
 

@@ -185,3 +185,30 @@ def test_weight_only_errors(oc):
     with pytest.raises(ValueError):
         dev.qgemm_w4(1, 4, 64, 0, np.zeros(64, np.float32), np.zeros(128, np.uint8), np.ones(8, np.float32))
     dev.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_weight_only_launched_by_name(oc, oracle, bits):
+    # the kernels the opencuda-blas qgemm_w8 / qgemm_w4 functions launch through
+    # GpuDevice::launch_kernel: [A, Wq, scales, bias, Y ptr; m, n, k (, group) usize]
+    K = oc.KernelArg
+    m, k, n, group = 24, 256, 130, 32
+    A, WT, bias = synth.qgemm_case(m, k, n, 31, 32, 33)
+    wq, ws = _quant(oracle, WT, bits, group)
+    y_ref = oracle.qgemm_weight_only(bits, m, k, n, k if bits == 8 else group, A, wq, ws, bias)
+    dev = oc.Device(0)
+    bufs = [dev.alloc(x.nbytes) for x in (A, wq, ws, bias)] + [dev.alloc(m * n * 4)]
+    for p, x in zip(bufs, (A, wq, ws, bias)):
+        dev.memcpy_h2d(p, np.ascontiguousarray(x))
+    args = [K.ptr(p) for p in bufs] + [K.usize(m), K.usize(n), K.usize(k)]
+    if bits == 4:
+        args.append(K.usize(group))
+    dev.launch_kernel("qgemm_w8" if bits == 8 else "qgemm_w4", args)
+    dev.synchronize()
+    y = np.zeros(m * n, np.float32)
+    dev.memcpy_d2h(y, bufs[4])
+    assert rel_fro(y, y_ref) <= REL_FRO
+    with pytest.raises(ValueError):  # a too-small output allocation is refused before any launch
+        small = dev.alloc(16)
+        dev.launch_kernel("qgemm_w8" if bits == 8 else "qgemm_w4", args[:4] + [K.ptr(small)] + args[5:])
+    dev.close()
