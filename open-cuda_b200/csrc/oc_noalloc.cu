@@ -23,7 +23,10 @@
 //    every scratch byte it reads, so no clearing is needed.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress, once per device, with that device current).
-//    Make that first call before any stream capture begins.
+//    Make that first call before any stream capture begins.  The address is
+//    cached for the life of the process, like the library's other per-device
+//    state (status word, kernel attributes, scratch buffers): cudaDeviceReset
+//    on a device while the library is in use there is not supported.
 #include <map>
 #include <mutex>
 

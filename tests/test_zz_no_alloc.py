@@ -50,10 +50,11 @@ def _noalloc(oc, A, Wq, ws, bias):
     return Y
 
 
-@pytest.mark.parametrize("m,k,n", [(2048, 768, 3072), (5, 768, 1000)])
+@pytest.mark.parametrize("m,k,n", [(2048, 768, 3072), (5, 768, 1000), (20, 100, 96)])
 def test_noalloc_matches_workspace_entry_point_twice(oc, m, k, n):
     # two calls in a row on different inputs: the shared scratch keeps the
     # previous call's contents, which must not leak into the next result
+    # (tensor-core GEMM, skinny kernel, and the scalar kernel for k % 16 != 0)
     for seed in (21, 42):
         A, Wq, ws, bias = _case(oc, m, k, n, seed)
         y_ref = oc.qgemm_w8a8(A, Wq, ws, bias)
@@ -72,3 +73,23 @@ def test_noalloc_rejects_oversize(oc):
     rc = oc.lib().oc_qgemm_w8a8_noalloc(m, 64, k, 16, 16, 16, None, 16, None)
     assert rc == oc.OC_ERR_INVALID_VALUE
     assert "16 MiB" in oc.last_error()
+
+
+@pytest.mark.parametrize("m,k,n", [(1500, 768, 2048), (7, 512, 300), (24, 100, 96)])
+def test_noalloc_allocates_no_device_memory(oc, m, k, n):
+    # The entry point's claim: no device allocation, even on the first call at
+    # a size it has not seen.  The workspace entry point runs first at the same
+    # size, so the kernels on this path are already loaded; then the device's
+    # free memory must be the same before and after the allocation-free call.
+    A, Wq, ws, bias = _case(oc, m, k, n, 7)
+    y_ref = oc.qgemm_w8a8(A, Wq, ws, bias)
+    Y = torch.empty(m, n, dtype=torch.float32, device=A.device)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    rc = oc.lib().oc_qgemm_w8a8_noalloc(m, n, k, A.data_ptr(), Wq.data_ptr(), ws.data_ptr(), bias.data_ptr(),
+                                        Y.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    oc.check(rc)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"free device memory changed by {free0 - free1} bytes"
+    assert np.array_equal(Y.cpu().numpy().view(np.uint32), y_ref.cpu().numpy().view(np.uint32))
