@@ -1,4 +1,4 @@
-"""Column-sharded W4A8 GEMM on 2+ GPUs (one process per GPU, NCCL
+"""Column-sharded INT4 GEMM (W4A8 and weight-only) on 2+ GPUs (one process per GPU, NCCL
 all-gather): the gathered [M][N] result must equal, bit for bit, the
 shards' products computed on one GPU and laid side by side (the exchange
 and layout add nothing to the arithmetic).
@@ -22,7 +22,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, shape, q):
+def _worker(rank, world, port, shape, q, weight_only=False):
     import torch
     import torch.distributed as dist
 
@@ -45,14 +45,16 @@ def _worker(rank, world, port, shape, q):
         Ad = torch.from_numpy(A).to(dev)
         bd = torch.from_numpy(bias).to(dev)
         plan = shard.ColumnShard(n, world)
-        y = shard.sharded_qgemm_w4a8(Ad, q4, s4, g, bd, plan, rank)
+        sharded = shard.sharded_qgemm_w4 if weight_only else shard.sharded_qgemm_w4a8
+        single = (lambda a, w, sc, grp, b: oc.qgemm_w4(a, w, sc, grp, bias=b)) if weight_only else oc.qgemm_w4a8
+        y = sharded(Ad, q4, s4, g, bd, plan, rank)
         # the gathered result must equal, bit for bit, each shard's product
         # computed on one GPU and laid side by side
         parts = []
         for r in range(world):
             (b0, b1), (s0, s1) = plan.w4_slices(r, k, g)
             r0, r1 = plan.rows(r)
-            parts.append(oc.qgemm_w4a8(Ad, q4[b0:b1], s4[s0:s1], g, bd[r0:r1]))
+            parts.append(single(Ad, q4[b0:b1], s4[s0:s1], g, bd[r0:r1]))
         full = torch.cat(parts, dim=1)
         torch.cuda.synchronize()
         ok = torch.equal(y.view(torch.int32), full.view(torch.int32))
@@ -63,8 +65,9 @@ def _worker(rank, world, port, shape, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("weight_only", [False, True])
 @pytest.mark.parametrize("shape", [(64, 3584, 3584, 32), (512, 3584, 18944, 32), (1, 3584, 152064, 32)])
-def test_sharded_w4a8_matches_single_gpu(shape):
+def test_sharded_w4a8_matches_single_gpu(shape, weight_only):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -73,7 +76,7 @@ def test_sharded_w4a8_matches_single_gpu(shape):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, q, weight_only)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
