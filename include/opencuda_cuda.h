@@ -240,6 +240,15 @@ int oc_gpt_load_random(oc_gpt *model, uint64_t seed);
  * lnf_w, 15 lnf_b, 16 lm_head_w [H][V], 17 lm_head_b.  Linear weights are
  * weight_t = [in][out] as the reference stores them. */
 int oc_gpt_set_weight(oc_gpt *model, int which, int layer, const float *host, size_t len);
+/* enable_mla_kv_compression (llm:822-838): K and V rows are kept as d_c-dim
+ * latents per head (KvCacheHead::push, llm:564-583) and attention reads
+ * their reconstruction (current_kv, llm:586-595), with per-layer, per-head
+ * projections drawn from SplitMix64(seed) in the reference's order (down
+ * [head_dim][d_c], then up [d_c][head_dim], next_f32(0.02)), bit-identical
+ * to its values.  0 < d_c < head_dim, else OC_ERR_INVALID_VALUE.  Weight ids
+ * 18 / 19 of oc_gpt_get_weight / oc_gpt_set_weight are then a layer's
+ * down / up projections, [heads][head_dim][d_c] / [heads][d_c][head_dim]. */
+int oc_gpt_enable_mla(oc_gpt *model, size_t d_c, uint64_t seed);
 /* Copies one weight tensor back to host memory (same ids and shapes). */
 int oc_gpt_get_weight(oc_gpt *model, int which, int layer, float *host, size_t len);
 /* GptModel::generate (llm:910-929), greedy, for `batch` independent

@@ -256,6 +256,50 @@ __global__ void __launch_bounds__(kAttnThreads)
   }
 }
 
+// MLA-compressed KV cache (enable_mla_kv_compression, llm:822-838;
+// KvCacheHead::push / current_kv, llm:564-595): the K and V rows just
+// written for positions *pos0 .. *pos0 + L - 1 are compressed per head to
+// d_c latents, lat[c] = sum_j x[j] * down[j][c] (mla_compress_kv: sgemm with
+// m = 1, ascending j, no FMA, then 1 * acc + 0), stored in the latent cache
+// [batch][max_seq][heads][2][d_c], and reconstructed, x'[j] = sum_c lat[c] *
+// up[c][j] (mla_decompress_kv, ascending c), in place of the row.  The
+// reference decompresses all n rows every step; the reconstruction of a row
+// is the same at every step, so doing it once at push time feeds the
+// attention the same keys and values.  Grid (rows * heads, 2: K and V).
+__global__ void __launch_bounds__(128) mla_roundtrip_kernel(int L, const int* __restrict__ pos0, int H, int heads,
+                                                            int d, int dc, float* __restrict__ kc,
+                                                            float* __restrict__ vc, int max_seq,
+                                                            const float* __restrict__ down,
+                                                            const float* __restrict__ up, float* __restrict__ lat,
+                                                            int rows) {
+  __shared__ float xs[kAttnMaxD], ls[kAttnMaxD];
+  pdl_wait();
+  pdl_launch();
+  const int gw = blockIdx.x;
+  if (gw >= rows * heads) return;
+  const int r = gw / heads, h = gw % heads, kv = blockIdx.y;
+  const int b = r / L, p = *pos0 + r % L;
+  float* row = (kv ? vc : kc) + ((size_t)b * max_seq + p) * H + (size_t)h * d;
+  const float* dn = down + (size_t)h * d * dc;
+  const float* upp = up + (size_t)h * dc * d;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) xs[j] = row[j];
+  __syncthreads();
+  float* lrow = lat + ((((size_t)b * max_seq + p) * heads + h) * 2 + kv) * dc;
+  for (int c = threadIdx.x; c < dc; c += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < d; ++j) acc = __fadd_rn(acc, __fmul_rn(xs[j], dn[(size_t)j * dc + c]));
+    acc = __fadd_rn(acc, 0.0f);  // alpha * acc + beta * 0 with alpha = 1, beta = 0
+    ls[c] = acc;
+    lrow[c] = acc;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    float acc = 0.0f;
+    for (int c = 0; c < dc; ++c) acc = __fadd_rn(acc, __fmul_rn(ls[c], upp[(size_t)c * d + j]));
+    row[j] = __fadd_rn(acc, 0.0f);
+  }
+}
+
 // argmax of each row, first maximum wins (llm:932-942): strict > keeps the
 // lowest index on ties; NaN never wins; all NaN / -inf gives index 0.  Grid
 // (chunks of kArgChunk logits, batch): each CTA reduces its chunk to
@@ -705,6 +749,11 @@ struct oc_gpt {
   size_t counter_count = 0;
   ArgmaxScratch arg{};
   float *kc, *vc;  // [layer][batch][max_seq][H]
+  // MLA-compressed KV cache (enable_mla_kv_compression): projections
+  // down [layer][head][d][d_c], up [layer][head][d_c][d], latents
+  // [layer][batch][max_seq][head][2][d_c]; mla_dc == 0: off
+  int mla_dc = 0;
+  float *mla_down = nullptr, *mla_up = nullptr, *mla_lat = nullptr;
   uint32_t *tok_in, *next, *out_tokens;
   int *pos, *step;
   float* keep_logits = nullptr;
@@ -851,6 +900,14 @@ int forward(oc_gpt* g, int batch, int L, const uint32_t* tokens, uint32_t* out, 
     float* kc = g->kc + li * (size_t)g->max_batch * ms * H;
     float* vc = g->vc + li * (size_t)g->max_batch * ms * H;
     if ((rc = linear_fwd(g, Ly.qkv, g->hidden, rows, g->qkv, kEpiQkv, n, kc, vc, L, Ly.ln1w, Ly.ln1b))) return rc;
+    if (g->mla_dc) {  // the rows just written -> latents -> reconstructed rows
+      const int d = H / nh, dc = g->mla_dc;
+      launch_pdl(mla_roundtrip_kernel, dim3(rows * nh, 2), dim3(128), 0, s, L, (const int*)g->pos, H, nh, d, dc, kc,
+                 vc, ms, (const float*)(g->mla_down + li * (size_t)nh * d * dc),
+                 (const float*)(g->mla_up + li * (size_t)nh * dc * d),
+                 g->mla_lat + li * (size_t)g->max_batch * ms * nh * 2 * dc, rows);
+      *n += 1;
+    }
     launch_pdl(decode_attention_kernel, dim3(rows * nh), dim3(kAttnThreads), attn_smem, s,
         g->qkv, L, g->pos, H, nh, H / nh, kc, vc, ms, g->ctx, rows, scale);
     if ((rc = linear_fwd(g, Ly.ao, g->ctx, rows, g->hidden, kEpiResidual, n))) return rc;
@@ -1009,6 +1066,44 @@ int oc_gpt_load_random(oc_gpt* g, uint64_t seed) {
 
 // Uploads one weight tensor (ids as in oc_gpt_weight_id below) from host
 // memory, e.g. from a safetensors file (llm:661-731).
+// enable_mla_kv_compression (llm:822-838): per layer and head a down
+// projection [d][d_c] then an up projection [d_c][d], drawn in that order
+// from one SplitMix64(seed) stream with next_f32(0.02), bit-identical to the
+// reference's; 0 < d_c < d.  The decode graph is captured again.
+int oc_gpt_enable_mla(oc_gpt* g, size_t d_c, uint64_t seed) {
+  OC_REQUIRE(g, "NULL model");
+  const oc_gpt_config& c = g->cfg;
+  const size_t d = c.hidden_size / c.num_heads, nh = c.num_heads, nl = c.num_layers;
+  if (!(d_c > 0 && d_c < d))
+    return fail(OC_ERR_INVALID_VALUE, "open-cuda-llm: enable_mla_kv_compression: d_c=" + std::to_string(d_c) +
+                                          " must satisfy 0 < d_c < head_dim=" + std::to_string(d));
+  Scope sc(g->device);
+  cudaStream_t s = g->stream;
+  const size_t per = d * d_c;
+  int rc;
+  if (g->mla_dc != (int)d_c) {  // earlier buffers stay owned by the model until it is destroyed
+    if ((rc = galloc_t(g, nl * nh * per, &g->mla_down)) || (rc = galloc_t(g, nl * nh * per, &g->mla_up)) ||
+        (rc = galloc_t(g, nl * (size_t)g->max_batch * c.max_seq_len * nh * 2 * d_c, &g->mla_lat)))
+      return rc;
+  }
+  uint64_t off = 0;
+  for (size_t li = 0; li < nl; ++li)
+    for (size_t h = 0; h < nh; ++h) {
+      float* dn = g->mla_down + (li * nh + h) * per;
+      float* up = g->mla_up + (li * nh + h) * per;
+      splitmix_fill_kernel<<<ew_blocks(per), 256, 0, s>>>(dn, per, seed, off, 0.02f);
+      off += per;
+      splitmix_fill_kernel<<<ew_blocks(per), 256, 0, s>>>(up, per, seed, off, 0.02f);
+      off += per;
+    }
+  OC_CHECK_CUDA(cudaGetLastError());
+  OC_CHECK_CUDA(cudaStreamSynchronize(s));
+  g->mla_dc = (int)d_c;
+  if (g->graph) cudaGraphExecDestroy(g->graph);  // the decode step gains a kernel per layer
+  g->graph = nullptr;
+  return OC_OK;
+}
+
 static int weight_slot(oc_gpt* g, int which, int layer, float** out_dst, size_t* out_n, GptLinear** out_lin);
 
 int oc_gpt_set_weight(oc_gpt* g, int which, int layer, const float* host, size_t len) {
@@ -1073,6 +1168,14 @@ static int weight_slot(oc_gpt* g, int which, int layer, float** out_dst, size_t*
         case 11: dst = Ly->ln1b; n = H; break;
         case 12: dst = Ly->ln2w; n = H; break;
         case 13: dst = Ly->ln2b; n = H; break;
+        case 18:  // MLA projections of the layer, [head][d][d_c] / [head][d_c][d]
+        case 19: {
+          OC_REQUIRE(g->mla_dc > 0, "gpt weight: MLA compression is not enabled");
+          const size_t per = (H / c.num_heads) * (size_t)g->mla_dc * c.num_heads;
+          dst = (which == 18 ? g->mla_down : g->mla_up) + (size_t)layer * per;
+          n = per;
+          break;
+        }
         default: return fail(OC_ERR_INVALID_VALUE, "gpt_set_weight: unknown weight id");
       }
   }

@@ -42,12 +42,14 @@ _SIGS = {
                                   C.POINTER(C.c_int)]),
     "oc_gpt_stream": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "oc_gpt_kernel_launches": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),
+    "oc_gpt_enable_mla": (C.c_int, [C.c_void_p, C.c_size_t, C.c_uint64]),
 }
 
 WEIGHT_IDS = {
     "wte": 0, "wpe": 1, "qkv_w": 2, "qkv_b": 3, "attn_out_w": 4, "attn_out_b": 5,
     "fc_w": 6, "fc_b": 7, "proj_w": 8, "proj_b": 9, "ln1_w": 10, "ln1_b": 11,
     "ln2_w": 12, "ln2_b": 13, "lnf_w": 14, "lnf_b": 15, "lm_head_w": 16, "lm_head_b": 17,
+    "mla_down": 18, "mla_up": 19,
 }
 
 
@@ -95,7 +97,8 @@ class GptModel:
         H, V, I, ctx = c.hidden_size, c.vocab_size, c.intermediate_size, c.max_seq_len
         return {"wte": V * H, "wpe": ctx * H, "qkv_w": H * 3 * H, "qkv_b": 3 * H, "attn_out_w": H * H,
                 "attn_out_b": H, "fc_w": H * I, "fc_b": I, "proj_w": I * H, "proj_b": H, "ln1_w": H, "ln1_b": H,
-                "ln2_w": H, "ln2_b": H, "lnf_w": H, "lnf_b": H, "lm_head_w": H * V, "lm_head_b": V}[name]
+                "ln2_w": H, "ln2_b": H, "lnf_w": H, "lnf_b": H, "lm_head_w": H * V, "lm_head_b": V,
+                "mla_down": H * getattr(self, "mla_dc", 0), "mla_up": H * getattr(self, "mla_dc", 0)}[name]
 
     def set_weight(self, name: str, values, layer: int = 0):
         v = np.ascontiguousarray(values, np.float32).ravel()
@@ -106,6 +109,12 @@ class GptModel:
         oc.check(_lib().oc_gpt_get_weight(self._h, WEIGHT_IDS[name], layer, out.ctypes.data_as(C.c_void_p),
                                           out.size))
         return out
+
+    def enable_mla_kv_compression(self, d_c: int, seed: int):
+        """enable_mla_kv_compression (llm:822-838): K/V kept as d_c-dim latents
+        per head, attention over their reconstruction; 0 < d_c < head_dim."""
+        oc.check(_lib().oc_gpt_enable_mla(self._h, d_c, seed))
+        self.mla_dc = d_c
 
     def kernel_launches(self) -> int:
         """Kernels launched by generate on this model so far."""

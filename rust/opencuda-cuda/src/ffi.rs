@@ -252,6 +252,7 @@ extern "C" {
     ) -> c_int;
     pub fn oc_gpt_destroy(model: *mut oc_gpt) -> c_int;
     pub fn oc_gpt_load_random(model: *mut oc_gpt, seed: u64) -> c_int;
+    pub fn oc_gpt_enable_mla(model: *mut oc_gpt, d_c: usize, seed: u64) -> c_int;
     pub fn oc_gpt_set_weight(model: *mut oc_gpt, which: c_int, layer: c_int, values: *const f32, len: usize) -> c_int;
     pub fn oc_gpt_generate(
         model: *mut oc_gpt,

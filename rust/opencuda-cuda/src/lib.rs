@@ -239,6 +239,12 @@ impl CudaGpt {
         check(unsafe { ffi::oc_gpt_load_random(self.raw, seed) })
     }
 
+    /// GptModel::enable_mla_kv_compression (llm:822-838): a d_c-dim latent
+    /// K/V cache per head; 0 < d_c < head_dim.
+    pub fn enable_mla_kv_compression(&mut self, d_c: usize, seed: u64) -> Result<()> {
+        check(unsafe { ffi::oc_gpt_enable_mla(self.raw, d_c, seed) })
+    }
+
     /// Uploads one tensor of a checkpoint (ids as in the C header).
     pub fn set_weight(&mut self, which: i32, layer: usize, values: &[f32]) -> Result<()> {
         check(unsafe { ffi::oc_gpt_set_weight(self.raw, which, layer as c_int, values.as_ptr(), values.len()) })

@@ -185,3 +185,79 @@ def test_gpt2_checkpoint_matches_oracle(gptmod, oracle):
     assert np.max(np.abs(dl - rl)) < LOGIT_TOL
     assert np.array_equal(dev.weight("lm_head_w"), ref.weight("lm_head_w"))
     dev.close()
+
+
+@pytest.mark.parametrize("seed,d_c,text,n", [(42, 2, "hi", 8), (7, 4, "mla compressed cache", 10),
+                                             (2026, 6, "x", 6)])
+def test_mla_kv_compression_matches_oracle(gptmod, oracle, seed, d_c, text, n):
+    """enable_mla_kv_compression (llm:822-838): projections bit-identical to
+    the oracle's, greedy tokens identical and logits within 1e-4 with the
+    latent K/V cache (llm:564-595)."""
+    cfg = gptmod.GptConfig.tiny(oracle.BYTE_VOCAB_SIZE)
+    prompt = oracle.byte_encode(text)
+    ref = oracle.GptModel(_oracle_cfg(oracle, cfg), seed)
+    ref.set_attention(flash=True, block=4)
+    ref.enable_mla_kv_compression(d_c, seed + 1)
+    rt, rl = ref.generate(prompt, n, want_logits=True)
+    dev = gptmod.GptModel.load_random(cfg, seed, max_batch=2)
+    dt0 = dev.generate(prompt, n)  # uncompressed first: enabling MLA re-captures the decode step
+    dev.enable_mla_kv_compression(d_c, seed + 1)
+    heads = cfg.num_heads
+    for layer in range(cfg.num_layers):
+        for name in ("mla_down", "mla_up"):
+            want = np.concatenate([ref.weight(name, layer, h) for h in range(heads)])
+            assert np.array_equal(dev.weight(name, layer).view(np.uint32), want.view(np.uint32)), (name, layer)
+    dt, dl = dev.generate(prompt, n, want_logits=True)
+    assert dt.tolist() == rt.tolist()
+    assert np.max(np.abs(dl - rl)) < LOGIT_TOL
+    # batch 2: both sequences equal their single-sequence results
+    bt = dev.generate(np.stack([prompt, prompt]), n)
+    assert bt[0].tolist() == rt.tolist() and bt[1].tolist() == rt.tolist()
+    assert len(dt0) == n
+    dev.close()
+
+
+def test_mla_kv_compression_changes_output_and_bounds(gptmod, oracle):
+    """The reference's checks (llm:1035-1069): d_c must satisfy 0 < d_c <
+    head_dim, and the compressed cache changes the generation for at least one
+    of five seeds (the path is really taken)."""
+    cfg = gptmod.GptConfig.tiny(oracle.BYTE_VOCAB_SIZE)  # head_dim 8
+    dev = gptmod.GptModel.load_random(cfg, 1)
+    with pytest.raises(ValueError):
+        dev.enable_mla_kv_compression(8, 1)
+    with pytest.raises(ValueError):
+        dev.enable_mla_kv_compression(0, 1)
+    dev.close()
+    prompt = oracle.byte_encode("does compression change output")
+    differs = False
+    for seed in (1, 2, 3, 4, 5):
+        base = gptmod.GptModel.load_random(cfg, seed)
+        comp = gptmod.GptModel.load_random(cfg, seed)
+        comp.enable_mla_kv_compression(2, seed)
+        if base.generate(prompt, 6).tolist() != comp.generate(prompt, 6).tolist():
+            differs = True
+        base.close()
+        comp.close()
+        if differs:
+            break
+    assert differs
+
+
+def test_mla_kv_compression_gpt2_124m(gptmod, oracle):
+    """GPT-2 124M (load_random seed 3) with a 32-dim latent cache per head:
+    tokens identical and logits within 1e-4 of the oracle, batch 1 and 4."""
+    cfg = gptmod.GptConfig.gpt2_124m()
+    prompts = synth.gpt_prompts(4, 32)
+    ref = oracle.GptModel(_oracle_cfg(oracle, cfg), 3)
+    ref.set_attention(flash=True, block=64)
+    ref.enable_mla_kv_compression(32, 11)
+    rt, rl = ref.generate(prompts[0], 8, want_logits=True)
+    dev = gptmod.GptModel.load_random(cfg, 3, max_batch=4, max_prompt_len=32)
+    dev.enable_mla_kv_compression(32, 11)
+    dt, dl = dev.generate(prompts[0], 8, want_logits=True)
+    assert dt.tolist() == rt.tolist()
+    assert np.max(np.abs(dl - rl)) < LOGIT_TOL
+    bt = dev.generate(prompts, 4)
+    for b in range(4):
+        assert bt[b].tolist() == ref.generate(prompts[b], 4).tolist(), b
+    dev.close()
