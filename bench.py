@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qgemm", choices=["qgemm", "sgemm", "gpt2", "int4", "moe", "mla"])
+    ap.add_argument("--workload", default="qgemm", choices=["qgemm", "qgemm_a8", "sgemm", "gpt2", "int4", "moe", "mla"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-once", action="store_true",
                     help="run one warm pass of the workload's kernels and exit (for ncu launch lists)")
@@ -387,7 +387,7 @@ def _rotating_us(ctx, launch_of, nsets: int, reps: int = 32) -> float:
     return ctx.kernel_us(launch, reps=reps)
 
 
-def qgemm_cold_gemv(ctx):
+def qgemm_cold_gemv(ctx, once: bool = False):
     """Config-4 decode GEMV from cold HBM: M=1, K=3584, N=152064, weight-only
     INT8 (545 MB of weights) and INT4 g32 (272 MB packed + 68 MB scales)."""
     torch, oc = ctx.torch, ctx.oc
@@ -407,6 +407,10 @@ def qgemm_cold_gemv(ctx):
             else:
                 oc.qgemm_w4(A, q4, s4, Q_G, bias=b, out=Y)
 
+        if once:
+            launch()
+            torch.cuda.synchronize()
+            continue
         us = ctx.kernel_us(launch, reps=8)
         nb = wo_bytes(kind, 1, V_K, V_N)
         out[f"{kind}_M1_K{V_K}_N{V_N}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1),
@@ -550,10 +554,11 @@ def run_qgemm(ctx):
             launches = step(i)
         graphs.append(g)
     torch.cuda.synchronize()
-    if args.profile_once:
+    if args.profile_once:  # one replay of every set, then one cold-HBM GEMV of each weight type
         for g in graphs:
             g.replay()
         torch.cuda.synchronize()
+        qgemm_cold_gemv(ctx, once=True)
         return
     for i in range(args.warmup):
         graphs[i % Q_SETS].replay()
@@ -645,6 +650,144 @@ def run_qgemm(ctx):
     emit(ctx, Q_METRIC, value, "TOPS", ms_step, "f32 (f32 activations x dequantized int8 / int4 weights)", config,
          launches * args.steps, roof, clk, e2e, cpu, extra)
     ctx.finish()
+
+
+# ----------------------------------------------------------------------------
+# qgemm_a8: the same sweep with int8 activations (W8A8 / W4A8, exact int32)
+# ----------------------------------------------------------------------------
+
+A8_SETS = 8
+A8_BIG = ((2048, 18944), (4096, 18944), (2048, 152064), (4096, 152064))  # W8A8 at K=3584
+
+
+def cpu_qgemm_a8(target_s: float = 6.0):
+    """The exact int8-activation product (the oracle's W8A8 / W4A8, no
+    reference counterpart: the reference has no int8-activation path), all
+    host cores, rows sampled per call as in cpu_qgemm."""
+    import oracle
+    import synth
+
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    A_full, WT, bias = synth.qgemm_case(max(Q_M), Q_K, Q_N)
+    t8 = oracle.quantize_int8(WT.ravel(), Q_K)
+    t4 = oracle.quantize_int4(WT.ravel(), Q_G)
+    budget = target_s / (2 * len(Q_M))
+    t_total, sample = 0.0, []
+
+    def timed(bits, rows):
+        t0 = time.perf_counter()
+        if bits == 8:
+            oracle.qgemm_w8a8(rows, Q_K, Q_N, A_full[:rows], t8.data, t8.scales, bias)
+        else:
+            oracle.qgemm_w4a8(rows, Q_K, Q_N, Q_G, A_full[:rows], t4.data, t4.scales, bias)
+        return time.perf_counter() - t0
+
+    for bits in (8, 4):
+        t1, t2 = timed(bits, 1), timed(bits, 8)
+        per_row = max((t2 - t1) / 7, 1e-9)
+        fixed = max(t1 - per_row, 0.0)
+        for m in Q_M:
+            rows = max(1, min(m, int(max(budget - fixed, per_row) / per_row)))
+            dt = timed(bits, rows)
+            t_total += dt if rows == m else (dt - fixed) * (m / rows) + fixed
+            sample.append(f"W{bits}A8 M={m}: {rows} rows")
+    return {"value": q_ops() / t_total / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": "exact int8-activation oracle in C (no reference counterpart); " + "; ".join(sample)
+                      + "; sampled calls scaled as fixed + rows * per-row time"}
+
+
+def run_qgemm_a8(ctx):
+    torch, oc, args = ctx.torch, ctx.oc, ctx.args
+    import synth
+
+    A, WT, bias = synth.qgemm_case(max(Q_M), Q_K, Q_N)
+    Wd = torch.from_numpy(WT).to(ctx.device)
+    q8, s8 = oc.quantize_int8(Wd, Q_K)
+    q4, s4 = oc.quantize_int4(Wd, Q_G)
+    torch.cuda.synchronize()
+    sets = []
+    for _ in range(A8_SETS):
+        sets.append({
+            "A": {m: torch.from_numpy(A[:m]).to(ctx.device) for m in Q_M},
+            "q8": q8.clone().view(Q_N, Q_K), "s8": s8.clone(), "q4": q4.clone(), "s4": s4.clone(),
+            "bias": torch.from_numpy(bias).to(ctx.device),
+            "Y": {m: torch.empty(m, Q_N, dtype=torch.float32, device=ctx.device) for m in Q_M},
+        })
+
+    def step(i):
+        s = sets[i % A8_SETS]
+        for m in Q_M:
+            oc.qgemm_w8a8(s["A"][m], s["q8"], s["s8"], s["bias"], out=s["Y"][m])
+            oc.qgemm_w4a8(s["A"][m], s["q4"], s["s4"], Q_G, s["bias"], out=s["Y"][m])
+        return 4 * len(Q_M)  # row quantization + GEMM per matmul
+
+    oc.workspace(max(Q_M), Q_K, ctx.device)
+    with torch.cuda.stream(ctx.stream):
+        for i in range(A8_SETS):
+            step(i)
+    ctx.stream.synchronize()
+    graphs = []
+    for i in range(A8_SETS):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=ctx.stream):
+            launches = step(i)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    if args.profile_once:
+        for g in graphs:
+            g.replay()
+        torch.cuda.synchronize()
+        return
+    for i in range(args.warmup):
+        graphs[i % A8_SETS].replay()
+    torch.cuda.synchronize()
+    ms_step, clk = ctx.timed(lambda i: graphs[i % A8_SETS].replay(), args.steps)
+    value = q_ops() * ctx.world / (ms_step * 1e-3) / 1e12
+    per = {}
+    pre = [{m: oc.quantize_rows_int8(s["A"][m]) for m in Q_M} for s in sets]
+    torch.cuda.synchronize()
+    for kind in ("w8", "w4"):
+        for m in Q_M:
+            def call(j, kind=kind, m=m):
+                s, (qa, sa) = sets[j], pre[j][m]
+                if kind == "w8":
+                    oc.igemm_w8a8(qa, sa, s["q8"], s["s8"], s["bias"], out=s["Y"][m])
+                else:
+                    oc.igemm_w4a8(qa, sa, s["q4"], s["s4"], Q_G, s["bias"], out=s["Y"][m])
+
+            us = _rotating_us(ctx, call, A8_SETS)
+            per[f"{kind}a8_M{m}"] = {"us": round(us, 3), "TOPS": round(2 * m * Q_K * Q_N / us / 1e6, 2),
+                                     "GB/s": round(a8_bytes(kind, m) / us / 1e3, 1)}
+    dom = max(per, key=lambda k: per[k]["us"])
+    dkind, dm = dom.split("a8_M")
+    dm = int(dm)
+    roof = roofline(f"gemm_{dkind}a8 M={dm}", 2 * dm * Q_K * Q_N, a8_bytes(dkind, dm), per[dom]["us"], ctx.peaks)
+    # W8A8 at 7B-class shapes (K=3584): the kind::i8 GEMM where the epilogue is amortised over a long K
+    big = {}
+    K = 3584
+    g = torch.Generator(device=ctx.device).manual_seed(9)
+    for m, n in A8_BIG:
+        W = torch.randn(n, K, generator=g, device=ctx.device) * 0.02
+        qw, sw = oc.quantize_int8(W.view(-1), K)
+        del W
+        qa, sa = oc.quantize_rows_int8(torch.rand(m, K, generator=g, device=ctx.device) * 2 - 1)
+        Y = torch.empty(m, n, device=ctx.device)
+        us = ctx.kernel_us(lambda: oc.igemm_w8a8(qa, sa, qw.view(n, K), sw, None, out=Y), reps=4)
+        ops = 2 * m * n * K
+        big[f"w8a8_M{m}_K{K}_N{n}"] = {"us": round(us, 1), "TOPS": round(ops / us / 1e6, 1),
+                                       "frac_int8_dense": round(ops / us / 1e6 / ctx.peaks[1], 4),
+                                       "int8_peak_source": f"{ctx.peaks[3]}: 2 x bf16_tflops"}
+        del qw, sw, qa, Y
+    torch.cuda.empty_cache()
+    cpu = cpu_qgemm_a8() if ctx.rank == 0 and not args.no_cpu_baseline else None
+    config = {"workload": WORKLOADS["qgemm_a8"], "parallelism": f"replicas x{ctx.world}",
+              "l2": f"{A8_SETS} rotating device input sets (~300 MB) > 126 MB L2",
+              "graph": "one CUDA graph per set (row quantization + GEMM per matmul)"}
+    emit(ctx, "INT8-activation quantized GEMM TOPS (W8A8 / W4A8, M in {1,16,128,2048}, K=768, N=3072)", value,
+         "TOPS", ms_step, "int8 x int8 -> int32 (f32 in/out)", config, launches * args.steps, roof, clk, None, cpu,
+         {"per_kernel": per, "w8a8_k3584": big})
+    ctx.close(*graphs)
 
 
 # ----------------------------------------------------------------------------
@@ -1230,6 +1373,9 @@ def run_mla(ctx):
 WORKLOADS = {
     "qgemm": "config-2 quantized GEMM sweep: M in {1,16,128,2048}, K=768, N=3072, f32 activations, INT8 per-channel "
              "and INT4 group-32 weights (weight-only: sgemm(A, dequantize(W)^T) + bias), f32 bias and output",
+    "qgemm_a8": "config-2 shapes with int8 activations: M in {1,16,128,2048}, K=768, N=3072, W8A8 per-channel + "
+                "W4A8 group-32 (activation rows quantized on the device, exact int32 products), f32 bias and output; "
+                "W8A8 at K=3584 beside it",
     "sgemm": "config-1 sgemm: A[512x768] . B[768x2304] + bias, N(0,0.02) seed 0, 3xTF32",
     "gpt2": "config-3 GPT-2 124M random-init (load_random seed 3), prompt 32, 128 greedy tokens, "
             "batch 32 (32 independent sequences)",
@@ -1243,6 +1389,8 @@ WORKLOADS = {
 
 REF = {
     "qgemm": (cpu_qgemm, Q_METRIC, "TOPS", lambda v: q_ops() / (v * 1e12) * 1e3),
+    "qgemm_a8": (cpu_qgemm_a8, "INT8-activation quantized GEMM TOPS (W8A8 / W4A8, M in {1,16,128,2048}, K=768, "
+                 "N=3072)", "TOPS", lambda v: q_ops() / (v * 1e12) * 1e3),
     "sgemm": (cpu_sgemm, "sgemm TFLOP/s (f32 via 3xTF32, 512x768x2304 + bias)", "TFLOP/s",
               lambda v: 2 * S_M * S_K * S_N / (v * 1e12) * 1e3),
     "gpt2": (cpu_gpt2, "GPT-2 124M greedy decode tok/s (batch 32, prompt 32, 128 new tokens)", "tok/s",
@@ -1286,7 +1434,7 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
     ctx = Ctx(args)
-    {"qgemm": run_qgemm, "sgemm": run_sgemm, "gpt2": run_gpt2, "int4": run_int4, "moe": run_moe,
+    {"qgemm": run_qgemm, "qgemm_a8": run_qgemm_a8, "sgemm": run_sgemm, "gpt2": run_gpt2, "int4": run_int4, "moe": run_moe,
      "mla": run_mla}[args.workload](ctx)
 
 

@@ -54,13 +54,15 @@ namespace oc {
 
 // ---- tensor-core GEMM ---------------------------------------------------------
 
-template <int BM_, int WT_>
+template <int BM_, int WT_, int BK_ = 32>
 struct WoGemmT {
   static constexpr int BN = 128;   // weight rows per tile (MMA M) = output columns
   static constexpr int BM = BM_;   // activation rows per tile (MMA N)
   static constexpr int WT = WT_;   // weight terms: 1 (INT8 values) or 2 (INT4 hi / lo)
   static constexpr int HALF = BM / 2, NBH = HALF / 32;  // rows and 32-row blocks per epilogue half
-  static constexpr int BK = 64;    // k per stage: 128-byte f16 rows
+  // k per stage: 64 (128-byte f16 rows, 128-byte swizzle) or 32 (64-byte
+  // rows, 64-byte swizzle: twice the stages in the same shared memory)
+  static constexpr int BK = BK_;
   static constexpr int A_BYTES = BM * BK * 2;  // one activation-term tile
   static constexpr int W_BYTES = BN * BK * 2;  // one weight-term tile
   static constexpr int STAGE_BYTES = 2 * A_BYTES + WT * W_BYTES;
@@ -70,9 +72,10 @@ struct WoGemmT {
   static constexpr int YSTAGE_BYTES = EPI_WARPS * 4096;  // one 32 x 32 f32 block per epilogue warp
   static constexpr size_t FIXED = 1024 + YSTAGE_BYTES + 256;
   static constexpr int STAGES_FIT = (int)((227 * 1024 - FIXED) / STAGE_BYTES);
-  static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+  static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
   static constexpr size_t SMEM = FIXED + (size_t)STAGES * STAGE_BYTES;
   static_assert(BM == 256 || BM == 192, "tile heights");
+  static_assert(BK == 64 || BK == 32, "k per stage");
   static_assert(WT == 1 || WT == 2, "weight terms");
   static_assert(STAGES >= 2, "at least a double-buffered ring");
   static_assert(A_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1024-byte operand alignment");
@@ -97,14 +100,14 @@ __device__ __forceinline__ float wo_scale(float v, float rf, float cf, float b) 
 // (WT = 2) or [N][K] (WT = 1) f16 (box 64 x 128); tmOut: Y [M][N] f32 (box
 // 32 x 32, when out_tma); tmPart: split-K partial sums [rows][128] f32.
 // colf[n]: sw[n] (INT8) or 1 / c_n (INT4); rowf[m]: 1 / c_m.
-template <int BM, int WT>
-__global__ void __launch_bounds__(WoGemmT<BM, WT>::THREADS, 1)
+template <int BM, int WT, int BK>
+__global__ void __launch_bounds__(WoGemmT<BM, WT, BK>::THREADS, 1)
     gemm_wo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPart, int out_tma,
                    int M, int N, int K, int full, int ksplit, int nsplit, const float* __restrict__ rowf,
                    const float* __restrict__ colf, const float* __restrict__ bias, float* __restrict__ Y, int ldy,
                    float* __restrict__ part, int* __restrict__ ready, int* status) {
-  using C = WoGemmT<BM, WT>;
+  using C = WoGemmT<BM, WT, BK>;
   pdl_wait();  // the operand terms and the zeroed ready counters come from the kernel just before this one
   pdl_launch();
   const int tiles_m = (M + C::BM - 1) / C::BM;
@@ -164,13 +167,16 @@ __global__ void __launch_bounds__(WoGemmT<BM, WT>::THREADS, 1)
             goto done;
           }
           mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
-          tma_load_2d(sAh(stage), &tmA, 2 * kb * C::BK, it.tm * C::BM, &full_bar[stage]);
-          tma_load_2d(sAl(stage), &tmA, 2 * kb * C::BK + C::BK, it.tm * C::BM, &full_bar[stage]);
+          // the terms' layout: 64-k block b holds hi at columns [128 b, 128 b
+          // + 64) and lo at [128 b + 64, 128 b + 128)
+          const int k0 = kb * C::BK, xh = 128 * (k0 >> 6) + (k0 & 63);
+          tma_load_2d(sAh(stage), &tmA, xh, it.tm * C::BM, &full_bar[stage]);
+          tma_load_2d(sAl(stage), &tmA, xh + 64, it.tm * C::BM, &full_bar[stage]);
           if (WT == 2) {
-            tma_load_2d(sW(stage, 0), &tmW, 2 * kb * C::BK, it.tn * C::BN, &full_bar[stage]);
-            tma_load_2d(sW(stage, 1), &tmW, 2 * kb * C::BK + C::BK, it.tn * C::BN, &full_bar[stage]);
+            tma_load_2d(sW(stage, 0), &tmW, xh, it.tn * C::BN, &full_bar[stage]);
+            tma_load_2d(sW(stage, 1), &tmW, xh + 64, it.tn * C::BN, &full_bar[stage]);
           } else {
-            tma_load_2d(sW(stage, 0), &tmW, kb * C::BK, it.tn * C::BN, &full_bar[stage]);
+            tma_load_2d(sW(stage, 0), &tmW, k0, it.tn * C::BN, &full_bar[stage]);
           }
           if (++stage == C::STAGES) {
             stage = 0;
@@ -201,12 +207,13 @@ __global__ void __launch_bounds__(WoGemmT<BM, WT>::THREADS, 1)
           tc_fence_after();
           const uint32_t ah = smem_u32(sAh(stage)), al = smem_u32(sAl(stage));
           const uint32_t w0 = smem_u32(sW(stage, 0)), w1 = smem_u32(sW(stage, WT - 1));
+          auto desc = [](uint32_t a) { return BK == 64 ? desc_kmajor_sw128(a) : desc_kmajor_sw64(a); };
 #pragma unroll
           for (int kk = 0; kk < C::BK / 16; ++kk) {  // K = 16 f16 per MMA: 32 bytes of each row
-            const uint64_t dah = desc_kmajor_sw128(ah + kk * 32), dal = desc_kmajor_sw128(al + kk * 32);
-            const uint64_t dw0 = desc_kmajor_sw128(w0 + kk * 32);
+            const uint64_t dah = desc(ah + kk * 32), dal = desc(al + kk * 32);
+            const uint64_t dw0 = desc(w0 + kk * 32);
             mma_f16(d, dw0, dah, idesc, (kb | kk) != 0 ? 1u : 0u);
-            if (WT == 2) mma_f16(d, desc_kmajor_sw128(w1 + kk * 32), dah, idesc, 1u);
+            if (WT == 2) mma_f16(d, desc(w1 + kk * 32), dah, idesc, 1u);
             mma_f16(d, dw0, dal, idesc, 1u);
           }
           tc_commit(&empty_bar[stage]);

@@ -307,6 +307,13 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// The same for a K-major tile with the 64-byte swizzle: rows of 64 bytes,
+// 8-row core groups 512 bytes apart, layout type 4.
+__device__ __forceinline__ uint64_t desc_kmajor_sw64(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+
 // Descriptor for an MN-major operand tile with the 128-byte swizzle: each
 // 128-byte row holds 128 bytes of the MN dimension for one k; 8 consecutive
 // k rows form a 1024-byte swizzle atom.  lbo = byte distance between

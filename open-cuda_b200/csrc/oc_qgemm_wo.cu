@@ -22,6 +22,13 @@
 namespace oc {
 
 constexpr int kWoSkinnyM = 16;
+// k per pipeline stage of the tensor-core GEMM (oc_gemm_wo.cuh): 64-k
+// stages (2-3 of them) and 32-k stages (4-6, 64-byte swizzle) measured the
+// same within 5 % (2048 x 768 x 3072: 31 / 34 us INT8, 40 / 39 us INT4;
+// 4096 x 3584 x 18944: 1066 / 1010 us, 1587 / 1598 us): the stage depth is
+// not what bounds it.
+constexpr int kWoBK = 64;
+constexpr CUtensorMapSwizzle kWoSwizzle = kWoBK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
 // Expanded weight terms of one column chunk stay below this many bytes, so
 // that they are written and read back in L2.
 constexpr size_t kWoChunkBytes = (size_t)40 << 20;
@@ -106,13 +113,13 @@ static bool wo_tc_ok(int bits, int m, int k, int group, const void* A) {
 template <int BM, int WT>
 static int launch_wo_gemm(const CUtensorMap& ta, const CUtensorMap& tw, int m, int nc, int k, int ldy,
                           const float* icm, const float* colf, const float* bias, float* Yc, cudaStream_t s) {
-  using C = WoGemmT<BM, WT>;
-  auto kern = gemm_wo_kernel<BM, WT>;
+  using C = WoGemmT<BM, WT, kWoBK>;
+  auto kern = gemm_wo_kernel<BM, WT, kWoBK>;
   if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_wo_kernel) failed");
   const int sms = std::max(1, sm_count());
   const int tiles_m = (m + BM - 1) / BM, tiles = tiles_m * ((nc + C::BN - 1) / C::BN);
-  const int nrb = k / C::BK;
+  const int nrb = k / C::BK;  // k % 64 == 0 on this path
   // Split K only for long K where the tiles do not fill the GPU: every tile
   // then, in up to 8 slices (the last slice's CTA adds the others in slice
   // order).  Short K is not split: a slice writes a whole tile of partial
@@ -156,7 +163,7 @@ static int launch_wo_gemm(const CUtensorMap& ta, const CUtensorMap& tw, int m, i
 // ready counters in the preparation launch): the same rule as launch_wo_gemm.
 static int wo_nsplit(int m, int nc, int k, int bm) {
   const int sms = std::max(1, sm_count());
-  const int tiles = (m + bm - 1) / bm * ((nc + 127) / 128), nrb = k / 64;
+  const int tiles = (m + bm - 1) / bm * ((nc + 127) / 128), nrb = k / kWoBK;
   if (tiles < sms && k >= 2048 && std::min(nrb, std::min(8, sms / tiles)) > 1) return tiles;
   return 0;
 }
@@ -182,7 +189,7 @@ static int run_wo_gemm(int m, int n, int k, int group, const float* A, const voi
   const int bm = rounds(192) * 875 < rounds(256) * 1030 ? 192 : 256;
   CUtensorMap ta;
   int rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
-                        64, bm, CU_TENSOR_MAP_SWIZZLE_128B);
+                        kWoBK, bm, kWoSwizzle);
   if (rc) return rc;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -217,7 +224,7 @@ static int run_wo_gemm(int m, int n, int k, int group, const float* A, const voi
     }
     CUtensorMap tw;
     rc = make_tmap_2d(&tw, wx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * WT, (uint64_t)ncur,
-                      (uint64_t)k * WT * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+                      (uint64_t)k * WT * 2, kWoBK, 128, kWoSwizzle);
     if (rc) return rc;
     const float* colf = WT == 2 ? icn : sw + n0;
     const float* bc = bias ? bias + n0 : nullptr;

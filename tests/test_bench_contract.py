@@ -25,7 +25,7 @@ def _args(workload, steps, warmup):
 
 
 def test_every_workload_has_one_description():
-    choices = {"qgemm", "sgemm", "gpt2", "int4", "moe", "mla"}
+    choices = {"qgemm", "qgemm_a8", "sgemm", "gpt2", "int4", "moe", "mla"}
     assert set(bench.WORKLOADS) == choices
     assert set(bench.REF) == choices
 
