@@ -59,6 +59,8 @@ WO_SHAPES = [
     (40, 96, 72), (20, 160, 96),
     # K % 16 != 0: the scalar kernel
     (5, 100, 33), (20, 100, 96),
+    # skinny GEMV: columns not a multiple of 16, one 32-k chunk, long K; INT8 with K % 32 == 16
+    (12, 256, 130), (9, 32, 17), (2, 3584, 18944), (6, 48, 80),
 ]
 
 
@@ -78,7 +80,8 @@ def test_weight_only_matches_oracle(oc, oracle, bits, m, k, n):
     assert worst <= 10 * REL_FRO, worst
 
 
-@pytest.mark.parametrize("m,k,n,group", [(7, 96, 50, 40), (30, 128, 70, 48), (24, 256, 130, 64), (24, 256, 130, 128)])
+@pytest.mark.parametrize("m,k,n,group", [(7, 96, 50, 40), (30, 128, 70, 48), (24, 256, 130, 64), (24, 256, 130, 128),
+                                         (12, 256, 130, 64), (3, 512, 50, 128), (5, 96, 40, 48)])
 def test_w4_group_sizes(oc, oracle, m, k, n, group):
     # groups that straddle weight rows (40, 48: the flat quantization of the
     # reference) and groups of 64 / 128 on the tensor-core path
