@@ -10,11 +10,14 @@
 //    memory (rows padded to d+1 floats: conflict-free column reads); f32
 //    throughout.  The reference's block_size only tiles its loops; this
 //    kernel uses its own 64-key tiles (same result up to rounding).
+//    Head dims 64 and 128 run on the tcgen05 tensor cores instead
+//    (oc_flash_tc.cuh: f16 hi / lo terms, S and O in tensor memory).
 //  * oc_sdpa: the unfused scaled_dot_product_attention (blas:411-540):
 //    scores = Q.K^T / sqrt(d) on oc_sgemm, row softmax, P.V on oc_sgemm.
 #include <algorithm>
 #include <cmath>
 
+#include "oc_flash_tc.cuh"
 #include "oc_internal.h"
 
 namespace oc {
@@ -138,8 +141,25 @@ __global__ void __launch_bounds__(kFaRows * 32)
   }
 }
 
+template <int D>
+static int launch_flash_tc(const float* q, const float* k, const float* v, float* o, int bh, int sq, int skv,
+                           float scale, int causal, cudaStream_t s) {
+  using C = FlashTc<D>;
+  auto kern = flash_tc_kernel<D>;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
+    return fail(OC_ERR_LAUNCH_FAILED, "flash_tc_kernel: shared memory attribute refused");
+  dim3 grid((sq + C::BQ - 1) / C::BQ, bh);
+  kern<<<grid, C::THREADS, C::SMEM, s>>>(q, k, v, o, sq, skv, scale, causal, device_status_word());
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "flash_tc_kernel");
+}
+
 int launch_flash(const float* q, const float* k, const float* v, float* o, int bh, int sq, int skv, int d,
                  float scale, int causal, cudaStream_t s) {
+  if ((d == 64 || d == 128) && is_sm100() && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) &&
+      bh <= 65535)
+    return d == 64 ? launch_flash_tc<64>(q, k, v, o, bh, sq, skv, scale, causal, s)
+                   : launch_flash_tc<128>(q, k, v, o, bh, sq, skv, scale, causal, s);
   const size_t smem = (size_t)(2 * kFaTile * (d + 1) + kFaRows * d) * sizeof(float);
   dim3 grid((sq + kFaRows - 1) / kFaRows, bh);
   auto go = [&](auto kern) {

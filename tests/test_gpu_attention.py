@@ -190,3 +190,49 @@ def test_launch_kernel_by_name(oc, oracle):
     with pytest.raises(ValueError):
         dev.launch_kernel("softmax", [K.ptr(12345), K.usize(1), K.usize(1)])
     dev.close()
+
+
+def _ref_rows(oracle, q, k, v, causal):
+    bh, sq, d = q.shape
+    skv = k.shape[1]
+    ref = np.zeros((bh, sq, d), np.float32)
+    for h in range(bh):
+        if not causal and sq == skv:
+            ref[h] = oracle.flash_attention(q[h].ravel(), k[h].ravel(), v[h].ravel(), sq, d, 64).reshape(sq, d)
+            continue
+        for i in range(sq):
+            n = i + (skv - sq) + 1 if causal else skv
+            ref[h, i] = oracle.attend_one(q[h, i], k[h, :n].ravel(), v[h, :n].ravel(), n, d, flash=True, block=64)
+    return ref
+
+
+@pytest.mark.parametrize("bh,sq,skv,d,causal", [(4, 1024, 1024, 64, True), (3, 700, 1300, 128, False),
+                                               (2, 257, 1000, 64, True), (5, 128, 128, 128, True),
+                                               (2, 1, 300, 64, False), (1, 1000, 1000, 64, False)])
+def test_flash_tensor_core_shapes(oc, oracle, bh, sq, skv, d, causal):
+    """Head dims 64 and 128 run on the tcgen05 kernel (f16 hi / lo terms of
+    Q, K, V and P, S and O in tensor memory): ragged query / key tiles,
+    causal and cross lengths, 1e-5 relative Frobenius against the oracle's
+    flash attention (blas:589-678)."""
+    q = synth.normal(bh + sq, bh * sq * d, 0, 1).reshape(bh, sq, d)
+    k = synth.normal(bh + skv + 1, bh * skv * d, 0, 1).reshape(bh, skv, d)
+    v = synth.normal(bh + skv + 2, bh * skv * d, 0, 1).reshape(bh, skv, d)
+    got = oc.flash_attention_fwd(cu(q), cu(k), cu(v), causal=causal).cpu().numpy()
+    ref = _ref_rows(oracle, q, k, v, causal)
+    assert rel(got, ref) < TOL, rel(got, ref)
+    worst = max(rel(got[h, i], ref[h, i]) for h in range(bh) for i in range(0, sq, max(1, sq // 50)))
+    assert worst < 10 * TOL, worst
+
+
+@pytest.mark.parametrize("qs,ks,vs", [(1e-3, 1e-3, 1e-20), (30.0, 1.0, 1e6), (1e-6, 1e6, 1.0), (1.0, 1.0, 1e-30)])
+def test_flash_tensor_core_value_range(oc, oracle, qs, ks, vs):
+    # per-row powers of two for Q and K, per-tile for V: large and tiny
+    # magnitudes keep their precision; a very peaked softmax (qs = 30)
+    bh, sq, d = 2, 200, 64
+    q = (synth.normal(5, bh * sq * d, 0, 1) * np.float32(qs)).reshape(bh, sq, d).astype(np.float32)
+    k = (synth.normal(6, bh * sq * d, 0, 1) * np.float32(ks)).reshape(bh, sq, d).astype(np.float32)
+    v = (synth.normal(7, bh * sq * d, 0, 1) * np.float32(vs)).reshape(bh, sq, d).astype(np.float32)
+    got = oc.flash_attention_fwd(cu(q), cu(k), cu(v)).cpu().numpy()
+    ref = _ref_rows(oracle, q, k, v, False)
+    assert np.all(np.isfinite(got))
+    assert rel(got, ref) < TOL, rel(got, ref)
