@@ -22,18 +22,17 @@
 // runs on the transcendental unit: the splits are bit masks and subtractions
 // and the f16 packing is cvt.rn.f16x2.f32; only 2^x uses it.
 //
-// One CTA per (head, 128-query tile), 288 threads:
+// One CTA per (head, 128-query tile), 416 threads:
 //   warp 0      TMEM allocator + MMA issuer (lane 0)
-//   warps 1..4  converters: the Q tile once, then each K and V tile (f32 from
+//   warps 1..8  converters: the Q tile once, then each K and V tile (f32 from
 //               global memory, coalesced, -> f16 terms in the 128-byte
 //               swizzled layout); K and V have their own full / empty
 //               barriers, so K(t+1) is converted while the softmax of tile t
 //               runs and V(t+1) while S(t+1) is computed
-//   warps 5..8  softmax: thread = query row = TMEM lane; S' from TMEM, P
-//               terms back to TMEM, o = o * corr + O' / c_v in TMEM
-// Tensor memory (512 columns): S' [0, 128), O' [128, 128 + d), P hi / lo
-// [256, 320) / [320, 384), the running o in [192, 256) (d = 64) or
-// [384, 512) (d = 128).  Every wait is bounded (oc_ptx.cuh).
+//   warps 9..12 softmax: thread = query row = TMEM lane; S' from TMEM, P
+//               terms back to TMEM over S', o = o * corr + O' / c_v in TMEM
+// Tensor memory: S' / P [0, 128), O' [128, 128 + d), the running o
+// [128 + d, 128 + 2d).  Every wait is bounded (oc_ptx.cuh).
 #pragma once
 #include <cuda_fp16.h>
 
@@ -47,12 +46,14 @@ struct FlashTc {
   static constexpr int BQ = 128, BKV = 128;
   static constexpr int PANEL = 128 * 128;                // bytes of one 64-feature panel of a 128-row tile
   static constexpr int T_BYTES = 128 * D * 2;            // one f16 term of a 128-row tile (Q, K or V)
-  static constexpr int THREADS = 32 * 9;
-  static constexpr int S_COL = 0, O_COL = 128, PH_COL = 256, PL_COL = 320, TMEM_COLS = 512;
-  static constexpr int A_COL = D == 64 ? 192 : 384;     // running output o (f32, d columns)
+  static constexpr int THREADS = 32 * (1 + 8 + 4);  // MMA, converters, softmax
+  // S' [0, 128) (P hi / lo written over it chunk by chunk), O' [128, 128 + d),
+  // running output o [128 + d, 128 + 2d)
+  static constexpr int S_COL = 0, O_COL = 128, A_COL = 128 + D, TMEM_COLS = D == 64 ? 256 : 512;
+  static constexpr int MIN_BLOCKS = 1;
   static constexpr int NBAR = 10;
   static constexpr size_t SMEM =
-      1024 + 6 * (size_t)T_BYTES + (size_t)(BQ + 2 * BKV + 2 + 8) * 4 + NBAR * 8 + 16;
+      1024 + 6 * (size_t)T_BYTES + (size_t)(BQ + 2 * BKV + 2 + 16) * 4 + NBAR * 8 + 16;
   static_assert(D == 64 || D == 128, "head dims");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
@@ -126,24 +127,27 @@ __device__ __forceinline__ void fa_load_rows(float4 (&x)[NB], const float* __res
 }
 
 // Rows [0, 128) of a [rows][D] f32 block (rows >= valid read as zero) -> hi /
-// lo terms of a 128-row tile.  Converter warp w (0..3) owns rows
-// [32w, 32w + 32); D / 4 lanes read one row (a coalesced segment), each lane
+// lo terms of a 128-row tile.  Converter warp w (0..kFaConv-1) owns rows
+// [16w, 16w + 16); D / 4 lanes read one row (a coalesced segment), each lane
 // one float4, all of the warp's rows loaded before the first is converted.
-// Row mode (Q, K): c per row, sign / c stored to inv[row].  Tile mode (V): c
-// from the tile's max |x| (the four warps' partial maxima through `part` and
-// the `vmax` barrier, phase `ph`), 1 / c stored to *inv.  Returns false when
-// the barrier wait gave up.
+// Row mode (Q, K): c per row, sign / c stored to inv[row]; the rows' maxima
+// are reduced round by round across all rows, so the shuffles pipeline.  Tile
+// mode (V): c from the tile's max |x| (the warps' partial maxima through
+// `part` and the `vmax` barrier, phase `ph`), 1 / c stored to *inv.  Returns
+// false when the barrier wait gave up.
+constexpr int kFaConv = 8;  // converter warps
 template <int D, bool TILE>
 __device__ __forceinline__ bool fa_convert_tile(const float* __restrict__ src, int valid, uint8_t* thi, uint8_t* tlo,
                                                 float* inv, float sign, int w, int lane, float* part,
                                                 uint64_t* vmax, uint32_t ph, volatile int* abort_flag) {
-  constexpr int LPR = D / 4;     // lanes per row
-  constexpr int RPS = 32 / LPR;  // rows per warp step
-  constexpr int NS = 32 / RPS;   // steps per warp (32 rows)
+  constexpr int RPW = 128 / kFaConv;  // rows per warp
+  constexpr int LPR = D / 4;          // lanes per row
+  constexpr int RPS = 32 / LPR;       // rows per warp step
+  constexpr int NS = RPW / RPS;       // steps per warp
   const int q4 = lane % LPR, ro = lane / LPR;
   float4 x[NS];
-  fa_load_rows<D, NS>(x, src, valid, w * 32 + ro, RPS, q4);
-  float c = 1.0f;
+  fa_load_rows<D, NS>(x, src, valid, w * RPW + ro, RPS, q4);
+  float cr[NS];
   if constexpr (TILE) {
     float mx = 0.0f;
 #pragma unroll
@@ -155,24 +159,33 @@ __device__ __forceinline__ bool fa_convert_tile(const float* __restrict__ src, i
       mbar_arrive(vmax);
     }
     if (!mbar_wait(vmax, ph, abort_flag)) return false;
-    const int ce = fa_range_exp(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])));
-    c = exp2_int(ce);
+    float m = part[0];
+#pragma unroll
+    for (int j = 1; j < kFaConv; ++j) m = fmaxf(m, part[j]);
+    const int ce = fa_range_exp(m);
+#pragma unroll
+    for (int s = 0; s < NS; ++s) cr[s] = exp2_int(ce);
     if (w == 0 && lane == 0) *inv = exp2_int(-ce);
+  } else {
+    float mx[NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) mx[s] = fa_absmax4(x[s]);
+#pragma unroll
+    for (int off = LPR / 2; off > 0; off >>= 1)
+#pragma unroll
+      for (int s = 0; s < NS; ++s) mx[s] = fmaxf(mx[s], __shfl_xor_sync(0xffffffffu, mx[s], off));
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      const int ce = fa_range_exp(mx[s]);
+      if (q4 == 0) inv[w * RPW + s * RPS + ro] = __fmul_rn(sign, exp2_int(-ce));
+      cr[s] = exp2_int(ce);
+    }
   }
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
-    const int r = w * 32 + s * RPS + ro;
-    float cr = c;
-    if constexpr (!TILE) {
-      float mx = fa_absmax4(x[s]);
-#pragma unroll
-      for (int off = LPR / 2; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const int ce = fa_range_exp(mx);
-      if (q4 == 0) inv[r] = __fmul_rn(sign, exp2_int(-ce));
-      cr = exp2_int(ce);
-    }
+    const int r = w * RPW + s * RPS + ro;
     uint2 hi, lo;
-    fa_split4(x[s], cr, hi, lo);
+    fa_split4(x[s], cr[s], hi, lo);
     const uint32_t off = fa_tile_off(r, 4 * q4);
     *reinterpret_cast<uint2*>(thi + off) = hi;
     *reinterpret_cast<uint2*>(tlo + off) = lo;
@@ -228,7 +241,7 @@ __device__ __forceinline__ float fa_p_chunk(const uint32_t (&r)[32], const float
 }
 
 template <int D>
-__global__ void __launch_bounds__(FlashTc<D>::THREADS, 1)
+__global__ void __launch_bounds__(FlashTc<D>::THREADS, FlashTc<D>::MIN_BLOCKS)
     flash_tc_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                     float* __restrict__ o, int sq, int skv, float scale, int causal, int* status) {
   using C = FlashTc<D>;
@@ -244,12 +257,12 @@ __global__ void __launch_bounds__(FlashTc<D>::THREADS, 1)
   float* icq = reinterpret_cast<float*>(k_lo + C::T_BYTES);  // [128]   1 / c_q per query row
   float* ick = icq + C::BQ;                                   // [2][128] sign(scale) / c_k per key row, per parity
   float* icv = ick + 2 * C::BKV;                              // [2]      1 / c_v of the V tile, per parity
-  float* vpart = icv + 2;                                     // [2][4]   converter warps' max |v|, per parity
-  uint64_t* bars = reinterpret_cast<uint64_t*>(vpart + 8);
-  uint64_t* q_full = bars;        // converters (4 warps) -> MMA
-  uint64_t* k_full = bars + 1;    // converters (4 warps) -> MMA, per tile
+  float* vpart = icv + 2;                                     // [2][8]   converter warps' max |v|, per parity
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vpart + 2 * kFaConv);
+  uint64_t* q_full = bars;        // converters (8 warps) -> MMA
+  uint64_t* k_full = bars + 1;    // converters (8 warps) -> MMA, per tile
   uint64_t* k_empty = bars + 2;   // MMA commit (S done) -> converters
-  uint64_t* v_full = bars + 3;    // converters (4 warps) -> MMA, per tile
+  uint64_t* v_full = bars + 3;    // converters (8 warps) -> MMA, per tile
   uint64_t* v_empty = bars + 4;   // MMA commit (PV done) -> converters
   uint64_t* s_full = bars + 5;    // MMA commit (S done) -> softmax
   uint64_t* p_full = bars + 6;    // softmax (4 warps) -> MMA
@@ -273,16 +286,16 @@ __global__ void __launch_bounds__(FlashTc<D>::THREADS, 1)
   const int ntiles = kv_end > 0 ? (kv_end + C::BKV - 1) / C::BKV : 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 4);
-    mbar_init(k_full, 4);
+    mbar_init(q_full, kFaConv);
+    mbar_init(k_full, kFaConv);
     mbar_init(k_empty, 1);
-    mbar_init(v_full, 4);
+    mbar_init(v_full, kFaConv);
     mbar_init(v_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(p_full, 4);
     mbar_init(o_full, 1);
     mbar_init(o_empty, 4);
-    mbar_init(vmax, 4);
+    mbar_init(vmax, kFaConv);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -336,15 +349,18 @@ __global__ void __launch_bounds__(FlashTc<D>::THREADS, 1)
           const uint32_t off = (uint32_t)kk * 2048;
           const uint64_t vh = desc_mnmajor_sw128(smem_u32(v_hi) + off, C::PANEL, 1024);
           const uint64_t vl = desc_mnmajor_sw128(smem_u32(v_lo) + off, C::PANEL, 1024);
-          mma_f16_ta(tmem + C::O_COL, tmem + C::PH_COL + kk * 8, vh, idesc_o, kk != 0 ? 1u : 0u);
-          mma_f16_ta(tmem + C::O_COL, tmem + C::PH_COL + kk * 8, vl, idesc_o, 1u);
-          mma_f16_ta(tmem + C::O_COL, tmem + C::PL_COL + kk * 8, vh, idesc_o, 1u);
+          // P of keys [16 kk, 16 kk + 16): chunk kk / 2 of S's columns, hi in
+          // its first 16 columns, lo in the next 16
+          const uint32_t pcol = tmem + C::S_COL + (uint32_t)(kk >> 1) * 32 + (uint32_t)(kk & 1) * 8;
+          mma_f16_ta(tmem + C::O_COL, pcol, vh, idesc_o, kk != 0 ? 1u : 0u);
+          mma_f16_ta(tmem + C::O_COL, pcol, vl, idesc_o, 1u);
+          mma_f16_ta(tmem + C::O_COL, pcol + 16, vh, idesc_o, 1u);
         }
         tc_commit(o_full);
         tc_commit(v_empty);
       }
     }
-  } else if (warp <= 4) {
+  } else if (warp <= kFaConv) {
     const int w = warp - 1;
     const float ksign = scale < 0.0f ? -1.0f : 1.0f;
     fa_convert_tile<D, false>(qb, qvalid, q_hi, q_lo, icq, 1.0f, w, lane, nullptr, nullptr, 0, abort_flag);
@@ -365,7 +381,7 @@ __global__ void __launch_bounds__(FlashTc<D>::THREADS, 1)
       if (lane == 0) mbar_arrive(k_full);
       if (!mbar_wait(v_empty, ph ^ 1u, abort_flag) ||
           !fa_convert_tile<D, true>(vb + (size_t)j0 * D, kvalid, v_hi, v_lo, icv + (t & 1), 1.0f, w, lane,
-                                    vpart + (t & 1) * 4, vmax, ph, abort_flag)) {
+                                    vpart + (t & 1) * kFaConv, vmax, ph, abort_flag)) {
         kernel_fail(status, abort_flag, kDevTimeoutProducer);
         goto done;
       }
@@ -425,8 +441,9 @@ __global__ void __launch_bounds__(FlashTc<D>::THREADS, 1)
         const int cl = plim - cb * 32;
         psum = __fadd_rn(psum, (cl >= 32 && !guard) ? fa_p_chunk<false>(r, ik + cb * 32, rq2, nb, cl, ph16, pl16)
                                                     : fa_p_chunk<true>(r, ik + cb * 32, rq2, nb, cl, ph16, pl16));
-        tmem_st16(lane_base + C::PH_COL + cb * 16, ph16);
-        tmem_st16(lane_base + C::PL_COL + cb * 16, pl16);
+        // over S' chunk cb, which this thread has read
+        tmem_st16(lane_base + C::S_COL + cb * 32, ph16);
+        tmem_st16(lane_base + C::S_COL + cb * 32 + 16, pl16);
       }
       tmem_st_wait();
       tc_fence_before();
