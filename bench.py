@@ -20,6 +20,8 @@ Other workloads (same JSON contract, one line each):
             INT8) + 1 shared, top-8; experts sharded over the ranks with NCCL
             all-to-all dispatch/combine (strong scaling)
   mla       MLA: KV[16384 x 7168] -> latent 512 -> K and V [16384 x 16384]
+  flash     fused multi-head attention, 96 x 2048 x 64 and 32 x 4096 x 128,
+            causal and full (tcgen05, f16 hi / lo operand terms)
 
 value   = algorithmic work of one step / device time (CUDA events on the
           launching stream, max over ranks), whole job.
@@ -55,7 +57,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qgemm", choices=["qgemm", "qgemm_a8", "sgemm", "gpt2", "int4", "moe", "mla"])
+    ap.add_argument("--workload", default="qgemm", choices=["qgemm", "qgemm_a8", "sgemm", "gpt2", "int4", "moe", "mla",
+                                                           "flash"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-once", action="store_true",
                     help="run one warm pass of the workload's kernels and exit (for ncu launch lists)")
@@ -640,6 +643,7 @@ def run_qgemm(ctx):
     graphs = []
     extra["gemv_cold_hbm"] = qgemm_cold_gemv(ctx)
     extra["gpt2_batch1"] = qgemm_gpt2_batch1(ctx)
+    extra["flash_attention"] = flash_cases(ctx)
     if ctx.world > 1:
         extra["sharded"] = qgemm_sharded(ctx)
     cpu = cpu_qgemm() if ctx.rank == 0 and not args.no_cpu_baseline else None
@@ -1367,6 +1371,135 @@ def run_mla(ctx):
 
 
 # ----------------------------------------------------------------------------
+# flash: fused multi-head attention on the tensor cores
+# ----------------------------------------------------------------------------
+
+# (batch * heads, seq, head_dim, causal); q_len = kv_len = seq
+F_CASES = ((96, 2048, 64, True), (96, 2048, 64, False), (32, 4096, 128, True), (32, 4096, 128, False))
+F_METRIC = ("fused attention TFLOP/s (f32; [batch*heads] x seq x head_dim = 96x2048x64 and 32x4096x128, "
+            "causal and full)")
+
+
+def f_flops(case) -> float:
+    """4 * d flops per visible (query, key) pair: Q.K^T and P.V."""
+    bh, s, d, causal = case
+    pairs = s * (s + 1) / 2 if causal else s * s
+    return 4.0 * bh * pairs * d
+
+
+def f_tensor_peak(peaks) -> float:
+    """Dense f16 tensor rate (= the measured bf16 rate) / 3: three MMAs per
+    f32 product (hi.hi + hi.lo + lo.hi)."""
+    return peaks[1] / 2.0 / 3.0
+
+
+def cpu_flash(target_s: float = 2.0):
+    """The reference's flash_attention (blas:589-678, full attention, block
+    64) restated in C, query rows spread over all host threads, on whole
+    heads of 2048 x 64."""
+    import oracle
+    import synth
+
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    s, d = 2048, 64
+    q = synth.normal(95, s * d, 0.0, 1.0)
+    k = synth.normal(96, s * d, 0.0, 1.0)
+    v = synth.normal(97, s * d, 0.0, 1.0)
+    t0 = time.perf_counter()
+    oracle.flash_attention(q, k, v, s, d, 64)
+    one = time.perf_counter() - t0
+    n = max(1, min(64, int(target_s / max(one, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        oracle.flash_attention(q, k, v, s, d, 64)
+    dt = time.perf_counter() - t0
+    return {"value": 4.0 * s * s * d * n / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{n} heads of {s} x {d} (full attention, block 64), rows over {cores} threads"}
+
+
+def flash_cases(ctx, reps: int = 5):
+    """Device time of each F_CASES launch (median of 3 x `reps`), its TFLOP/s
+    and fraction of the f16 tensor rate / 3, beside torch's f32
+    scaled_dot_product_attention on the same tensors (a library kernel,
+    for context)."""
+    torch, oc = ctx.torch, ctx.oc
+    F = torch.nn.functional
+    out = {}
+    peak = f_tensor_peak(ctx.peaks)
+    for i, case in enumerate(F_CASES):
+        bh, s, d, causal = case
+        g = torch.Generator(device=ctx.device).manual_seed(100 + i)
+        q, k, v = (torch.randn(bh, s, d, generator=g, device=ctx.device) for _ in range(3))
+        us = ctx.kernel_us(lambda: oc.flash_attention_fwd(q, k, v, causal=causal), reps=reps, graph=False)
+        us_t = ctx.kernel_us(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal), reps=reps,
+                             graph=False)
+        tf = f_flops(case) / us / 1e6
+        out[f"{bh}x{s}x{d}{'_causal' if causal else ''}"] = {
+            "us": round(us, 1), "TFLOPs": round(tf, 1), "frac_tensor": round(tf / peak, 4),
+            "kernel": f"flash_tc_kernel<{d}>", "torch_sdpa_f32_us": round(us_t, 1)}
+        del q, k, v
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_flash(ctx):
+    torch, oc, args = ctx.torch, ctx.oc, ctx.args
+    gen = torch.Generator(device=ctx.device).manual_seed(100)
+    data = [tuple(torch.randn(bh, s, d, generator=gen, device=ctx.device) for _ in range(3))
+            for (bh, s, d, _c) in F_CASES]
+
+    def step(i):
+        for (q, k, v), case in zip(data, F_CASES):
+            oc.flash_attention_fwd(q, k, v, causal=case[3])
+        return len(F_CASES)
+
+    with torch.cuda.stream(ctx.stream):
+        for i in range(1 if args.profile_once else max(3, args.warmup)):
+            launches = step(i)
+    torch.cuda.synchronize()
+    if args.profile_once:
+        return
+    steps = max(3, min(args.steps, 20))
+    ms_step, clk = ctx.timed(step, steps)
+    total = sum(f_flops(c) for c in F_CASES)
+    value = total * ctx.world / (ms_step * 1e-3) / 1e12
+    per = flash_cases(ctx)
+    big = F_CASES[3]
+    key = f"{big[0]}x{big[1]}x{big[2]}"
+    peak = f_tensor_peak(ctx.peaks)
+    us = per[key]["us"]
+    roof = {"bound": "tensor", "kernel": f"flash_tc_kernel<{big[2]}> {key} full", "achieved": per[key]["TFLOPs"],
+            "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(per[key]["TFLOPs"] / peak, 4),
+            "peak_source": f"{ctx.peaks[3]} bf16_tflops / 3 (f16 MMAs at the bf16 rate, three per f32 product)",
+            "algorithmic_ops": int(f_flops(big)), "algorithmic_bytes": int(4 * 4 * big[0] * big[1] * big[2]),
+            "us_per_launch": us, "traffic": None}
+    # e2e: pinned host inputs -> device, the public call, outputs -> host
+    host = [tuple(t.cpu().pin_memory() for t in qkv) for qkv in data]
+    outs = [torch.empty_like(qkv[0], device="cpu").pin_memory() for qkv in host]
+
+    def e2e_step():
+        for (hq, hk, hv), ho, case in zip(host, outs, F_CASES):
+            q, k, v = (t.to(ctx.device, non_blocking=True) for t in (hq, hk, hv))
+            ho.copy_(oc.flash_attention_fwd(q, k, v, causal=case[3]), non_blocking=True)
+        torch.cuda.synchronize()
+
+    e2e_step()
+    t0 = time.perf_counter()
+    e2e_step()
+    t_e2e = ctx.max_over_ranks(time.perf_counter() - t0)
+    nbytes = sum(4 * bh * s * d for (bh, s, d, _c) in F_CASES)
+    e2e = {"value": total * ctx.world / t_e2e / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * nbytes,
+           "d2h_bytes_per_step": nbytes, "ms_per_step": round(t_e2e * 1e3, 2)}
+    cpu = cpu_flash() if ctx.rank == 0 and not args.no_cpu_baseline else None
+    config = {"workload": WORKLOADS["flash"], "parallelism": f"replicas x{ctx.world}",
+              "l2": "q, k, v of each case 151-201 MB > 126 MB L2"}
+    emit(ctx, F_METRIC, value, "TFLOP/s", ms_step, "f32 (f16 hi / lo operand terms on tcgen05, f32 accumulate)",
+         config, launches * steps, roof, clk, e2e, cpu, {"per_kernel": per})
+    ctx.close()
+
+
+# ----------------------------------------------------------------------------
 # reference arm
 # ----------------------------------------------------------------------------
 
@@ -1384,6 +1517,8 @@ WORKLOADS = {
     "moe": "config-5 MoE: 8192 tokens x d 7168, 256 experts (d_ff 2048, INT8 per-channel) + 1 shared, top-8 over "
            "N(0,1) router logits, grouped W8A8 GEMMs",
     "mla": "config-5 MLA: KV[16384x7168] . down[7168x512] -> latent; latent . up_K/up_V [512x16384], N(0,0.02) weights",
+    "flash": "fused attention (flash_attention, blas:589-678, multi-head): [batch*heads] x seq x head_dim = "
+             "96 x 2048 x 64 and 32 x 4096 x 128, causal and full, N(0,1) q/k/v, scale 1/sqrt(head_dim)",
 }
 
 
@@ -1399,6 +1534,7 @@ REF = {
     "moe": (cpu_moe, "MoE block TOPS (8192 tokens, 256 experts top-8 + shared, INT8)", "TOPS",
             lambda v: e_ops() / (v * 1e12) * 1e3),
     "mla": (cpu_mla, "MLA compress+decompress TFLOP/s (3xTF32)", "TFLOP/s", lambda v: l_flops() / (v * 1e12) * 1e3),
+    "flash": (cpu_flash, F_METRIC, "TFLOP/s", lambda v: sum(f_flops(c) for c in F_CASES) / (v * 1e12) * 1e3),
 }
 
 
@@ -1407,7 +1543,7 @@ def run_reference(args):
         return
     fn, metric, unit, ms_of = REF[args.workload]
     vals, last = [], None
-    heavy = args.workload in ("gpt2", "moe", "int4")  # samples of 10 s and more: fewer of them
+    heavy = args.workload in ("gpt2", "moe", "int4", "flash")  # samples of seconds: fewer of them
     n = max(1, min(args.steps, 3)) if heavy else args.steps
     w = min(args.warmup, 3) if heavy else args.warmup
     for i in range(w + n):
@@ -1435,7 +1571,7 @@ def main():
         return run_reference(args)
     ctx = Ctx(args)
     {"qgemm": run_qgemm, "qgemm_a8": run_qgemm_a8, "sgemm": run_sgemm, "gpt2": run_gpt2, "int4": run_int4, "moe": run_moe,
-     "mla": run_mla}[args.workload](ctx)
+     "mla": run_mla, "flash": run_flash}[args.workload](ctx)
 
 
 if __name__ == "__main__":

@@ -186,7 +186,8 @@ int oc_softmax_rows(float *data, int rows, int cols, void *stream);
  * scale 1/sqrt(head_dim) and an online softmax (flash_attention,
  * blas:589-678).  block_size must be > 0; head_dim and block_size <= 256
  * (the limits the reference's shader enforces,
- * crates/opencuda-vulkan/src/real.rs:524-533).  The kernel tiles keys by 64
+ * crates/opencuda-vulkan/src/real.rs:524-533).  The kernels tile keys by
+ * 128 (head_dim 64 and 128: tcgen05 tensor cores) or 64 (other head dims)
  * regardless of block_size; results match the reference up to rounding. */
 int oc_flash_attention(const float *q, const float *k, const float *v, float *o, int seq_len, int head_dim,
                        int block_size, void *stream);
@@ -194,7 +195,11 @@ int oc_flash_attention(const float *q, const float *k, const float *v, float *o,
  * [batch_heads][kv_len][head_dim], any scale; causal = 1 lets query i see
  * keys j <= i + (kv_len - q_len).  Covers multi-head SDPA (BERT,
  * crates/open-cuda-bert/src/lib.rs:141-167) and q_len != kv_len cross
- * attention (crates/open-cuda-whisper/src/lib.rs:288-300). */
+ * attention (crates/open-cuda-whisper/src/lib.rs:288-300).  head_dim 64 and
+ * 128 with 16-byte-aligned pointers run on the tcgen05 tensor cores: Q, K
+ * (per row), V (per 128-key tile) and P are carried as two f16 terms each
+ * (~22 significant bits), f32 accumulation; other shapes run a CUDA-core
+ * f32 kernel. */
 int oc_flash_attention_fwd(const float *q, const float *k, const float *v, float *o, int batch_heads, int q_len,
                            int kv_len, int head_dim, float scale, int causal, void *stream);
 /* Unfused scaled_dot_product_attention (blas:411-540): scores = Q.K^T /

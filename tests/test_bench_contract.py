@@ -25,7 +25,7 @@ def _args(workload, steps, warmup):
 
 
 def test_every_workload_has_one_description():
-    choices = {"qgemm", "qgemm_a8", "sgemm", "gpt2", "int4", "moe", "mla"}
+    choices = {"qgemm", "qgemm_a8", "sgemm", "gpt2", "int4", "moe", "mla", "flash"}
     assert set(bench.WORKLOADS) == choices
     assert set(bench.REF) == choices
 
@@ -34,6 +34,7 @@ def test_every_workload_has_one_description():
     ("qgemm", 4, 5, 4, 5),   # light samples: every requested step
     ("gpt2", 50, 5, 3, 3),   # samples of 10 s and more: at most 3 and 3
     ("mla", 2, 3, 2, 3),
+    ("flash", 50, 5, 3, 3),
 ])
 def test_reference_line(monkeypatch, workload, steps, warmup, want_steps, want_warmup):
     calls = []
