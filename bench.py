@@ -784,13 +784,63 @@ def run_qgemm_a8(ctx):
                                        "int8_peak_source": f"{ctx.peaks[3]}: 2 x bf16_tflops"}
         del qw, sw, qa, Y
     torch.cuda.empty_cache()
+    # W4A8 at M=2048: the two-term kind::f16 path (the default) against the
+    # exact per-group kind::i8 kernel, which runs when the int32 group
+    # partials are requested (it writes them: 4 * M * N * K / 32 bytes)
+    s0, m = sets[0], max(Q_M)
+    acc = torch.empty(m, Q_N, Q_K // Q_G, dtype=torch.int32, device=ctx.device)
+    ws = oc.workspace(m, Q_K, ctx.device)
+    L = oc.lib()
+    us_f16 = ctx.kernel_us(lambda: oc.qgemm_w4a8(s0["A"][m], s0["q4"], s0["s4"], Q_G, s0["bias"], out=s0["Y"][m]),
+                           reps=8)
+    us_i8 = ctx.kernel_us(lambda: oc.check(L.oc_qgemm_w4a8(m, Q_N, Q_K, Q_G, s0["A"][m].data_ptr(),
+                                                           s0["q4"].data_ptr(), s0["s4"].data_ptr(),
+                                                           s0["bias"].data_ptr(), s0["Y"][m].data_ptr(),
+                                                           ws.data_ptr(), ws.numel(), acc.data_ptr(),
+                                                           ctx.stream.cuda_stream)), reps=4)
+    ops = 2 * m * Q_K * Q_N
+    w4_paths = {"two_term_f16": {"us": round(us_f16, 1), "TOPS": round(ops / us_f16 / 1e6, 1),
+                                 "ceiling": "f16 MMA rate (bf16_tflops) / 2 MMAs = 1/4 of INT8 dense"},
+                "exact_i8_per_group": {"us": round(us_i8, 1), "TOPS": round(ops / us_i8 / 1e6, 1),
+                                       "partials_bytes": int(acc.numel() * 4),
+                                       "ceiling": "INT8 dense for the MMAs; the drain promotes M*N*K/32 group sums "
+                                                  "in group order and stores the partials"}}
+    del acc
+    torch.cuda.empty_cache()
+    # e2e through the host-slice C ABI (oc_blas_qgemm_w8a8 / _w4a8) with pinned host buffers
+    dev = oc.Device(ctx.local)
+    hA = {mm: torch.from_numpy(A[:mm]).pin_memory() for mm in Q_M}
+    hq8, hs8 = s0["q8"].cpu().pin_memory(), s0["s8"].cpu().pin_memory()
+    hq4, hs4 = s0["q4"].cpu().pin_memory(), s0["s4"].cpu().pin_memory()
+    hb = torch.from_numpy(bias).pin_memory()
+    hY = {mm: torch.empty(mm * Q_N, dtype=torch.float32).pin_memory() for mm in Q_M}
+
+    def e2e_step():
+        for mm in Q_M:
+            oc.check(L.oc_blas_qgemm_w8a8(dev.handle, mm, Q_N, Q_K, hA[mm].data_ptr(), hq8.data_ptr(),
+                                          hs8.data_ptr(), hb.data_ptr(), hY[mm].data_ptr()))
+            oc.check(L.oc_blas_qgemm_w4a8(dev.handle, mm, Q_N, Q_K, Q_G, hA[mm].data_ptr(), hq4.data_ptr(),
+                                          hs4.data_ptr(), hb.data_ptr(), hY[mm].data_ptr()))
+
+    for _ in range(max(2, args.warmup)):
+        e2e_step()
+    n_e2e = max(5, args.steps // 5)
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        e2e_step()
+    t_e2e = ctx.max_over_ranks((time.perf_counter() - t0) / n_e2e)
+    per_m_w = hq8.numel() + hs8.numel() * 4 + hq4.numel() + hs4.numel() * 4 + 2 * hb.numel() * 4
+    e2e = {"value": q_ops() * ctx.world / t_e2e / 1e12, "unit": "TOPS",
+           "h2d_bytes_per_step": sum(2 * mm * Q_K * 4 + per_m_w for mm in Q_M),
+           "d2h_bytes_per_step": sum(mm * Q_N * 4 for mm in Q_M) * 2, "ms_per_step": round(t_e2e * 1e3, 3)}
+    dev.close()
     cpu = cpu_qgemm_a8() if ctx.rank == 0 and not args.no_cpu_baseline else None
     config = {"workload": WORKLOADS["qgemm_a8"], "parallelism": f"replicas x{ctx.world}",
               "l2": f"{A8_SETS} rotating device input sets (~300 MB) > 126 MB L2",
               "graph": "one CUDA graph per set (row quantization + GEMM per matmul)"}
     emit(ctx, "INT8-activation quantized GEMM TOPS (W8A8 / W4A8, M in {1,16,128,2048}, K=768, N=3072)", value,
-         "TOPS", ms_step, "int8 x int8 -> int32 (f32 in/out)", config, launches * args.steps, roof, clk, None, cpu,
-         {"per_kernel": per, "w8a8_k3584": big})
+         "TOPS", ms_step, "int8 x int8 -> int32 (f32 in/out)", config, launches * args.steps, roof, clk, e2e, cpu,
+         {"per_kernel": per, "w8a8_k3584": big, "w4a8_M2048_paths": w4_paths})
     ctx.close(*graphs)
 
 
