@@ -605,9 +605,19 @@ __global__ void __launch_bounds__(256) wo_skinny_kernel(int m, int n, int k, int
   {
     const float4* a4 = reinterpret_cast<const float4*>(A);
     const int per_row = nch * J;
-    for (int i = threadIdx.x; i < m * per_row; i += blockDim.x) {
-      const int r = i / per_row, rem = i - r * per_row, c = rem / J, j = rem - c * J;
-      s_a4[(r * J + j) * nch + c] = __ldg(a4 + i);
+    if (m * per_row <= (int)blockDim.x) {  // one float4 per thread at most: a plain load
+      const int i = threadIdx.x;
+      if (i < m * per_row) {
+        const int r = i / per_row, rem = i - r * per_row, c = rem / J, j = rem - c * J;
+        s_a4[(r * J + j) * nch + c] = __ldg(a4 + i);
+      }
+    } else {  // every copy in flight at once (a register round trip per float4 would serialize them)
+      for (int i = threadIdx.x; i < m * per_row; i += blockDim.x) {
+        const int r = i / per_row, rem = i - r * per_row, c = rem / J, j = rem - c * J;
+        cp_async16(s_a4 + (r * J + j) * nch + c, a4 + i);
+      }
+      cp_async_commit();
+      cp_async_wait0();
     }
   }
   __syncthreads();
@@ -678,6 +688,108 @@ __global__ void __launch_bounds__(256) wo_skinny_kernel(int m, int n, int k, int
       const float bc = bias ? __ldg(bias + col) : 0.0f;
       Y[(size_t)r * n + col] = BITS == 8 ? __fmaf_rn(sum, __ldg(sw + col), bc) : __fadd_rn(sum, bc);
     }
+  }
+}
+
+// A few rows (4 <= m <= MR <= 16) whose activations fit shared memory: lane
+// = output column (32 per CTA), the 8 warps split k into consecutive ranges
+// of 16-byte weight chunks.  A lane streams its own weight row (four chunks
+// in flight) and reads the activations of its chunk as shared-memory
+// broadcasts (every lane of the warp reads the same address), so no lane
+// idles on a short row and no cross-lane reduction is needed; the warps'
+// partial sums meet in shared memory and are added in warp order.
+template <int BITS, int MR>
+__global__ void __launch_bounds__(256) wo_cols_kernel(int m, int n, int k, int group, const float* __restrict__ A,
+                                                      const uint8_t* __restrict__ wq, const float* __restrict__ sw,
+                                                      const float* __restrict__ bias, float* __restrict__ Y) {
+  const size_t rowb = BITS == 8 ? (size_t)k : (size_t)k / 2;  // bytes per weight row
+  const int nch = (int)(rowb >> 4);                            // 16-byte chunks per weight row
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col = blockIdx.x * 32 + lane;
+  const bool live = col < n;
+  const int cpw = (nch + 7) / 8;
+  const int c0 = warp * cpw, c1 = min(nch, c0 + cpw);
+  const int4* wr = reinterpret_cast<const int4*>(wq + (size_t)(live ? col : 0) * rowb);
+  constexpr int PF = 4;  // weight chunks in flight per lane
+  int4 wc[PF];           // the first PF chunks before the wait
+#pragma unroll
+  for (int i = 0; i < PF; ++i) wc[i] = (live && c0 + i < c1) ? __ldg(wr + c0 + i) : make_int4(0, 0, 0, 0);
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ float4 s_x4[];  // [m][k / 4] activations, then [8][MR][32] partial sums
+  float* red = reinterpret_cast<float*>(s_x4 + (size_t)m * (k >> 2));
+  {  // every copy in flight at once
+    const float4* a4 = reinterpret_cast<const float4*>(A);
+    for (int i = threadIdx.x; i < m * (k >> 2); i += blockDim.x) cp_async16(s_x4 + i, a4 + i);
+    cp_async_commit();
+    cp_async_wait0();
+  }
+  __syncthreads();
+  const int G = BITS == 8 ? 1 : k / group;
+  const uint64_t zero2 = f2_pack(0.0f, 0.0f);
+  uint64_t acc[MR];
+#pragma unroll
+  for (int r = 0; r < MR; ++r) acc[r] = zero2;
+  for (int cb = c0; cb < c1; cb += PF) {
+    int4 wn[PF];  // the next group of chunks, in flight during this one
+#pragma unroll
+    for (int i = 0; i < PF; ++i) wn[i] = (live && cb + PF + i < c1) ? __ldg(wr + cb + PF + i) : make_int4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < PF; ++i) {
+    const int c = cb + i;
+    if (c >= c1) break;
+#pragma unroll
+    for (int h = 0; h < (BITS == 8 ? 1 : 2); ++h) {  // 16-weight halves of the chunk
+      uint64_t wf[8];
+      weights_to_f2<BITS>(wc[i], h, wf);
+      uint64_t sc = zero2;
+      if (BITS == 4) {
+        const float s1 = live ? __ldg(sw + (size_t)col * G + (32 * c + 16 * h) / group) : 0.0f;
+        sc = f2_pack(s1, s1);
+      }
+      const int k0 = BITS == 8 ? 16 * c : 32 * c + 16 * h;  // first activation of the half
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        if (r < m) {
+          const float4* xr = s_x4 + (size_t)r * (k >> 2) + (k0 >> 2);
+          uint64_t a[8];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const float4 v = xr[jj];
+            a[2 * jj] = f2_pack(v.x, v.y);
+            a[2 * jj + 1] = f2_pack(v.z, v.w);
+          }
+          if (BITS == 8) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[r] = f2_fma(a[e], wf[e], acc[r]);
+          } else {
+            uint64_t d = zero2;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d = f2_fma(a[e], wf[e], d);
+            acc[r] = f2_fma(d, sc, acc[r]);  // the half's group scale
+          }
+        }
+      }
+    }
+    }
+#pragma unroll
+    for (int i = 0; i < PF; ++i) wc[i] = wn[i];
+  }
+#pragma unroll
+  for (int r = 0; r < MR; ++r) {
+    float lo, hi;
+    f2_unpack(acc[r], lo, hi);
+    red[(warp * MR + r) * 32 + lane] = __fadd_rn(lo, hi);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < m * 32; e += blockDim.x) {
+    const int r = e >> 5, cc = blockIdx.x * 32 + (e & 31);
+    if (cc >= n) continue;
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t = __fadd_rn(t, red[(w * MR + r) * 32 + (e & 31)]);
+    const float bc = bias ? __ldg(bias + cc) : 0.0f;
+    Y[(size_t)r * n + cc] = BITS == 8 ? __fmaf_rn(t, __ldg(sw + cc), bc) : __fadd_rn(t, bc);
   }
 }
 

@@ -117,13 +117,6 @@ __global__ void layernorm_kernel(const float* __restrict__ x, size_t x_stride, f
 // (dimension, key parity) for P.V.  head_dim d <= 128.
 constexpr int kAttnThreads = 128, kAttnTile = 128, kAttnMaxD = 128;
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
 // rows j0 .. j0+cnt-1 of a [*, row stride H] cache slice -> dst [cnt][d];
 // one commit group per call (empty when cnt == 0)
 __device__ __forceinline__ void attn_stage(float* dst, const float* src, int j0, int cnt, int d, int H, bool vec) {

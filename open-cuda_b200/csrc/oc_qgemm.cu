@@ -89,7 +89,10 @@ __global__ void __launch_bounds__(256) w8a8_skinny_kernel(int m, int n, int k, c
   };
   int4 wc[COLS];
   load_w(cg, lane, wc);  // in flight during the staging below
-  for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x) s_qa4[i] = __ldg(reinterpret_cast<const int4*>(qa) + i);
+  // every copy in flight at once (a register round trip per chunk would serialize them)
+  for (int i = threadIdx.x; i < m * nchunk; i += blockDim.x) cp_async16(s_qa4 + i, reinterpret_cast<const int4*>(qa) + i);
+  cp_async_commit();
+  cp_async_wait0();
   __syncthreads();
   for (; cg < ngroups; cg += gstride) {
     int acc[COLS][MR];

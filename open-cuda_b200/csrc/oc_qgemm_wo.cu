@@ -6,8 +6,9 @@
 // crates/opencuda-blas/src/lib.rs:922-945) within the f32 tolerance.
 //
 // Paths (kernels in oc_gemm_wo.cuh):
-//  * m <= 16: wo_skinny_kernel, CUDA-core dot products streaming the weights
-//    once (HBM-bound for decode-sized inputs);
+//  * m <= 16: wo_skinny_kernel (lanes along k), or for 4..16 rows with
+//    activations of at most 64 KB wo_cols_kernel (lane = column, warps along
+//    k): CUDA-core dot products streaming the weights once;
 //  * larger m, K % 64 == 0: wo_prep_kernel + gemm_wo_kernel, the tcgen05
 //    f16-term GEMM, in column chunks whose expanded weight terms fit in L2;
 //  * other shapes: the skinny kernel over 16-row chunks, or the scalar
@@ -61,11 +62,27 @@ static int launch_wo_skinny_mr(int m, int n, int k, int group, const float* A, c
                       "wo_skinny_kernel");
 }
 
+// 4..16 rows whose activations take at most kWoColsSmem bytes: wo_cols_kernel.
+constexpr size_t kWoColsSmem = (size_t)64 << 10;
+template <int BITS, int MR>
+static int launch_wo_cols(int m, int n, int k, int group, const float* A, const uint8_t* wq, const float* sw,
+                          const float* bias, float* Y, cudaStream_t s) {
+  auto kern = wo_cols_kernel<BITS, MR>;
+  const size_t smem = (size_t)m * k * 4 + (size_t)8 * MR * 32 * 4;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), smem))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(wo_cols_kernel) failed");
+  return wo_launch_rc(launch_pdl_ex(kern, dim3((n + 31) / 32), dim3(256), smem, s, m, n, k, group, A, wq, sw, bias, Y),
+                      "wo_cols_kernel");
+}
+
 // Up to 16 rows per launch; fewer when the rows' activations exceed the
 // shared-memory budget (200 KB).
 template <int BITS>
 static int run_wo_skinny(int m, int n, int k, int group, const float* A, const uint8_t* wq, const float* sw,
                          const float* bias, float* Y, cudaStream_t s) {
+  if (m >= 4 && m <= kWoSkinnyM && (size_t)m * k * 4 <= kWoColsSmem)
+    return m <= 8 ? launch_wo_cols<BITS, 8>(m, n, k, group, A, wq, sw, bias, Y, s)
+                  : launch_wo_cols<BITS, 16>(m, n, k, group, A, wq, sw, bias, Y, s);
   const int fit = (int)std::max<size_t>(1, ((size_t)200 << 10) / ((size_t)k * 4));
   const int step = std::min(kWoSkinnyM, fit);
   for (int r0 = 0; r0 < m; r0 += step) {
