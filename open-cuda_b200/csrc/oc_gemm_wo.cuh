@@ -692,14 +692,15 @@ __global__ void __launch_bounds__(256) wo_skinny_kernel(int m, int n, int k, int
 }
 
 // A few rows (4 <= m <= MR <= 16) whose activations fit shared memory: lane
-// = output column (32 per CTA), the 8 warps split k into consecutive ranges
+// = output column (32 per CTA), the kWoColsWarps warps split k into consecutive ranges
 // of 16-byte weight chunks.  A lane streams its own weight row (four chunks
 // in flight) and reads the activations of its chunk as shared-memory
 // broadcasts (every lane of the warp reads the same address), so no lane
 // idles on a short row and no cross-lane reduction is needed; the warps'
 // partial sums meet in shared memory and are added in warp order.
+constexpr int kWoColsWarps = 16;
 template <int BITS, int MR>
-__global__ void __launch_bounds__(256) wo_cols_kernel(int m, int n, int k, int group, const float* __restrict__ A,
+__global__ void __launch_bounds__(32 * kWoColsWarps) wo_cols_kernel(int m, int n, int k, int group, const float* __restrict__ A,
                                                       const uint8_t* __restrict__ wq, const float* __restrict__ sw,
                                                       const float* __restrict__ bias, float* __restrict__ Y) {
   const size_t rowb = BITS == 8 ? (size_t)k : (size_t)k / 2;  // bytes per weight row
@@ -707,7 +708,7 @@ __global__ void __launch_bounds__(256) wo_cols_kernel(int m, int n, int k, int g
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = blockIdx.x * 32 + lane;
   const bool live = col < n;
-  const int cpw = (nch + 7) / 8;
+  const int cpw = (nch + kWoColsWarps - 1) / kWoColsWarps;
   const int c0 = warp * cpw, c1 = min(nch, c0 + cpw);
   const int4* wr = reinterpret_cast<const int4*>(wq + (size_t)(live ? col : 0) * rowb);
   constexpr int PF = 4;  // weight chunks in flight per lane
@@ -716,7 +717,7 @@ __global__ void __launch_bounds__(256) wo_cols_kernel(int m, int n, int k, int g
   for (int i = 0; i < PF; ++i) wc[i] = (live && c0 + i < c1) ? __ldg(wr + c0 + i) : make_int4(0, 0, 0, 0);
   pdl_wait();
   pdl_launch();
-  extern __shared__ float4 s_x4[];  // [m][k / 4] activations, then [8][MR][32] partial sums
+  extern __shared__ float4 s_x4[];  // [m][k / 4] activations, then [warps][MR][32] partial sums
   float* red = reinterpret_cast<float*>(s_x4 + (size_t)m * (k >> 2));
   {  // every copy in flight at once
     const float4* a4 = reinterpret_cast<const float4*>(A);
@@ -787,7 +788,7 @@ __global__ void __launch_bounds__(256) wo_cols_kernel(int m, int n, int k, int g
     if (cc >= n) continue;
     float t = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) t = __fadd_rn(t, red[(w * MR + r) * 32 + (e & 31)]);
+    for (int w = 0; w < kWoColsWarps; ++w) t = __fadd_rn(t, red[(w * MR + r) * 32 + (e & 31)]);
     const float bc = bias ? __ldg(bias + cc) : 0.0f;
     Y[(size_t)r * n + cc] = BITS == 8 ? __fmaf_rn(t, __ldg(sw + cc), bc) : __fadd_rn(t, bc);
   }

@@ -68,10 +68,11 @@ template <int BITS, int MR>
 static int launch_wo_cols(int m, int n, int k, int group, const float* A, const uint8_t* wq, const float* sw,
                           const float* bias, float* Y, cudaStream_t s) {
   auto kern = wo_cols_kernel<BITS, MR>;
-  const size_t smem = (size_t)m * k * 4 + (size_t)8 * MR * 32 * 4;
+  const size_t smem = (size_t)m * k * 4 + (size_t)kWoColsWarps * MR * 32 * 4;
   if (!smem_attr_once(reinterpret_cast<const void*>(kern), smem))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(wo_cols_kernel) failed");
-  return wo_launch_rc(launch_pdl_ex(kern, dim3((n + 31) / 32), dim3(256), smem, s, m, n, k, group, A, wq, sw, bias, Y),
+  return wo_launch_rc(launch_pdl_ex(kern, dim3((n + 31) / 32), dim3(32 * kWoColsWarps), smem, s, m, n, k, group, A, wq,
+                                    sw, bias, Y),
                       "wo_cols_kernel");
 }
 
