@@ -369,6 +369,214 @@ done:
   }
 }
 
+// ---- tensor-core GEMM, K split over a thread-block cluster ---------------------
+//
+// For grids whose tiles fill at most half the GPU: the ks slices of a tile
+// run as one cluster (CTA rank = slice, grid (ks, column tiles, row tiles)).
+// Each slice computes its k-blocks' partial product in TMEM (the producer and
+// MMA roles of gemm_wo_kernel), scales it by the row and column factors and
+// parks it as f32 in its own shared memory (the drained pipeline stages).
+// After a cluster barrier each slice adds, for its share of the tile's rows,
+// the ks partials in slice order through distributed shared memory, adds the
+// bias and stores the rows; a second barrier keeps every CTA resident until
+// its peers have read its partial.  No partial sum goes through global
+// memory.  Both barriers sit where every thread arrives unconditionally
+// (bounded waits that give up only set the status word).
+template <int BM_, int WT_>
+struct WoClT {
+  static constexpr int BN = 128, BM = BM_, WT = WT_, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2, W_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = 2 * A_BYTES + WT * W_BYTES;
+  static constexpr int EPI_WARPS = 8, THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int PART_BYTES = BM * BN * 4;  // the scaled partial tile, [BM][BN] f32
+  static constexpr int STAGES_FIT = (int)((227 * 1024 - 1024 - 256) / STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+  static constexpr int RING = STAGES * STAGE_BYTES > PART_BYTES ? STAGES * STAGE_BYTES : PART_BYTES;
+  static constexpr size_t SMEM = 1024 + (size_t)RING + 256;
+  static constexpr int TMEM_COLS = BM <= 128 ? 128 : 256;
+  static constexpr int HALF = BM / 2, NBH = HALF / 32;  // rows and 32-row blocks per epilogue half
+  static_assert(BM == 128 || BM == 192 || BM == 256, "tile heights");
+  static_assert(STAGES >= 2, "double-buffered ring");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+template <int BM, int WT>
+__global__ void __launch_bounds__(WoClT<BM, WT>::THREADS, 1)
+    gemm_wo_cl_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, int M, int N,
+                      int K, const float* __restrict__ rowf, const float* __restrict__ colf,
+                      const float* __restrict__ bias, float* __restrict__ Y, int ldy, int vec_out, int* status) {
+  using C = WoClT<BM, WT>;
+  pdl_wait();  // operand terms from the preparation launch; TMEM only after the predecessors are done
+  pdl_launch();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto sAh = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
+  auto sAl = [&](int s) { return sAh(s) + C::A_BYTES; };
+  auto sW = [&](int s, int t) { return sAh(s) + 2 * C::A_BYTES + t * C::W_BYTES; };
+  float* pbuf = reinterpret_cast<float*>(smem);  // the partial tile, after the mainloop
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::RING);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* tfull = empty_bar + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int ks = (int)gridDim.x, slice = (int)cluster_ctarank();
+  const int tn = (int)blockIdx.y, tm = (int)blockIdx.z;
+  const int nrb = K / C::BK;
+  const int rb0 = (int)((long long)slice * nrb / ks), rb1 = (int)((long long)(slice + 1) * nrb / ks);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = rb0; kb < rb1; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+          kernel_fail(status, abort_flag, kDevTimeoutProducer);
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+        const int k0 = kb * C::BK, xh = 128 * (k0 >> 6);  // the hi term of block kb, then the lo term
+        tma_load_2d(sAh(stage), &tmA, xh, tm * C::BM, &full_bar[stage]);
+        tma_load_2d(sAl(stage), &tmA, xh + 64, tm * C::BM, &full_bar[stage]);
+        if (WT == 2) {
+          tma_load_2d(sW(stage, 0), &tmW, xh, tn * C::BN, &full_bar[stage]);
+          tma_load_2d(sW(stage, 1), &tmW, xh + 64, tn * C::BN, &full_bar[stage]);
+        } else {
+          tma_load_2d(sW(stage, 0), &tmW, k0, tn * C::BN, &full_bar[stage]);
+        }
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(C::BN, C::BM);  // MMA M = weight rows, N = activation rows
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = 0; kb < rb1 - rb0; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+          kernel_fail(status, abort_flag, kDevTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ah = smem_u32(sAh(stage)), al = smem_u32(sAl(stage));
+        const uint32_t w0 = smem_u32(sW(stage, 0)), w1 = smem_u32(sW(stage, WT - 1));
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk) {
+          const uint64_t dah = desc_kmajor_sw128(ah + kk * 32), dal = desc_kmajor_sw128(al + kk * 32);
+          const uint64_t dw0 = desc_kmajor_sw128(w0 + kk * 32);
+          mma_f16(tmem_base, dw0, dah, idesc, (kb | kk) != 0 ? 1u : 0u);
+          if (WT == 2) mma_f16(tmem_base, desc_kmajor_sw128(w1 + kk * 32), dah, idesc, 1u);
+          mma_f16(tmem_base, dw0, dal, idesc, 1u);
+        }
+        tc_commit(&empty_bar[stage]);
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) tc_commit(tfull);
+    }
+    __syncwarp();
+  } else {
+    // Epilogue warp: TMEM lanes 32 q .. 32 q + 31 = weight rows (output
+    // columns), tile rows [HALF eh, HALF eh + HALF) in 32-row blocks ->
+    // scaled partials at pbuf[row][column].
+    const int q = warp & 3, eh = (warp - 2) >> 2;
+    const int col = tn * C::BN + q * 32 + lane;
+    const float cf = col < N ? __ldg(colf + col) : 0.0f;
+    const int row0 = tm * C::BM + eh * C::HALF;
+    float rfr[C::NBH];
+#pragma unroll
+    for (int i = 0; i < C::NBH; ++i) {
+      const int rr = row0 + 32 * i + lane;
+      rfr[i] = rr < M ? __ldg(rowf + rr) : 0.0f;
+    }
+    if (mbar_wait(tfull, 0, abort_flag)) {
+      tc_fence_after();
+      const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(eh * C::HALF);
+#pragma unroll 1
+      for (int bi = 0; bi < C::NBH; ++bi) {
+        uint32_t r[32];
+        tmem_ld32(tl + 32 * bi, r);
+        tmem_ld_wait();
+        float* prow = pbuf + (size_t)(eh * C::HALF + 32 * bi) * C::BN + q * 32 + lane;
+#pragma unroll
+        for (int j2 = 0; j2 < 32; ++j2) {
+          const float rf = __shfl_sync(0xffffffffu, rfr[bi], j2);
+          prow[(size_t)j2 * C::BN] = wo_scale(__uint_as_float(r[j2]), rf, cf, 0.0f);
+        }
+      }
+    } else {
+      kernel_fail(status, abort_flag, kDevTimeoutEpilogue);
+    }
+  }
+  // every slice's partial is in its shared memory
+  cluster_sync_all();
+  if (!*abort_flag) {
+    // this slice's rows of the tile: the slices' partials in slice order, + bias
+    const int rows = min(C::BM, M - tm * C::BM);
+    const int per = (C::BM + ks - 1) / ks, r_lo = slice * per, r_hi = min(rows, r_lo + per);
+    const uint32_t pb = smem_u32(pbuf);
+    for (int i = threadIdx.x; i < (r_hi > r_lo ? (r_hi - r_lo) * (C::BN / 4) : 0); i += C::THREADS) {
+      const int r = r_lo + i / (C::BN / 4), c4 = i % (C::BN / 4);
+      const int c = tn * C::BN + 4 * c4;
+      if (c >= N) continue;
+      const uint32_t off = (uint32_t)((r * C::BN + 4 * c4) * 4);
+      float4 t = ld_cluster_f4(cluster_map(pb + off, 0));
+      for (int j = 1; j < ks; ++j) {
+        const float4 v = ld_cluster_f4(cluster_map(pb + off, (uint32_t)j));
+        t.x = __fadd_rn(t.x, v.x);
+        t.y = __fadd_rn(t.y, v.y);
+        t.z = __fadd_rn(t.z, v.z);
+        t.w = __fadd_rn(t.w, v.w);
+      }
+      float* yr = Y + (size_t)(tm * C::BM + r) * ldy + c;
+      if (vec_out && c + 3 < N) {
+        const float4 b4 = bias ? __ldg(reinterpret_cast<const float4*>(bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(yr) =
+            make_float4(__fadd_rn(t.x, b4.x), __fadd_rn(t.y, b4.y), __fadd_rn(t.z, b4.z), __fadd_rn(t.w, b4.w));
+      } else {
+        const float tv[4] = {t.x, t.y, t.z, t.w};
+        for (int e = 0; e < 4 && c + e < N; ++e) yr[e] = __fadd_rn(tv[e], bias ? __ldg(bias + c + e) : 0.0f);
+      }
+    }
+  }
+  // no CTA leaves while a peer may still read its partial
+  cluster_sync_all();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
 // ---- operand preparation --------------------------------------------------------
 
 // log2(c_m) for an activation row with max |a| = mx: |a * c_m| < 2^15

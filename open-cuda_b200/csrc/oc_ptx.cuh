@@ -283,6 +283,36 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---- thread-block clusters (distributed shared memory) -----------------------
+
+// Every thread of every CTA of the cluster arrives, then waits for all.  Only
+// for points that each thread reaches unconditionally (no early exit before
+// it), so the barrier always completes; release / acquire at cluster scope
+// order the shared-memory writes before it with the peers' reads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address in CTA `rank`'s shared memory of the variable at `smem_addr` (a
+// shared::cta address of this CTA).
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 // 16-byte global -> shared copies that do not pass through registers: a
 // thread issues all of its copies, then waits once.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {

@@ -11,6 +11,9 @@
 //    k): CUDA-core dot products streaming the weights once;
 //  * larger m, K % 64 == 0: wo_prep_kernel + gemm_wo_kernel, the tcgen05
 //    f16-term GEMM, in column chunks whose expanded weight terms fit in L2;
+//    when a chunk's tiles fill at most half the GPU, gemm_wo_cl_kernel
+//    instead: K split over a thread-block cluster, the slices' partial
+//    tiles added in distributed shared memory;
 //  * other shapes: the skinny kernel over 16-row chunks, or the scalar
 //    wo_generic_kernel.
 #include <algorithm>
@@ -177,6 +180,86 @@ static int launch_wo_gemm(const CUtensorMap& ta, const CUtensorMap& tw, int m, i
                       "gemm_wo_kernel");
 }
 
+// ---- K split over a thread-block cluster (gemm_wo_cl_kernel) ------------------
+
+// Activation-tile height of the cluster path: 128 rows when the input fits
+// one such tile, else 192.
+static int wo_cl_bm(int m) { return m <= 128 ? 128 : 192; }
+
+template <int BM, int WT>
+static int wo_cl_max_clusters(int ks) {
+  // co-resident clusters of ks CTAs for this instantiation, cached per ks
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(ks);
+  if (it != cache.end()) return it->second;
+  using C = WoClT<BM, WT>;
+  auto kern = gemm_wo_cl_kernel<BM, WT>;
+  int n = 0;
+  if (smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM)) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ks, 1, 1);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+  }
+  cache[ks] = n;
+  return n;
+}
+
+// Slices per tile for the cluster path, or 0 when the tiles fill more than
+// half the GPU (or k has fewer than two 64-k blocks): the largest ks <= 8
+// whose clusters all fit at once with tiles * ks <= SMs.
+template <int WT>
+static int wo_cl_ks(int m, int nc, int k) {
+  const int sms = std::max(1, sm_count()), bm = wo_cl_bm(m);
+  const int tiles = (m + bm - 1) / bm * ((nc + 127) / 128), nrb = k / 64;
+  if (2 * tiles > sms || nrb < 2) return 0;
+  for (int ks = std::min(8, std::min(nrb, sms / tiles)); ks >= 2; --ks) {
+    const int fit = bm == 128 ? wo_cl_max_clusters<128, WT>(ks) : wo_cl_max_clusters<192, WT>(ks);
+    if (fit >= tiles) return ks;
+  }
+  return 0;
+}
+
+template <int BM, int WT>
+static int launch_wo_cl(const CUtensorMap& ta, const CUtensorMap& tw, int ks, int m, int nc, int k, int ldy,
+                        const float* icm, const float* colf, const float* bias, float* Yc, cudaStream_t s) {
+  using C = WoClT<BM, WT>;
+  auto kern = gemm_wo_cl_kernel<BM, WT>;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_wo_cl_kernel) failed");
+  const int vec_out = (ldy % 4 == 0 && aligned16(Yc) && (!bias || aligned16(bias))) ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ks, (nc + C::BN - 1) / C::BN, (m + BM - 1) / BM);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return wo_launch_rc(cudaLaunchKernelEx(&cfg, kern, ta, tw, m, nc, k, icm, colf, bias, Yc, ldy, vec_out,
+                                         device_status_word()),
+                      "gemm_wo_cl_kernel");
+}
+
 // Number of split tiles the GEMM of a chunk will use (to size and zero the
 // ready counters in the preparation launch): the same rule as launch_wo_gemm.
 static int wo_nsplit(int m, int nc, int k, int bm) {
@@ -224,7 +307,8 @@ static int run_wo_gemm(int m, int n, int k, int group, const float* A, const voi
   }
   for (int n0 = 0; n0 < n; n0 += nc) {
     const int ncur = std::min(nc, n - n0);
-    const int nsplit = wo_nsplit(m, ncur, k, bm);
+    const int cl_ks = wo_cl_ks<WT>(m, ncur, k);
+    const int nsplit = cl_ks ? 0 : wo_nsplit(m, ncur, k, bm);
     int* ready = nullptr;
     if (nsplit) {
       ready = reinterpret_cast<int*>(g_wo_ready.get((size_t)nsplit, s));
@@ -247,10 +331,19 @@ static int run_wo_gemm(int m, int n, int k, int group, const float* A, const voi
     const float* colf = WT == 2 ? icn : sw + n0;
     const float* bc = bias ? bias + n0 : nullptr;
     float* Yc = Y + n0;
-    if (bm == 192)
+    if (cl_ks) {  // few tiles: K split over a cluster, reduced in distributed shared memory
+      const int bmc = wo_cl_bm(m);
+      CUtensorMap tac;
+      rc = make_tmap_2d(&tac, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
+                        kWoBK, bmc, kWoSwizzle);
+      if (rc) return rc;
+      rc = bmc == 128 ? launch_wo_cl<128, WT>(tac, tw, cl_ks, m, ncur, k, n, icm, colf, bc, Yc, s)
+                      : launch_wo_cl<192, WT>(tac, tw, cl_ks, m, ncur, k, n, icm, colf, bc, Yc, s);
+    } else if (bm == 192) {
       rc = launch_wo_gemm<192, WT>(ta, tw, m, ncur, k, n, icm, colf, bc, Yc, s);
-    else
+    } else {
       rc = launch_wo_gemm<256, WT>(ta, tw, m, ncur, k, n, icm, colf, bc, Yc, s);
+    }
     if (rc) return rc;
   }
   if (nc == n && !skip_expand) {
