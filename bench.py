@@ -10,7 +10,7 @@ each = activation row quantization + exact-int32 tensor-core GEMM (or the
 skinny dp4a kernel for M <= 16) + dequantizing epilogue.
 
 Other workloads (same JSON contract, one line each):
-  sgemm     f32 A[512x768] . B[768x2304] + bias (GPT-2 c_attn shape), 3xTF32
+  sgemm     f32 A[512x768] . B[768x2304] + bias (GPT-2 c_attn shape), f16-term GEMM
   gpt2      GPT-2 124M random-init (load_random seed 3), 32-token prompts,
             128 greedy tokens, batch 32 (batch 1 reported beside it)
   int4      INT4 group-32 sweep K=3584, N in {3584, 18944, 152064},
@@ -133,7 +133,10 @@ def roofline(kernel: str, ops: float, nbytes: float, us: float, peaks, ops_unit=
     time (ops / dense peak) and the HBM time (algorithmic bytes / copy
     bandwidth) is longer; achieved and peak are in that bound's unit."""
     hbm, int8, tf32, src = peaks
-    tensor_peak = int8 if ops_unit == "TOPS" else tf32 / 3.0  # 3xTF32: three MMAs per product
+    if ops_unit == "F16T3":  # f32 products as three f16-term MMAs at the bf16 rate
+        tensor_peak = int8 / 2.0 / 3.0
+    else:
+        tensor_peak = int8 if ops_unit == "TOPS" else tf32 / 3.0  # 3xTF32: three MMAs per product
     t_tensor = ops / (tensor_peak * 1e12)
     t_hbm = nbytes / (hbm * 1e9)
     tr = None  # DRAM traffic comes from ncu captures, never from a timed run
@@ -145,8 +148,9 @@ def roofline(kernel: str, ops: float, nbytes: float, us: float, peaks, ops_unit=
                 "traffic": tr}
     ach = ops / (us * 1e-6) / 1e12
     unit = "TOPS" if ops_unit == "TOPS" else "TFLOP/s"
-    how = ("int8 dense = 2 x measured bf16_tflops" if ops_unit == "TOPS"
-           else "3xTF32 effective = measured bf16_tflops / 2 (tf32 rate) / 3")
+    how = {"TOPS": "int8 dense = 2 x measured bf16_tflops",
+           "F16T3": "measured bf16_tflops / 3 (f16 MMAs at the bf16 rate, three per f32 product)"}.get(
+        ops_unit, "3xTF32 effective = measured bf16_tflops / 2 (tf32 rate) / 3")
     return {"bound": "tensor", "kernel": kernel, "achieved": round(ach, 2), "peak": round(tensor_peak, 1),
             "unit": unit, "frac": round(ach / tensor_peak, 4), "peak_source": f"{src}: {how}",
             "algorithmic_bytes": int(nbytes), "algorithmic_ops": int(ops), "us_per_launch": round(us, 3),
@@ -845,7 +849,7 @@ def run_qgemm_a8(ctx):
 
 
 # ----------------------------------------------------------------------------
-# sgemm: f32 GEMM of the GPT-2 c_attn shape (3xTF32 tensor cores)
+# sgemm: f32 GEMM of the GPT-2 c_attn shape (f16-term tensor-core GEMM)
 # ----------------------------------------------------------------------------
 
 S_M, S_K, S_N = 512, 768, 2304
@@ -889,7 +893,7 @@ def run_sgemm(ctx):
     def step(i):
         s = sets[i % S_SETS]
         oc.sgemm(s["A"], s["B"], C=s["C"], bias=s["bias"])
-        return 2  # B split into tf32 hi/lo + GEMM
+        return 3  # B's column maxima, the f16 terms of A and B, the GEMM
 
     with torch.cuda.stream(ctx.stream):
         for i in range(S_SETS):
@@ -911,31 +915,19 @@ def run_sgemm(ctx):
     ms_step, clk = ctx.timed(lambda i: graphs[i % S_SETS].replay(), args.steps)
     flops = 2 * S_M * S_K * S_N
     value = flops * ctx.world / (ms_step * 1e-3) / 1e12
-    # the GEMM kernel alone (B pre-split once per set)
-    L = oc.lib()
-    import ctypes as C
-    sz = C.c_size_t(0)
-    oc.check(L.oc_sgemm_prepared_b_size(S_K, S_N, C.byref(sz)))
-    preps = []
-    for s in sets:
-        p = torch.empty(sz.value // 4, dtype=torch.float32, device=d)
-        oc.check(L.oc_sgemm_prepare_b(S_K, S_N, s["B"].data_ptr(), S_N, 0, p.data_ptr(),
-                                      torch.cuda.current_stream().cuda_stream))
-        preps.append(p)
-    torch.cuda.synchronize()
+    # the call alone (column maxima, f16 terms, GEMM), rotating over the sets
     ctr = [0]
 
     def launch():
         j = ctr[0] % S_SETS
         ctr[0] += 1
         s = sets[j]
-        oc.check(L.oc_sgemm_prepared(S_M, S_N, S_K, 1.0, s["A"].data_ptr(), S_K, preps[j].data_ptr(), 0.0,
-                                     s["C"].data_ptr(), S_N, s["bias"].data_ptr(),
-                                     torch.cuda.current_stream().cuda_stream))
+        oc.sgemm(s["A"], s["B"], C=s["C"], bias=s["bias"])
 
     us = ctx.kernel_us(launch, reps=32)
-    nbytes = 4 * (S_M * S_K + 2 * S_K * S_N + S_N + S_M * S_N)  # A, B hi+lo, bias, C
-    roof = roofline("sgemm_tf32x3 512x768x2304", flops, nbytes, us, ctx.peaks, ops_unit="TFLOP")
+    nbytes = 4 * (S_M * S_K + S_K * S_N + S_N + S_M * S_N)  # A, B, bias, C
+    roof = roofline("sgemm call (f32_colmax + f32_terms + gemm_wo<WT=2>) 512x768x2304", flops, nbytes, us,
+                    ctx.peaks, ops_unit="F16T3")
     # e2e: the reference's blas-level sgemm (host slices in and out) + the caller's host bias add
     dev = oc.Device(ctx.local)
     hA = torch.from_numpy(A).pin_memory().numpy()
@@ -960,9 +952,9 @@ def run_sgemm(ctx):
     config = {"workload": WORKLOADS["sgemm"],
               "parallelism": f"replicas x{ctx.world}", "l2": f"{S_SETS} rotating sets (213 MB) > 126 MB L2",
               "graph": "one CUDA graph per set"}
-    emit(ctx, "sgemm TFLOP/s (f32 via 3xTF32, 512x768x2304 + bias)", value, "TFLOP/s", ms_step,
-         "f32 (3xTF32 tensor cores, f32 accumulate)", config, launches * args.steps, roof, clk, e2e, cpu,
-         {"gemm_kernel_us": round(us, 3)})
+    emit(ctx, "sgemm TFLOP/s (f32, 512x768x2304 + bias)", value, "TFLOP/s", ms_step,
+         "f32 (f16 hi/lo terms of both operands on tensor cores, f32 accumulate)", config, launches * args.steps, roof, clk, e2e, cpu,
+         {"call_us": round(us, 3)})
     ctx.close(*graphs)
 
 
@@ -1319,7 +1311,7 @@ def run_moe(ctx):
 
 
 # ----------------------------------------------------------------------------
-# mla: MLA compress / decompress as 3xTF32 GEMMs
+# mla: MLA compress / decompress as f16-term tensor-core GEMMs
 # ----------------------------------------------------------------------------
 
 L_SEQ, L_DH, L_DC, L_UP = 4 * 4096, 7168, 512, 128 * 128
@@ -1369,7 +1361,7 @@ def run_mla(ctx):
         lat = oc.mla_compress_kv(kv, down)
         oc.mla_decompress_kv(lat, upk)
         oc.mla_decompress_kv(lat, upv)
-        return 6  # each: B split + GEMM
+        return 9  # each: B's column maxima, the f16 terms of both operands, the GEMM
 
     with torch.cuda.stream(ctx.stream):
         for i in range(2 if args.profile_once else max(3, args.warmup)):
@@ -1384,8 +1376,8 @@ def run_mla(ctx):
     us_c = ctx.kernel_us(lambda: oc.mla_compress_kv(kv, down), reps=3, graph=False)
     us_d = ctx.kernel_us(lambda: oc.mla_decompress_kv(lat, upk), reps=3, graph=False)
     fl_d = 2 * L_SEQ * L_DC * L_UP
-    roof = roofline("mla_decompress (3xTF32 GEMM incl. B split)", fl_d,
-                    4 * (L_SEQ * L_DC + 2 * L_DC * L_UP + L_SEQ * L_UP), us_d, ctx.peaks, ops_unit="TFLOP")
+    roof = roofline("mla_decompress call (f32_colmax + f32_terms + gemm_wo<WT=2>)", fl_d,
+                    4 * (L_SEQ * L_DC + L_DC * L_UP + L_SEQ * L_UP), us_d, ctx.peaks, ops_unit="F16T3")
     per = {"compress_us": round(us_c, 1), "compress_TFLOPs": round(2 * L_SEQ * L_DH * L_DC / us_c / 1e6, 1),
            "decompress_us": round(us_d, 1), "decompress_TFLOPs": round(fl_d / us_d / 1e6, 1)}
     # e2e through the host-slice C ABI
@@ -1414,8 +1406,8 @@ def run_mla(ctx):
     cpu = cpu_mla() if ctx.rank == 0 and not args.no_cpu_baseline else None
     config = {"workload": WORKLOADS["mla"], "parallelism": f"replicas x{ctx.world}",
               "l2": "operands 0.5-1 GB > 126 MB L2"}
-    emit(ctx, "MLA compress+decompress TFLOP/s (3xTF32)", value, "TFLOP/s", ms_step,
-         "f32 (3xTF32 tensor cores, f32 accumulate)", config, launches * steps, roof, clk, e2e, cpu,
+    emit(ctx, "MLA compress+decompress TFLOP/s (f32)", value, "TFLOP/s", ms_step,
+         "f32 (f16 hi/lo terms of both operands on tensor cores, f32 accumulate)", config, launches * steps, roof, clk, e2e, cpu,
          {"per_kernel": per})
     ctx.close()
 
@@ -1559,7 +1551,7 @@ WORKLOADS = {
     "qgemm_a8": "config-2 shapes with int8 activations: M in {1,16,128,2048}, K=768, N=3072, W8A8 per-channel + "
                 "W4A8 group-32 (activation rows quantized on the device, exact int32 products), f32 bias and output; "
                 "W8A8 at K=3584 beside it",
-    "sgemm": "config-1 sgemm: A[512x768] . B[768x2304] + bias, N(0,0.02) seed 0, 3xTF32",
+    "sgemm": "config-1 sgemm: A[512x768] . B[768x2304] + bias, N(0,0.02) seed 0",
     "gpt2": "config-3 GPT-2 124M random-init (load_random seed 3), prompt 32, 128 greedy tokens, "
             "batch 32 (32 independent sequences)",
     "int4": "config-4 INT4 group-32 sweep K=3584, N in {3584,18944,152064}, M in {1,8,64,512,4096}, f32 activations "
@@ -1576,14 +1568,14 @@ REF = {
     "qgemm": (cpu_qgemm, Q_METRIC, "TOPS", lambda v: q_ops() / (v * 1e12) * 1e3),
     "qgemm_a8": (cpu_qgemm_a8, "INT8-activation quantized GEMM TOPS (W8A8 / W4A8, M in {1,16,128,2048}, K=768, "
                  "N=3072)", "TOPS", lambda v: q_ops() / (v * 1e12) * 1e3),
-    "sgemm": (cpu_sgemm, "sgemm TFLOP/s (f32 via 3xTF32, 512x768x2304 + bias)", "TFLOP/s",
+    "sgemm": (cpu_sgemm, "sgemm TFLOP/s (f32, 512x768x2304 + bias)", "TFLOP/s",
               lambda v: 2 * S_M * S_K * S_N / (v * 1e12) * 1e3),
     "gpt2": (cpu_gpt2, "GPT-2 124M greedy decode tok/s (batch 32, prompt 32, 128 new tokens)", "tok/s",
              lambda v: 32 * G_NEW / v * 1e3),
     "int4": (cpu_int4, "INT4 g32 GEMM TOPS (K=3584 sweep)", "TOPS", lambda v: i_ops() / (v * 1e12) * 1e3),
     "moe": (cpu_moe, "MoE block TOPS (8192 tokens, 256 experts top-8 + shared, INT8)", "TOPS",
             lambda v: e_ops() / (v * 1e12) * 1e3),
-    "mla": (cpu_mla, "MLA compress+decompress TFLOP/s (3xTF32)", "TFLOP/s", lambda v: l_flops() / (v * 1e12) * 1e3),
+    "mla": (cpu_mla, "MLA compress+decompress TFLOP/s (f32)", "TFLOP/s", lambda v: l_flops() / (v * 1e12) * 1e3),
     "flash": (cpu_flash, F_METRIC, "TFLOP/s", lambda v: sum(f_flops(c) for c in F_CASES) / (v * 1e12) * 1e3),
 }
 

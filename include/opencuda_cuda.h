@@ -159,10 +159,14 @@ int oc_get_device_status(int *status);
 /* C = alpha * A.op(B) + beta * C (+ bias[n] per column if bias != NULL).
  * A [m][lda], op(B) = B [k][ldb] (trans_b = 0, the reference's b[kk*n+col])
  * or B^T with B [n][ldb] (trans_b = 1, the transpose_b form of
- * launch_naive_gemm, blas:206-210); C [m][ldc].  f32 in and out; products on
- * the tcgen05 tf32 tensor cores with the 3xTF32 split (f32-level accuracy),
- * small m on a CUDA-core split-K GEMV.  beta == 0 does not read C.  Replaces
- * the GemmPath::CuBlas arm of sgemm (blas:293). */
+ * launch_naive_gemm, blas:206-210); C [m][ldc].  f32 in and out, f32-level
+ * accuracy (<= 1e-5 relative Frobenius): for beta == 0, m > 16, k % 64 == 0
+ * (A 16-byte aligned, lda % 4 == 0; for trans_b the same for B) on tcgen05
+ * f16 tensor cores with both operands split into two f16 terms after a
+ * power-of-two scale per row of A and per column of op(B) (three MMAs per
+ * product step); other large shapes on tf32 tensor cores with the 3xTF32
+ * split; small m on a CUDA-core split-K GEMV.  beta == 0 does not read C.
+ * Replaces the GemmPath::CuBlas arm of sgemm (blas:293). */
 int oc_sgemm(int m, int n, int k, float alpha, const float *A, int lda, const float *B, int ldb, int trans_b,
              float beta, float *C, int ldc, const float *bias, void *stream);
 /* For a B that is reused across calls (weights): oc_sgemm splits B into

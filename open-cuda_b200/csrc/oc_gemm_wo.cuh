@@ -599,12 +599,12 @@ __device__ __forceinline__ void split_act_pair(float x0, float x1, float c, uint
   lo2 = l0 | (l1 << 16);
 }
 
-// Activation row `row` by one CTA of 128 threads: row max, then the hi / lo
-// terms into ax [m][2k] (64-k blocks: hi, then lo) and 1 / c_m into icm.
-// k % 64 == 0, A 16-byte aligned.
-__device__ __forceinline__ void split_act_row(const float* __restrict__ A, int k, __half* __restrict__ ax,
+// Activation row `row` (row stride lda) by one CTA of 128 threads: row max,
+// then the hi / lo terms into ax [m][2k] (64-k blocks: hi, then lo) and
+// 1 / c_m into icm.  k % 64 == 0, lda % 4 == 0, A 16-byte aligned.
+__device__ __forceinline__ void split_act_row(const float* __restrict__ A, int lda, int k, __half* __restrict__ ax,
                                               float* __restrict__ icm, int row, float* red) {
-  const float4* a4 = reinterpret_cast<const float4*>(A + (size_t)row * k);
+  const float4* a4 = reinterpret_cast<const float4*>(A + (size_t)row * lda);
   const int n4 = k >> 2;
   float mx = 0.0f;
   for (int i = threadIdx.x; i < n4; i += 128) {
@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(128) wo_prep_kernel(const float* __restrict__ 
     for (int i = threadIdx.x; i < nready; i += 128) ready[i] = 0;
   const int eb = (nc + 3) / 4;
   if ((int)blockIdx.x >= eb) {
-    if ((int)blockIdx.x - eb < ma) split_act_row(A, k, ax, icm, (int)blockIdx.x - eb, red);
+    if ((int)blockIdx.x - eb < ma) split_act_row(A, k, k, ax, icm, (int)blockIdx.x - eb, red);
     return;
   }
   const int nr = 4 * (int)blockIdx.x + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -709,6 +709,125 @@ __global__ void __launch_bounds__(128) wo_prep_kernel(const float* __restrict__ 
     expand_w4_row(static_cast<const uint8_t*>(wq), sw, k, group, wx, icn, n0 + nr, nr, lane);
   else
     expand_w8_row(static_cast<const int8_t*>(wq), k, wx, n0 + nr, nr, lane);
+}
+
+// ---- dense f32 B (sgemm with beta = 0) ------------------------------------------
+//
+// A column chunk [n0, n0 + nc) of op(B) (B [k][ldb], or B [n][ldb] when TB)
+// becomes the weight-term layout of the GEMM above: column n scaled by c_n =
+// 2^(14 - e) (e the exponent of its max |b|, as the activation rows), hi =
+// f16(t), lo = f16(t - hi) into wx [nc][2k] (64-k blocks: hi, then lo), and
+// colf[n] = alpha / c_n, so the epilogue forms alpha * A.B + bias.  k % 64 ==
+// 0; TB additionally ldb % 4 == 0 and B 16-byte aligned.
+
+constexpr int kF32MaxSlice = 256;  // k rows per block of the column-maximum pass (TB = 0)
+
+// TB = 0, pass 1: block (strip of 32 columns, k slice) -> the slice's column
+// maxima at pmax[slice][column] (lane = column: each row read is coalesced).
+__global__ void __launch_bounds__(128) f32_colmax_kernel(const float* __restrict__ B, int ldb, int n, int n0, int nc,
+                                                         int k, float* __restrict__ pmax) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float cm[4][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cl = 32 * (int)blockIdx.x + lane, col = n0 + cl;
+  const bool live = cl < nc && col < n;
+  const int k0 = (int)blockIdx.y * kF32MaxSlice, k1 = min(k, k0 + kF32MaxSlice);
+  float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
+  if (live) {
+    int kk = k0 + warp;
+    for (; kk + 12 < k1; kk += 16) {  // four independent loads in flight
+      m0 = fmaxf(m0, fabsf(__ldg(B + (size_t)kk * ldb + col)));
+      m1 = fmaxf(m1, fabsf(__ldg(B + (size_t)(kk + 4) * ldb + col)));
+      m2 = fmaxf(m2, fabsf(__ldg(B + (size_t)(kk + 8) * ldb + col)));
+      m3 = fmaxf(m3, fabsf(__ldg(B + (size_t)(kk + 12) * ldb + col)));
+    }
+    for (; kk < k1; kk += 4) m0 = fmaxf(m0, fabsf(__ldg(B + (size_t)kk * ldb + col)));
+  }
+  cm[warp][lane] = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+  __syncthreads();
+  if (warp == 0 && cl < nc)
+    pmax[(size_t)blockIdx.y * nc + cl] = fmaxf(fmaxf(cm[0][lane], cm[1][lane]), fmaxf(cm[2][lane], cm[3][lane]));
+}
+
+// Blocks [0, eb): the columns (TB: a warp per row of B, 4 rows per block;
+// else block (strip, 64-k block) over eb = strips * k / 64, the column
+// maxima from pmax's nsl slices); blocks [eb, eb + ma) split the activation
+// rows; block 0 zeroes the GEMM's ready counters.
+template <int TB>
+__global__ void __launch_bounds__(128) f32_terms_kernel(const float* __restrict__ A, int lda, int ma, int k,
+                                                        __half* __restrict__ ax, float* __restrict__ icm,
+                                                        const float* __restrict__ B, int ldb, int n, int n0, int nc,
+                                                        float alpha, const float* __restrict__ pmax, int nsl,
+                                                        __half* __restrict__ wx, float* __restrict__ colf,
+                                                        int* __restrict__ ready, int nready) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float red[4];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nready; i += 128) ready[i] = 0;
+  const int eb = TB ? (nc + 3) / 4 : (nc + 31) / 32 * (k >> 6);
+  if ((int)blockIdx.x >= eb) {
+    if ((int)blockIdx.x - eb < ma) split_act_row(A, lda, k, ax, icm, (int)blockIdx.x - eb, red);
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (TB) {
+    const int nr = 4 * (int)blockIdx.x + warp;  // chunk column = row of B
+    if (nr >= nc) return;
+    const float4* b4 = reinterpret_cast<const float4*>(B + (size_t)(n0 + nr) * ldb);
+    float mx = 0.0f;
+    for (int i = lane; i < (k >> 2); i += 32) {
+      const float4 v = __ldg(b4 + i);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int ce = act_range_exp(mx);
+    const float c = exp2_int(ce);
+    if (lane == 0) colf[nr] = __fmul_rn(alpha, exp2_int(-ce));
+    __half* xrow = wx + (size_t)nr * 2 * k;
+    for (int i = lane; i < (k >> 2); i += 32) {
+      const float4 v = __ldg(b4 + i);
+      uint2 hi, lo;
+      split_act_pair(v.x, v.y, c, hi.x, lo.x);
+      split_act_pair(v.z, v.w, c, hi.y, lo.y);
+      const int k0 = 4 * i;
+      __half* dst = xrow + 128 * (k0 >> 6) + (k0 & 63);
+      *reinterpret_cast<uint2*>(dst) = hi;
+      *reinterpret_cast<uint2*>(dst + 64) = lo;
+    }
+    return;
+  }
+  // block (strip, kb): tile [64 k][32 columns] (lane = column for the loads),
+  // then thread (column j, part p) converts k = 16 p .. 16 p + 15 of it
+  __shared__ float cs[32];
+  __shared__ float tile[64][33];
+  const int nkb = k >> 6, strip = (int)blockIdx.x / nkb, kb = (int)blockIdx.x - strip * nkb;
+  const int cl0 = 32 * strip, col = n0 + cl0 + lane;
+  const bool live = cl0 + lane < nc && col < n;
+  for (int r = warp; r < 64; r += 4) tile[r][lane] = live ? __ldg(B + (size_t)(64 * kb + r) * ldb + col) : 0.0f;
+  if (warp == 0) {
+    float m = 0.0f;
+    if (cl0 + lane < nc)
+      for (int j = 0; j < nsl; ++j) m = fmaxf(m, pmax[(size_t)j * nc + cl0 + lane]);
+    const int ce = act_range_exp(m);
+    cs[lane] = exp2_int(ce);
+    if (kb == 0 && cl0 + lane < nc) colf[cl0 + lane] = __fmul_rn(alpha, exp2_int(-ce));
+  }
+  __syncthreads();
+  const int j = threadIdx.x >> 2, p = threadIdx.x & 3;
+  if (cl0 + j < nc) {
+    const float cj = cs[j];
+    uint32_t h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split_act_pair(tile[16 * p + 2 * e][j], tile[16 * p + 2 * e + 1][j], cj, h[e], l[e]);
+    __half* dst = wx + (size_t)(cl0 + j) * 2 * k + 128 * kb + 16 * p;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(dst + 8) = make_uint4(h[4], h[5], h[6], h[7]);
+    *reinterpret_cast<uint4*>(dst + 64) = make_uint4(l[0], l[1], l[2], l[3]);
+    *reinterpret_cast<uint4*>(dst + 72) = make_uint4(l[4], l[5], l[6], l[7]);
+  }
 }
 
 // ---- skinny path (m <= 16) -----------------------------------------------------

@@ -126,6 +126,12 @@ struct StreamScratch {
 int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
                  const float* bias, float* Y, cudaStream_t s, bool weights_ready);
 
+// C = alpha * A . op(B) + bias (beta = 0) on the f16-term tensor-core GEMM of
+// the weight-only path (oc_qgemm_wo.cu), when sgemm_terms_ok.
+bool sgemm_terms_ok(int m, int k, const float* A, int lda, const float* B, int ldb, int trans_b);
+int run_sgemm_terms(int m, int n, int k, float alpha, const float* A, int lda, const float* B, int ldb, int trans_b,
+                    float* C, int ldc, const float* bias, cudaStream_t s);
+
 // Launches `kern` with programmatic stream serialization (the kernel must
 // begin with pdl_wait(), oc_ptx.cuh); returns the launch status.
 template <typename... KArgs, typename... Args>

@@ -115,6 +115,8 @@ static int run_wo_skinny(int m, int n, int k, int group, const float* A, const u
 // chunk (wx, then icn), split-K partial sums and ready counters; one buffer
 // each per (device, stream).
 static StreamScratch g_wo_ax, g_wo_wx, g_wo_part, g_wo_ready;
+// sgemm on f16 terms: per-slice column maxima of B (column-major case)
+static StreamScratch g_sg_pmax;
 
 // The weights whose terms the (device, stream) scratch holds, when one chunk
 // covered all columns: a later call with weights_ready on the same stream
@@ -349,6 +351,94 @@ static int run_wo_gemm(int m, int n, int k, int group, const float* A, const voi
   if (nc == n && !skip_expand) {
     std::lock_guard<std::mutex> lk(g_wo_mu);
     g_wo_expanded[key] = WoExpanded{wq, sw, WT == 2 ? 4 : 8, n, k, group};
+  }
+  return OC_OK;
+}
+
+// f32 C = alpha * A . op(B) + bias (beta = 0) on the f16-term GEMM: B's
+// columns prepared like the INT4 weights' (two terms, a power of two per
+// column, alpha folded into the column factor), in the same L2-sized column
+// chunks and with the same tile and split rules.  k % 64 == 0, A 16-byte
+// aligned with lda % 4 == 0 (and for trans_b, B likewise with ldb % 4 == 0).
+bool sgemm_terms_ok(int m, int k, const float* A, int lda, const float* B, int ldb, int trans_b) {
+  return m > kWoSkinnyM && is_sm100() && k % 64 == 0 && aligned16(A) && lda % 4 == 0 &&
+         (!trans_b || (aligned16(B) && ldb % 4 == 0));
+}
+
+int run_sgemm_terms(int m, int n, int k, float alpha, const float* A, int lda, const float* B, int ldb, int trans_b,
+                    float* C, int ldc, const float* bias, cudaStream_t s) {
+  constexpr int WT = 2;
+  const size_t col_bytes = (size_t)k * 4 + 4;  // two f16 terms (+ the column factor) per column
+  const int nc = (int)std::min<size_t>((size_t)n, std::max<size_t>(128, kWoChunkBytes / col_bytes / 128 * 128));
+  float* axb = g_wo_ax.get((size_t)m * k + (size_t)m, s);
+  float* wxb = g_wo_wx.get((size_t)nc * k + (size_t)nc, s);
+  if (!axb || !wxb) return fail(OC_ERR_OUT_OF_MEMORY, "sgemm: scratch allocation failed");
+  __half* ax = reinterpret_cast<__half*>(axb);
+  float* icm = axb + (size_t)m * k;
+  __half* wx = reinterpret_cast<__half*>(wxb);
+  float* colf = wxb + (size_t)nc * k;
+  {  // the term scratch no longer holds any weight-only call's weights
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_wo_mu);
+    g_wo_expanded[std::make_pair(dev, s)] = WoExpanded{};
+  }
+  const int sms = std::max(1, sm_count()), tiles_n = (nc + 127) / 128;
+  auto rounds = [&](int bm) { return ((m + bm - 1) / bm * tiles_n + sms - 1) / sms; };
+  const int bm = rounds(192) * 875 < rounds(256) * 1030 ? 192 : 256;
+  CUtensorMap ta;
+  int rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
+                        kWoBK, bm, kWoSwizzle);
+  if (rc) return rc;
+  for (int n0 = 0; n0 < n; n0 += nc) {
+    const int ncur = std::min(nc, n - n0);
+    const int cl_ks = wo_cl_ks<WT>(m, ncur, k);
+    const int nsplit = cl_ks ? 0 : wo_nsplit(m, ncur, k, bm);
+    int* ready = nullptr;
+    if (nsplit) {
+      ready = reinterpret_cast<int*>(g_wo_ready.get((size_t)nsplit, s));
+      if (!ready) return fail(OC_ERR_OUT_OF_MEMORY, "sgemm: scratch allocation failed");
+    }
+    const int ma = n0 == 0 ? m : 0;
+    if (trans_b) {
+      rc = wo_launch_rc(launch_pdl_ex(f32_terms_kernel<1>, dim3((ncur + 3) / 4 + ma), dim3(128), 0, s, A, lda, ma, k,
+                                      ax, icm, B, ldb, n, n0, ncur, alpha, (const float*)nullptr, 0, wx, colf, ready,
+                                      nsplit),
+                        "f32_terms_kernel");
+    } else {  // column maxima over k slices first, then the 64-k blocks in parallel
+      const int strips = (ncur + 31) / 32, nsl = (k + kF32MaxSlice - 1) / kF32MaxSlice;
+      float* pmax = g_sg_pmax.get((size_t)nsl * ncur, s);
+      if (!pmax) return fail(OC_ERR_OUT_OF_MEMORY, "sgemm: scratch allocation failed");
+      rc = wo_launch_rc(launch_pdl_ex(f32_colmax_kernel, dim3(strips, nsl), dim3(128), 0, s, B, ldb, n, n0, ncur, k,
+                                      pmax),
+                        "f32_colmax_kernel");
+      if (rc) return rc;
+      rc = wo_launch_rc(launch_pdl_ex(f32_terms_kernel<0>, dim3(strips * (k >> 6) + ma), dim3(128), 0, s, A, lda, ma,
+                                      k, ax, icm, B, ldb, n, n0, ncur, alpha, (const float*)pmax, nsl, wx, colf, ready,
+                                      nsplit),
+                        "f32_terms_kernel");
+    }
+    if (rc) return rc;
+    CUtensorMap tw;
+    rc = make_tmap_2d(&tw, wx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)ncur, (uint64_t)k * 4,
+                      kWoBK, 128, kWoSwizzle);
+    if (rc) return rc;
+    const float* bc = bias ? bias + n0 : nullptr;
+    float* Cc = C + n0;
+    if (cl_ks) {
+      const int bmc = wo_cl_bm(m);
+      CUtensorMap tac;
+      rc = make_tmap_2d(&tac, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
+                        kWoBK, bmc, kWoSwizzle);
+      if (rc) return rc;
+      rc = bmc == 128 ? launch_wo_cl<128, WT>(tac, tw, cl_ks, m, ncur, k, ldc, icm, colf, bc, Cc, s)
+                      : launch_wo_cl<192, WT>(tac, tw, cl_ks, m, ncur, k, ldc, icm, colf, bc, Cc, s);
+    } else if (bm == 192) {
+      rc = launch_wo_gemm<192, WT>(ta, tw, m, ncur, k, ldc, icm, colf, bc, Cc, s);
+    } else {
+      rc = launch_wo_gemm<256, WT>(ta, tw, m, ncur, k, ldc, icm, colf, bc, Cc, s);
+    }
+    if (rc) return rc;
   }
   return OC_OK;
 }

@@ -4,7 +4,12 @@
 // b[kk*n + col]) or B^T with B [n][ldb] (trans_b = 1, the transpose_b form,
 // blas:206-210).
 //
-// Large shapes: persistent tcgen05 kind::tf32 kernel with the 3xTF32 split
+// beta == 0 with m > 16 and k % 64 == 0 (the Linear / MLA / blas calls) runs
+// the f16-term GEMM of the weight-only path (run_sgemm_terms, oc_qgemm_wo.cu):
+// each row of A and column of op(B) scaled by a power of two, split into
+// hi = f16(t) and lo = f16(t - hi), three kind::f16 MMAs per K = 16 step.
+//
+// Other large shapes: persistent tcgen05 kind::tf32 kernel with the 3xTF32 split
 //   a*b ~= lo(a)hi(b) + hi(a)lo(b) + hi(a)hi(b),  hi = rna_tf32(x),
 //   lo = rna_tf32(x - hi)
 // Both operands are K-major in shared memory (128-byte swizzle):
@@ -611,6 +616,11 @@ int oc_sgemm(int m, int n, int k, float alpha, const float* A, int lda, const fl
     return launch_reduce(m, n, 0, nullptr, alpha, beta, C, ldc, bias, s);
   }
   OC_REQUIRE(A && B, "sgemm: NULL pointer");
+  // beta = 0 (Linear::forward, the blas entry points, MLA): the f16-term
+  // GEMM, three kind::f16 MMAs per K = 16 step where 3xTF32 takes three
+  // kind::tf32 MMAs per K = 8
+  if (beta == 0.0f && m > kGemvM && sgemm_terms_ok(m, k, A, lda, B, ldb, trans_b))
+    return run_sgemm_terms(m, n, k, alpha, A, lda, B, ldb, trans_b, C, ldc, bias, s);
   const bool tma_ok = is_sm100() && aligned16(A) && (lda % 4 == 0);
   if (m > kGemvM && tma_ok) {
     const int kp = kpad(k);

@@ -1,4 +1,4 @@
-"""GPU parity of oc_sgemm (3xTF32 tcgen05 GEMM and the small-m GEMV) against
+"""GPU parity of oc_sgemm (f16-term and 3xTF32 tcgen05 GEMMs, the small-m GEMV) against
 the oracle's restatement of the reference's naive sgemm (blas:148-295).
 
 Tolerance: 1e-5 relative Frobenius error (the bound the north star sets for
@@ -100,3 +100,28 @@ def test_sgemm_k_zero_scales_c(oc):
     C0 = torch.full((3, 5), 2.0, device="cuda")
     out = oc.sgemm(torch.empty(3, 0, device="cuda"), torch.empty(0, 5, device="cuda"), beta=0.5, C=C0)
     assert torch.all(out == 1.0)
+
+
+@pytest.mark.parametrize("trans_b", [False, True])
+@pytest.mark.parametrize("m,k,n", [(200, 640, 300), (64, 768, 20000), (40, 2048, 2304)])
+def test_sgemm_value_ranges(oc, oracle, m, k, n, trans_b):
+    """beta = 0 with k % 64 == 0 and m > 16 runs the f16-term GEMM: every row
+    of A and column of op(B) is scaled by its own power of two before the
+    split, so rows and columns far apart in magnitude (1e-25 .. 1e6), zero
+    rows and columns, alpha != 1 and column chunks past the first (n = 20000)
+    keep the f32 bound."""
+    A = synth.uniform(21, m * k).reshape(m, k) * (10.0 ** np.linspace(-25, 6, m))[:, None]
+    Bkn = synth.uniform(22, k * n).reshape(k, n) * (10.0 ** np.linspace(-20, 5, n))[None, :]
+    A[3] = 0.0
+    Bkn[:, 7] = 0.0
+    A, Bkn = A.astype(np.float32), Bkn.astype(np.float32)
+    B = np.ascontiguousarray(Bkn.T) if trans_b else Bkn
+    alpha = 0.37
+    ref = oracle.sgemm(m, k, n, alpha, A, B, 0.0, np.zeros(m * n), transpose_b=trans_b).reshape(m, n)
+    got = oc.sgemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), alpha=alpha, transpose_b=trans_b)
+    got = got.cpu().numpy()
+    assert rel_fro(got, ref) < TOL
+    # per row as well: a row 1e-25 times the largest keeps its own relative error
+    for r in (0, 1, m // 2, m - 1):
+        assert rel_fro(got[r], ref[r]) < TOL, r
+    assert np.all(got[3] == 0.0) and np.all(got[:, 7] == 0.0)
