@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-once", action="store_true",
                     help="run one warm pass of the workload's kernels and exit (for ncu launch lists)")
+    ap.add_argument("--a8-k3584", action="store_true",
+                    help="with --workload qgemm_a8 --profile-once: only the W8A8 GEMM at M=2048 K=3584 N=18944, "
+                         "twice (for an ncu capture of the long-K kind::i8 kernel)")
     return ap.parse_args()
 
 
@@ -527,6 +530,16 @@ def run_qgemm(ctx):
     torch, oc, args = ctx.torch, ctx.oc, ctx.args
     import synth
 
+    if args.profile_once and args.a8_k3584:
+        m, n, K = A8_BIG[0][0], A8_BIG[0][1], 3584
+        g = torch.Generator(device=ctx.device).manual_seed(9)
+        qw, sw = oc.quantize_int8((torch.randn(n, K, generator=g, device=ctx.device) * 0.02).view(-1), K)
+        qa, sa = oc.quantize_rows_int8(torch.rand(m, K, generator=g, device=ctx.device) * 2 - 1)
+        Y = torch.empty(m, n, device=ctx.device)
+        for _ in range(2):
+            oc.igemm_w8a8(qa, sa, qw.view(n, K), sw, None, out=Y)
+        torch.cuda.synchronize()
+        return
     A, WT, bias = synth.qgemm_case(max(Q_M), Q_K, Q_N)
     Wd = torch.from_numpy(WT).to(ctx.device)
     q8, s8 = oc.quantize_int8(Wd, Q_K)       # per output channel
@@ -709,6 +722,16 @@ def run_qgemm_a8(ctx):
     torch, oc, args = ctx.torch, ctx.oc, ctx.args
     import synth
 
+    if args.profile_once and args.a8_k3584:
+        m, n, K = A8_BIG[0][0], A8_BIG[0][1], 3584
+        g = torch.Generator(device=ctx.device).manual_seed(9)
+        qw, sw = oc.quantize_int8((torch.randn(n, K, generator=g, device=ctx.device) * 0.02).view(-1), K)
+        qa, sa = oc.quantize_rows_int8(torch.rand(m, K, generator=g, device=ctx.device) * 2 - 1)
+        Y = torch.empty(m, n, device=ctx.device)
+        for _ in range(2):
+            oc.igemm_w8a8(qa, sa, qw.view(n, K), sw, None, out=Y)
+        torch.cuda.synchronize()
+        return
     A, WT, bias = synth.qgemm_case(max(Q_M), Q_K, Q_N)
     Wd = torch.from_numpy(WT).to(ctx.device)
     q8, s8 = oc.quantize_int8(Wd, Q_K)
