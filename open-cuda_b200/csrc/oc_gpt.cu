@@ -164,13 +164,21 @@ __global__ void __launch_bounds__(kAttnThreads)
   float* red = part + kAttnThreads;       // [32]
   float* qs = red + 32;                   // [kAttnMaxD]
   float* s = qs + kAttnMaxD;              // [max_seq] scores, then exp
-  pdl_wait();
-  pdl_launch();
   const int gw = blockIdx.x;
-  if (gw >= rows * heads) return;
+  if (gw >= rows * heads) {
+    pdl_wait();
+    pdl_launch();
+    return;
+  }
   const int r = gw / heads, h = gw % heads;
   const int b = r / L, i = r % L;
-  const int n = *pos0 + i + 1;
+  // The position counter and the cache rows before it were written by
+  // earlier forwards, and every kernel of this stream waits for its
+  // predecessor before it lets its successor start, so all but the
+  // predecessor (the QKV linear writing rows p0 ..) have completed here:
+  // those are read ahead of the dependency wait.
+  const int p0 = *pos0;
+  const int n = p0 + i + 1;
   const float* q = qkv + (size_t)r * 3 * H + h * d;
   const float* kb = kc + (size_t)b * max_seq * H + h * d;
   const float* vb = vc + (size_t)b * max_seq * H + h * d;
@@ -180,8 +188,13 @@ __global__ void __launch_bounds__(kAttnThreads)
   // one tile of keys: V goes into the second buffer together with K, so its
   // loads are in flight during the scores (K waits alone below)
   const bool one = ntiles == 1;
-  attn_stage(buf, kb, 0, min(kAttnTile, n), d, H, vec);
-  if (one) attn_stage(buf + tile_f, vb, 0, n, d, H, vec);
+  const int t0 = min(kAttnTile, n), pre = min(t0, p0);  // tile 0: rows cached before this forward
+  attn_stage(buf, kb, 0, pre, d, H, vec);
+  if (one) attn_stage(buf + tile_f, vb, 0, pre, d, H, vec);
+  pdl_wait();
+  pdl_launch();
+  attn_stage(buf + pre * d, kb, pre, t0 - pre, d, H, vec);
+  if (one) attn_stage(buf + tile_f + pre * d, vb, pre, n - pre, d, H, vec);
   for (int c = threadIdx.x; c < d; c += kAttnThreads) qs[c] = q[c];
   // pass 1: scores
   float mx = -INFINITY;
@@ -409,6 +422,8 @@ struct GemvArgs {
   int L, H, max_seq;
   const float *ln_w, *ln_b;  // optional LayerNorm of the x rows (llm:252-262) before the product
   float ln_eps;
+  int cb;       // gemv_cols_kernel: output columns per CTA (W is then [n][k])
+  int* status;  // device status word (bounded waits)
 };
 
 // bias = a.bias[col] and old = the output's previous value (kEpiResidual),
@@ -435,6 +450,71 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int r, int col,
     }
     default:
       *o = y;
+  }
+}
+
+// LayerNorm statistics of each x row (warp per row, 256 threads): mean =
+// sum / k, var = sum (x - mean)^2 / k, inv = 1 / sqrt(var + eps) into
+// mean[r], inv[r].  Rows of up to 1024 floats stay in registers between the
+// two sums (one read of x).
+__device__ __forceinline__ void ln_row_stats(const GemvArgs& a, float* ln_mean, float* ln_inv) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < a.m; r += 8) {
+    const float* xr = a.x + (size_t)r * a.k;
+    float sm = 0.0f;
+    if ((a.k & 3) == 0 && a.k <= 1024) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane * 4 + 128 * j;
+        v[j] = c < a.k ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (lane * 4 + 128 * j < a.k) sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v[j].x), v[j].y), v[j].z), v[j].w);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+      const float mean = __fdiv_rn(sm, (float)a.k);
+      float vs = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (lane * 4 + 128 * j < a.k) {
+          const float d0 = __fsub_rn(v[j].x, mean), d1 = __fsub_rn(v[j].y, mean);
+          const float d2 = __fsub_rn(v[j].z, mean), d3 = __fsub_rn(v[j].w, mean);
+          vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+      if (lane == 0) {
+        ln_mean[r] = mean;
+        ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)a.k), a.ln_eps)));
+      }
+      continue;
+    }
+    if ((a.k & 3) == 0) {
+#pragma unroll 4
+      for (int c = lane * 4; c < a.k; c += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + c);
+        sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v.x), v.y), v.z), v.w);
+      }
+    } else {
+      for (int c = lane; c < a.k; c += 32) sm = __fadd_rn(sm, xr[c]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+    const float mean = __fdiv_rn(sm, (float)a.k);
+    float vs = 0.0f;
+    for (int c = lane; c < a.k; c += 32) {
+      const float dv = __fsub_rn(xr[c], mean);
+      vs = __fmaf_rn(dv, dv, vs);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+    if (lane == 0) {
+      ln_mean[r] = mean;
+      ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)a.k), a.ln_eps)));
+    }
   }
 }
 
@@ -508,66 +588,7 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
   pdl_wait();  // x, out, the KV cache and the counters belong to the predecessors until here
   pdl_launch();
   if (a.ln_w) {
-    // LayerNorm statistics of each x row (warp per row): mean = sum / k,
-    // var = sum (x - mean)^2 / k, inv = 1 / sqrt(var + eps).  Rows of up to
-    // 1024 floats stay in registers between the two sums (one read of x).
-    for (int r = warp; r < a.m; r += 8) {
-      const float* xr = a.x + (size_t)r * a.k;
-      float sm = 0.0f;
-      if ((a.k & 3) == 0 && a.k <= 1024) {
-        float4 v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int c = lane * 4 + 128 * j;
-          v[j] = c < a.k ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (lane * 4 + 128 * j < a.k) sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v[j].x), v[j].y), v[j].z), v[j].w);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
-        const float mean = __fdiv_rn(sm, (float)a.k);
-        float vs = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (lane * 4 + 128 * j < a.k) {
-            const float d0 = __fsub_rn(v[j].x, mean), d1 = __fsub_rn(v[j].y, mean);
-            const float d2 = __fsub_rn(v[j].z, mean), d3 = __fsub_rn(v[j].w, mean);
-            vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
-        if (lane == 0) {
-          ln_mean[r] = mean;
-          ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)a.k), a.ln_eps)));
-        }
-        continue;
-      }
-      if ((a.k & 3) == 0) {
-#pragma unroll 4
-        for (int c = lane * 4; c < a.k; c += 128) {
-          const float4 v = *reinterpret_cast<const float4*>(xr + c);
-          sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v.x), v.y), v.z), v.w);
-        }
-      } else {
-        for (int c = lane; c < a.k; c += 32) sm = __fadd_rn(sm, xr[c]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
-      const float mean = __fdiv_rn(sm, (float)a.k);
-      float vs = 0.0f;
-      for (int c = lane; c < a.k; c += 32) {
-        const float dv = __fsub_rn(xr[c], mean);
-        vs = __fmaf_rn(dv, dv, vs);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
-      if (lane == 0) {
-        ln_mean[r] = mean;
-        ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)a.k), a.ln_eps)));
-      }
-    }
+    ln_row_stats(a, ln_mean, ln_inv);
     __syncthreads();
   }
   for (int i = threadIdx.x; i < MR * a.ks; i += 256) {
@@ -686,6 +707,163 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const GemvArgs a) {
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
 }
 
+// Decode GEMV with the weights transposed to [n][k] (a.W = the linear's wt):
+// CTA b computes columns b*cb .. +cb over the whole of k, so no partial sum
+// leaves the CTA (no second pass, no counter).  Its weights are one
+// contiguous block of cb*k floats, requested by one bulk copy into shared
+// memory before the dependency wait, so they stream in while the preceding
+// kernel still runs.  After the wait the CTA copies its x rows into shared
+// memory (normalised there when ln_w) and waits for the weights (bounded); then
+// T = 256 / cb threads per column sum float4 strips of k (each quarter warp
+// reads 128 contiguous bytes: no bank conflicts), the T sums meet by
+// shuffles (and through shared memory when T = 64), and the column's first
+// thread applies the epilogue.  Requires cb in {4, 8, 16, 32}, k % 4 == 0,
+// W, x 16-byte aligned, rows <= MR, (cb + MR) * k * 4 bytes of shared memory.
+template <int MR>
+__global__ void __launch_bounds__(256) gemv_cols_kernel(const GemvArgs a) {
+  extern __shared__ __align__(16) float gsm[];
+  const int cb = a.cb, k = a.k, k4 = k >> 2;
+  float* ws = gsm;                   // [cb][k]
+  float* xs = gsm + (size_t)cb * k;  // [MR][k]
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  __shared__ float ln_mean[MR], ln_inv[MR];
+  __shared__ float wsum[8][MR];
+  const int c0 = (int)blockIdx.x * cb, ncol = min(cb, a.n - c0);
+  const uint32_t wbytes = (uint32_t)ncol * (uint32_t)k * 4u;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    // the weights are written by no kernel of the step: safe before the wait
+    mbar_arrive_expect_tx(&bar, wbytes);
+    bulk_load_1d(ws, a.W + (size_t)c0 * k, wbytes, &bar);
+  }
+  const int T = 256 / cb, col = (int)threadIdx.x / T, part = (int)threadIdx.x - col * T;
+  const bool live = col < ncol;
+  const float bias = live ? __ldg(a.bias + c0 + col) : 0.0f;  // a constant parameter
+  pdl_wait();  // x, out and the KV cache belong to the predecessors until here
+  pdl_launch();
+  // x rows into shared memory (x is read once); the residual's previous
+  // output values in flight at the same time
+  for (int i = threadIdx.x; i < a.m * k4; i += 256) {
+    const int r = i / k4, c = 4 * (i - r * k4);
+    *reinterpret_cast<float4*>(xs + (size_t)r * k + c) = *reinterpret_cast<const float4*>(a.x + (size_t)r * k + c);
+  }
+  float old[MR];
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+    old[r] = a.epi == kEpiResidual && live && part == 0 && r < a.m ? a.out[(size_t)r * a.n + c0 + col] : 0.0f;
+  __syncthreads();
+  if (a.ln_w) {
+    // LayerNorm statistics (warp per row; the sums in the order of
+    // ln_row_stats), then the rows normalised in place
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r = warp; r < a.m; r += 8) {
+      const float* xr = xs + (size_t)r * k;
+      float sm = 0.0f;
+      for (int c = lane * 4; c < k; c += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + c);
+        sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v.x), v.y), v.z), v.w);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+      const float mean = __fdiv_rn(sm, (float)k);
+      float vs = 0.0f;
+      for (int c = lane * 4; c < k; c += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + c);
+        const float d0 = __fsub_rn(v.x, mean), d1 = __fsub_rn(v.y, mean);
+        const float d2 = __fsub_rn(v.z, mean), d3 = __fsub_rn(v.w, mean);
+        vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+      if (lane == 0) {
+        ln_mean[r] = mean;
+        ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)k), a.ln_eps)));
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < a.m * k4; i += 256) {
+      const int r = i / k4, c = 4 * (i - r * k4);
+      float4 v = *reinterpret_cast<const float4*>(xs + (size_t)r * k + c);
+      const float4 w = __ldg(reinterpret_cast<const float4*>(a.ln_w + c));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(a.ln_b + c));
+      const float mu = ln_mean[r], inv = ln_inv[r];
+      v.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu), inv), w.x), b.x);
+      v.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu), inv), w.y), b.y);
+      v.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu), inv), w.z), b.z);
+      v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu), inv), w.w), b.w);
+      *reinterpret_cast<float4*>(xs + (size_t)r * k + c) = v;
+    }
+  }
+  __syncthreads();
+  if (!mbar_wait(&bar, 0, &abort_flag)) {
+    // the weight copy did not land within the wall-clock limit: report it
+    // (the host turns the status into an error) instead of waiting on
+    if (threadIdx.x == 0) kernel_fail(a.status, &abort_flag, kDevTimeoutProducer);
+    return;
+  }
+  float acc[MR];
+#pragma unroll
+  for (int r = 0; r < MR; ++r) acc[r] = 0.0f;
+  if (live) {
+    const float4* wr = reinterpret_cast<const float4*>(ws + (size_t)col * k);
+    const float4* xr = reinterpret_cast<const float4*>(xs);
+#pragma unroll 4
+    for (int j = part; j < k4; j += T) {
+      const float4 w = wr[j];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        if (r < a.m) {
+          const float4 xv = xr[r * k4 + j];
+          acc[r] = __fmaf_rn(xv.w, w.w, __fmaf_rn(xv.z, w.z, __fmaf_rn(xv.y, w.y, __fmaf_rn(xv.x, w.x, acc[r]))));
+        }
+      }
+    }
+  }
+  // the T partial sums of a column: lanes of one group (T <= 32 lanes, groups
+  // aligned to T) by shuffles, then the column's warps in order (T = 64)
+  const int tw = T < 32 ? T : 32;
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+    for (int o = tw >> 1; o > 0; o >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+  if (T > 32) {
+    const int warp = threadIdx.x >> 5, nw = T >> 5;
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) wsum[warp][r] = acc[r];
+    __syncthreads();
+    if (part == 0)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        float t = 0.0f;
+        for (int i = 0; i < nw; ++i) t = __fadd_rn(t, wsum[warp + i][r]);
+        acc[r] = t;
+      }
+  }
+  if (!live || part != 0) return;
+  const int cc = c0 + col;
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+    if (r < a.m) gemv_epilogue(a, r, cc, acc[r], bias, old[r]);
+}
+
+// Transposes a linear's weights w [in][out] into wt [out][in] (32 x 32 tiles).
+__global__ void transpose_kernel(const float* __restrict__ w, int in, int out, float* __restrict__ wt) {
+  __shared__ float t[32][33];
+  const int o0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int i = i0 + r, o = o0 + threadIdx.x;
+    t[r][threadIdx.x] = (i < in && o < out) ? w[(size_t)i * out + o] : 0.0f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int o = o0 + r, i = i0 + threadIdx.x;
+    if (o < out && i < in) wt[(size_t)o * in + i] = t[threadIdx.x][r];
+  }
+}
+
 struct GemvPlan {
   int vec, tn, tiles, ks, slices;
   size_t smem;
@@ -719,6 +897,7 @@ struct GptLinear {
   float* w = nullptr;     // [in][out]
   float* b = nullptr;     // [out]
   float* prep = nullptr;  // tf32 hi/lo [out][in] for the tensor-core path
+  float* wt = nullptr;    // [out][in] copy of w for gemv_cols_kernel (null: not used)
   int in = 0, out = 0;
 };
 
@@ -739,6 +918,7 @@ struct oc_gpt {
   float *hidden, *normed, *qkv, *ctx, *inter, *logits, *part;
   size_t part_floats = 0;
   unsigned* counters = nullptr;  // decode GEMV column-tile counters
+  int* status = nullptr;         // device status word (bounded in-kernel waits)
   size_t counter_count = 0;
   ArgmaxScratch arg{};
   float *kc, *vc;  // [layer][batch][max_seq][H]
@@ -780,6 +960,18 @@ int galloc_t(oc_gpt* g, size_t count, T** p) {
   return rc;
 }
 
+// Output columns per CTA of gemv_cols_kernel for a linear in -> out: the
+// smallest power of two in [4, 32] that makes at most two CTAs per SM, if
+// that CTA's weights (cb * in floats) fit 64 KB of shared memory; else 0
+// (the linear runs the split-K GEMV).
+static int gemv_cols_cb(int in, int out) {
+  if (in % 4) return 0;
+  const int ctas = 2 * std::max(1, sm_count());
+  for (int cb = 4; cb <= 32; cb *= 2)
+    if ((out + cb - 1) / cb <= ctas) return (size_t)cb * in * sizeof(float) <= (64u << 10) ? cb : 0;
+  return 0;
+}
+
 int linear_alloc(oc_gpt* g, GptLinear& L, int in, int out) {
   L.in = in;
   L.out = out;
@@ -789,6 +981,7 @@ int linear_alloc(oc_gpt* g, GptLinear& L, int in, int out) {
   if ((rc = galloc_t(g, (size_t)in * out, &L.w)) || (rc = galloc_t(g, (size_t)out, &L.b)) ||
       (rc = galloc_t(g, pb / sizeof(float), &L.prep)))
     return rc;
+  if (gemv_cols_cb(in, out) && (rc = galloc_t(g, (size_t)in * out, &L.wt))) return rc;
   return OC_OK;
 }
 
@@ -826,6 +1019,14 @@ static void launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
   launch_pdl(kern, dim3(p.tiles, p.slices), dim3(256), p.smem, s, a);
 }
 
+template <int MR>
+static void launch_cols(const GemvArgs& a, cudaStream_t s) {
+  auto kern = gemv_cols_kernel<MR>;
+  const size_t smem = ((size_t)a.cb + MR) * a.k * sizeof(float);
+  smem_attr_once(reinterpret_cast<const void*>(kern), std::max<size_t>(smem, 48 * 1024));
+  launch_pdl(kern, dim3((a.n + a.cb - 1) / a.cb), dim3(256), smem, s, a);
+}
+
 // Rows up to which a linear runs as the fused split-K GEMV; more rows go to
 // the 3xTF32 tensor-core GEMM (split-K when its tiles are few).
 constexpr int kGptGemvRows = 16;
@@ -859,6 +1060,13 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
     int rc = sgemm_prepared_epi(rows, L.out, L.in, x, L.in, L.prep, out, L.out, L.b, ge, s);
     if (rc) return rc;
     *n += 1;  // one tensor-core GEMM launch (plus its split-K reduction when split)
+  } else if (const int cb = L.wt && rows <= 4 ? gemv_cols_cb(L.in, L.out) : 0) {
+    // whole-k columns per CTA from the transposed copy
+    GemvArgs a{rows, L.out, L.in, L.in, 1, epi, x, L.wt, L.b, nullptr, nullptr, out,
+               kc, vc, g->pos, seq_rows, H, ms, ln_w, ln_b, g->cfg.layer_norm_eps, cb, g->status};
+    if (rows <= 1) launch_cols<1>(a, s);
+    else launch_cols<4>(a, s);
+    *n += 1;
   } else {
     const GemvPlan p = gemv_plan(L.in, L.out, rows);
     GemvArgs a{rows, L.out, L.in, p.ks, p.slices, epi, x, L.w, L.b, g->part, g->counters, out,
@@ -995,6 +1203,8 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
   const size_t attn_smem = attn_smem_bytes((int)ms, (int)(H / cfg->num_heads));
   if (!smem_attr_once(reinterpret_cast<const void*>(decode_attention_kernel), attn_smem))
     return bail(fail(OC_ERR_NOT_SUPPORTED, "gpt_create: max_seq_len too large for the attention kernel"));
+  if (!(g->status = device_status_word()))
+    return bail(fail(OC_ERR_LAUNCH_FAILED, "gpt_create: device status word unavailable"));
   *out = g;
   return OC_OK;
 }
@@ -1010,10 +1220,18 @@ int oc_gpt_destroy(oc_gpt* g) {
   return OC_OK;
 }
 
+// The derived copies of a linear's weights: the tensor-core GEMM's tf32
+// planes and, where the linear has one, the transposed copy of the GEMV.
+static int prepare_linear(oc_gpt* g, GptLinear& L) {
+  int rc = oc_sgemm_prepare_b(L.in, L.out, L.w, L.out, 0, L.prep, g->stream);
+  if (rc || !L.wt) return rc;
+  transpose_kernel<<<dim3((L.out + 31) / 32, (L.in + 31) / 32), dim3(32, 8), 0, g->stream>>>(L.w, L.in, L.out, L.wt);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OC_OK : from_cuda(e, "gpt: weight transpose");
+}
+
 static int prepare_all(oc_gpt* g) {
-  auto prep = [&](GptLinear& L) {
-    return oc_sgemm_prepare_b(L.in, L.out, L.w, L.out, 0, L.prep, g->stream);
-  };
+  auto prep = [&](GptLinear& L) { return prepare_linear(g, L); };
   int rc;
   for (auto& Ly : g->layers)
     if ((rc = prep(Ly.qkv)) || (rc = prep(Ly.ao)) || (rc = prep(Ly.fc)) || (rc = prep(Ly.pj))) return rc;
@@ -1110,7 +1328,7 @@ int oc_gpt_set_weight(oc_gpt* g, int which, int layer, const float* host, size_t
   Scope sc(g->device);
   OC_CHECK_CUDA(cudaMemcpyAsync(dst, host, n * sizeof(float), cudaMemcpyHostToDevice, g->stream));
   if (lin) {
-    rc = oc_sgemm_prepare_b(lin->in, lin->out, lin->w, lin->out, 0, lin->prep, g->stream);
+    rc = prepare_linear(g, *lin);
     if (rc) return rc;
   }
   OC_CHECK_CUDA(cudaStreamSynchronize(g->stream));
