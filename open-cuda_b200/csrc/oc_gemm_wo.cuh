@@ -720,38 +720,59 @@ __global__ void __launch_bounds__(128) wo_prep_kernel(const float* __restrict__ 
 // colf[n] = alpha / c_n, so the epilogue forms alpha * A.B + bias.  k % 64 ==
 // 0; TB additionally ldb % 4 == 0 and B 16-byte aligned.
 
-constexpr int kF32MaxSlice = 256;  // k rows per block of the column-maximum pass (TB = 0)
+constexpr int kF32MaxSlice = 64;  // k rows per block of the column-maximum pass (TB = 0)
+constexpr int kF32MaxStrip = 128;  // columns per block of that pass: 4 per lane
 
-// TB = 0, pass 1: block (strip of 32 columns, k slice) -> the slice's column
-// maxima at pmax[slice][column] (lane = column: each row read is coalesced).
+// TB = 0, pass 1: block (strip of 128 columns, 64-row k slice) -> the
+// slice's column maxima at pmax[slice][column].  Lane = 4 adjacent columns
+// (one 16-byte load when B allows it), warp = every 4th row of the slice:
+// sixteen loads per thread in flight, 512 contiguous bytes per warp load.
 __global__ void __launch_bounds__(128) f32_colmax_kernel(const float* __restrict__ B, int ldb, int n, int n0, int nc,
                                                          int k, float* __restrict__ pmax) {
   pdl_wait();
   pdl_launch();
-  __shared__ float cm[4][32];
+  __shared__ float4 cm[4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cl = 32 * (int)blockIdx.x + lane, col = n0 + cl;
-  const bool live = cl < nc && col < n;
+  const int cl = kF32MaxStrip * (int)blockIdx.x + 4 * lane, col = n0 + cl;
   const int k0 = (int)blockIdx.y * kF32MaxSlice, k1 = min(k, k0 + kF32MaxSlice);
-  float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f;
-  if (live) {
-    int kk = k0 + warp;
-    for (; kk + 12 < k1; kk += 16) {  // four independent loads in flight
-      m0 = fmaxf(m0, fabsf(__ldg(B + (size_t)kk * ldb + col)));
-      m1 = fmaxf(m1, fabsf(__ldg(B + (size_t)(kk + 4) * ldb + col)));
-      m2 = fmaxf(m2, fabsf(__ldg(B + (size_t)(kk + 8) * ldb + col)));
-      m3 = fmaxf(m3, fabsf(__ldg(B + (size_t)(kk + 12) * ldb + col)));
+  float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const bool vec = (ldb & 3) == 0 && (reinterpret_cast<uintptr_t>(B) & 15u) == 0 && col + 3 < n && cl + 3 < nc;
+  if (vec) {
+    float4 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int kk = k0 + warp + 4 * u;
+      v[u] = kk < k1 ? __ldg(reinterpret_cast<const float4*>(B + (size_t)kk * ldb + col))
+                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
-    for (; kk < k1; kk += 4) m0 = fmaxf(m0, fabsf(__ldg(B + (size_t)kk * ldb + col)));
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      m.x = fmaxf(m.x, fabsf(v[u].x));
+      m.y = fmaxf(m.y, fabsf(v[u].y));
+      m.z = fmaxf(m.z, fabsf(v[u].z));
+      m.w = fmaxf(m.w, fabsf(v[u].w));
+    }
+  } else {
+    float* mm = &m.x;
+    for (int kk = k0 + warp; kk < k1; kk += 4)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (cl + j < nc && col + j < n) mm[j] = fmaxf(mm[j], fabsf(__ldg(B + (size_t)kk * ldb + col + j)));
   }
-  cm[warp][lane] = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+  cm[warp][lane] = m;
   __syncthreads();
-  if (warp == 0 && cl < nc)
-    pmax[(size_t)blockIdx.y * nc + cl] = fmaxf(fmaxf(cm[0][lane], cm[1][lane]), fmaxf(cm[2][lane], cm[3][lane]));
+  if (warp == 0) {
+    const float4 a = cm[0][lane], b = cm[1][lane], c = cm[2][lane], d = cm[3][lane];
+    const float r[4] = {fmaxf(fmaxf(a.x, b.x), fmaxf(c.x, d.x)), fmaxf(fmaxf(a.y, b.y), fmaxf(c.y, d.y)),
+                        fmaxf(fmaxf(a.z, b.z), fmaxf(c.z, d.z)), fmaxf(fmaxf(a.w, b.w), fmaxf(c.w, d.w))};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (cl + j < nc) pmax[(size_t)blockIdx.y * nc + cl + j] = r[j];
+  }
 }
 
 // Blocks [0, eb): the columns (TB: a warp per row of B, 4 rows per block;
-// else block (strip, 64-k block) over eb = strips * k / 64, the column
+// else block (64-column strip, 64-k block) over eb = strips * k / 64, the column
 // maxima from pmax's nsl slices); blocks [eb, eb + ma) split the activation
 // rows; block 0 zeroes the GEMM's ready counters.
 template <int TB>
@@ -766,7 +787,7 @@ __global__ void __launch_bounds__(128) f32_terms_kernel(const float* __restrict_
   __shared__ float red[4];
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < nready; i += 128) ready[i] = 0;
-  const int eb = TB ? (nc + 3) / 4 : (nc + 31) / 32 * (k >> 6);
+  const int eb = TB ? (nc + 3) / 4 : (nc + 63) / 64 * (k >> 6);
   if ((int)blockIdx.x >= eb) {
     if ((int)blockIdx.x - eb < ma) split_act_row(A, lda, k, ax, icm, (int)blockIdx.x - eb, red);
     return;
@@ -799,34 +820,53 @@ __global__ void __launch_bounds__(128) f32_terms_kernel(const float* __restrict_
     }
     return;
   }
-  // block (strip, kb): tile [64 k][32 columns] (lane = column for the loads),
-  // then thread (column j, part p) converts k = 16 p .. 16 p + 15 of it
-  __shared__ float cs[32];
-  __shared__ float tile[64][33];
+  // block (strip of 64 columns, kb): tile [64 k][64 columns], lane = two
+  // adjacent columns for the loads (warp = every 4th row: sixteen loads per
+  // thread in flight); then thread (column j, half p) converts k = 32 p ..
+  // 32 p + 31 of column j
+  __shared__ float cs[64];
+  __shared__ float tile[64][65];
   const int nkb = k >> 6, strip = (int)blockIdx.x / nkb, kb = (int)blockIdx.x - strip * nkb;
-  const int cl0 = 32 * strip, col = n0 + cl0 + lane;
-  const bool live = cl0 + lane < nc && col < n;
-  for (int r = warp; r < 64; r += 4) tile[r][lane] = live ? __ldg(B + (size_t)(64 * kb + r) * ldb + col) : 0.0f;
-  if (warp == 0) {
+  const int cl0 = 64 * strip, cl = cl0 + 2 * lane, col = n0 + cl;
+  const float* bp = B + (size_t)(64 * kb) * ldb + col;
+  if ((ldb & 1) == 0 && (reinterpret_cast<uintptr_t>(B) & 7u) == 0 && cl + 1 < nc && col + 1 < n) {
+    float2 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = __ldg(reinterpret_cast<const float2*>(bp + (size_t)(warp + 4 * u) * ldb));
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      tile[warp + 4 * u][2 * lane] = v[u].x;
+      tile[warp + 4 * u][2 * lane + 1] = v[u].y;
+    }
+  } else {
+    for (int u = 0; u < 16; ++u)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        tile[warp + 4 * u][2 * lane + j] =
+            cl + j < nc && col + j < n ? __ldg(bp + (size_t)(warp + 4 * u) * ldb + j) : 0.0f;
+  }
+  if (threadIdx.x < 64) {
+    const int c = cl0 + (int)threadIdx.x;
     float m = 0.0f;
-    if (cl0 + lane < nc)
-      for (int j = 0; j < nsl; ++j) m = fmaxf(m, pmax[(size_t)j * nc + cl0 + lane]);
+    if (c < nc)
+      for (int j = 0; j < nsl; ++j) m = fmaxf(m, pmax[(size_t)j * nc + c]);
     const int ce = act_range_exp(m);
-    cs[lane] = exp2_int(ce);
-    if (kb == 0 && cl0 + lane < nc) colf[cl0 + lane] = __fmul_rn(alpha, exp2_int(-ce));
+    cs[threadIdx.x] = exp2_int(ce);
+    if (kb == 0 && c < nc) colf[c] = __fmul_rn(alpha, exp2_int(-ce));
   }
   __syncthreads();
-  const int j = threadIdx.x >> 2, p = threadIdx.x & 3;
+  const int j = threadIdx.x & 63, p = threadIdx.x >> 6;
   if (cl0 + j < nc) {
     const float cj = cs[j];
-    uint32_t h[8], l[8];
+    uint32_t h[16], l[16];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) split_act_pair(tile[16 * p + 2 * e][j], tile[16 * p + 2 * e + 1][j], cj, h[e], l[e]);
-    __half* dst = wx + (size_t)(cl0 + j) * 2 * k + 128 * kb + 16 * p;
-    *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(dst + 8) = make_uint4(h[4], h[5], h[6], h[7]);
-    *reinterpret_cast<uint4*>(dst + 64) = make_uint4(l[0], l[1], l[2], l[3]);
-    *reinterpret_cast<uint4*>(dst + 72) = make_uint4(l[4], l[5], l[6], l[7]);
+    for (int e = 0; e < 16; ++e) split_act_pair(tile[32 * p + 2 * e][j], tile[32 * p + 2 * e + 1][j], cj, h[e], l[e]);
+    __half* dst = wx + (size_t)(cl0 + j) * 2 * k + 128 * kb + 32 * p;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+      *reinterpret_cast<uint4*>(dst + 64 + 8 * q) = make_uint4(l[4 * q], l[4 * q + 1], l[4 * q + 2], l[4 * q + 3]);
+    }
   }
 }
 

@@ -406,10 +406,11 @@ int run_sgemm_terms(int m, int n, int k, float alpha, const float* A, int lda, c
                                       nsplit),
                         "f32_terms_kernel");
     } else {  // column maxima over k slices first, then the 64-k blocks in parallel
-      const int strips = (ncur + 31) / 32, nsl = (k + kF32MaxSlice - 1) / kF32MaxSlice;
+      const int strips = (ncur + 63) / 64, nsl = (k + kF32MaxSlice - 1) / kF32MaxSlice;
       float* pmax = g_sg_pmax.get((size_t)nsl * ncur, s);
       if (!pmax) return fail(OC_ERR_OUT_OF_MEMORY, "sgemm: scratch allocation failed");
-      rc = wo_launch_rc(launch_pdl_ex(f32_colmax_kernel, dim3(strips, nsl), dim3(128), 0, s, B, ldb, n, n0, ncur, k,
+      rc = wo_launch_rc(launch_pdl_ex(f32_colmax_kernel, dim3((ncur + kF32MaxStrip - 1) / kF32MaxStrip, nsl),
+                                      dim3(128), 0, s, B, ldb, n, n0, ncur, k,
                                       pmax),
                         "f32_colmax_kernel");
       if (rc) return rc;
