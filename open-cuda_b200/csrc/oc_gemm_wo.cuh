@@ -48,6 +48,7 @@
 #include <cuda_fp16.h>
 
 #include "oc_gemm_common.cuh"
+#include "oc_gemm_epi.cuh"
 #include "oc_ptx.cuh"
 
 namespace oc {
@@ -395,7 +396,7 @@ struct WoClT {
   static constexpr size_t SMEM = 1024 + (size_t)RING + 256;
   static constexpr int TMEM_COLS = BM <= 128 ? 128 : 256;
   static constexpr int HALF = BM / 2, NBH = HALF / 32;  // rows and 32-row blocks per epilogue half
-  static_assert(BM == 128 || BM == 192 || BM == 256, "tile heights");
+  static_assert(BM == 64 || BM == 128 || BM == 192 || BM == 256, "tile heights");
   static_assert(STAGES >= 2, "double-buffered ring");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
@@ -404,7 +405,8 @@ template <int BM, int WT>
 __global__ void __launch_bounds__(WoClT<BM, WT>::THREADS, 1)
     gemm_wo_cl_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, int M, int N,
                       int K, const float* __restrict__ rowf, const float* __restrict__ colf,
-                      const float* __restrict__ bias, float* __restrict__ Y, int ldy, int vec_out, int* status) {
+                      const float* __restrict__ bias, float* __restrict__ Y, int ldy, int vec_out, int* status,
+                      const GemmEpi epi) {
   using C = WoClT<BM, WT>;
   pdl_wait();  // operand terms from the preparation launch; TMEM only after the predecessors are done
   pdl_launch();
@@ -557,7 +559,14 @@ __global__ void __launch_bounds__(WoClT<BM, WT>::THREADS, 1)
         t.w = __fadd_rn(t.w, v.w);
       }
       float* yr = Y + (size_t)(tm * C::BM + r) * ldy + c;
-      if (vec_out && c + 3 < N) {
+      if (epi.mode != kGemmEpiPlain) {  // the GPT linears' epilogues (oc_gemm_epi.cuh)
+        const float tv[4] = {t.x, t.y, t.z, t.w};
+        for (int e = 0; e < 4 && c + e < N; ++e) {
+          const float y = gemm_epi_value(epi, tv[e], 0.0f, bias ? __ldg(bias + c + e) : 0.0f, yr + e);
+          yr[e] = y;
+          gemm_epi_kv(epi, tm * C::BM + r, c + e, y);
+        }
+      } else if (vec_out && c + 3 < N) {
         const float4 b4 = bias ? __ldg(reinterpret_cast<const float4*>(bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(yr) =
             make_float4(__fadd_rn(t.x, b4.x), __fadd_rn(t.y, b4.y), __fadd_rn(t.z, b4.z), __fadd_rn(t.w, b4.w));
@@ -599,16 +608,18 @@ __device__ __forceinline__ void split_act_pair(float x0, float x1, float c, uint
   lo2 = l0 | (l1 << 16);
 }
 
-// Activation row `row` (row stride lda) by one CTA of 128 threads: row max,
-// then the hi / lo terms into ax [m][2k] (64-k blocks: hi, then lo) and
-// 1 / c_m into icm.  k % 64 == 0, lda % 4 == 0, A 16-byte aligned.
-__device__ __forceinline__ void split_act_row(const float* __restrict__ A, int lda, int k, __half* __restrict__ ax,
-                                              float* __restrict__ icm, int row, float* red) {
-  const float4* a4 = reinterpret_cast<const float4*>(A + (size_t)row * lda);
+// Activation row `row`, at ar, by one CTA of 128 threads: row max, then the
+// hi / lo terms into ax [m][2k] (64-k blocks: hi, then lo) and 1 / c_m into
+// icm.  k % 64 == 0, ar 16-byte aligned.  LDG false: ar may have been
+// written by this kernel, or sit in shared memory (no read-only-cache loads).
+template <bool LDG>
+__device__ __forceinline__ void split_act_rowp(const float* __restrict__ ar, int k, __half* __restrict__ ax,
+                                               float* __restrict__ icm, int row, float* red) {
+  const float4* a4 = reinterpret_cast<const float4*>(ar);
   const int n4 = k >> 2;
   float mx = 0.0f;
   for (int i = threadIdx.x; i < n4; i += 128) {
-    const float4 v = __ldg(a4 + i);
+    const float4 v = LDG ? __ldg(a4 + i) : a4[i];
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
 #pragma unroll
@@ -621,7 +632,7 @@ __device__ __forceinline__ void split_act_row(const float* __restrict__ A, int l
   if (threadIdx.x == 0) icm[row] = exp2_int(-ce);
   __half* xrow = ax + (size_t)row * 2 * k;
   for (int i = threadIdx.x; i < n4; i += 128) {  // elements 4i .. 4i + 3
-    const float4 v = __ldg(a4 + i);
+    const float4 v = LDG ? __ldg(a4 + i) : a4[i];
     uint2 hi, lo;
     split_act_pair(v.x, v.y, c, hi.x, lo.x);
     split_act_pair(v.z, v.w, c, hi.y, lo.y);
@@ -630,6 +641,12 @@ __device__ __forceinline__ void split_act_row(const float* __restrict__ A, int l
     *reinterpret_cast<uint2*>(dst) = hi;
     *reinterpret_cast<uint2*>(dst + 64) = lo;
   }
+}
+
+// Row `row` of A (row stride lda, lda % 4 == 0, A 16-byte aligned).
+__device__ __forceinline__ void split_act_row(const float* __restrict__ A, int lda, int k, __half* __restrict__ ax,
+                                              float* __restrict__ icm, int row, float* red) {
+  split_act_rowp<true>(A + (size_t)row * lda, k, ax, icm, row, red);
 }
 
 // INT4 weight row n (packed [N][K/2], scales [N][K/group], group % 8 == 0)
@@ -868,6 +885,55 @@ __global__ void __launch_bounds__(128) f32_terms_kernel(const float* __restrict_
       *reinterpret_cast<uint4*>(dst + 64 + 8 * q) = make_uint4(l[4 * q], l[4 * q + 1], l[4 * q + 2], l[4 * q + 3]);
     }
   }
+}
+
+// ---- activation terms with an optional LayerNorm (the GPT linears) -----------------
+//
+// Row blockIdx.x of x [rows][ldx] -> its hi / lo terms in ax [rows][2k] and
+// 1 / c_m in icm, as split_act_row; with ln_w the row is first normalised,
+// LayerNorm(x; ln_w, ln_b) (mean and variance over the row, inv = 1 /
+// sqrt(var + eps), llm:252-262), in shared memory (k floats of dynamic
+// shared memory), and the terms are taken from there.  128 threads;
+// k % 64 == 0, ldx % 4 == 0, x 16-byte aligned.
+__device__ __forceinline__ float block128_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();  // red is free again
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+}
+
+__global__ void __launch_bounds__(128) act_terms_kernel(const float* __restrict__ x, int ldx, int k,
+                                                        const float* __restrict__ ln_w, const float* __restrict__ ln_b,
+                                                        float eps, __half* __restrict__ ax, float* __restrict__ icm) {
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ __align__(16) float nrow[];  // [k] with ln_w
+  __shared__ float red[4];
+  const int row = blockIdx.x;
+  if (!ln_w) {
+    split_act_row(x, ldx, k, ax, icm, row, red);
+    return;
+  }
+  const float* xr = x + (size_t)row * ldx;
+  float sm = 0.0f;
+  for (int c = threadIdx.x; c < k; c += 128) {
+    const float v = xr[c];
+    nrow[c] = v;
+    sm = __fadd_rn(sm, v);
+  }
+  const float mean = __fdiv_rn(block128_sum(sm, red), (float)k);
+  float vs = 0.0f;
+  for (int c = threadIdx.x; c < k; c += 128) {
+    const float d = __fsub_rn(nrow[c], mean);
+    vs = __fmaf_rn(d, d, vs);
+  }
+  const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(block128_sum(vs, red), (float)k), eps)));
+  for (int c = threadIdx.x; c < k; c += 128)
+    nrow[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(nrow[c], mean), inv), __ldg(ln_w + c)), __ldg(ln_b + c));
+  __syncthreads();  // the normalised row is complete; red is free for the split
+  split_act_rowp<false>(nrow, k, ax, icm, row, red);
 }
 
 // ---- skinny path (m <= 16) -----------------------------------------------------

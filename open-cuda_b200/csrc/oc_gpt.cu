@@ -898,6 +898,8 @@ struct GptLinear {
   float* b = nullptr;     // [out]
   float* prep = nullptr;  // tf32 hi/lo [out][in] for the tensor-core path
   float* wt = nullptr;    // [out][in] copy of w for gemv_cols_kernel (null: not used)
+  __half* wx = nullptr;   // f16 terms [out][2 in] of w for 17-128 rows (null: not used)
+  float* colf = nullptr;  // [out] 1 / c_n of those terms
   int in = 0, out = 0;
 };
 
@@ -919,6 +921,9 @@ struct oc_gpt {
   size_t part_floats = 0;
   unsigned* counters = nullptr;  // decode GEMV column-tile counters
   int* status = nullptr;         // device status word (bounded in-kernel waits)
+  __half* ax = nullptr;          // activation terms [kGptTermRows][2 * max in] (17-128 rows)
+  float* icm = nullptr;          // [kGptTermRows] 1 / c_m of those terms
+  float* pmax = nullptr;         // column maxima scratch of the weight-term preparation
   size_t counter_count = 0;
   ArgmaxScratch arg{};
   float *kc, *vc;  // [layer][batch][max_seq][H]
@@ -982,6 +987,9 @@ int linear_alloc(oc_gpt* g, GptLinear& L, int in, int out) {
       (rc = galloc_t(g, pb / sizeof(float), &L.prep)))
     return rc;
   if (gemv_cols_cb(in, out) && (rc = galloc_t(g, (size_t)in * out, &L.wt))) return rc;
+  if (in % 64 == 0 &&
+      ((rc = galloc_t(g, (size_t)in * out * 2, &L.wx)) || (rc = galloc_t(g, (size_t)out, &L.colf))))
+    return rc;
   return OC_OK;
 }
 
@@ -1027,9 +1035,12 @@ static void launch_cols(const GemvArgs& a, cudaStream_t s) {
   launch_pdl(kern, dim3((a.n + a.cb - 1) / a.cb), dim3(256), smem, s, a);
 }
 
-// Rows up to which a linear runs as the fused split-K GEMV; more rows go to
-// the 3xTF32 tensor-core GEMM (split-K when its tiles are few).
-constexpr int kGptGemvRows = 16;
+// Rows up to which a linear runs as the fused split-K GEMV; up to
+// kGptTermRows the f16-term tensor-core GEMM (weights' terms prepared once,
+// the activation terms by one launch with the LayerNorm fused, the epilogue
+// where the K-split cluster finishes its sums); more rows go to the 3xTF32
+// tensor-core GEMM (split-K when its tiles are few).
+constexpr int kGptGemvRows = 16, kGptTermRows = 128;
 
 // out[rows][L.out] = epilogue(x[rows][L.in] . W + b) (GemvEpi); *n += kernels
 // launched.  Up to 32 rows: one split-K GEMV with the epilogue fused; more
@@ -1041,6 +1052,23 @@ int linear_fwd(oc_gpt* g, const GptLinear& L, const float* x, int rows, float* o
                const float* ln_b = nullptr) {
   cudaStream_t s = g->stream;
   const int H = (int)g->cfg.hidden_size, ms = (int)g->cfg.max_seq_len;
+  if (rows > kGptGemvRows && rows <= kGptTermRows && L.wx) {
+    int rc = run_act_terms(rows, L.in, x, L.in, ln_w, ln_b, g->cfg.layer_norm_eps, g->ax, g->icm, s);
+    if (rc) return rc;
+    GemmEpi ge;
+    ge.mode = epi == kEpiGelu ? kGemmEpiGelu : epi == kEpiResidual ? kGemmEpiResidual
+              : epi == kEpiQkv ? kGemmEpiQkv : kGemmEpiPlain;
+    ge.kc = kc;
+    ge.vc = vc;
+    ge.pos = g->pos;
+    ge.L = seq_rows;
+    ge.H = H;
+    ge.max_seq = ms;
+    rc = gemm_terms_epi(rows, L.out, L.in, g->ax, g->icm, L.wx, L.colf, L.b, out, L.out, ge, s);
+    if (rc) return rc;
+    *n += 2;  // the activation terms, the GEMM
+    return OC_OK;
+  }
   if (rows > kGptGemvRows && ln_w) {
     layernorm_kernel<<<rows, 256, 0, s>>>(x, L.in, g->normed, L.in, ln_w, ln_b, g->cfg.layer_norm_eps);
     *n += 1;
@@ -1182,6 +1210,16 @@ int oc_gpt_create(int device, const oc_gpt_config* cfg, int max_batch, int max_p
       g->counter_count = std::max(g->counter_count, (size_t)p.tiles);
     }
   }
+  {  // f16-term GEMM scratch: activation terms for up to kGptTermRows rows of the widest input, and the
+     // column maxima of the weight-term preparation ((in / 64) * out floats for the largest linear)
+    const size_t kin = std::max(H, I), trows = std::min<size_t>(R, kGptTermRows);
+    size_t pm = 0;
+    for (const GptLinear* L : {&g->lm, &g->layers[0].qkv, &g->layers[0].ao, &g->layers[0].fc, &g->layers[0].pj})
+      pm = std::max(pm, (size_t)(L->in / 64 + 1) * L->out);
+    if ((rc = galloc_t(g, trows * 2 * kin, &g->ax)) || (rc = galloc_t(g, trows, &g->icm)) ||
+        (rc = galloc_t(g, pm, &g->pmax)))
+      return bail(rc);
+  }
   if ((rc = galloc_t(g, R * H, &g->hidden)) || (rc = galloc_t(g, R * H, &g->normed)) ||
       (rc = galloc_t(g, R * 3 * H, &g->qkv)) || (rc = galloc_t(g, R * H, &g->ctx)) ||
       (rc = galloc_t(g, R * I, &g->inter)) ||
@@ -1224,6 +1262,7 @@ int oc_gpt_destroy(oc_gpt* g) {
 // planes and, where the linear has one, the transposed copy of the GEMV.
 static int prepare_linear(oc_gpt* g, GptLinear& L) {
   int rc = oc_sgemm_prepare_b(L.in, L.out, L.w, L.out, 0, L.prep, g->stream);
+  if (!rc && L.wx) rc = prepare_weight_terms(L.in, L.out, L.w, L.wx, L.colf, g->pmax, g->stream);
   if (rc || !L.wt) return rc;
   transpose_kernel<<<dim3((L.out + 31) / 32, (L.in + 31) / 32), dim3(32, 8), 0, g->stream>>>(L.w, L.in, L.out, L.wt);
   const cudaError_t e = cudaGetLastError();

@@ -3,6 +3,7 @@
 // map encoding and the per-device properties cache.
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -125,6 +126,19 @@ struct StreamScratch {
 // weights, so the terms it expanded may be reused (checked inside).
 int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
                  const float* bias, float* Y, cudaStream_t s, bool weights_ready);
+
+// GPT linears on the f16-term GEMM (oc_qgemm_wo.cu):
+//  * prepare_weight_terms: W [k][n] (row-major) -> wx [n][2k] f16 terms and
+//    colf[n] = 1 / c_n, once per weight; pmax: (k / 64) * n floats of scratch;
+//  * run_act_terms: rows of x (LayerNorm(x; ln_w, ln_b) first when ln_w) ->
+//    ax [m][2k] terms and icm[m] = 1 / c_m;
+//  * gemm_terms_epi: Y = epilogue(A . W + bias) from those terms (k % 64 == 0).
+struct GemmEpi;
+int prepare_weight_terms(int k, int n, const float* W, __half* wx, float* colf, float* pmax, cudaStream_t s);
+int run_act_terms(int m, int k, const float* x, int ldx, const float* ln_w, const float* ln_b, float eps, __half* ax,
+                  float* icm, cudaStream_t s);
+int gemm_terms_epi(int m, int n, int k, const __half* ax, const float* icm, const __half* wx, const float* colf,
+                   const float* bias, float* Y, int ldy, const GemmEpi& epi, cudaStream_t s);
 
 // C = alpha * A . op(B) + bias (beta = 0) on the f16-term tensor-core GEMM of
 // the weight-only path (oc_qgemm_wo.cu), when sgemm_terms_ok.

@@ -186,7 +186,7 @@ static int launch_wo_gemm(const CUtensorMap& ta, const CUtensorMap& tw, int m, i
 
 // Activation-tile height of the cluster path: 128 rows when the input fits
 // one such tile, else 192.
-static int wo_cl_bm(int m) { return m <= 128 ? 128 : 192; }
+static int wo_cl_bm(int m) { return m <= 64 ? 64 : m <= 128 ? 128 : 192; }
 
 template <int BM, int WT>
 static int wo_cl_max_clusters(int ks) {
@@ -229,7 +229,9 @@ static int wo_cl_ks(int m, int nc, int k) {
   const int tiles = (m + bm - 1) / bm * ((nc + 127) / 128), nrb = k / 64;
   if (2 * tiles > sms || nrb < 2) return 0;
   for (int ks = std::min(8, std::min(nrb, sms / tiles)); ks >= 2; --ks) {
-    const int fit = bm == 128 ? wo_cl_max_clusters<128, WT>(ks) : wo_cl_max_clusters<192, WT>(ks);
+    const int fit = bm == 64    ? wo_cl_max_clusters<64, WT>(ks)
+                    : bm == 128 ? wo_cl_max_clusters<128, WT>(ks)
+                                : wo_cl_max_clusters<192, WT>(ks);
     if (fit >= tiles) return ks;
   }
   return 0;
@@ -237,7 +239,8 @@ static int wo_cl_ks(int m, int nc, int k) {
 
 template <int BM, int WT>
 static int launch_wo_cl(const CUtensorMap& ta, const CUtensorMap& tw, int ks, int m, int nc, int k, int ldy,
-                        const float* icm, const float* colf, const float* bias, float* Yc, cudaStream_t s) {
+                        const float* icm, const float* colf, const float* bias, float* Yc, cudaStream_t s,
+                        const GemmEpi& epi = GemmEpi{}) {
   using C = WoClT<BM, WT>;
   auto kern = gemm_wo_cl_kernel<BM, WT>;
   if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
@@ -258,7 +261,7 @@ static int launch_wo_cl(const CUtensorMap& ta, const CUtensorMap& tw, int ks, in
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   return wo_launch_rc(cudaLaunchKernelEx(&cfg, kern, ta, tw, m, nc, k, icm, colf, bias, Yc, ldy, vec_out,
-                                         device_status_word()),
+                                         device_status_word(), epi),
                       "gemm_wo_cl_kernel");
 }
 
@@ -339,8 +342,9 @@ static int run_wo_gemm(int m, int n, int k, int group, const float* A, const voi
       rc = make_tmap_2d(&tac, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
                         kWoBK, bmc, kWoSwizzle);
       if (rc) return rc;
-      rc = bmc == 128 ? launch_wo_cl<128, WT>(tac, tw, cl_ks, m, ncur, k, n, icm, colf, bc, Yc, s)
-                      : launch_wo_cl<192, WT>(tac, tw, cl_ks, m, ncur, k, n, icm, colf, bc, Yc, s);
+      rc = bmc == 64    ? launch_wo_cl<64, WT>(tac, tw, cl_ks, m, ncur, k, n, icm, colf, bc, Yc, s)
+           : bmc == 128 ? launch_wo_cl<128, WT>(tac, tw, cl_ks, m, ncur, k, n, icm, colf, bc, Yc, s)
+                        : launch_wo_cl<192, WT>(tac, tw, cl_ks, m, ncur, k, n, icm, colf, bc, Yc, s);
     } else if (bm == 192) {
       rc = launch_wo_gemm<192, WT>(ta, tw, m, ncur, k, n, icm, colf, bc, Yc, s);
     } else {
@@ -432,8 +436,9 @@ int run_sgemm_terms(int m, int n, int k, float alpha, const float* A, int lda, c
       rc = make_tmap_2d(&tac, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4,
                         kWoBK, bmc, kWoSwizzle);
       if (rc) return rc;
-      rc = bmc == 128 ? launch_wo_cl<128, WT>(tac, tw, cl_ks, m, ncur, k, ldc, icm, colf, bc, Cc, s)
-                      : launch_wo_cl<192, WT>(tac, tw, cl_ks, m, ncur, k, ldc, icm, colf, bc, Cc, s);
+      rc = bmc == 64    ? launch_wo_cl<64, WT>(tac, tw, cl_ks, m, ncur, k, ldc, icm, colf, bc, Cc, s)
+           : bmc == 128 ? launch_wo_cl<128, WT>(tac, tw, cl_ks, m, ncur, k, ldc, icm, colf, bc, Cc, s)
+                        : launch_wo_cl<192, WT>(tac, tw, cl_ks, m, ncur, k, ldc, icm, colf, bc, Cc, s);
     } else if (bm == 192) {
       rc = launch_wo_gemm<192, WT>(ta, tw, m, ncur, k, ldc, icm, colf, bc, Cc, s);
     } else {
@@ -442,6 +447,61 @@ int run_sgemm_terms(int m, int n, int k, float alpha, const float* A, int lda, c
     if (rc) return rc;
   }
   return OC_OK;
+}
+
+// ---- GPT linears on prepared f16 terms ---------------------------------------------
+
+int prepare_weight_terms(int k, int n, const float* W, __half* wx, float* colf, float* pmax, cudaStream_t s) {
+  if (k % 64 || n <= 0) return fail(OC_ERR_INVALID_VALUE, "weight terms: k % 64 != 0");
+  const int nsl = (k + kF32MaxSlice - 1) / kF32MaxSlice;
+  int rc = wo_launch_rc(launch_pdl_ex(f32_colmax_kernel, dim3((n + kF32MaxStrip - 1) / kF32MaxStrip, nsl), dim3(128),
+                                      0, s, W, n, n, 0, n, k, pmax),
+                        "f32_colmax_kernel");
+  if (rc) return rc;
+  return wo_launch_rc(launch_pdl_ex(f32_terms_kernel<0>, dim3((n + 63) / 64 * (k >> 6)), dim3(128), 0, s,
+                                    (const float*)nullptr, 0, 0, k, (__half*)nullptr, (float*)nullptr, W, n, n, 0, n,
+                                    1.0f, (const float*)pmax, nsl, wx, colf, (int*)nullptr, 0),
+                      "f32_terms_kernel");
+}
+
+int run_act_terms(int m, int k, const float* x, int ldx, const float* ln_w, const float* ln_b, float eps, __half* ax,
+                  float* icm, cudaStream_t s) {
+  const size_t smem = ln_w ? (size_t)k * sizeof(float) : 0;
+  if (smem > 48 * 1024 && !smem_attr_once(reinterpret_cast<const void*>(act_terms_kernel), smem))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(act_terms_kernel) failed");
+  return wo_launch_rc(launch_pdl_ex(act_terms_kernel, dim3(m), dim3(128), smem, s, x, ldx, k, ln_w, ln_b, eps, ax, icm),
+                      "act_terms_kernel");
+}
+
+int gemm_terms_epi(int m, int n, int k, const __half* ax, const float* icm, const __half* wx, const float* colf,
+                   const float* bias, float* Y, int ldy, const GemmEpi& epi, cudaStream_t s) {
+  const int sms = std::max(1, sm_count());
+  CUtensorMap tw;
+  int rc = make_tmap_2d(&tw, wx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)n, (uint64_t)k * 4,
+                        kWoBK, 128, kWoSwizzle);
+  if (rc) return rc;
+  const int tiles_n = (n + 127) / 128;
+  if (epi.mode == kGemmEpiPlain && (m + 191) / 192 * tiles_n >= sms) {
+    // enough tiles for every SM: the persistent kernel (no K split)
+    const int bm = (m + 191) / 192 * tiles_n <= sms * 2 || m <= 192 ? 192 : 256;
+    CUtensorMap ta;
+    rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4, kWoBK,
+                      bm, kWoSwizzle);
+    if (rc) return rc;
+    return bm == 192 ? launch_wo_gemm<192, 2>(ta, tw, m, n, k, ldy, icm, colf, bias, Y, s)
+                     : launch_wo_gemm<256, 2>(ta, tw, m, n, k, ldy, icm, colf, bias, Y, s);
+  }
+  // K split over a cluster (one CTA per slice when no split fits); the
+  // epilogue runs where the slices' sums are finished
+  const int ks = std::max(1, wo_cl_ks<2>(m, n, k));
+  const int bmc = wo_cl_bm(m);
+  CUtensorMap ta;
+  rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4, kWoBK,
+                    bmc, kWoSwizzle);
+  if (rc) return rc;
+  return bmc == 64    ? launch_wo_cl<64, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi)
+         : bmc == 128 ? launch_wo_cl<128, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi)
+                      : launch_wo_cl<192, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi);
 }
 
 int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
