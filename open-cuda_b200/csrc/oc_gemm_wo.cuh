@@ -936,6 +936,83 @@ __global__ void __launch_bounds__(128) act_terms_kernel(const float* __restrict_
   split_act_rowp<false>(nrow, k, ax, icm, row, red);
 }
 
+// The same with a warp per row (no block-wide reductions on the critical
+// path) for k <= 32 * 4 * kActWarpMaxV4: four rows per 128-thread block, the
+// row held in registers (lane = float4s at 4 lane + 128 j).
+constexpr int kActWarpMaxV4 = 24;
+__global__ void __launch_bounds__(128) act_terms_warp_kernel(int m, const float* __restrict__ x, int ldx, int k,
+                                                             const float* __restrict__ ln_w,
+                                                             const float* __restrict__ ln_b, float eps,
+                                                             __half* __restrict__ ax, float* __restrict__ icm) {
+  pdl_wait();
+  pdl_launch();
+  const int lane = threadIdx.x & 31, row = 4 * (int)blockIdx.x + (threadIdx.x >> 5);
+  if (row >= m) return;
+  const float* xr = x + (size_t)row * ldx;
+  float4 v[kActWarpMaxV4];
+#pragma unroll
+  for (int j = 0; j < kActWarpMaxV4; ++j) {
+    const int c = 4 * lane + 128 * j;
+    v[j] = c < k ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  if (ln_w) {
+    float sm = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kActWarpMaxV4; ++j)
+      if (4 * lane + 128 * j < k) sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v[j].x), v[j].y), v[j].z), v[j].w);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+    const float mean = __fdiv_rn(sm, (float)k);
+    float vs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kActWarpMaxV4; ++j) {
+      if (4 * lane + 128 * j < k) {
+        const float d0 = __fsub_rn(v[j].x, mean), d1 = __fsub_rn(v[j].y, mean);
+        const float d2 = __fsub_rn(v[j].z, mean), d3 = __fsub_rn(v[j].w, mean);
+        vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)k), eps)));
+#pragma unroll
+    for (int j = 0; j < kActWarpMaxV4; ++j) {
+      const int c = 4 * lane + 128 * j;
+      if (c < k) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(ln_w + c));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(ln_b + c));
+        v[j].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].x, mean), inv), w.x), b.x);
+        v[j].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].y, mean), inv), w.y), b.y);
+        v[j].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].z, mean), inv), w.z), b.z);
+        v[j].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].w, mean), inv), w.w), b.w);
+      }
+    }
+  }
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kActWarpMaxV4; ++j)
+    if (4 * lane + 128 * j < k)
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int ce = act_range_exp(mx);
+  const float c = exp2_int(ce);
+  if (lane == 0) icm[row] = exp2_int(-ce);
+  __half* xrow = ax + (size_t)row * 2 * k;
+#pragma unroll
+  for (int j = 0; j < kActWarpMaxV4; ++j) {
+    const int k0 = 4 * lane + 128 * j;
+    if (k0 < k) {
+      uint2 hi, lo;
+      split_act_pair(v[j].x, v[j].y, c, hi.x, lo.x);
+      split_act_pair(v[j].z, v[j].w, c, hi.y, lo.y);
+      __half* dst = xrow + 128 * (k0 >> 6) + (k0 & 63);
+      *reinterpret_cast<uint2*>(dst) = hi;
+      *reinterpret_cast<uint2*>(dst + 64) = lo;
+    }
+  }
+}
+
 // ---- skinny path (m <= 16) -----------------------------------------------------
 
 // Float sums of V values per lane across the warp: a transposing butterfly

@@ -466,6 +466,10 @@ int prepare_weight_terms(int k, int n, const float* W, __half* wx, float* colf, 
 
 int run_act_terms(int m, int k, const float* x, int ldx, const float* ln_w, const float* ln_b, float eps, __half* ax,
                   float* icm, cudaStream_t s) {
+  if (k <= 128 * kActWarpMaxV4 && ldx % 4 == 0 && aligned16(x))
+    return wo_launch_rc(launch_pdl_ex(act_terms_warp_kernel, dim3((m + 3) / 4), dim3(128), 0, s, m, x, ldx, k, ln_w,
+                                      ln_b, eps, ax, icm),
+                        "act_terms_warp_kernel");
   const size_t smem = ln_w ? (size_t)k * sizeof(float) : 0;
   if (smem > 48 * 1024 && !smem_attr_once(reinterpret_cast<const void*>(act_terms_kernel), smem))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(act_terms_kernel) failed");
@@ -481,8 +485,8 @@ int gemm_terms_epi(int m, int n, int k, const __half* ax, const float* icm, cons
                         kWoBK, 128, kWoSwizzle);
   if (rc) return rc;
   const int tiles_n = (n + 127) / 128;
-  if (epi.mode == kGemmEpiPlain && (m + 191) / 192 * tiles_n >= sms) {
-    // enough tiles for every SM: the persistent kernel (no K split)
+  if (epi.mode == kGemmEpiPlain && m > 128 && (m + 191) / 192 * tiles_n >= sms) {
+    // enough tall tiles for every SM: the persistent kernel (no K split)
     const int bm = (m + 191) / 192 * tiles_n <= sms * 2 || m <= 192 ? 192 : 256;
     CUtensorMap ta;
     rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4, kWoBK,
