@@ -94,7 +94,7 @@ def test_w4_group_sizes(oc, oracle, m, k, n, group):
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("a_scale,w_scale", [(1e-30, 1.0), (1e6, 1.0), (1.0, 1e-30), (1.0, 1e6), (1e-15, 1e-12),
                                              (1e-20, 1e-15)])
-@pytest.mark.parametrize("m", [8, 300])
+@pytest.mark.parametrize("m", [2, 3, 8, 300])
 def test_weight_only_value_range(oc, oracle, bits, a_scale, w_scale, m):
     # per-row and per-column powers of two keep the f16 terms in range for
     # any magnitude of activations and weights; one row and one weight
@@ -215,3 +215,26 @@ def test_weight_only_launched_by_name(oc, oracle, bits):
         small = dev.alloc(16)
         dev.launch_kernel("qgemm_w8" if bits == 8 else "qgemm_w4", args[:4] + [K.ptr(small)] + args[5:])
     dev.close()
+
+
+@pytest.mark.parametrize("a_scale", [1.0, 1e-30, 1e6])
+@pytest.mark.parametrize("m,group", [(1, 32), (2, 64), (3, 128)])
+def test_w4_skinny_chunk_outliers(oc, oracle, m, group, a_scale):
+    # skinny INT4 rows with one element per 32-element chunk 1000x the
+    # others, some 1e-6x, a chunk of zeros, and rows of any magnitude keep
+    # the f32 tolerance, per row as well
+    k, n = 1024, 96
+    A, WT, bias = synth.qgemm_case(m, k, n, 21, 22, 23)
+    A = (A * np.float32(a_scale)).astype(np.float32)
+    bias = (bias * np.float32(a_scale)).astype(np.float32)
+    A[:, 5::32] *= np.float32(1000.0)
+    A[:, 9::32] *= np.float32(1e-6)
+    A[:, 64:96] = 0.0
+    A = A.astype(np.float32)
+    wq, ws = _quant(oracle, WT, 4, group)
+    y_ref = oracle.qgemm_weight_only(4, m, k, n, group, A, wq, ws, bias)
+    y = _run(oc, 4, A, wq, ws, group, bias)
+    assert rel_fro(y, y_ref) <= REL_FRO, rel_fro(y, y_ref)
+    yr, rr = y.reshape(m, n), y_ref.reshape(m, n)
+    for r in range(m):
+        assert rel_fro(yr[r], rr[r]) <= REL_FRO, (r, rel_fro(yr[r], rr[r]))
