@@ -406,10 +406,8 @@ __global__ void __launch_bounds__(WoClT<BM, WT>::THREADS, 1)
     gemm_wo_cl_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, int M, int N,
                       int K, const float* __restrict__ rowf, const float* __restrict__ colf,
                       const float* __restrict__ bias, float* __restrict__ Y, int ldy, int vec_out, int* status,
-                      const GemmEpi epi) {
+                      const GemmEpi epi, int w_early) {
   using C = WoClT<BM, WT>;
-  pdl_wait();  // operand terms from the preparation launch; TMEM only after the predecessors are done
-  pdl_launch();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   auto sAh = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
@@ -427,6 +425,11 @@ __global__ void __launch_bounds__(WoClT<BM, WT>::THREADS, 1)
   const int nrb = K / C::BK;
   const int rb0 = (int)((long long)slice * nrb / ks), rb1 = (int)((long long)(slice + 1) * nrb / ks);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // w_early: the weight terms are written by no kernel in flight (prepared
+  // once, ahead of the stream), so the first stages' weight tiles are
+  // requested before the dependency wait and stream in while the
+  // predecessor runs; the activation terms (and TMEM) only after it
+  const int npre = w_early ? min(C::STAGES, rb1 - rb0) : 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -437,7 +440,19 @@ __global__ void __launch_bounds__(WoClT<BM, WT>::THREADS, 1)
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmW);
+    for (int s = 0; s < npre; ++s) {
+      const int xh = 128 * (((rb0 + s) * C::BK) >> 6);
+      mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+      if (WT == 2) {
+        tma_load_2d(sW(s, 0), &tmW, xh, tn * C::BN, &full_bar[s]);
+        tma_load_2d(sW(s, 1), &tmW, xh + 64, tn * C::BN, &full_bar[s]);
+      } else {
+        tma_load_2d(sW(s, 0), &tmW, (rb0 + s) * C::BK, tn * C::BN, &full_bar[s]);
+      }
+    }
   }
+  pdl_wait();  // operand terms from the preparation launch; TMEM only after the predecessors are done
+  pdl_launch();
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
@@ -452,12 +467,21 @@ __global__ void __launch_bounds__(WoClT<BM, WT>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int kb = rb0; kb < rb1; ++kb) {
+        const int k0 = kb * C::BK, xh = 128 * (k0 >> 6);  // the hi term of block kb, then the lo term
+        if (kb - rb0 < npre) {  // weights already requested: the activation tiles only
+          tma_load_2d(sAh(stage), &tmA, xh, tm * C::BM, &full_bar[stage]);
+          tma_load_2d(sAl(stage), &tmA, xh + 64, tm * C::BM, &full_bar[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          continue;
+        }
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
           kernel_fail(status, abort_flag, kDevTimeoutProducer);
           break;
         }
         mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
-        const int k0 = kb * C::BK, xh = 128 * (k0 >> 6);  // the hi term of block kb, then the lo term
         tma_load_2d(sAh(stage), &tmA, xh, tm * C::BM, &full_bar[stage]);
         tma_load_2d(sAl(stage), &tmA, xh + 64, tm * C::BM, &full_bar[stage]);
         if (WT == 2) {

@@ -132,7 +132,9 @@ int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const
 //    colf[n] = 1 / c_n, once per weight; pmax: (k / 64) * n floats of scratch;
 //  * run_act_terms: rows of x (LayerNorm(x; ln_w, ln_b) first when ln_w) ->
 //    ax [m][2k] terms and icm[m] = 1 / c_m;
-//  * gemm_terms_epi: Y = epilogue(A . W + bias) from those terms (k % 64 == 0).
+//  * gemm_terms_epi: Y = epilogue(A . W + bias) from those terms (k % 64 == 0);
+//    wx and colf must not be written by any kernel still in flight (its
+//    first weight tiles are requested before the kernel's dependency wait).
 struct GemmEpi;
 int prepare_weight_terms(int k, int n, const float* W, __half* wx, float* colf, float* pmax, cudaStream_t s);
 int run_act_terms(int m, int k, const float* x, int ldx, const float* ln_w, const float* ln_b, float eps, __half* ax,

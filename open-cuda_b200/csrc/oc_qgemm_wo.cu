@@ -240,7 +240,7 @@ static int wo_cl_ks(int m, int nc, int k) {
 template <int BM, int WT>
 static int launch_wo_cl(const CUtensorMap& ta, const CUtensorMap& tw, int ks, int m, int nc, int k, int ldy,
                         const float* icm, const float* colf, const float* bias, float* Yc, cudaStream_t s,
-                        const GemmEpi& epi = GemmEpi{}) {
+                        const GemmEpi& epi = GemmEpi{}, int w_early = 0) {
   using C = WoClT<BM, WT>;
   auto kern = gemm_wo_cl_kernel<BM, WT>;
   if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
@@ -261,7 +261,7 @@ static int launch_wo_cl(const CUtensorMap& ta, const CUtensorMap& tw, int ks, in
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   return wo_launch_rc(cudaLaunchKernelEx(&cfg, kern, ta, tw, m, nc, k, icm, colf, bias, Yc, ldy, vec_out,
-                                         device_status_word(), epi),
+                                         device_status_word(), epi, w_early),
                       "gemm_wo_cl_kernel");
 }
 
@@ -496,16 +496,18 @@ int gemm_terms_epi(int m, int n, int k, const __half* ax, const float* icm, cons
                      : launch_wo_gemm<256, 2>(ta, tw, m, n, k, ldy, icm, colf, bias, Y, s);
   }
   // K split over a cluster (one CTA per slice when no split fits); the
-  // epilogue runs where the slices' sums are finished
+  // epilogue runs where the slices' sums are finished; the weight terms
+  // were prepared ahead of the stream, so their first tiles are requested
+  // before the kernel's dependency wait
   const int ks = std::max(1, wo_cl_ks<2>(m, n, k));
   const int bmc = wo_cl_bm(m);
   CUtensorMap ta;
   rc = make_tmap_2d(&ta, ax, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k * 2, (uint64_t)m, (uint64_t)k * 4, kWoBK,
                     bmc, kWoSwizzle);
   if (rc) return rc;
-  return bmc == 64    ? launch_wo_cl<64, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi)
-         : bmc == 128 ? launch_wo_cl<128, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi)
-                      : launch_wo_cl<192, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi);
+  return bmc == 64    ? launch_wo_cl<64, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi, 1)
+         : bmc == 128 ? launch_wo_cl<128, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi, 1)
+                      : launch_wo_cl<192, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi, 1);
 }
 
 int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
