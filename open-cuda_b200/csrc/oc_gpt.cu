@@ -725,76 +725,134 @@ __global__ void __launch_bounds__(256) gemv_cols_kernel(const GemvArgs a) {
   const int cb = a.cb, k = a.k, k4 = k >> 2;
   float* ws = gsm;                   // [cb][k]
   float* xs = gsm + (size_t)cb * k;  // [MR][k]
+  float* lnw = xs + (size_t)MR * k;  // [k] LayerNorm gain, then [k] shift (with ln_w)
+  float* lnb = lnw + k;
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
-  __shared__ float ln_mean[MR], ln_inv[MR];
   __shared__ float wsum[8][MR];
   const int c0 = (int)blockIdx.x * cb, ncol = min(cb, a.n - c0);
   const uint32_t wbytes = (uint32_t)ncol * (uint32_t)k * 4u;
+  // rows of up to 1024 floats are normalised by a warp each in registers
+  const bool ln_reg = a.ln_w && k <= 1024;
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&bar, 1);
     fence_mbar_init();
-    // the weights are written by no kernel of the step: safe before the wait
-    mbar_arrive_expect_tx(&bar, wbytes);
+    // the weights and LayerNorm parameters are written by no kernel of the
+    // step: safe before the wait
+    mbar_arrive_expect_tx(&bar, wbytes + (ln_reg ? 8u * (uint32_t)k : 0u));
     bulk_load_1d(ws, a.W + (size_t)c0 * k, wbytes, &bar);
+    if (ln_reg) {
+      bulk_load_1d(lnw, a.ln_w, 4u * (uint32_t)k, &bar);
+      bulk_load_1d(lnb, a.ln_b, 4u * (uint32_t)k, &bar);
+    }
   }
   const int T = 256 / cb, col = (int)threadIdx.x / T, part = (int)threadIdx.x - col * T;
   const bool live = col < ncol;
   const float bias = live ? __ldg(a.bias + c0 + col) : 0.0f;  // a constant parameter
-  pdl_wait();  // x, out and the KV cache belong to the predecessors until here
+  __syncthreads();  // the barrier is initialised before any thread waits on it
+  pdl_wait();       // x, out and the KV cache belong to the predecessors until here
   pdl_launch();
-  // x rows into shared memory (x is read once); the residual's previous
-  // output values in flight at the same time
-  for (int i = threadIdx.x; i < a.m * k4; i += 256) {
-    const int r = i / k4, c = 4 * (i - r * k4);
-    *reinterpret_cast<float4*>(xs + (size_t)r * k + c) = *reinterpret_cast<const float4*>(a.x + (size_t)r * k + c);
-  }
+  // the residual's previous output values in flight with x
   float old[MR];
 #pragma unroll
   for (int r = 0; r < MR; ++r)
     old[r] = a.epi == kEpiResidual && live && part == 0 && r < a.m ? a.out[(size_t)r * a.n + c0 + col] : 0.0f;
-  __syncthreads();
-  if (a.ln_w) {
-    // LayerNorm statistics (warp per row; the sums in the order of
-    // ln_row_stats), then the rows normalised in place
+  if (ln_reg) {
+    // warp r: row r in registers (lane = float4s at 4 lane + 128 j), mean
+    // and variance by shuffles (the sums in the order of ln_row_stats),
+    // normalised with the gain and shift from shared memory into xs
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r = warp; r < a.m; r += 8) {
-      const float* xr = xs + (size_t)r * k;
-      float sm = 0.0f;
-      for (int c = lane * 4; c < k; c += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(xr + c);
-        sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v.x), v.y), v.z), v.w);
+    if (warp < a.m) {
+      const float* xr = a.x + (size_t)warp * k;
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane * 4 + 128 * j;
+        v[j] = c < k ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
+      float sm = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (lane * 4 + 128 * j < k) sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v[j].x), v[j].y), v[j].z), v[j].w);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
       const float mean = __fdiv_rn(sm, (float)k);
       float vs = 0.0f;
-      for (int c = lane * 4; c < k; c += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(xr + c);
-        const float d0 = __fsub_rn(v.x, mean), d1 = __fsub_rn(v.y, mean);
-        const float d2 = __fsub_rn(v.z, mean), d3 = __fsub_rn(v.w, mean);
-        vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (lane * 4 + 128 * j < k) {
+          const float d0 = __fsub_rn(v[j].x, mean), d1 = __fsub_rn(v[j].y, mean);
+          const float d2 = __fsub_rn(v[j].z, mean), d3 = __fsub_rn(v[j].w, mean);
+          vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
+        }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
-      if (lane == 0) {
-        ln_mean[r] = mean;
-        ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)k), a.ln_eps)));
+      const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)k), a.ln_eps)));
+      const bool got = mbar_wait(&bar, 0, &abort_flag);  // the gain and shift have landed
+      if (!got) abort_flag = 1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = lane * 4 + 128 * j;
+        if (got && c < k) {
+          const float4 w = *reinterpret_cast<const float4*>(lnw + c), b = *reinterpret_cast<const float4*>(lnb + c);
+          float4 y;
+          y.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].x, mean), inv), w.x), b.x);
+          y.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].y, mean), inv), w.y), b.y);
+          y.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].z, mean), inv), w.z), b.z);
+          y.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j].w, mean), inv), w.w), b.w);
+          *reinterpret_cast<float4*>(xs + (size_t)warp * k + c) = y;
+        }
       }
     }
-    __syncthreads();
+  } else {
+    // x rows into shared memory (x is read once)
     for (int i = threadIdx.x; i < a.m * k4; i += 256) {
       const int r = i / k4, c = 4 * (i - r * k4);
-      float4 v = *reinterpret_cast<const float4*>(xs + (size_t)r * k + c);
-      const float4 w = __ldg(reinterpret_cast<const float4*>(a.ln_w + c));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(a.ln_b + c));
-      const float mu = ln_mean[r], inv = ln_inv[r];
-      v.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu), inv), w.x), b.x);
-      v.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu), inv), w.y), b.y);
-      v.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu), inv), w.z), b.z);
-      v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu), inv), w.w), b.w);
-      *reinterpret_cast<float4*>(xs + (size_t)r * k + c) = v;
+      *reinterpret_cast<float4*>(xs + (size_t)r * k + c) = *reinterpret_cast<const float4*>(a.x + (size_t)r * k + c);
+    }
+    if (a.ln_w) {  // rows longer than 1024: statistics (warp per row) and normalisation in shared memory
+      __shared__ float ln_mean[MR], ln_inv[MR];
+      __syncthreads();
+      const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+      for (int r = warp; r < a.m; r += 8) {
+        const float* xr = xs + (size_t)r * k;
+        float sm = 0.0f;
+        for (int c = lane * 4; c < k; c += 128) {
+          const float4 v = *reinterpret_cast<const float4*>(xr + c);
+          sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, v.x), v.y), v.z), v.w);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+        const float mean = __fdiv_rn(sm, (float)k);
+        float vs = 0.0f;
+        for (int c = lane * 4; c < k; c += 128) {
+          const float4 v = *reinterpret_cast<const float4*>(xr + c);
+          const float d0 = __fsub_rn(v.x, mean), d1 = __fsub_rn(v.y, mean);
+          const float d2 = __fsub_rn(v.z, mean), d3 = __fsub_rn(v.w, mean);
+          vs = __fmaf_rn(d3, d3, __fmaf_rn(d2, d2, __fmaf_rn(d1, d1, __fmaf_rn(d0, d0, vs))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) vs = __fadd_rn(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+        if (lane == 0) {
+          ln_mean[r] = mean;
+          ln_inv[r] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(vs, (float)k), a.ln_eps)));
+        }
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < a.m * k4; i += 256) {
+        const int r = i / k4, c = 4 * (i - r * k4);
+        float4 v = *reinterpret_cast<const float4*>(xs + (size_t)r * k + c);
+        const float4 w = __ldg(reinterpret_cast<const float4*>(a.ln_w + c));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(a.ln_b + c));
+        const float mu = ln_mean[r], inv = ln_inv[r];
+        v.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu), inv), w.x), b.x);
+        v.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu), inv), w.y), b.y);
+        v.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu), inv), w.z), b.z);
+        v.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu), inv), w.w), b.w);
+        *reinterpret_cast<float4*>(xs + (size_t)r * k + c) = v;
+      }
     }
   }
   __syncthreads();
@@ -804,14 +862,28 @@ __global__ void __launch_bounds__(256) gemv_cols_kernel(const GemvArgs a) {
     if (threadIdx.x == 0) kernel_fail(a.status, &abort_flag, kDevTimeoutProducer);
     return;
   }
-  float acc[MR];
+  // two independent FMA chains per row (even and odd strips), added at the end
+  float acc[MR], acc2[MR];
 #pragma unroll
-  for (int r = 0; r < MR; ++r) acc[r] = 0.0f;
+  for (int r = 0; r < MR; ++r) acc[r] = acc2[r] = 0.0f;
   if (live) {
     const float4* wr = reinterpret_cast<const float4*>(ws + (size_t)col * k);
     const float4* xr = reinterpret_cast<const float4*>(xs);
-#pragma unroll 4
-    for (int j = part; j < k4; j += T) {
+    int j = part;
+#pragma unroll 2
+    for (; j + T < k4; j += 2 * T) {
+      const float4 w = wr[j], w2 = wr[j + T];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        if (r < a.m) {
+          const float4 xv = xr[r * k4 + j], xv2 = xr[r * k4 + j + T];
+          acc[r] = __fmaf_rn(xv.w, w.w, __fmaf_rn(xv.z, w.z, __fmaf_rn(xv.y, w.y, __fmaf_rn(xv.x, w.x, acc[r]))));
+          acc2[r] =
+              __fmaf_rn(xv2.w, w2.w, __fmaf_rn(xv2.z, w2.z, __fmaf_rn(xv2.y, w2.y, __fmaf_rn(xv2.x, w2.x, acc2[r]))));
+        }
+      }
+    }
+    if (j < k4) {
       const float4 w = wr[j];
 #pragma unroll
       for (int r = 0; r < MR; ++r) {
@@ -822,6 +894,8 @@ __global__ void __launch_bounds__(256) gemv_cols_kernel(const GemvArgs a) {
       }
     }
   }
+#pragma unroll
+  for (int r = 0; r < MR; ++r) acc[r] = __fadd_rn(acc[r], acc2[r]);
   // the T partial sums of a column: lanes of one group (T <= 32 lanes, groups
   // aligned to T) by shuffles, then the column's warps in order (T = 64)
   const int tw = T < 32 ? T : 32;
@@ -1030,7 +1104,7 @@ static void launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
 template <int MR>
 static void launch_cols(const GemvArgs& a, cudaStream_t s) {
   auto kern = gemv_cols_kernel<MR>;
-  const size_t smem = ((size_t)a.cb + MR) * a.k * sizeof(float);
+  const size_t smem = ((size_t)a.cb + MR + 2) * a.k * sizeof(float);  // weights, x rows, LayerNorm gain and shift
   smem_attr_once(reinterpret_cast<const void*>(kern), std::max<size_t>(smem, 48 * 1024));
   launch_pdl(kern, dim3((a.n + a.cb - 1) / a.cb), dim3(256), smem, s, a);
 }
