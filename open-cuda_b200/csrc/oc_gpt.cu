@@ -135,6 +135,21 @@ __device__ __forceinline__ void attn_stage(float* dst, const float* src, int j0,
   cp_async_commit();
 }
 
+// sum over keys j = g, g + G, ... < cnt of p[j] * v[j][dim] in four
+// independent FMA chains (the loads of four keys in flight together)
+__device__ __forceinline__ float attn_pv(const float* p, const float* v, int g, int G, int cnt, int d, int dim) {
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  int j = g;
+  for (; j + 3 * G < cnt; j += 4 * G) {
+    a0 = __fmaf_rn(p[j], v[j * d + dim], a0);
+    a1 = __fmaf_rn(p[j + G], v[(j + G) * d + dim], a1);
+    a2 = __fmaf_rn(p[j + 2 * G], v[(j + 2 * G) * d + dim], a2);
+    a3 = __fmaf_rn(p[j + 3 * G], v[(j + 3 * G) * d + dim], a3);
+  }
+  for (; j < cnt; j += G) a0 = __fmaf_rn(p[j], v[j * d + dim], a0);
+  return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+}
+
 __device__ __forceinline__ float attn_block_reduce(float v, float* red, bool is_max) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -208,12 +223,33 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int j = threadIdx.x, cnt = min(kAttnTile, n - t * kAttnTile);
     if (j < cnt) {
       const float* kr = kt + j * d;
-      const int st = j % d;  // rotated start column: the lanes of a warp hit distinct banks
-      float p = 0.0f;
-      for (int c0 = 0; c0 < d; ++c0) {
-        int c = c0 + st;
-        if (c >= d) c -= d;
-        p = __fmaf_rn(qs[c], kr[c], p);
+      float p;
+      if (vec) {
+        // float4 columns from a rotated start (a quarter warp's rows hit
+        // distinct banks), four independent FMA chains
+        const int d4 = d >> 2, st = j % d4;
+        const float4* kr4 = reinterpret_cast<const float4*>(kr);
+        const float4* q4 = reinterpret_cast<const float4*>(qs);
+        float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+#pragma unroll 4
+        for (int c0 = 0; c0 < d4; ++c0) {
+          int c = c0 + st;
+          if (c >= d4) c -= d4;
+          const float4 kv = kr4[c], qv = q4[c];
+          p0 = __fmaf_rn(qv.x, kv.x, p0);
+          p1 = __fmaf_rn(qv.y, kv.y, p1);
+          p2 = __fmaf_rn(qv.z, kv.z, p2);
+          p3 = __fmaf_rn(qv.w, kv.w, p3);
+        }
+        p = __fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
+      } else {
+        const int st = j % d;  // rotated start column: the lanes of a warp hit distinct banks
+        p = 0.0f;
+        for (int c0 = 0; c0 < d; ++c0) {
+          int c = c0 + st;
+          if (c >= d) c -= d;
+          p = __fmaf_rn(qs[c], kr[c], p);
+        }
       }
       p = __fmul_rn(p, scale);
       s[t * kAttnTile + j] = p;
@@ -237,8 +273,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     cp_async_wait0();
     __syncthreads();
     const float* vt = buf + tile_f;
-    if (g < G && threadIdx.x < G * d)
-      for (int j = g; j < n; j += G) acc = __fmaf_rn(s[j], vt[j * d + dim], acc);
+    if (g < G && threadIdx.x < G * d) acc = attn_pv(s, vt, g, G, n, d, dim);
   } else {
     attn_stage(buf, vb, 0, min(kAttnTile, n), d, H, vec);
   }
@@ -249,8 +284,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     __syncthreads();
     const float* vt = buf + (t & 1) * tile_f;
     const int cnt = min(kAttnTile, n - t * kAttnTile);
-    if (g < G && threadIdx.x < G * d)
-      for (int j = g; j < cnt; j += G) acc = __fmaf_rn(s[t * kAttnTile + j], vt[j * d + dim], acc);
+    if (g < G && threadIdx.x < G * d) acc = __fadd_rn(acc, attn_pv(s + t * kAttnTile, vt, g, G, cnt, d, dim));
     __syncthreads();
   }
   part[threadIdx.x] = acc;
