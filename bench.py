@@ -526,6 +526,59 @@ def qgemm_sharded(ctx):
     return out
 
 
+def moe_ep_extra(ctx):
+    """N > 1: the config-5 MoE block run expert-parallel (E/g experts and T/g
+    tokens per rank, the shared expert on every rank): count all-to-all, row
+    all-to-all, output all-to-all (NCCL).  Timed with the exchanges inside
+    (max over ranks), and the three all-to-alls alone with the same splits
+    beside it."""
+    import moe
+    import synth
+
+    torch = ctx.torch
+    import torch.distributed as dist
+
+    g = ctx.world
+    w = moe.random_weights(E_E // g, E_D, E_F, 5 + ctx.rank, ctx.device)
+    T = E_T // g
+    x = torch.from_numpy(synth.uniform(70 + ctx.rank, T * E_D).reshape(T, E_D)).to(ctx.device)
+    lg = torch.from_numpy(synth.normal(71 + ctx.rank, T * E_E).reshape(T, E_E)).to(ctx.device)
+    torch.cuda.synchronize()
+
+    def step(_i):
+        return moe.moe_forward_ep(x, lg, w, E_E, E_K)
+
+    with torch.cuda.stream(ctx.stream):
+        for _ in range(2):
+            step(0)
+    torch.cuda.synchronize()
+    ms, _ = ctx.timed(step, 5)
+    # the exchanges alone, with this block's splits
+    idx, _tw = moe.route(lg, E_K)
+    dest = torch.div(idx, E_E // g, rounding_mode="floor").reshape(-1)
+    cnt_send = torch.bincount(dest, minlength=g).to(torch.int32)
+    cnt_recv = torch.empty_like(cnt_send)
+    dist.all_to_all_single(cnt_recv, cnt_send)
+    send, recv = [int(v) for v in cnt_send.tolist()], [int(v) for v in cnt_recv.tolist()]
+    row_bytes = E_D + 8  # int8 row, f32 scale, int32 local expert id
+    sb = torch.empty(sum(send), row_bytes, dtype=torch.uint8, device=ctx.device)
+    rb = torch.empty(sum(recv), row_bytes, dtype=torch.uint8, device=ctx.device)
+    ob = torch.empty(sum(recv), E_D, device=ctx.device)
+    bb = torch.empty(sum(send), E_D, device=ctx.device)
+
+    def exchange(_i):
+        dist.all_to_all_single(cnt_recv, cnt_send)
+        dist.all_to_all_single(rb, sb, recv, send)
+        dist.all_to_all_single(bb, ob, send, recv)
+
+    ms_x, _ = ctx.timed(exchange, 5)
+    ops = e_ops() / g  # this rank's share of the block's work
+    return {"ranks": g, "experts_per_rank": E_E // g, "tokens_per_rank": T, "collective": "NCCL all_to_all_single x3",
+            "ms": round(ms, 3), "all_to_all_ms": round(ms_x, 3), "all_to_all_share": round(ms_x / ms, 3),
+            "TOPS": round(ops * g / (ms * 1e-3) / 1e12, 1),
+            "rows_sent": sum(send), "MB_exchanged_per_rank": round((sum(send) * row_bytes + sum(recv) * E_D * 4) / 2 ** 20, 1)}
+
+
 def run_qgemm(ctx):
     torch, oc, args = ctx.torch, ctx.oc, ctx.args
     import synth
@@ -663,6 +716,7 @@ def run_qgemm(ctx):
     extra["flash_attention"] = flash_cases(ctx)
     if ctx.world > 1:
         extra["sharded"] = qgemm_sharded(ctx)
+        extra["moe_expert_parallel"] = moe_ep_extra(ctx)
     cpu = cpu_qgemm() if ctx.rank == 0 and not args.no_cpu_baseline else None
     config = {"workload": WORKLOADS["qgemm"],
               "parallelism": f"replicas x{ctx.world}",
