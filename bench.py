@@ -467,6 +467,63 @@ def qgemm_gpt2_batch1(ctx):
             "note": "per-token time includes the amortised 32-token prefill"}
 
 
+def other_configs(ctx):
+    """Compact device-timed figures of the other configs, so that the default
+    line carries one of each (the per-workload lines hold the full sweeps):
+    config 1 sgemm, config 4's vocabulary-shaped INT4 GEMM at M = 64 and
+    4096, config 5's MLA projections and MoE block.  CUDA events, inputs
+    resident in HBM, rotating sets or operands larger than L2."""
+    import moe
+    import synth
+
+    torch, oc = ctx.torch, ctx.oc
+    d = ctx.device
+    out = {}
+    # config 1: sgemm 512x768x2304 + bias (16 rotating sets, 213 MB)
+    A, B, bias = s_case()
+    sets = [(torch.from_numpy(A).to(d), torch.from_numpy(B).to(d), torch.from_numpy(bias).to(d),
+             torch.empty(S_M, S_N, device=d)) for _ in range(S_SETS)]
+    us = _rotating_us(ctx, lambda j: oc.sgemm(sets[j][0], sets[j][1], C=sets[j][3], bias=sets[j][2]), S_SETS)
+    out["sgemm_512x768x2304"] = {"us": round(us, 2), "TFLOP/s": round(2 * S_M * S_K * S_N / us / 1e6, 1)}
+    del sets
+    # config 4: INT4 g32 weight-only at K=3584, N=152064 (340 MB of weights and scales)
+    g = torch.Generator(device=d).manual_seed(5)
+    W = torch.randn(V_N, V_K, generator=g, device=d) * 0.02
+    q4, s4 = oc.quantize_int4(W.view(-1), Q_G)
+    del W
+    for m in (64, 4096):
+        Am = torch.rand(m, V_K, generator=g, device=d) * 2 - 1
+        Y = torch.empty(m, V_N, device=d)
+        us = ctx.kernel_us(lambda: oc.qgemm_w4(Am, q4, s4, Q_G, out=Y), reps=3, graph=False)
+        out[f"int4_M{m}_K{V_K}_N{V_N}"] = {"us": round(us, 1), "TFLOP/s": round(2 * m * V_K * V_N / us / 1e6, 1)}
+        del Am, Y
+    del q4, s4
+    torch.cuda.empty_cache()
+    # config 5: MLA compress 16384x7168 -> 512 and one decompress 512 -> 16384
+    kv = torch.randn(L_SEQ, L_DH, generator=g, device=d) * 0.02
+    down = torch.randn(L_DH, L_DC, generator=g, device=d) * 0.02
+    up = torch.randn(L_DC, L_UP, generator=g, device=d) * 0.02
+    lat = oc.mla_compress_kv(kv, down)
+    us_c = ctx.kernel_us(lambda: oc.mla_compress_kv(kv, down), reps=3, graph=False)
+    us_d = ctx.kernel_us(lambda: oc.mla_decompress_kv(lat, up), reps=3, graph=False)
+    out["mla"] = {"compress_us": round(us_c, 1), "compress_TFLOP/s": round(2 * L_SEQ * L_DH * L_DC / us_c / 1e6, 1),
+                  "decompress_us": round(us_d, 1), "decompress_TFLOP/s": round(2 * L_SEQ * L_DC * L_UP / us_d / 1e6, 1)}
+    del kv, down, up, lat
+    torch.cuda.empty_cache()
+    # config 5: MoE block, 8192 tokens, 256 INT8 experts top-8 + the shared expert (one GPU)
+    w = moe.random_weights(E_E, E_D, E_F, 5, d)
+    x = torch.from_numpy(synth.uniform(70, E_T * E_D).reshape(E_T, E_D)).to(d)
+    lg = torch.from_numpy(synth.normal(71, E_T * E_E).reshape(E_T, E_E)).to(d)
+    with torch.cuda.stream(ctx.stream):
+        moe.moe_forward(x, lg, w, E_K)
+    torch.cuda.synchronize()
+    us = ctx.kernel_us(lambda: moe.moe_forward(x, lg, w, E_K), reps=3, graph=False)
+    out["moe_block"] = {"us": round(us, 1), "TOPS": round(e_ops() / us / 1e6, 1)}
+    del w, x, lg
+    torch.cuda.empty_cache()
+    return out
+
+
 def qgemm_sharded(ctx):
     """N > 1: the config-4 column-sharded INT4 g32 weight-only GEMM (K=3584,
     N=152064): each rank computes its N/g columns, one NCCL all-gather plus
@@ -714,6 +771,7 @@ def run_qgemm(ctx):
     extra["gemv_cold_hbm"] = qgemm_cold_gemv(ctx)
     extra["gpt2_batch1"] = qgemm_gpt2_batch1(ctx)
     extra["flash_attention"] = flash_cases(ctx)
+    extra["other_configs"] = other_configs(ctx)
     if ctx.world > 1:
         extra["sharded"] = qgemm_sharded(ctx)
         extra["moe_expert_parallel"] = moe_ep_extra(ctx)
