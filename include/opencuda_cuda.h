@@ -169,11 +169,12 @@ int oc_get_device_status(int *status);
  * Replaces the GemmPath::CuBlas arm of sgemm (blas:293). */
 int oc_sgemm(int m, int n, int k, float alpha, const float *A, int lda, const float *B, int ldb, int trans_b,
              float beta, float *C, int ldc, const float *bias, void *stream);
-/* For a B that is reused across calls (weights): oc_sgemm splits B into
- * tf32 hi/lo halves laid out [n][k] on every call; these entry points do it
- * once.  prepared holds oc_sgemm_prepared_b_size() bytes; then
- * oc_sgemm_prepared computes the same product as oc_sgemm on the tensor
- * cores (A must be 16-byte aligned with lda % 4 == 0). */
+/* For a B that is reused across calls (weights): oc_sgemm prepares B's
+ * tensor-core operands on every call; these entry points split B into tf32
+ * hi/lo halves laid out [n][k] once.  prepared holds
+ * oc_sgemm_prepared_b_size() bytes; then oc_sgemm_prepared computes the same
+ * product on the tf32 tensor cores with the 3xTF32 split (A must be 16-byte
+ * aligned with lda % 4 == 0). */
 int oc_sgemm_prepared_b_size(int k, int n, size_t *bytes);
 int oc_sgemm_prepare_b(int k, int n, const float *B, int ldb, int trans_b, float *prepared, void *stream);
 int oc_sgemm_prepared(int m, int n, int k, float alpha, const float *A, int lda, const float *prepared, float beta,
