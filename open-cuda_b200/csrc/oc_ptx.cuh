@@ -218,6 +218,19 @@ __device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem], signed 8-bit operands, s32 accumulate.  A
+// (M = 128 rows) lives in TMEM with row i in lane i and K packed four bytes
+// per 32-bit column (byte j of column c = K position 4c + j).
+__device__ __forceinline__ void mma_i8_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem], tf32 operands, f32 accumulate.
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
@@ -231,6 +244,16 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
 
 // Loads 32 consecutive 32-bit TMEM columns of this thread's lane
 // (32x32b shape: warp w reads lanes 32*(w%4) .. +31).
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -244,6 +267,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+
 // 16 consecutive 32-bit TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -252,6 +276,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+
+// NC consecutive columns (NC % 4 == 0) from taddr into r[0 .. NC), in
+// 32-, 16-, 8- and 4-column loads; completes at the next tmem_ld_wait.
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
+  static_assert(NC % 4 == 0 && NC > 0, "whole 4-column loads");
+  if constexpr (NC >= 32) {
+    tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+    if constexpr (NC > 32) tmem_ld_cols<NC - 32>(taddr + 32, r + 32);
+  } else if constexpr (NC >= 16) {
+    tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(r));
+    if constexpr (NC > 16) tmem_ld_cols<NC - 16>(taddr + 16, r + 16);
+  } else if constexpr (NC >= 8) {
+    tmem_ld8(taddr, *reinterpret_cast<uint32_t(*)[8]>(r));
+    if constexpr (NC > 8) tmem_ld_cols<NC - 8>(taddr + 8, r + 8);
+  } else {
+    tmem_ld4(taddr, *reinterpret_cast<uint32_t(*)[4]>(r));
+  }
 }
 
 // Stores the same 32-bit value into 32 consecutive TMEM columns of this

@@ -21,6 +21,7 @@
 #include <mutex>
 
 #include "oc_gemm_wo.cuh"
+#include "oc_gemm_wo4g.cuh"
 #include "oc_internal.h"
 
 namespace oc {
@@ -510,9 +511,59 @@ int gemm_terms_epi(int m, int n, int k, const __half* ax, const float* icm, cons
                       : launch_wo_cl<192, 2>(ta, tw, ks, m, n, k, ldy, icm, colf, bias, Y, s, epi, 1);
 }
 
+// INT4 group 32 with 1-64 rows over enough 128-row weight tiles to fill the
+// GPU, K % 128 == 0: gemm_wo4g_kernel (the packed weights read once and
+// widened to int8 in tensor memory, the activations as three int8 digits,
+// exact int32 group sums scaled on their way out), after one launch that
+// writes the digits.
+static bool wo4g_ok(int m, int n, int k, int group, const float* A, const void* wq, const float* sw) {
+  return m >= 1 && m <= 64 && k % 128 == 0 && group == 32 && is_sm100() && aligned16(A) && aligned16(wq) &&
+         aligned16(sw) && (n + 127) / 128 >= std::max(1, sm_count());
+}
+
+template <int BM, int LCW>
+static int launch_wo4g(int m, int n, int k, const float* A, const void* wq, const float* sw, const float* bias,
+                       float* Y, cudaStream_t s) {
+  using C = Wo4G<BM>;
+  float* scratch = g_wo_ax.get((size_t)3 * BM * k / 4 + 128, s);  // digit images (3 BM k bytes), then rowf [128]
+  if (!scratch) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm (weight-only): scratch allocation failed");
+  int8_t* dig = reinterpret_cast<int8_t*>(scratch);
+  float* rowf = scratch + (size_t)3 * BM * k / 4;
+  CUtensorMap tw, tsc;
+  int rc = make_tmap_2d(&tw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, (uint64_t)k / 2,
+                        C::RBK / 2, C::BN, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tsc, sw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k / 32, (uint64_t)n, (uint64_t)k / 8,
+                    C::SCB * C::RBK / 32, C::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  auto kern = gemm_wo4g_kernel<BM, LCW>;
+  if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
+    return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_wo4g_kernel) failed");
+  rc = wo_launch_rc(launch_pdl_ex(wo4g_prep_kernel, dim3(BM), dim3(128), 0, s, A, m, k, dig, rowf),
+                    "wo4g_prep_kernel");
+  if (rc) return rc;
+  const int grid = std::min((n + C::BN - 1) / C::BN, std::max(1, sm_count()));
+  return wo_launch_rc(launch_pdl_ex(kern, dim3(grid), dim3(C::THREADS), C::SMEM, s, tw, tsc, (const int8_t*)dig, m, n, k,
+                                    (const float*)rowf, bias, Y, device_status_word()),
+                      "gemm_wo4g_kernel");
+}
+
+static int run_wo4g(int m, int n, int k, const float* A, const void* wq, const float* sw, const float* bias,
+                    float* Y, cudaStream_t s) {
+  // the drain loads 3 columns per live row of a group (in 4-column steps)
+  if (m == 1) return launch_wo4g<16, 4>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m == 2) return launch_wo4g<16, 8>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m <= 5) return launch_wo4g<16, 16>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m <= 10) return launch_wo4g<16, 32>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m <= 16) return launch_wo4g<16, 48>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m <= 32) return launch_wo4g<32, 48>(m, n, k, A, wq, sw, bias, Y, s);
+  return launch_wo4g<64, 96>(m, n, k, A, wq, sw, bias, Y, s);
+}
+
 int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,
                  const float* bias, float* Y, cudaStream_t s, bool weights_ready) {
   const uint8_t* w8 = static_cast<const uint8_t*>(wq);
+  if (bits == 4 && wo4g_ok(m, n, k, group, A, wq, sw)) return run_wo4g(m, n, k, A, wq, sw, bias, Y, s);
   if (wo_tc_ok(bits, m, k, group, A) && aligned16(wq))
     return bits == 8 ? run_wo_gemm<1>(m, n, k, group, A, wq, sw, bias, Y, s, weights_ready)
                      : run_wo_gemm<2>(m, n, k, group, A, wq, sw, bias, Y, s, weights_ready);

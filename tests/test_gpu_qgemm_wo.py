@@ -238,3 +238,60 @@ def test_w4_skinny_chunk_outliers(oc, oracle, m, group, a_scale):
     yr, rr = y.reshape(m, n), y_ref.reshape(m, n)
     for r in range(m):
         assert rel_fro(yr[r], rr[r]) <= REL_FRO, (r, rel_fro(yr[r], rr[r]))
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 7, 12, 16, 17, 33, 64])
+def test_w4_few_rows_many_columns(oc, oracle, m):
+    # 1-64 rows over enough 128-column weight tiles to fill the GPU (here
+    # 19000 columns, the last tile ragged), groups of 32: the packed weights
+    # are widened to int8 in tensor memory, the activations enter as three
+    # int8 digits and each group's exact int32 sums are scaled on their way
+    # out; every output against the oracle
+    k, n = 1024, 19000
+    A, WT, bias = synth.qgemm_case(m, k, n, 31, 32, 33)
+    A[0, :] *= np.float32(1e-3)  # a row far smaller than the others
+    wq, ws = _quant(oracle, WT, 4, 32)
+    y_ref = oracle.qgemm_weight_only(4, m, k, n, 32, A, wq, ws, bias)
+    y = _run(oc, 4, A, wq, ws, 32, bias)
+    assert rel_fro(y, y_ref) <= REL_FRO, rel_fro(y, y_ref)
+    yr, rr = y.reshape(m, n), y_ref.reshape(m, n)
+    for r in range(m):
+        assert rel_fro(yr[r], rr[r]) <= REL_FRO, (r, rel_fro(yr[r], rr[r]))
+    assert rel_fro(yr[:, -37:], rr[:, -37:]) <= REL_FRO  # the ragged last tile
+
+
+@pytest.mark.parametrize("a_scale", [1.0, 1e-30, 1e6])
+@pytest.mark.parametrize("m", [1, 5, 40])
+def test_w4_few_rows_many_columns_outliers(oc, oracle, m, a_scale):
+    # the int8-digit path with one element per 32-element chunk 1000x the
+    # others, some 1e-6x, a chunk of zeros and rows of any magnitude: the
+    # digits round to 2^-23 of each row's largest |a|, inside the f32
+    # tolerance per row
+    k, n = 1024, 19000
+    A, WT, bias = synth.qgemm_case(m, k, n, 41, 42, 43)
+    A = (A * np.float32(a_scale)).astype(np.float32)
+    bias = (bias * np.float32(a_scale)).astype(np.float32)
+    A[:, 5::32] *= np.float32(1000.0)
+    A[:, 9::32] *= np.float32(1e-6)
+    A[:, 64:96] = 0.0
+    A = A.astype(np.float32)
+    wq, ws = _quant(oracle, WT, 4, 32)
+    y_ref = oracle.qgemm_weight_only(4, m, k, n, 32, A, wq, ws, bias)
+    y = _run(oc, 4, A, wq, ws, 32, bias)
+    yr, rr = y.reshape(m, n), y_ref.reshape(m, n)
+    for r in range(m):
+        assert rel_fro(yr[r], rr[r]) <= REL_FRO, (r, rel_fro(yr[r], rr[r]))
+
+
+def test_w4_few_rows_many_columns_nonfinite_row(oc, oracle):
+    # a NaN or an infinity in an activation row of the int8-digit path makes
+    # that row's outputs NaN; the other rows are unaffected
+    m, k, n = 3, 1024, 19000
+    A, WT, bias = synth.qgemm_case(m, k, n, 51, 52, 53)
+    wq, ws = _quant(oracle, WT, 4, 32)
+    A[0, 77] = np.nan
+    A[2, 500] = np.inf
+    y = _run(oc, 4, A, wq, ws, 32, bias).reshape(m, n)
+    assert np.all(np.isnan(y[0])) and np.all(np.isnan(y[2]))
+    y_ref = oracle.qgemm_weight_only(4, 1, k, n, 32, A[1:2].copy(), wq, ws, bias)
+    assert rel_fro(y[1], y_ref) <= REL_FRO
