@@ -38,11 +38,14 @@
 // multiple of 4) and issues a batch's loads before one wait: TMEM load
 // latency, paid once per group, otherwise sets the pace at small M.
 // Roles (persistent over 128-row tiles):
-//   warp 0      TMA producer: raw blocks (128 k of packed weights, 64-byte
-//               swizzle), the raw block's group scales, its digit tile
-//   warp 1      TMEM allocator + MMA issuer (one MMA per group)
+//   warp 0      weight producer: raw blocks (128 k of packed weights, 64-byte
+//               swizzle) by TMA, gated only by the converters
+//   warp 1      TMEM allocator + MMA issuer (one MMA per group); with
+//               ISSUERS = 2 warp 7 issues every other block
 //   warps 2-5   converters: thread = weight row (TMEM lane quadrant warp % 4)
-//   warps 6-    drainers (4 per CPW activation rows): thread = weight row;
+//   warp 6      operand producer: scale tiles (TMA) and digit images (bulk
+//               copies), gated by the drain and by MMA completion
+//   DRAIN0-     drainers (4 per CPW activation rows): thread = weight row;
 //               the tile's outputs stored once all its groups are in
 // Every wait is bounded (oc_ptx.cuh).
 #pragma once
@@ -51,30 +54,35 @@
 
 namespace oc {
 
-template <int BM_>
+template <int NC_>
 struct Wo4G {
-  static constexpr int BN = 128, BM = BM_, RBK = 128;  // weight rows per tile; activation rows; k per raw block
-  static constexpr int N3 = 3 * BM;                    // MMA N: digit planes 0, 1, 2
+  static constexpr int BN = 128, RBK = 128;            // weight rows per tile; k per raw block
+  static constexpr int N3 = NC_;                       // MMA N: 3 digit rows per activation row, padded
+  static constexpr int BM = N3 / 3;                    // activation rows a tile holds
   static constexpr int CPW = BM <= 32 ? 16 : 32;       // activation rows per drain warp
-  static constexpr int DRAIN_WARPS = 4 * (BM / CPW);
+  static constexpr int DRAIN_WARPS = 4 * ((BM + CPW - 1) / CPW);
   static constexpr int STAGES = 4;                     // digit tiles and converted weight blocks in flight
   static constexpr int RSTAGES = 8, SSTAGES = 3;
   static constexpr int SCB = 4;                          // raw blocks per scale tile
   static constexpr int RAW_BYTES = BN * RBK / 2;         // packed nibbles [128][64 bytes]
   static constexpr int SCL_BYTES = BN * SCB * (RBK / 32) * 4;  // scale tile [128][16] f32 (64-byte rows)
-  static constexpr int DIG_BYTES = N3 * RBK;             // digit tile [3 BM][128 k] int8
+  static constexpr int DIG_BYTES = N3 * RBK;             // digit image [N3][128 k] int8
   static constexpr int ACOLS = RBK / 4;                  // TMEM columns of a converted raw block
   static constexpr int D_COL0 = STAGES * ACOLS;          // the accumulator ring follows the weight ring
-  static constexpr int NB = (512 - D_COL0) / N3 < 8 ? (512 - D_COL0) / N3 : 8;
+  static constexpr int NB_FIT = (512 - D_COL0) / N3 < 24 ? (512 - D_COL0) / N3 : 24;
   // groups per accumulator batch (one wait and one commit each), batches in the ring
-  static constexpr int GB = NB >= 8 ? 4 : NB >= 4 ? 2 : 1, NBATCH = NB / GB;
+  static constexpr int GB = NB_FIT >= 8 ? 4 : NB_FIT >= 4 ? 2 : 1, NBATCH = NB_FIT / GB, NB = GB * NBATCH;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int THREADS = 32 * (6 + DRAIN_WARPS);
+  // MMA issuers: warp 1, and with one batch per block also warp 7, each
+  // taking every other block (its stages alternate with the other's): one
+  // thread's waits and commits, not the tensor pipe, bound the MMA rate
+  static constexpr int ISSUERS = (GB == RBK / 32 && STAGES % 2 == 0) ? 2 : 1;
+  static constexpr int DRAIN0 = 6 + ISSUERS;  // first drain warp
+  static constexpr int THREADS = 32 * (DRAIN0 + DRAIN_WARPS);
   static constexpr int BAR_BYTES = 8 * (2 * RSTAGES + 2 * STAGES + 2 * NBATCH + 2 * SSTAGES) + 16;
   static constexpr size_t SMEM = 1024 + (size_t)RSTAGES * RAW_BYTES + (size_t)STAGES * DIG_BYTES +
                                  (size_t)SSTAGES * SCL_BYTES + 2 * 64 * 4 + BAR_BYTES;
-  static_assert(BM == 16 || BM == 32 || BM == 64, "activation rows per tile");
-  static_assert(N3 % 16 == 0 && N3 <= 256, "MMA N for M = 128");
+  static_assert(N3 == 16 || N3 == 32 || N3 == 48 || N3 == 96 || N3 == 192, "MMA N for M = 128");
   static_assert(NB >= 2 && D_COL0 + NB * N3 <= TMEM_COLS, "tensor memory budget");
   static_assert(NBATCH >= 2 && (RBK / 32) % GB == 0, "at least two accumulator batches; whole batches per block");
   static_assert(DIG_BYTES % 1024 == 0 && RAW_BYTES % 1024 == 0, "1024-byte tile alignment");
@@ -83,28 +91,32 @@ struct Wo4G {
 
 // Activation row -> digits, written as the shared-memory image of the
 // GEMM's B operand, so that one contiguous bulk copy per raw block loads it:
-// for raw block rb (128 k) an image of 3 BM rows x 128 bytes (BM = the
+// for raw block rb (128 k) an image of NC rows x 128 bytes (NC >= 3 x the
 // grid size), row 3 m + p holding digit p of activation row m, 16-byte
 // chunk c of a row stored at chunk c ^ (row & 7) (the 128-byte swizzle), k
 // permuted within each 8-k block to position (k & 1) 4 + (k & 7) / 2.
 // Block b < M: row b of A ([M][K] f32, K % 128 == 0, 16-byte aligned) ->
 // its digits, rowf[b] = 2^-min(ce, 126) and rowf[64 + b] = 2^-(ce - min(ce,
 // 126)) (rowf[b] NaN for a row holding a NaN or an infinity).  Blocks b >=
-// M zero their rows.
-__global__ void __launch_bounds__(128) wo4g_prep_kernel(const float* __restrict__ A, int M, int K,
+// M zero their rows, block 0 also the rows past 3 x the grid size.
+__global__ void __launch_bounds__(128) wo4g_prep_kernel(const float* __restrict__ A, int M, int K, int NC,
                                                         int8_t* __restrict__ dig, float* __restrict__ rowf) {
   pdl_wait();
   pdl_launch();
   __shared__ float red[4];
   __shared__ int redb[4];
   const int row = blockIdx.x;
-  const size_t img_bytes = (size_t)3 * gridDim.x * 128;  // one raw block's image
-  // the 8 bytes of digit plane p for the 8-k block b8 of this row
-  auto slot = [&](int p, int b8) -> uint2* {
-    const int rr = 3 * row + p, c = (b8 & 15) >> 1;
+  const size_t img_bytes = (size_t)NC * 128;  // one raw block's image
+  // the 8 bytes of image row rr for the 8-k block b8
+  auto slot_rr = [&](int rr, int b8) -> uint2* {
+    const int c = (b8 & 15) >> 1;
     return reinterpret_cast<uint2*>(dig + (size_t)(b8 >> 4) * img_bytes + rr * 128 + ((c ^ (rr & 7)) << 4) +
                                     8 * (b8 & 1));
   };
+  auto slot = [&](int p, int b8) { return slot_rr(3 * row + p, b8); };
+  if (row == 0)
+    for (int rr = 3 * (int)gridDim.x; rr < NC; ++rr)
+      for (int b8 = threadIdx.x; b8 < K / 8; b8 += 128) *slot_rr(rr, b8) = make_uint2(0u, 0u);
   if (row >= M) {
     for (int b8 = threadIdx.x; b8 < K / 8; b8 += 128) {
       *slot(0, b8) = make_uint2(0u, 0u);
@@ -175,12 +187,12 @@ __device__ __forceinline__ void nib8_to_i8(uint32_t w, uint32_t& lo, uint32_t& h
 // the prep kernel's digit images ([K/128][DIG_BYTES]); rowf: its factors.  Groups of 32, K % 128 == 0, M <= BM; LCW (a
 // multiple of 4, at most 3 CPW): columns a drain warp loads per group, at
 // least 3 min(M, CPW).
-template <int BM, int LCW>
-__global__ void __launch_bounds__(Wo4G<BM>::THREADS, 1)
+template <int NC, int LCW>
+__global__ void __launch_bounds__(Wo4G<NC>::THREADS, 1)
     gemm_wo4g_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                      const int8_t* __restrict__ dimg, int M, int N, int K, const float* __restrict__ rowf,
                      const float* __restrict__ bias, float* __restrict__ Y, int* status) {
-  using C = Wo4G<BM>;
+  using C = Wo4G<NC>;
   constexpr int GPB = C::RBK / 32;  // groups per raw block
   const int tiles = (N + C::BN - 1) / C::BN, nrb = K / C::RBK;
   if (threadIdx.x == 0 && (int)blockIdx.x < tiles)  // the first tile's packed weights into L2 before the wait
@@ -241,17 +253,62 @@ __global__ void __launch_bounds__(Wo4G<BM>::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {  // producer: raw block rb of the tile, its scale tile (every SCB blocks), its digit image
-      int ci = 0, sc = 0;
+    if (lane == 0) {  // weight producer: raw block rb of the tile
+      int ci = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
         for (int rb = 0; rb < nrb; ++rb, ++ci) {
-          const int rs = ci % C::RSTAGES, st = ci % C::STAGES;
+          const int rs = ci % C::RSTAGES;
           if (!mbar_wait(&raw_empty[rs], ((uint32_t)(ci / C::RSTAGES) & 1u) ^ 1u, abort_flag)) {
             kernel_fail(status, abort_flag, kDevTimeoutProducer);
             goto done;
           }
           mbar_arrive_expect_tx(&raw_full[rs], C::RAW_BYTES);
           tma_load_2d(raw(rs), &tmW, rb * (C::RBK / 2), t * C::BN, &raw_full[rs]);
+        }
+      }
+    }
+  } else if (warp == 1 || (C::ISSUERS == 2 && warp == 7)) {
+    if (lane == 0) {  // MMA: D_g = W . [t0; t1; t2] over the group's 32 k, one accumulator per group
+      constexpr uint32_t idesc = idesc_i8(C::BN, C::N3);
+      const int issuer = warp == 1 ? 0 : 1;
+      int ci = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        for (int rb = 0; rb < nrb; ++rb, ++ci) {
+          if (ci % C::ISSUERS != issuer) continue;  // the other issuer's block
+          const int st = ci % C::STAGES;
+          if (!mbar_wait(&stage_full[st], (uint32_t)(ci / C::STAGES) & 1u, abort_flag)) {
+            kernel_fail(status, abort_flag, kDevTimeoutMma);
+            goto done;
+          }
+          tc_fence_after();
+          const uint32_t a_tm = tmem_base + (uint32_t)(st * C::ACOLS);
+          const uint32_t b0 = smem_u32(dtile(st));
+#pragma unroll
+          for (int gb = 0; gb < GPB / C::GB; ++gb) {
+            const int bi = ci * (GPB / C::GB) + gb, d = bi % C::NBATCH;
+            if (!mbar_wait(&d_empty[d], ((uint32_t)(bi / C::NBATCH) & 1u) ^ 1u, abort_flag)) {
+              kernel_fail(status, abort_flag, kDevTimeoutMma);
+              goto done;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int u = 0; u < C::GB; ++u) {
+              const int g4 = gb * C::GB + u;
+              mma_i8_ta(tmem_base + (uint32_t)(C::D_COL0 + (d * C::GB + u) * C::N3), a_tm + (uint32_t)(g4 * 8),
+                        desc_kmajor_sw128(b0 + (uint32_t)(g4 * 32)), idesc, 0u);
+            }
+            tc_commit(&d_full[d]);
+          }
+          tc_commit(&blk_done[st]);
+        }
+      }
+    }
+  } else if (warp == 6) {
+    if (lane == 0) {  // operand producer: the scale tile every SCB blocks, each block's digit image
+      int ci = 0, sc = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        for (int rb = 0; rb < nrb; ++rb, ++ci) {
+          const int st = ci % C::STAGES;
           if (rb % C::SCB == 0) {
             const int ss = sc % C::SSTAGES;
             if (!mbar_wait(&s_empty[ss], ((uint32_t)(sc / C::SSTAGES) & 1u) ^ 1u, abort_flag)) {
@@ -269,40 +326,6 @@ __global__ void __launch_bounds__(Wo4G<BM>::THREADS, 1)
           }
           mbar_arrive_expect_tx(&stage_full[st], C::DIG_BYTES);
           bulk_load_1d(dtile(st), dimg + (size_t)rb * C::DIG_BYTES, C::DIG_BYTES, &stage_full[st]);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {  // MMA: D_g = W . [t0; t1; t2] over the group's 32 k, one accumulator per group
-      constexpr uint32_t idesc = idesc_i8(C::BN, C::N3);
-      int ci = 0, bi = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        for (int rb = 0; rb < nrb; ++rb, ++ci) {
-          const int st = ci % C::STAGES;
-          if (!mbar_wait(&stage_full[st], (uint32_t)(ci / C::STAGES) & 1u, abort_flag)) {
-            kernel_fail(status, abort_flag, kDevTimeoutMma);
-            goto done;
-          }
-          tc_fence_after();
-          const uint32_t a_tm = tmem_base + (uint32_t)(st * C::ACOLS);
-          const uint32_t b0 = smem_u32(dtile(st));
-#pragma unroll
-          for (int gb = 0; gb < GPB / C::GB; ++gb, ++bi) {
-            const int d = bi % C::NBATCH;
-            if (!mbar_wait(&d_empty[d], ((uint32_t)(bi / C::NBATCH) & 1u) ^ 1u, abort_flag)) {
-              kernel_fail(status, abort_flag, kDevTimeoutMma);
-              goto done;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int u = 0; u < C::GB; ++u) {
-              const int g4 = gb * C::GB + u;
-              mma_i8_ta(tmem_base + (uint32_t)(C::D_COL0 + (d * C::GB + u) * C::N3), a_tm + (uint32_t)(g4 * 8),
-                        desc_kmajor_sw128(b0 + (uint32_t)(g4 * 32)), idesc, 0u);
-            }
-            tc_commit(&d_full[d]);
-          }
-          tc_commit(&blk_done[st]);
         }
       }
     }
@@ -352,7 +375,7 @@ __global__ void __launch_bounds__(Wo4G<BM>::THREADS, 1)
     constexpr int JR = LCW / 3 < C::CPW ? LCW / 3 : C::CPW;  // rows a warp can hold
     constexpr int GL = C::GB < 64 / LCW ? C::GB : (64 / LCW > 0 ? 64 / LCW : 1);  // groups per load round
     static_assert(LCW % 4 == 0 && LCW <= 3 * C::CPW && C::GB % GL == 0, "drain load shape");
-    const int q = warp & 3, r = 32 * q + lane, j0 = ((warp - 6) >> 2) * C::CPW;
+    const int q = warp & 3, r = 32 * q + lane, j0 = ((warp - C::DRAIN0) >> 2) * C::CPW;
     const int jn = min(JR, M - j0);  // live rows of this warp (may be <= 0)
     int bi = 0, sc = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {

@@ -521,14 +521,14 @@ static bool wo4g_ok(int m, int n, int k, int group, const float* A, const void* 
          aligned16(sw) && (n + 127) / 128 >= std::max(1, sm_count());
 }
 
-template <int BM, int LCW>
+template <int NC, int LCW>
 static int launch_wo4g(int m, int n, int k, const float* A, const void* wq, const float* sw, const float* bias,
                        float* Y, cudaStream_t s) {
-  using C = Wo4G<BM>;
-  float* scratch = g_wo_ax.get((size_t)3 * BM * k / 4 + 128, s);  // digit images (3 BM k bytes), then rowf [128]
+  using C = Wo4G<NC>;
+  float* scratch = g_wo_ax.get((size_t)NC * k / 4 + 128, s);  // digit images (NC k bytes), then rowf [128]
   if (!scratch) return fail(OC_ERR_OUT_OF_MEMORY, "qgemm (weight-only): scratch allocation failed");
   int8_t* dig = reinterpret_cast<int8_t*>(scratch);
-  float* rowf = scratch + (size_t)3 * BM * k / 4;
+  float* rowf = scratch + (size_t)NC * k / 4;
   CUtensorMap tw, tsc;
   int rc = make_tmap_2d(&tw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, (uint64_t)k / 2,
                         C::RBK / 2, C::BN, CU_TENSOR_MAP_SWIZZLE_64B);
@@ -536,10 +536,10 @@ static int launch_wo4g(int m, int n, int k, const float* A, const void* wq, cons
   rc = make_tmap_2d(&tsc, sw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k / 32, (uint64_t)n, (uint64_t)k / 8,
                     C::SCB * C::RBK / 32, C::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  auto kern = gemm_wo4g_kernel<BM, LCW>;
+  auto kern = gemm_wo4g_kernel<NC, LCW>;
   if (!smem_attr_once(reinterpret_cast<const void*>(kern), C::SMEM))
     return fail(OC_ERR_LAUNCH_FAILED, "cudaFuncSetAttribute(gemm_wo4g_kernel) failed");
-  rc = wo_launch_rc(launch_pdl_ex(wo4g_prep_kernel, dim3(BM), dim3(128), 0, s, A, m, k, dig, rowf),
+  rc = wo_launch_rc(launch_pdl_ex(wo4g_prep_kernel, dim3(C::BM), dim3(128), 0, s, A, m, k, NC, dig, rowf),
                     "wo4g_prep_kernel");
   if (rc) return rc;
   const int grid = std::min((n + C::BN - 1) / C::BN, std::max(1, sm_count()));
@@ -550,14 +550,15 @@ static int launch_wo4g(int m, int n, int k, const float* A, const void* wq, cons
 
 static int run_wo4g(int m, int n, int k, const float* A, const void* wq, const float* sw, const float* bias,
                     float* Y, cudaStream_t s) {
-  // the drain loads 3 columns per live row of a group (in 4-column steps)
+  // MMA N = 3 rows per activation row, padded to 16; the drain loads 3
+  // columns per live row of a group (in 4-column steps)
   if (m == 1) return launch_wo4g<16, 4>(m, n, k, A, wq, sw, bias, Y, s);
   if (m == 2) return launch_wo4g<16, 8>(m, n, k, A, wq, sw, bias, Y, s);
   if (m <= 5) return launch_wo4g<16, 16>(m, n, k, A, wq, sw, bias, Y, s);
-  if (m <= 10) return launch_wo4g<16, 32>(m, n, k, A, wq, sw, bias, Y, s);
-  if (m <= 16) return launch_wo4g<16, 48>(m, n, k, A, wq, sw, bias, Y, s);
-  if (m <= 32) return launch_wo4g<32, 48>(m, n, k, A, wq, sw, bias, Y, s);
-  return launch_wo4g<64, 96>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m <= 10) return launch_wo4g<32, 32>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m <= 16) return launch_wo4g<48, 48>(m, n, k, A, wq, sw, bias, Y, s);
+  if (m <= 32) return launch_wo4g<96, 48>(m, n, k, A, wq, sw, bias, Y, s);
+  return launch_wo4g<192, 96>(m, n, k, A, wq, sw, bias, Y, s);
 }
 
 int run_qgemm_wo(int bits, int m, int n, int k, int group, const float* A, const void* wq, const float* sw,

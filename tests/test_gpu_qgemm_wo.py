@@ -240,7 +240,7 @@ def test_w4_skinny_chunk_outliers(oc, oracle, m, group, a_scale):
         assert rel_fro(yr[r], rr[r]) <= REL_FRO, (r, rel_fro(yr[r], rr[r]))
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 7, 12, 16, 17, 33, 64])
+@pytest.mark.parametrize("m", [1, 2, 3, 7, 10, 12, 16, 17, 33, 64])
 def test_w4_few_rows_many_columns(oc, oracle, m):
     # 1-64 rows over enough 128-column weight tiles to fill the GPU (here
     # 19000 columns, the last tile ragged), groups of 32: the packed weights
