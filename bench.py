@@ -294,6 +294,15 @@ def q_ops() -> int:
     return 2 * sum(2 * m * Q_K * Q_N for m in Q_M)  # two weight types
 
 
+def wo_kernel_name(kind: str, m: int, k: int, n: int, group: int = Q_G) -> str:
+    """The weight-only route the library takes for this call (oc_qgemm_wo.cu)."""
+    if kind == "w4" and group == 32 and 1 <= m <= 64 and k % 128 == 0 and (n + 127) // 128 >= 148:
+        return "wo4g_prep_kernel + gemm_wo4g_kernel"
+    if m <= 16:
+        return "wo_skinny_kernel"
+    return "wo_prep_kernel + gemm_wo_kernel (one call)"
+
+
 def wo_bytes(kind: str, m: int, k: int, n: int, group: int = Q_G) -> int:
     """Algorithmic bytes of one weight-only call: f32 A + quantized weights +
     f32 scales + bias + f32 Y."""
@@ -425,7 +434,7 @@ def qgemm_cold_gemv(ctx, once: bool = False):
         nb = wo_bytes(kind, 1, V_K, V_N)
         out[f"{kind}_M1_K{V_K}_N{V_N}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1),
                                            "frac_hbm": round(nb / us / 1e3 / ctx.peaks[0], 4),
-                                           "bytes": nb, "kernel": "wo_skinny_kernel"}
+                                           "bytes": nb, "kernel": wo_kernel_name(kind, 1, V_K, V_N)}
     del q8, s8, q4, s4
     torch.cuda.empty_cache()
     return out
@@ -715,7 +724,7 @@ def run_qgemm(ctx):
     dom = max(per, key=lambda key: per[key]["us"])
     dkind, dm = dom.split("_M")
     dm = int(dm)
-    what = ("wo_skinny_kernel" if dm <= 16 else "wo_prep_kernel + gemm_wo_kernel (one call)") + f" {dkind} M={dm}"
+    what = wo_kernel_name(dkind, dm, Q_K, Q_N) + f" {dkind} M={dm}"
     roof = roofline_wo(dkind, dm, Q_K, Q_N, per[dom]["us"], ctx.peaks, what)
 
     # the int8-activation kernels (W8A8 / W4A8, exact int32) on the same sets
@@ -1249,7 +1258,10 @@ def run_int4(ctx):
             q4, s4 = c["w"][i % len(c["w"])]
             for m in I_M:
                 y = oc.qgemm_w4(c["A"][m], q4, s4, I_G, bias=c["bias"])
-                n_l += wo_launches(m, I_K) * (1 if m <= 16 else -(-c["plan"].cols // wo_chunk_cols(I_K)))
+                if wo_kernel_name("w4", m, I_K, c["plan"].cols, I_G).startswith("wo4g"):
+                    n_l += 2  # digit preparation + GEMM
+                else:
+                    n_l += wo_launches(m, I_K) * (1 if m <= 16 else -(-c["plan"].cols // wo_chunk_cols(I_K)))
                 if ctx.world > 1:
                     shard.gather_columns(y, c["plan"])
                     n_l += 1  # gather kernel (plus the NCCL all-gather)
@@ -1283,7 +1295,7 @@ def run_int4(ctx):
     dom = max(per, key=lambda k: per[k]["us"])
     dm, dn = [int(x[1:]) for x in dom.split("_")]
     nl = cases[dn]["plan"].cols
-    what = ("wo_skinny_kernel" if dm <= 16 else "wo_prep_kernel + gemm_wo_kernel (one call)") + f" M={dm} N={nl}"
+    what = wo_kernel_name("w4", dm, I_K, nl, I_G) + f" M={dm} N={nl}"
     roof = roofline_wo("w4", dm, I_K, nl, per[dom]["us"], ctx.peaks, what)
     # e2e: rank 0 runs the host-slice call for its shard (weights copied per call, as blas does)
     dev = oc.Device(ctx.local)
