@@ -337,11 +337,16 @@ int oc_qgemm_w4a8(int m, int n, int k, int group, const float *A, const uint8_t 
  *                                           W^T with group = k)
  *   x = (nib - 8) * w_scales[(n*k + k') / group]   (oc_qgemm_w4: quantize_int4
  *                                           of W^T, packed two per byte)
- * f32 work, within 1e-5 relative Frobenius of the f32 reference.  m <= 16
- * streams the weights once on the CUDA cores; larger m runs a tcgen05 GEMM
- * on f16 terms of both operands (~22 significant bits each, f32
- * accumulation), in column chunks whose expanded weights fit in L2.
- * Scratch for the expanded terms and K-split partial sums is kept per
+ * f32 work, within 1e-5 relative Frobenius of the f32 reference.  INT4
+ * with group 32, 1 <= m <= 64, k % 128 == 0 and n >= 18944 (enough
+ * 128-column tiles for every SM) runs a tcgen05 kind::i8 GEMM on the packed
+ * weights widened to int8 on chip and each activation row as three int8
+ * digits of a per-row power-of-two scaling (rounding at 2^-23 of the row's
+ * largest |a|; a row holding a NaN or an infinity yields NaN outputs).
+ * Otherwise m <= 16 streams the weights once on the CUDA cores; larger m
+ * runs a tcgen05 GEMM on f16 terms of both operands (~22 significant bits
+ * each, f32 accumulation), in column chunks whose expanded weights fit in L2.
+ * Scratch for the digits, the expanded terms and K-split partial sums is kept per
  * (device, stream) inside the library and grows on first use of a larger
  * shape (that first call synchronizes the device: make it before any stream
  * capture).  bias may be NULL.  Any group > 0 is accepted for INT4 (groups
