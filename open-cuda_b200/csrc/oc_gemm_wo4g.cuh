@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(Wo4G<NC>::THREADS, 1)
     // scales from its scale tile), rows past M skipped; the tile's outputs
     // once its groups are in
     constexpr int JR = LCW / 3 < C::CPW ? LCW / 3 : C::CPW;  // rows a warp can hold
-    constexpr int GL = C::GB < 64 / LCW ? C::GB : (64 / LCW > 0 ? 64 / LCW : 1);  // groups per load round
+    constexpr int GL = C::GB < 64 / LCW ? C::GB : (64 / LCW > 0 ? 64 / LCW : 1);  // groups per load pass
     static_assert(LCW % 4 == 0 && LCW <= 3 * C::CPW && C::GB % GL == 0, "drain load shape");
     const int q = warp & 3, r = 32 * q + lane, j0 = ((warp - C::DRAIN0) >> 2) * C::CPW;
     const int jn = min(JR, M - j0);  // live rows of this warp (may be <= 0)
