@@ -18,7 +18,7 @@
 // largest |a|, far inside the 1e-5 relative Frobenius bound of the f32 path.
 // A row holding a NaN or an infinity yields NaN outputs.
 //
-// Cost.  One kind::i8 MMA (M = 128, N = 3 BM, K = 32) per group of a tile.
+// Cost.  One kind::i8 MMA (M = 128, N = NC, K = 32) per group of a tile.
 // A tcgen05.mma costs about 61 cycles for any N up to 64 (69 at 128, 99 at
 // 192), so the MMA count sets the pace, and K = 32 halves it against f16
 // operands.  The packed weights are read once from HBM (0.5 byte per
@@ -29,9 +29,11 @@
 // rows = output columns; within each 8-k block, byte positions 0-3 hold k =
 // 0, 2, 4, 6 and 4-7 hold k = 1, 3, 5, 7: the low and the high nibbles of a
 // packed word), B = the activation digits in shared memory with the same k
-// order, row-interleaved (row 3 m + p holds digit p of activation row m, N
-// = 3 BM, K-major, 128-byte swizzle, one TMA box per raw block), D = a ring
-// of NB accumulators of 3 BM columns, one per group, handed to the drain in
+// order, row-interleaved (row 3 m + p holds digit p of activation row m; N
+// = NC = 16, 32, 48, 96 or 192 rows for up to 5, 10, 16, 32 or 64 activation
+// rows; K-major, 128-byte swizzle, one bulk copy of the prepared image per
+// raw block), D = a ring of NB accumulators of NC columns (NB as many as
+// tensor memory holds, up to 24), one per group, handed to the drain in
 // batches of GB groups (a try_wait costs about 60 cycles and a commit about
 // 37 even when nothing waits, against 61 for the MMA).  The drain loads only
 // the 3 M live columns of a group (LCW of them per warp, rounded up to a
